@@ -1,0 +1,378 @@
+// thompiler runner: loads compile.py's PTX with the CUDA driver's JIT and
+// launches it (the C ABI of include/thompiler_runner.h).
+//
+// The library links the CUDA runtime statically and reaches the driver API
+// through cudaGetDriverEntryPointByVersion, so it loads on a machine
+// without a GPU driver (the build host) and only needs libcuda at thr_init.
+// It contains no kernels: every kernel it runs is PTX text from the
+// compiler.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/thompiler_runner.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int status, const char *fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(THR_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---- driver entry points ------------------------------------------------
+
+typedef CUresult (*PFN_LoadDataEx)(CUmodule *, const void *, unsigned, CUjit_option *, void **);
+typedef CUresult (*PFN_Unload)(CUmodule);
+typedef CUresult (*PFN_GetFunction)(CUfunction *, CUmodule, const char *);
+typedef CUresult (*PFN_GetGlobal)(CUdeviceptr *, size_t *, CUmodule, const char *);
+typedef CUresult (*PFN_FuncGetAttribute)(int *, CUfunction_attribute, CUfunction);
+typedef CUresult (*PFN_FuncSetAttribute)(CUfunction, CUfunction_attribute, int);
+typedef CUresult (*PFN_LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned,
+                                     unsigned, unsigned, CUstream, void **, void **);
+typedef CUresult (*PFN_TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                             const cuuint64_t *, const cuuint64_t *,
+                                             const cuuint32_t *, const cuuint32_t *,
+                                             CUtensorMapInterleave, CUtensorMapSwizzle,
+                                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*PFN_GetErrorString)(CUresult, const char **);
+
+struct Driver {
+    bool ok = false;
+    PFN_LoadDataEx load = nullptr;
+    PFN_Unload unload = nullptr;
+    PFN_GetFunction get_function = nullptr;
+    PFN_GetGlobal get_global = nullptr;
+    PFN_FuncGetAttribute func_get = nullptr;
+    PFN_FuncSetAttribute func_set = nullptr;
+    PFN_LaunchKernel launch = nullptr;
+    PFN_TensorMapEncodeTiled tmap = nullptr;
+    PFN_GetErrorString err_string = nullptr;
+};
+
+Driver g_drv;
+std::mutex g_mu;
+
+template <typename T>
+bool entry(const char *name, T *out) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion(name, &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) return false;
+    *out = reinterpret_cast<T>(fn);
+    return true;
+}
+
+const char *cu_name(CUresult r) {
+    const char *s = nullptr;
+    if (g_drv.err_string && g_drv.err_string(r, &s) == CUDA_SUCCESS && s) return s;
+    return "unknown CUDA driver error";
+}
+
+int drv_fail(CUresult r, const char *what) {
+    return fail(r == CUDA_ERROR_NOT_FOUND ? THR_ERR_LOOKUP : THR_ERR_CUDA, "%s: %s (CUresult %d)",
+                what, cu_name(r), (int)r);
+}
+
+int ensure_driver() {
+    if (g_drv.ok) return THR_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_drv.ok) return THR_OK;
+    cudaError_t e = cudaFree(nullptr);  // creates / binds the primary context
+    if (e != cudaSuccess) return cuda_fail(e, "CUDA runtime initialisation");
+    Driver d;
+    bool all = entry("cuModuleLoadDataEx", &d.load) && entry("cuModuleUnload", &d.unload) &&
+               entry("cuModuleGetFunction", &d.get_function) &&
+               entry("cuModuleGetGlobal", &d.get_global) &&
+               entry("cuFuncGetAttribute", &d.func_get) && entry("cuFuncSetAttribute", &d.func_set) &&
+               entry("cuLaunchKernel", &d.launch) && entry("cuGetErrorString", &d.err_string);
+    entry("cuTensorMapEncodeTiled", &d.tmap);  // optional: only TMA kernels need it
+    if (!all) return fail(THR_ERR_CUDA, "the CUDA driver does not export the required entry points");
+    d.ok = true;
+    g_drv = d;
+    return THR_OK;
+}
+
+// ---- the runner's device buffers -----------------------------------------
+
+struct Slot {
+    void *ptr = nullptr;
+    uint64_t cap = 0;
+};
+std::vector<Slot> g_slots;
+
+int slot_buffer(size_t i, uint64_t nbytes, void **out) {
+    if (g_slots.size() <= i) g_slots.resize(i + 1);
+    Slot &s = g_slots[i];
+    if (s.cap < nbytes || s.ptr == nullptr) {
+        if (s.ptr) cudaFree(s.ptr);
+        s.ptr = nullptr;
+        s.cap = 0;
+        uint64_t want = std::max<uint64_t>(nbytes, 256);
+        cudaError_t e = cudaMalloc(&s.ptr, want);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc of a run buffer");
+        s.cap = want;
+    }
+    *out = s.ptr;
+    return THR_OK;
+}
+
+int wait_event(cudaEvent_t ev, double timeout_s) {
+    auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return THR_OK;
+        if (e != cudaErrorNotReady) return fail(THR_ERR_RUN, "launch failed: %s", cudaGetErrorString(e));
+        double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (timeout_s > 0 && el > timeout_s)
+            return fail(THR_ERR_TIMEOUT, "the launch did not finish within %.1f s", timeout_s);
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int thr_version(void) { return 1; }
+
+int thr_init(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(THR_ERR_REQUEST, "device %d of %d", device, n);
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    return ensure_driver();
+}
+
+int thr_device_info(int device, int *sm_count, int *cc_major, int *cc_minor, char *name, size_t name_len) {
+    cudaDeviceProp p;
+    cudaError_t e = cudaGetDeviceProperties(&p, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (sm_count) *sm_count = p.multiProcessorCount;
+    if (cc_major) *cc_major = p.major;
+    if (cc_minor) *cc_minor = p.minor;
+    if (name && name_len) {
+        strncpy(name, p.name, name_len - 1);
+        name[name_len - 1] = 0;
+    }
+    return THR_OK;
+}
+
+int thr_module_load(const char *ptx, uint64_t *module, char *log, size_t log_len) {
+    if (!ptx || !module) return fail(THR_ERR_REQUEST, "thr_module_load: null argument");
+    int s = ensure_driver();
+    if (s) return s;
+    std::vector<char> info(16384, 0), error(16384, 0);
+    CUjit_option opts[5] = {CU_JIT_INFO_LOG_BUFFER, CU_JIT_INFO_LOG_BUFFER_SIZE_BYTES,
+                            CU_JIT_ERROR_LOG_BUFFER, CU_JIT_ERROR_LOG_BUFFER_SIZE_BYTES,
+                            CU_JIT_LOG_VERBOSE};
+    void *vals[5] = {info.data(), (void *)(uintptr_t)info.size(), error.data(),
+                     (void *)(uintptr_t)error.size(), (void *)(uintptr_t)1};
+    CUmodule m = nullptr;
+    CUresult r = g_drv.load(&m, ptx, 5, opts, vals);
+    if (log && log_len) {
+        strncpy(log, info.data(), log_len - 1);
+        log[log_len - 1] = 0;
+    }
+    if (r != CUDA_SUCCESS)
+        return fail(THR_ERR_PTXAS, "PTX JIT failed (%s): %s", cu_name(r), error.data());
+    *module = (uint64_t)(uintptr_t)m;
+    return THR_OK;
+}
+
+int thr_module_unload(uint64_t module) {
+    int s = ensure_driver();
+    if (s) return s;
+    CUresult r = g_drv.unload((CUmodule)(uintptr_t)module);
+    return r == CUDA_SUCCESS ? THR_OK : drv_fail(r, "cuModuleUnload");
+}
+
+int thr_get_function(uint64_t module, const char *entry_name, uint64_t *function) {
+    int s = ensure_driver();
+    if (s) return s;
+    CUfunction f = nullptr;
+    CUresult r = g_drv.get_function(&f, (CUmodule)(uintptr_t)module, entry_name);
+    if (r != CUDA_SUCCESS) return fail(THR_ERR_LOOKUP, "no entry %s in the module (%s)", entry_name, cu_name(r));
+    *function = (uint64_t)(uintptr_t)f;
+    return THR_OK;
+}
+
+int thr_function_attrs(uint64_t function, int *num_regs, int *max_threads, int *static_smem, int *local_bytes) {
+    int s = ensure_driver();
+    if (s) return s;
+    CUfunction f = (CUfunction)(uintptr_t)function;
+    int v = 0;
+    if (num_regs && g_drv.func_get(&v, CU_FUNC_ATTRIBUTE_NUM_REGS, f) == CUDA_SUCCESS) *num_regs = v;
+    if (max_threads && g_drv.func_get(&v, CU_FUNC_ATTRIBUTE_MAX_THREADS_PER_BLOCK, f) == CUDA_SUCCESS) *max_threads = v;
+    if (static_smem && g_drv.func_get(&v, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, f) == CUDA_SUCCESS) *static_smem = v;
+    if (local_bytes && g_drv.func_get(&v, CU_FUNC_ATTRIBUTE_LOCAL_SIZE_BYTES, f) == CUDA_SUCCESS) *local_bytes = v;
+    return THR_OK;
+}
+
+int thr_module_global(uint64_t module, const char *name, uint64_t *dptr, uint64_t *nbytes) {
+    int s = ensure_driver();
+    if (s) return s;
+    CUdeviceptr p = 0;
+    size_t n = 0;
+    CUresult r = g_drv.get_global(&p, &n, (CUmodule)(uintptr_t)module, name);
+    if (r != CUDA_SUCCESS) return fail(THR_ERR_LOOKUP, "no global %s in the module (%s)", name, cu_name(r));
+    if (dptr) *dptr = (uint64_t)p;
+    if (nbytes) *nbytes = (uint64_t)n;
+    return THR_OK;
+}
+
+int thr_launch(uint64_t function, const uint32_t grid[3], const uint32_t block[3], uint32_t smem_bytes,
+               const uint64_t *args, int nargs, uint64_t stream) {
+    int s = ensure_driver();
+    if (s) return s;
+    if (!grid || !block || nargs < 0 || (nargs > 0 && !args)) return fail(THR_ERR_REQUEST, "thr_launch: bad arguments");
+    CUfunction f = (CUfunction)(uintptr_t)function;
+    if (smem_bytes > 48 * 1024) {
+        CUresult r = g_drv.func_set(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem_bytes);
+        if (r != CUDA_SUCCESS) return drv_fail(r, "raising the dynamic shared memory limit");
+    }
+    std::vector<uint64_t> vals(args, args + nargs);
+    std::vector<void *> params(nargs);
+    for (int i = 0; i < nargs; ++i) params[i] = &vals[i];
+    CUresult r = g_drv.launch(f, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem_bytes,
+                              (CUstream)(uintptr_t)stream, nargs ? params.data() : nullptr, nullptr);
+    return r == CUDA_SUCCESS ? THR_OK : fail(THR_ERR_RUN, "cuLaunchKernel: %s", cu_name(r));
+}
+
+int thr_run(uint64_t function, const uint32_t grid[3], const uint32_t block[3], uint32_t smem_bytes,
+            const thr_arg *args, int nargs, int warmup, int iters, double timeout_s, float *median_us,
+            uint64_t stream) {
+    int s = ensure_driver();
+    if (s) return s;
+    if (nargs < 0 || (nargs && !args) || warmup < 0 || iters < 0)
+        return fail(THR_ERR_REQUEST, "thr_run: bad arguments");
+    cudaStream_t st = (cudaStream_t)(uintptr_t)stream;
+    std::vector<uint64_t> dev(nargs);
+    for (int i = 0; i < nargs; ++i) {
+        void *p = nullptr;
+        if ((s = slot_buffer(i, args[i].nbytes, &p))) return s;
+        dev[i] = (uint64_t)(uintptr_t)p;
+        cudaError_t e = args[i].kind == THR_ARG_INPUT
+                            ? cudaMemcpyAsync(p, args[i].host, args[i].nbytes, cudaMemcpyHostToDevice, st)
+                            : cudaMemsetAsync(p, 0, args[i].nbytes, st);
+        if (e != cudaSuccess) return cuda_fail(e, "staging a run argument");
+    }
+    auto rezero = [&]() -> int {
+        for (int i = 0; i < nargs; ++i)
+            if (args[i].zero_each) {
+                cudaError_t e = cudaMemsetAsync((void *)(uintptr_t)dev[i], 0, args[i].nbytes, st);
+                if (e != cudaSuccess) return cuda_fail(e, "zeroing an output");
+            }
+        return THR_OK;
+    };
+    int total = warmup + std::max(iters, 1);
+    std::vector<cudaEvent_t> ev(2 * total, nullptr);
+    for (auto &e : ev)
+        if (cudaEventCreate(&e) != cudaSuccess) return fail(THR_ERR_CUDA, "cudaEventCreate");
+    int rc = THR_OK;
+    for (int k = 0; k < total && rc == THR_OK; ++k) {
+        if ((rc = rezero())) break;
+        cudaEventRecord(ev[2 * k], st);
+        rc = thr_launch(function, grid, block, smem_bytes, dev.data(), nargs, stream);
+        cudaEventRecord(ev[2 * k + 1], st);
+    }
+    if (rc == THR_OK) rc = wait_event(ev[2 * total - 1], timeout_s);
+    if (rc == THR_OK) {
+        std::vector<float> t;
+        for (int k = warmup; k < total; ++k) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, ev[2 * k], ev[2 * k + 1]);
+            t.push_back(ms * 1000.0f);
+        }
+        std::sort(t.begin(), t.end());
+        if (median_us) *median_us = t.empty() ? 0.0f : t[t.size() / 2];
+        for (int i = 0; i < nargs && rc == THR_OK; ++i)
+            if (args[i].kind == THR_ARG_OUTPUT) {
+                cudaError_t e = cudaMemcpyAsync(args[i].host, (void *)(uintptr_t)dev[i], args[i].nbytes,
+                                                cudaMemcpyDeviceToHost, st);
+                if (e != cudaSuccess) rc = cuda_fail(e, "copying an output back");
+            }
+        if (rc == THR_OK) {
+            cudaError_t e = cudaStreamSynchronize(st);
+            if (e != cudaSuccess) rc = fail(THR_ERR_RUN, "run failed: %s", cudaGetErrorString(e));
+        }
+    }
+    for (auto &e : ev) cudaEventDestroy(e);  // deferred by CUDA if still pending
+    return rc;
+}
+
+int thr_tensor_map(void *out128, int dtype_code, int rank, uint64_t base, const uint64_t *dims,
+                   const uint64_t *strides_bytes, const uint32_t *box, int swizzle) {
+    int s = ensure_driver();
+    if (s) return s;
+    if (!g_drv.tmap) return fail(THR_ERR_CUDA, "the driver has no cuTensorMapEncodeTiled");
+    if (!out128 || rank < 1 || rank > 5 || !dims || !box) return fail(THR_ERR_REQUEST, "thr_tensor_map: bad arguments");
+    CUtensorMapDataType dt = dtype_code == 0   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                             : dtype_code == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    CUtensorMapSwizzle sw = swizzle == 3   ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : swizzle == 2 ? CU_TENSOR_MAP_SWIZZLE_64B
+                            : swizzle == 1 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                           : CU_TENSOR_MAP_SWIZZLE_NONE;
+    cuuint64_t gd[5], gs[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        gd[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) gs[i] = strides_bytes[i];
+    }
+    CUresult r = g_drv.tmap((CUtensorMap *)out128, dt, (cuuint32_t)rank, (void *)(uintptr_t)base, gd, gs, bx, es,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? THR_OK : drv_fail(r, "cuTensorMapEncodeTiled");
+}
+
+int thr_memcpy_htod(uint64_t dst, const void *src, uint64_t nbytes, uint64_t stream) {
+    cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)dst, src, nbytes, cudaMemcpyHostToDevice,
+                                    (cudaStream_t)(uintptr_t)stream);
+    return e == cudaSuccess ? THR_OK : cuda_fail(e, "host to device copy");
+}
+
+int thr_synchronize(void) {
+    cudaError_t e = cudaDeviceSynchronize();
+    return e == cudaSuccess ? THR_OK : fail(THR_ERR_RUN, "device synchronise: %s", cudaGetErrorString(e));
+}
+
+int thr_release_buffers(void) {
+    for (auto &s : g_slots)
+        if (s.ptr) cudaFree(s.ptr);
+    g_slots.clear();
+    return THR_OK;
+}
+
+int thr_last_error(char *buf, size_t n) {
+    if (!buf || !n) return THR_ERR_REQUEST;
+    strncpy(buf, g_err.c_str(), n - 1);
+    buf[n - 1] = 0;
+    return THR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,42 @@
+"""The pipeline: KernelInfo -> PTX text.
+
+``compile_kernel`` first asks the family recognisers (thompiler.families)
+whether the kernel is one of the shapes this backend has a hand-tuned
+sm_100a body for (full sums, row reductions with an elementwise pass,
+pointwise maps, f16 tensor-core matmuls, attention).  A recognised kernel
+is emitted by its family; anything else goes through the generic
+statement-by-statement lowering.  Both produce one module with one entry
+named after the IR kernel and taking meta.json's ``arg_order`` pointers, and
+both are correct under meta.json's launch.  A family may add a tuned launch
+record (``// @thompiler-launch {...}``) that this backend's runner honours.
+
+``THOMPILER_GENERIC=1`` in the environment forces the generic lowering.
+"""
+
+from __future__ import annotations
+
+import os
+
+from thompiler import prologue
+from thompiler.emitter import Emitter
+from thompiler.load import KernelInfo
+from thompiler.walk import Walker
+
+
+def compile_generic(kernel: KernelInfo) -> str:
+    em = Emitter()
+    prologue.emit_param_loads(em, kernel)
+    Walker(em, kernel).body(kernel.body)
+    em.ins("ret")
+    return em.render(prologue.header(), kernel.name, prologue.params(kernel))
+
+
+def compile_kernel(kernel: KernelInfo, tuned: bool | None = None) -> str:
+    if tuned is None:
+        tuned = os.environ.get("THOMPILER_GENERIC", "") in ("", "0")
+    if tuned:
+        from thompiler import families
+        family = families.recognise(kernel)
+        if family is not None:
+            return family.emit()
+    return compile_generic(kernel)

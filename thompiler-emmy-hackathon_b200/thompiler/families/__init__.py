@@ -1,0 +1,13 @@
+"""Hand-tuned sm_100a kernel families, chosen by recognising the IR's shape.
+
+``recognise(kernel)`` returns an object with ``emit() -> str`` for a kernel
+this backend has a tuned body for, else None (generic lowering).
+"""
+
+from __future__ import annotations
+
+from thompiler.load import KernelInfo
+
+
+def recognise(kernel: KernelInfo):
+    return None

@@ -1,0 +1,271 @@
+"""Python client of the C-ABI runner (libthrunner.so, include/thompiler_runner.h).
+
+It mirrors the hackathon runner's two calls (the reference's docs/API.md):
+
+  * ``compile_ptx(ptx)`` -> ``{"ok", "entry_points", "registers", "stage", "stderr", "module"}``
+    (POST /compile; failures are returned with a stage, never raised);
+  * ``run(...)`` on host numpy buffers -> ``{"ok", "median_us", "outputs", "stage", "stderr"}``
+    (POST /run with args in arg_order, ``zero_outputs`` re-zeroed before
+    every launch);
+
+plus ``launch`` on device pointers for callers that keep data resident on
+the GPU (PyTorch tensors), and the launch plan: meta.json's geometry, or the
+tuned launch a family recorded in the PTX (``// @thompiler-launch``), with
+the module globals (tensor maps, scratch words) that launch needs.
+
+There is no fallback: without the built library every call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+
+from thompiler.emitter import read_sidecar
+
+LIB_PATH = Path(__file__).resolve().parent.parent / "libthrunner.so"
+
+STAGES = {1: "ptxas", 2: "lookup", 3: "run", 4: "request", 5: "timeout", 6: "cuda"}
+
+
+class RunnerError(RuntimeError):
+    def __init__(self, stage: str, message: str):
+        super().__init__(f"[{stage}] {message}")
+        self.stage = stage
+        self.message = message
+
+
+class ThrArg(ctypes.Structure):
+    _fields_ = [("host", ctypes.c_void_p), ("nbytes", ctypes.c_uint64),
+                ("kind", ctypes.c_int32), ("zero_each", ctypes.c_int32)]
+
+
+_lib = None
+_inited: set[int] = set()
+
+
+def library() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RunnerError("cuda", f"runner library {LIB_PATH} is not built (run __graft_entry__.build())")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        u64, i32, p = ctypes.c_uint64, ctypes.c_int, ctypes.c_void_p
+        u32x3 = ctypes.POINTER(ctypes.c_uint32)
+        sig = {
+            "thr_version": ([], i32),
+            "thr_init": ([i32], i32),
+            "thr_device_info": ([i32, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32),
+                                 ctypes.c_char_p, ctypes.c_size_t], i32),
+            "thr_module_load": ([ctypes.c_char_p, ctypes.POINTER(u64), ctypes.c_char_p, ctypes.c_size_t], i32),
+            "thr_module_unload": ([u64], i32),
+            "thr_get_function": ([u64, ctypes.c_char_p, ctypes.POINTER(u64)], i32),
+            "thr_function_attrs": ([u64] + [ctypes.POINTER(i32)] * 4, i32),
+            "thr_module_global": ([u64, ctypes.c_char_p, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
+            "thr_launch": ([u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(u64), i32, u64], i32),
+            "thr_run": ([u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(ThrArg), i32, i32, i32,
+                         ctypes.c_double, ctypes.POINTER(ctypes.c_float), u64], i32),
+            "thr_tensor_map": ([p, i32, i32, u64, ctypes.POINTER(u64), ctypes.POINTER(u64),
+                                ctypes.POINTER(ctypes.c_uint32), i32], i32),
+            "thr_memcpy_htod": ([u64, p, u64, u64], i32),
+            "thr_synchronize": ([], i32),
+            "thr_release_buffers": ([], i32),
+            "thr_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
+        }
+        for name, (args, res) in sig.items():
+            f = getattr(lib, name)
+            f.argtypes, f.restype = args, res
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(65536)
+    library().thr_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int, what: str) -> None:
+    if status:
+        raise RunnerError(STAGES.get(status, "cuda"), f"{what}: {last_error()}")
+
+
+def init(device: int = 0) -> None:
+    if device not in _inited:
+        check(library().thr_init(device), f"thr_init({device})")
+        _inited.add(device)
+
+
+def device_info(device: int = 0) -> dict:
+    init(device)
+    sm, ma, mi = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    name = ctypes.create_string_buffer(256)
+    check(library().thr_device_info(device, sm, ma, mi, name, 256), "thr_device_info")
+    return {"sm_count": sm.value, "cc": (ma.value, mi.value), "name": name.value.decode()}
+
+
+def _dims(v) -> ctypes.Array:
+    v = list(v) + [1, 1, 1]
+    return (ctypes.c_uint32 * 3)(*[int(x) for x in v[:3]])
+
+
+ENTRY = re.compile(r"^\s*\.(?:visible\s+)?\.entry\s+([A-Za-z_$][\w$]*)\s*\(", re.M)
+
+
+@dataclass
+class Function:
+    module: "Module"
+    name: str
+    handle: int
+    num_regs: int = 0
+    max_threads: int = 0
+    static_smem: int = 0
+    local_bytes: int = 0
+
+    def launch(self, grid, block, smem: int, ptrs: list[int], stream: int = 0) -> None:
+        a = (ctypes.c_uint64 * max(1, len(ptrs)))(*[int(p) for p in ptrs])
+        check(library().thr_launch(self.handle, _dims(grid), _dims(block), int(smem), a, len(ptrs), int(stream)),
+              f"launch of {self.name}")
+
+
+@dataclass
+class Module:
+    ptx: str
+    handle: int
+    log: str = ""
+    sidecar: dict | None = None
+    functions: dict = field(default_factory=dict)
+
+    @property
+    def entry_points(self) -> list[str]:
+        return ENTRY.findall(self.ptx)
+
+    def function(self, entry: str) -> Function:
+        f = self.functions.get(entry)
+        if f is None:
+            h = ctypes.c_uint64()
+            check(library().thr_get_function(self.handle, entry.encode(), ctypes.byref(h)), f"entry {entry}")
+            r, t, s, lb = ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+            check(library().thr_function_attrs(h.value, r, t, s, lb), "thr_function_attrs")
+            f = Function(self, entry, h.value, r.value, t.value, s.value, lb.value)
+            self.functions[entry] = f
+        return f
+
+    def global_ptr(self, name: str) -> tuple[int, int]:
+        p, n = ctypes.c_uint64(), ctypes.c_uint64()
+        check(library().thr_module_global(self.handle, name.encode(), ctypes.byref(p), ctypes.byref(n)),
+              f"module global {name}")
+        return p.value, n.value
+
+    def unload(self) -> None:
+        if self.handle:
+            library().thr_module_unload(self.handle)
+            self.handle = 0
+
+
+def load_module(ptx: str, device: int = 0) -> Module:
+    init(device)
+    h = ctypes.c_uint64()
+    log = ctypes.create_string_buffer(16384)
+    check(library().thr_module_load(ptx.encode(), ctypes.byref(h), log, len(log)), "PTX JIT")
+    return Module(ptx, h.value, log.value.decode(errors="replace"), read_sidecar(ptx))
+
+
+def compile_ptx(ptx: str, device: int = 0) -> dict:
+    """POST /compile: assemble ``ptx``; never raises for a bad module."""
+    try:
+        mod = load_module(ptx, device)
+    except RunnerError as e:
+        return {"ok": False, "stage": e.stage, "stderr": e.message}
+    regs = {}
+    for entry in mod.entry_points:
+        try:
+            regs[entry] = mod.function(entry).num_regs
+        except RunnerError as e:
+            return {"ok": False, "stage": e.stage, "stderr": e.message}
+    return {"ok": True, "entry_points": mod.entry_points, "registers": regs, "module": mod}
+
+
+# ---- launch plans -----------------------------------------------------------
+
+DTYPE_CODE = {"f16": 0, "bf16": 1, "f32": 2}
+
+
+@dataclass
+class LaunchPlan:
+    grid: tuple
+    block: tuple
+    smem: int
+    tuned: bool
+    tmaps: list = field(default_factory=list)     # [(global name, tensor-map spec)]
+
+
+def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> LaunchPlan:
+    """meta.json's geometry, or the tuned launch recorded in the PTX."""
+    side = module.sidecar
+    if side is None or honour_meta:
+        return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False)
+    return LaunchPlan(tuple(side["grid"]), tuple(side["block"]), int(side.get("smem_bytes", 0)), True,
+                      list(side.get("tmaps", [])))
+
+
+def encode_tensor_map(spec: dict, base: int) -> bytes:
+    out = ctypes.create_string_buffer(128)
+    dims = (ctypes.c_uint64 * 5)(*spec["dims"])
+    strides = (ctypes.c_uint64 * 4)(*(spec.get("strides") or [0]))
+    box = (ctypes.c_uint32 * 5)(*spec["box"])
+    check(library().thr_tensor_map(out, DTYPE_CODE[spec["dtype"]], len(spec["dims"]), int(base), dims, strides,
+                                   box, int(spec.get("swizzle", 0))), "tensor map")
+    return out.raw
+
+
+def prepare(module: Module, plan: LaunchPlan, arg_order: list[str], ptrs: dict[str, int], stream: int = 0) -> None:
+    """Write the tensor maps a tuned launch reads into the module's globals."""
+    for t in plan.tmaps:
+        raw = encode_tensor_map(t, ptrs[t["param"]])
+        dst, n = module.global_ptr(t["global"])
+        if n < 128:
+            raise RunnerError("lookup", f"tensor-map global {t['global']} is {n} bytes")
+        buf = ctypes.create_string_buffer(raw, 128)
+        check(library().thr_memcpy_htod(dst, buf, 128, int(stream)), "tensor map upload")
+        # the host buffer must outlive the async copy: synchronise right away
+        check(library().thr_synchronize(), "tensor map upload")
+
+
+def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0, iters: int = 1,
+        timeout_s: float = 20.0, stream: int = 0) -> dict:
+    """POST /run on host buffers.  ``args``: dicts with ``array`` (numpy; outputs
+    are written back into it), ``output`` (bool) and ``zero_each`` (bool)."""
+    arr = (ThrArg * max(1, len(args)))()
+    keep = []
+    for i, a in enumerate(args):
+        x = np.ascontiguousarray(a["array"])
+        keep.append(x)
+        arr[i].host = x.ctypes.data
+        arr[i].nbytes = x.nbytes
+        arr[i].kind = 1 if a.get("output") else 0
+        arr[i].zero_each = 1 if a.get("zero_each") else 0
+    med = ctypes.c_float()
+    st = library().thr_run(function.handle, _dims(plan.grid), _dims(plan.block), int(plan.smem), arr, len(args),
+                           int(warmup), int(iters), float(timeout_s), ctypes.byref(med), int(stream))
+    if st:
+        return {"ok": False, "stage": STAGES.get(st, "cuda"), "stderr": last_error()}
+    for a, x in zip(args, keep):
+        if a.get("output") and x is not a["array"]:
+            a["array"][...] = x
+    return {"ok": True, "median_us": float(med.value)}
+
+
+def release() -> None:
+    if _lib is not None:
+        _lib.thr_release_buffers()
+
+
+def cdiv(a: int, b: int) -> int:
+    return -(-a // b)
+
+
