@@ -1,0 +1,441 @@
+"""Benchmark: emitted sm_100a kernels on the benchmark workloads.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config rowops|sum|bigsum]
+    python bench.py --impl reference ...       # the reference's CPU path
+
+A step is one pass of the hot path over one batch of synthetic input:
+
+  rowops  (default) fused row ops on f32 [8192, 4096] N(0,1): row softmax,
+          RMSNorm (eps 1e-6, w ~ U[0.5, 1.5)) and row L2-normalise -- three
+          kernels compiled by compile.py from IR in emmy's one-row-per-CTA
+          schedule, each on its own input matrix (3 x 128 MiB of inputs,
+          larger than the 126 MB L2, so no step reads another's data from L2);
+          N GPUs each run their own [8192, 4096] matrices (weak scaling).
+  sum     r01-style single-kernel sum of f32[1,048,576] U[-1, 1).
+  bigsum  f32[2^30] U[-1, 1) split into contiguous slices over N GPUs: one
+          two-pass grid-reduction kernel per GPU, then an NCCL all-reduce of
+          the per-GPU partials.
+
+value is the whole-job algorithmic HBM bandwidth (bytes the workload must
+move / max-over-ranks device time of the K steps, CUDA events on the launch
+stream).  e2e is the same metric through the runner's host-buffer C ABI call
+(thr_run), host <-> device copies from pinned memory included.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import signal
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "thompiler-emmy-hackathon_b200"))
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch from the committed ncu summary of this kernel, if any."""
+    f = ROOT / "profiles" / f"{name}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            return int(line.split(":")[1].strip().replace(",", ""))
+    return None
+
+
+# ---- clocks ---------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.send_signal(signal.SIGTERM)
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = [r.split(", ") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows if len(r) >= 9 for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---- workloads -----------------------------------------------------------------------
+
+class RowOps:
+    name = "rowops"
+    metric = "achieved HBM GB/s (fused row ops: softmax + RMSNorm + L2-norm)"
+    unit = "GB/s"
+    dtype = "f32"
+
+    def __init__(self, rank: int, world: int, dev: int, rows: int = 8192, cols: int = 4096):
+        import torch
+        from thompiler import synth
+        from thompiler.device import DeviceKernel
+        self.torch, self.rows, self.cols, self.eps = torch, rows, cols, 1e-6
+        tmp = Path(tempfile.mkdtemp(prefix=f"bench_rowops_{rank}_"))
+        self.kinds = ("softmax", "rmsnorm", "l2norm")
+        self.k = {}
+        for kind in self.kinds:
+            d = synth.row_package(tmp / kind, kind, rows, cols, eps=self.eps)
+            meta = json.loads((d / "meta.json").read_text())
+            self.k[kind] = DeviceKernel(d / f"{meta['kernels'][0]['entry']}.ir.json", device=dev)
+        g = torch.Generator(device=f"cuda:{dev}").manual_seed(1000 + rank)
+        self.x = {kind: torch.randn(rows, cols, device=f"cuda:{dev}", generator=g) for kind in self.kinds}
+        self.y = {kind: torch.empty(rows, cols, device=f"cuda:{dev}") for kind in self.kinds}
+        self.w = torch.rand(cols, device=f"cuda:{dev}", generator=g) + 0.5
+        self.c_count = torch.tensor([float(cols)], device=f"cuda:{dev}")
+        self.c_eps = torch.tensor([self.eps], device=f"cuda:{dev}")
+        self.kbytes = {"softmax": 2 * rows * cols * 4, "l2norm": 2 * rows * cols * 4,
+                       "rmsnorm": 2 * rows * cols * 4 + cols * 4}
+        self.bytes_per_step = sum(self.kbytes.values())
+        self.launches_per_step = 3
+        self.dominant = "softmax"
+
+    def ptrs(self, kind: str) -> dict:
+        p = {"x": self.x[kind].data_ptr()}
+        out = {"softmax": "softmax", "rmsnorm": "mul_1", "l2norm": "div"}[kind]
+        p[out] = self.y[kind].data_ptr()
+        if kind == "rmsnorm":
+            p.update(w=self.w.data_ptr(), mean_count=self.c_count.data_ptr(), add_c1=self.c_eps.data_ptr())
+        return p
+
+    def step(self, stream: int, events=None) -> None:
+        for i, kind in enumerate(self.kinds):
+            if events is not None:
+                events[kind][0].record()
+            self.k[kind](self.ptrs(kind), stream)
+            if events is not None:
+                events[kind][1].record()
+
+    def check(self) -> None:
+        torch = self.torch
+        x, y = self.x["softmax"], self.y["softmax"]
+        ref = torch.softmax(x.double(), -1)
+        assert torch.allclose(y.double(), ref, rtol=1e-5, atol=1e-6), "softmax mismatch"
+        x, y = self.x["rmsnorm"], self.y["rmsnorm"]
+        ref = x.double() / torch.sqrt((x.double() ** 2).mean(-1, keepdim=True) + self.eps) * self.w.double()
+        assert torch.allclose(y.double(), ref, rtol=1e-5, atol=1e-5), "rmsnorm mismatch"
+        x, y = self.x["l2norm"], self.y["l2norm"]
+        ref = x.double() / torch.sqrt((x.double() ** 2).sum(-1, keepdim=True))
+        assert torch.allclose(y.double(), ref, rtol=1e-5, atol=1e-6), "l2norm mismatch"
+
+    def e2e(self, steps: int) -> dict:
+        """Host-buffer path (thr_run): each step copies inputs in and results out."""
+        from thompiler import runner
+        torch = self.torch
+        host = {}
+        for kind in self.kinds:
+            hx = torch.empty(self.rows, self.cols, pin_memory=True)
+            hx.copy_(self.x[kind])
+            hy = torch.empty(self.rows, self.cols, pin_memory=True)
+            host[kind] = (hx.numpy(), hy.numpy())
+        hw = torch.empty(self.cols, pin_memory=True)
+        hw.copy_(self.w)
+        consts = {"mean_count": torch.tensor([float(self.cols)]).numpy(), "add_c1": torch.tensor([self.eps]).numpy()}
+
+        def args(kind):
+            k = self.k[kind]
+            out = []
+            for n in k.arg_order:
+                if n == "x":
+                    out.append({"array": host[kind][0]})
+                elif n == "w":
+                    out.append({"array": hw.numpy()})
+                elif n in consts:
+                    out.append({"array": consts[n]})
+                else:
+                    out.append({"array": host[kind][1], "output": True})
+            return out
+
+        runs = {kind: args(kind) for kind in self.kinds}
+        for kind in self.kinds:                 # warm the runner's buffers
+            runner.run(self.k[kind].fn, self.k[kind].plan, runs[kind])
+        t = time.perf_counter()
+        for _ in range(steps):
+            for kind in self.kinds:
+                r = runner.run(self.k[kind].fn, self.k[kind].plan, runs[kind])
+                if not r["ok"]:
+                    raise RuntimeError(r["stderr"])
+        sec = (time.perf_counter() - t) / steps
+        runner.release()
+        h2d = sum(h[0].nbytes for h in host.values()) + hw.numel() * 4 + 8
+        d2h = sum(h[1].nbytes for h in host.values())
+        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3}
+
+    def cpu_baseline(self) -> dict:
+        from oracle import cpu_baseline
+        rows = 1024
+        r = cpu_baseline.rowops_sample(rows, self.cols, self.eps)
+        bytes_sample = self.bytes_per_step * rows / self.rows
+        return {"value": bytes_sample / r["seconds"] / 1e9, "unit": "GB/s", "cores": r["cores"], "kind": "port",
+                "sample": f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {self.cols}] (1/8 of a step), "
+                          "best of 3"}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"fused row ops f32[{self.rows}, {self.cols}] x3 (softmax, rmsnorm eps=1e-6, l2norm), "
+                            "one row per CTA", "rows_per_gpu": self.rows, "cols": self.cols,
+                "kernels": {k: self.k[k].family for k in self.kinds},
+                "l2": "inputs larger than L2 (3 x 128 MiB distinct input matrices per GPU)",
+                "parallelism": f"weak: {world} GPU(s), one matrix set each, no collective"}
+
+
+class FullSum:
+    name = "sum"
+    unit = "GB/s"
+    dtype = "f32"
+
+    def __init__(self, rank: int, world: int, dev: int, n_total: int = 1 << 20, sharded: bool = False):
+        import torch
+        from thompiler import synth
+        from thompiler.device import DeviceKernel
+        self.torch, self.rank, self.world, self.sharded = torch, rank, world, sharded
+        self.n = n_total // world if sharded else n_total
+        self.n_total = n_total
+        self.metric = ("achieved HBM GB/s (sharded sum + NCCL all-reduce)" if sharded
+                       else "achieved HBM GB/s (single-kernel array sum)")
+        tmp = Path(tempfile.mkdtemp(prefix=f"bench_sum_{rank}_"))
+        d = synth.sum_package(tmp / "sum", self.n)
+        self.k = DeviceKernel(d / "k_sum_1_reduce.ir.json", device=dev)
+        g = torch.Generator(device=f"cuda:{dev}").manual_seed(7 + rank)
+        self.x = torch.rand(self.n, device=f"cuda:{dev}", generator=g) * 2 - 1
+        self.out = torch.zeros(1, device=f"cuda:{dev}")
+        self.kbytes = {"sum": self.n * 4 + 4}
+        self.bytes_per_step = self.n * 4 * (world if sharded else 1) + 4 * world
+        self.launches_per_step = 1
+        self.dominant = "sum"
+        self.kinds = ("sum",)
+
+    def step(self, stream: int, events=None) -> None:
+        if events is not None:
+            events["sum"][0].record()
+        self.k({"x": self.x.data_ptr(), "sum_1": self.out.data_ptr()}, stream)
+        if events is not None:
+            events["sum"][1].record()
+        if self.sharded and self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(self.out)
+
+    def check(self) -> None:
+        torch = self.torch
+        want = self.x.double().sum()
+        if self.sharded and self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(want)
+            self.step(self.torch.cuda.current_stream().cuda_stream)
+        else:
+            self.step(self.torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        got = float(self.out.item())
+        assert abs(got - float(want)) <= 1e-5 * max(1.0, abs(float(want))) + 1e-3, f"sum mismatch {got} vs {want}"
+
+    def e2e(self, steps: int) -> dict:
+        from thompiler import runner
+        torch = self.torch
+        hx = torch.empty(self.n, pin_memory=True)
+        hx.copy_(self.x)
+        ho = torch.zeros(1)
+        args = [{"array": hx.numpy()}, {"array": ho.numpy(), "output": True}]
+        runner.run(self.k.fn, self.k.plan, args)
+        t = time.perf_counter()
+        for _ in range(steps):
+            r = runner.run(self.k.fn, self.k.plan, args)
+            if not r["ok"]:
+                raise RuntimeError(r["stderr"])
+            if self.sharded and self.world > 1:
+                import torch.distributed as dist
+                v = torch.tensor([float(ho[0])], device=self.x.device)
+                dist.all_reduce(v)
+                float(v.item())
+        sec = (time.perf_counter() - t) / steps
+        runner.release()
+        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": hx.numel() * 4,
+                "d2h_bytes_per_step": 4, "ms_per_step": sec * 1e3}
+
+    def cpu_baseline(self) -> dict:
+        from oracle import cpu_baseline
+        n = min(self.n_total, 1 << 26)
+        r = cpu_baseline.sum_sample(n)
+        return {"value": n * 4 / r["seconds"] / 1e9, "unit": "GB/s", "cores": r["cores"], "kind": "port",
+                "sample": f"torch CPU sum of f32[{n}], best of 3"}
+
+    def config(self, world: int) -> dict:
+        c = {"workload": (f"sharded sum f32[2^{self.n_total.bit_length() - 1}] -> per-GPU two-pass reduction "
+                          "+ NCCL all-reduce" if self.sharded else f"array sum f32[{self.n}] U[-1,1)"),
+             "elements_per_gpu": self.n, "kernel": self.k.family,
+             "launch": {"grid": list(self.k.plan.grid), "block": list(self.k.plan.block)},
+             "l2": ("inputs larger than L2" if self.n * 4 > 126e6 else
+                    "input (4 MiB) fits in L2: every step after the first reads it from L2")}
+        c["parallelism"] = f"{'contiguous slices' if self.sharded else 'replicas'} over {world} GPU(s)"
+        return c
+
+
+CONFIGS = {"rowops": lambda r, w, d: RowOps(r, w, d),
+           "sum": lambda r, w, d: FullSum(r, w, d, 1 << 20),
+           "bigsum": lambda r, w, d: FullSum(r, w, d, 1 << 30, sharded=True)}
+
+
+def reference_arm(args) -> None:
+    """The reference's CPU path on this host's cores, same metric and config."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_baseline
+    cfg = args.config
+    if cfg == "rowops":
+        rows, cols = 1024, 4096
+        samples = []
+        for _ in range(args.warmup):
+            cpu_baseline.rowops_sample(rows, cols)
+        for _ in range(args.steps):
+            samples.append(cpu_baseline.rowops_sample(rows, cols)["seconds"])
+        sec = statistics.median(samples)
+        nbytes = 3 * 2 * rows * cols * 4 + cols * 4
+        value, cores = nbytes / sec / 1e9, cpu_baseline.threads()
+        sample = f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {cols}] (1/8 of a [8192, 4096] step)"
+        metric = RowOps.metric
+        config = {"workload": "fused row ops f32[8192, 4096] x3 (softmax, rmsnorm eps=1e-6, l2norm)",
+                  "sample_rows": rows}
+    else:
+        n = 1 << 26
+        samples = []
+        for _ in range(args.warmup):
+            cpu_baseline.sum_sample(n)
+        for _ in range(args.steps):
+            samples.append(cpu_baseline.sum_sample(n)["seconds"])
+        sec = statistics.median(samples)
+        value, cores = n * 4 / sec / 1e9, cpu_baseline.threads()
+        sample = f"torch CPU sum of f32[{n}]"
+        metric = "achieved HBM GB/s (single-kernel array sum)" if cfg == "sum" else \
+            "achieved HBM GB/s (sharded sum + NCCL all-reduce)"
+        config = {"workload": f"{cfg} (CPU sample of {n} elements)"}
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from thompiler import runner
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    runner.init(local)
+    w = CONFIGS[args.config](rank, world, local)
+    stream = torch.cuda.current_stream().cuda_stream
+    w.check()
+    for _ in range(args.warmup):
+        w.step(stream)
+    events = {k: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)] for k in w.kinds}
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    start.record()
+    for i in range(args.steps):
+        w.step(stream, {k: events[k][i] for k in w.kinds})
+    end.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    per_kernel = {k: statistics.mean(a.elapsed_time(b) for a, b in events[k]) for k in w.kinds}
+    e2e = None
+    if not args.no_e2e:
+        e2e = w.e2e(max(1, min(args.steps, 5)))
+        if world > 1:
+            v = torch.tensor([e2e["ms_per_step"]], device=f"cuda:{local}")
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            e2e["value"] = w.bytes_per_step * world / (float(v.item()) / 1e3) / 1e9 if not \
+                getattr(w, "sharded", False) else w.bytes_per_step / (float(v.item()) / 1e3) / 1e9
+    if rank == 0:
+        pk = peaks()
+        dom = w.dominant
+        kms = per_kernel[dom]
+        achieved = w.kbytes[dom] / (kms / 1e3) / 1e9
+        kernel_name = f"{w.k[dom].info.name if isinstance(w.k, dict) else w.k.info.name}"
+        traffic = profile_traffic(f"{kernel_name}_{args.config}")
+        total_bytes = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
+        line = {
+            "metric": w.metric, "value": total_bytes / (ms_max / 1e3) / 1e9, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "weak" if not getattr(w, "sharded", False) else "strong",
+            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic", "config": w.config(world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "traffic": traffic, "kernel": kernel_name,
+                         "peak_source": pk["source"], "kernel_ms": kms,
+                         "per_kernel_ms": per_kernel},
+            "cpu_baseline": w.cpu_baseline() if world == 1 else None,
+            "e2e": e2e, "gpu_launches": w.launches_per_step * args.steps, "clocks": clk,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -630,6 +630,14 @@ def run_package(pdir: Path, inputs: dict | None = None) -> dict:
             else:
                 if inputs is not None and a["name"] in inputs:
                     params[a["name"]] = np.asarray(inputs[a["name"]], dtype=dt).reshape(shape)
+                elif "init" in a:
+                    ini = a["init"]
+                    rng = np.random.default_rng(ini.get("seed", a.get("seed", 0)))
+                    if ini["dist"] == "uniform":
+                        v = rng.uniform(ini.get("low", 0.0), ini.get("high", 1.0), list(shape) or [1])
+                    else:
+                        v = rng.standard_normal(list(shape) or [1]) * ini.get("std", 1.0) + ini.get("mean", 0.0)
+                    params[a["name"]] = v.astype(dt).reshape(shape)
                 else:
                     params[a["name"]] = seeded(shape, a["seed"], a["dtype"]).reshape(shape)
         for name in k.get("zero_outputs", []):

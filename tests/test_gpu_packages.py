@@ -72,8 +72,8 @@ def test_generic_matches_reference_ptx(name):
     ref = problems.run_package(pkg, ref_ptx)
     mine = problems.run_package(pkg, problems.compile_package(pkg, tuned=False))
     for out, want in ref["outputs"].items():
-        if name.startswith("m02"):     # split-K red.global.add: order of the atomic adds is unspecified
-            assert_close(mine["outputs"][out], want, 1e-6, 1e-6, f"{name}/{out}")
+        if name.startswith("m02"):     # 32 split-K red.global.add per element, in unspecified order
+            assert_close(mine["outputs"][out], want, *tol(name), f"{name}/{out}")
         else:
             assert_close(mine["outputs"][out], want, 0.0, 0.0, f"{name}/{out} vs reference PTX")
 

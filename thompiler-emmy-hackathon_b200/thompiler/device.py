@@ -1,0 +1,49 @@
+"""Compiled kernels launched on device-resident buffers.
+
+``DeviceKernel(ir_path)`` compiles one IR file with this backend, JIT-loads
+the module through the runner and plans its launch (the tuned launch a
+family recorded, else meta.json's).  Calling it launches the kernel on
+device pointers given by buffer name, in meta.json's ``arg_order``, on the
+given CUDA stream -- the path for callers that keep data in HBM (PyTorch
+tensors: pass ``t.data_ptr()``).  Tensor maps a tuned launch reads are
+encoded for the pointers of the first call and re-encoded whenever a
+pointer changes.
+"""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+from thompiler import runner
+from thompiler.compiler import compile_kernel
+from thompiler.load import load
+
+
+class DeviceKernel:
+    def __init__(self, ir_path: str | Path, device: int = 0, honour_meta: bool = False, tuned: bool = True,
+                 ptx: str | None = None):
+        ir_path = Path(ir_path)
+        meta = json.loads((ir_path.parent / "meta.json").read_text())
+        self.info = load(ir_path, meta)
+        self.kmeta = next(k for k in meta["kernels"] if k["entry"] == self.info.name)
+        self.ptx = ptx if ptx is not None else compile_kernel(self.info, tuned=tuned)
+        self.module = runner.load_module(self.ptx, device)
+        self.fn = self.module.function(self.info.name)
+        self.plan = runner.plan_launch(self.module, self.kmeta, honour_meta=honour_meta)
+        self.arg_order = list(self.kmeta["arg_order"])
+        self._tmap_ptrs: dict | None = None
+
+    @property
+    def family(self) -> str:
+        side = self.module.sidecar or {}
+        return side.get("family", "generic") if side else ("tuned" if "family:" in self.ptx else "generic")
+
+    def __call__(self, ptrs: dict[str, int], stream: int = 0) -> None:
+        if self.plan.tmaps and ptrs != self._tmap_ptrs:
+            runner.prepare(self.module, self.plan, self.arg_order, ptrs, stream)
+            self._tmap_ptrs = dict(ptrs)
+        self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, [ptrs[n] for n in self.arg_order], stream)
+
+    def close(self) -> None:
+        self.module.unload()

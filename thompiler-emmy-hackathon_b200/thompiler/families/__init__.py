@@ -10,4 +10,9 @@ from thompiler.load import KernelInfo
 
 
 def recognise(kernel: KernelInfo):
+    from thompiler.families import strided
+    for fam in (strided,):
+        k = fam.recognise(kernel)
+        if k is not None:
+            return k
     return None

@@ -54,8 +54,19 @@ def load_package(pdir: str | Path) -> Package:
     return Package(pdir, meta, dict(np.load(exp)) if exp.exists() else None)
 
 
-def seeded_input(shape, seed: int, dtype: str) -> np.ndarray:
-    return np.random.default_rng(seed).standard_normal(list(shape) or [1]).astype(NP_DTYPES[dtype])
+def seeded_input(shape, seed: int, dtype: str, init: dict | None = None) -> np.ndarray:
+    """The runner's seeded input (standard normal), or the distribution an
+    ``init`` record names (synthetic packages: ``uniform`` low/high,
+    ``normal`` mean/std)."""
+    shape = list(shape) or [1]
+    if init is None:
+        return np.random.default_rng(seed).standard_normal(shape).astype(NP_DTYPES[dtype])
+    rng = np.random.default_rng(init.get("seed", seed))
+    if init["dist"] == "uniform":
+        return rng.uniform(init.get("low", 0.0), init.get("high", 1.0), shape).astype(NP_DTYPES[dtype])
+    if init["dist"] == "normal":
+        return (rng.standard_normal(shape) * init.get("std", 1.0) + init.get("mean", 0.0)).astype(NP_DTYPES[dtype])
+    raise ValueError(f"input distribution {init['dist']!r}")
 
 
 def make_inputs(pkg: Package) -> dict[str, np.ndarray]:
@@ -68,7 +79,7 @@ def make_inputs(pkg: Package) -> dict[str, np.ndarray]:
             if "data" in a:
                 out[a["name"]] = np.asarray(a["data"], dtype=NP_DTYPES[a["dtype"]]).reshape(a["shape"])
             else:
-                out[a["name"]] = seeded_input(a["shape"], a["seed"], a["dtype"])
+                out[a["name"]] = seeded_input(a["shape"], a.get("seed", 0), a["dtype"], a.get("init"))
     return out
 
 

@@ -1,0 +1,245 @@
+"""Synthetic problem packages at any size, in the shipped Kernel IR vocabulary.
+
+emmy cannot run here, and the benchmark shapes (1M-element and 2^30-element
+sums, [8192, 4096] row ops, 4096^3 matmuls, [8, 16, 2048, 128] attention)
+have no shipped IR.  This module writes packages in the exact format of the
+reference's problem set (tools/generate.py:74-205 of the reference): a
+``<entry>.ir.json`` graph whose KernelOp body is the repr text of the
+statement tree, and a ``meta.json`` launch contract with ``arg_order``,
+``grid``, ``block``, ``smem_bytes``, ``zero_outputs``, per-arg records and
+``rtol`` / ``atol``.
+
+The schedules are emmy's own for these families, with the extents
+substituted (the shipped r01 and r02 IRs differ only in ``Dim(1024)`` vs
+``Dim(65536)``): one CTA of T threads striding a whole array for sums, one
+row per CTA for row reductions.  An arg may carry an ``init`` record
+(``{"dist": "uniform", "low", "high", "seed"}``) for non-normal inputs;
+``seed`` args keep the runner's standard-normal meaning.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import json
+from pathlib import Path
+
+from thompiler import ir
+
+F32T = ir.DataType("f32", "float32", 4)
+F16T = ir.DataType("f16", "float16", 2)
+
+# Constructor fields in the order emmy's repr writes them (the shipped IR).
+EMMY_FIELDS = {
+    "Tile": ("axes", "body", "block_threads", "aux_threads", "raster_axes", "raster_group", "raster_orient"),
+    "Loop": ("axis", "body", "unroll", "seed"),
+    "StridedLoop": ("axis", "start", "step", "body", "unroll", "end", "seed"),
+    "Axis": ("name", "extent", "window"),
+}
+
+
+def to_repr(o) -> str:
+    if isinstance(o, ir.DataType):
+        return f"DataType(name={o.name!r}, np=dtype({o.np!r}), nbytes={o.nbytes})"
+    if isinstance(o, ir.ElementwiseImpl):
+        return f"ElementwiseImpl({o.name!r})"
+    if isinstance(o, ir.Dim):
+        return f"Dim({o.value!r})"
+    if isinstance(o, tuple):
+        inner = ", ".join(to_repr(x) for x in o)
+        return f"({inner},)" if len(o) == 1 else f"({inner})"
+    if dataclasses.is_dataclass(o):
+        name = type(o).__name__
+        names = EMMY_FIELDS.get(name) or [f.name for f in dataclasses.fields(o)]
+        return f"{name}(" + ", ".join(f"{n}={to_repr(getattr(o, n))}" for n in names) + ")"
+    return repr(o)
+
+
+# ---- small builders ------------------------------------------------------------
+
+def V(n):
+    return ir.Var(n)
+
+
+def L(v, dt="int"):
+    return ir.Literal(v, dt)
+
+
+def B(op, a, b):
+    return ir.BinaryExpr(op, a, b)
+
+
+def E(name):
+    return ir.ElementwiseImpl(name)
+
+
+def axis(name, n):
+    return ir.Axis(name, ir.Dim(n), None)
+
+
+def assign(name, op, *args, dt=F32T):
+    return ir.Assign(name, E(op), tuple(args), dt)
+
+
+def combine_block(states, partners, combine, T):
+    """WarpShuffle + per-warp slots + barrier + TreeHalve, as emmy schedules it."""
+    warps = T // 32
+    out = [ir.WarpShuffle(tuple(states), tuple(partners), tuple(combine), 32, F32T)]
+    out += [ir.Smem(f"{s}_smem", (warps,), "float", 0) for s in states]
+    out.append(ir.Cond(B("==", V("lane"), L(0)),
+                       tuple(ir.Write(f"{s}_smem", (V("warp"),), (s,), F32T, False, "NONE") for s in states), ()))
+    out.append(ir.Sync(0, None, False))
+    out.append(ir.TreeHalve(tuple(f"{s}_smem" for s in states), tuple(states), tuple(partners), tuple(combine),
+                            warps, "warp", F32T, 0, None, None))
+    return out
+
+
+def add_combine(s):
+    return (assign(s, "add", s, f"{s}__o", dt=None),)
+
+
+def softmax_combine():
+    """The online-softmax merge of two (max, sum) states (f02's combine_states)."""
+    a, b, o, ob = "acc0", "acc1", "acc0__o", "acc1__o"
+
+    def c(name, op, *args):
+        return assign(name, op, *args, dt=None)
+
+    return (c(f"{o}__gn", "maximum", a, o), c(f"{o}__dg", "subtract", a, f"{o}__gn"),
+            c(f"{o}__alpha", "exp", f"{o}__dg"), c(f"{o}__dg_o", "subtract", o, f"{o}__gn"),
+            c(f"{o}__beta", "exp", f"{o}__dg_o"), c(f"{o}__acc1_sa", "multiply", f"{o}__alpha", b),
+            c(f"{o}__acc1_sb", "multiply", f"{o}__beta", ob),
+            c(b, "add", f"{o}__acc1_sa", f"{o}__acc1_sb"), c(a, "copy", f"{o}__gn"))
+
+
+# ---- packages ---------------------------------------------------------------------
+
+def _graph(inputs: dict, consts: dict, out_name: str, out_shape, kernel_name: str, body, dtype="f32") -> dict:
+    nodes = {}
+    for n, (shape, dt) in inputs.items():
+        nodes[n] = {"op": "InputOp", "op_fields": {}, "inputs": [], "outputs": [{"name": n, "shape": list(shape),
+                                                                              "dtype": dt}]}
+    for n, (value, dt) in consts.items():
+        nodes[n] = {"op": "ConstantOp", "op_fields": {"name": n, "value": value}, "inputs": [],
+                    "outputs": [{"name": n, "shape": [1], "dtype": dt}]}
+    nodes[out_name] = {"op": "KernelOp",
+                       "op_fields": {"body": [to_repr(body)], "name": kernel_name, "zero_delegated": [], "serial": []},
+                       "inputs": list(consts) + list(inputs),
+                       "outputs": [{"name": out_name, "shape": list(out_shape), "dtype": dtype}]}
+    return {"inputs": list(inputs), "outputs": [out_name], "nodes": nodes}
+
+
+def _write(outdir: Path, pid: str, code: str, entry: str, graph: dict, kmeta: dict, rtol: float, atol: float) -> Path:
+    outdir = Path(outdir)
+    outdir.mkdir(parents=True, exist_ok=True)
+    (outdir / f"{entry}.ir.json").write_text(json.dumps(graph, indent=1))
+    meta = {"id": pid, "code": code, "rtol": rtol, "atol": atol, "graph_inputs": graph["inputs"],
+            "graph_outputs": graph["outputs"], "kernels": [dict(kmeta, entry=entry, final=True)]}
+    (outdir / "meta.json").write_text(json.dumps(meta, indent=1))
+    return outdir
+
+
+def sum_package(outdir, n: int, kind: str = "sum", T: int = 128, init: dict | None = None) -> Path:
+    """Full sum (r01 / r02) or mean (r03) of an f32 vector, one CTA of T threads."""
+    co, a0 = "a0_co", "a0"
+    l1 = ir.StridedLoop(axis(a0, n), V(co), L(T), (
+        ir.Load(("in0",), "x", (V(a0),), F32T),
+        ir.Accum("acc0", "in0", E("add"), F32T, (a0,), None)), False, None, True)
+    if kind == "mean":
+        tail_body = (ir.Load(("in1",), "mean_count", (L(0),), F32T), assign("v0", "divide", "acc0", "in1"),
+                     ir.Write("mean", (), ("v0",), F32T, False, "NONE"))
+        out, consts = "mean", {"mean_count": (float(n), "f32")}
+    else:
+        tail_body = (ir.Write("sum_1", (), ("acc0",), F32T, False, "NONE"),)
+        out, consts = "sum_1", {}
+    body = ir.Tile((axis(co, T),), (l1, *combine_block(["acc0"], ["acc0__o"], add_combine("acc0"), T),
+                                    ir.Cond(B("==", V(co), L(0)), tail_body, ())), T, 0, None, None, "m")
+    entry = "k_sum_1_reduce" if kind == "sum" else "k_mean_reduce"
+    g = _graph({"x": ((n,), "f32")}, consts, out, (), entry, body)
+    xrec = {"name": "x", "dtype": "f32", "shape": [n], "seed": 0}
+    if init:
+        xrec["init"] = init
+    args = [xrec] + [{"name": c, "dtype": "f32", "shape": [1], "data": [v]} for c, (v, _) in consts.items()]
+    args.append({"name": out, "dtype": "f32", "shape": [1], "output": True})
+    kmeta = {"node": out, "arg_order": ["x"] + list(consts) + [out], "grid": [1, 1, 1], "block": [T, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    code = f"torch.rand({n}).sum()" if kind == "sum" else f"torch.rand({n}).mean()"
+    return _write(outdir, f"synth_{kind}_{n}", code, entry, g, kmeta, 1e-5, 1e-6)
+
+
+def row_package(outdir, kind: str, rows: int, cols: int, T: int = 128, eps: float = 1e-6,
+                init: dict | None = None, w_init: dict | None = None) -> Path:
+    """Row softmax / RMSNorm / L2-normalise / row sum of x[rows, cols], one row per CTA (f01/f02/f03/r04)."""
+    a0, co, a1, a2 = "a0", "a1_co", "a1", "a2"
+    x_at = lambda v: ir.Load(("in0",), "x", (V(a0), V(v)), F32T)  # noqa: E731
+    consts: dict = {}
+    inputs = {"x": ((rows, cols), "f32")}
+    if kind == "softmax":
+        l1 = ir.StridedLoop(axis(a1, cols), V(co), L(T), (
+            ir.Let("one", L(1.0, "float"), F32T), x_at(a1),
+            assign("in0__gn", "maximum", "acc0", "in0"), assign("in0__dg", "subtract", "acc0", "in0__gn"),
+            assign("in0__alpha", "exp", "in0__dg"), assign("in0__dg_o", "subtract", "in0", "in0__gn"),
+            assign("in0__beta", "exp", "in0__dg_o"), assign("in0__acc1_sa", "multiply", "acc1", "in0__alpha"),
+            assign("in0__acc1_sb", "multiply", "in0__beta", "one"),
+            ir.Accum("acc1", "in0__acc1_sb", E("add"), F32T, (a1,), "in0__acc1_sa"),
+            ir.Accum("acc0", "in0", E("maximum"), F32T, (a1,), None)), False, None, True)
+        states, partners, comb = ["acc0", "acc1"], ["acc0__o", "acc1__o"], softmax_combine()
+        mid = [assign("v2", "reciprocal", "acc1")]
+        tail = ir.StridedLoop(axis(a2, cols), V(co), L(T), (
+            ir.Load(("in2",), "x", (V(a0), V(a2)), F32T), assign("v3", "subtract", "in2", "acc0"),
+            assign("v4", "exp", "v3"), assign("v5", "multiply", "v2", "v4"),
+            ir.Write("softmax", (V(a0), V(a2)), ("v5",), F32T, False, "NONE")), False, None, True)
+        out, code = "softmax", f"torch.softmax(torch.randn({rows}, {cols}), dim=-1)"
+    elif kind in ("rmsnorm", "l2norm", "rowsum"):
+        sq = kind != "rowsum"
+        l1 = ir.StridedLoop(axis(a1, cols), V(co), L(T), (
+            (ir.Load(("in2",), "x", (V(a0), V(a1)), F32T), assign("v1", "multiply", "in2", "in2"),
+             ir.Accum("acc0", "v1", E("add"), F32T, (a1,), None)) if sq else
+            (x_at(a1), ir.Accum("acc0", "in0", E("add"), F32T, (a1,), None))), False, None, True)
+        states, partners, comb = ["acc0"], ["acc0__o"], add_combine("acc0")
+        if kind == "rmsnorm":
+            consts = {"mean_count": (float(cols), "f32"), "add_c1": (float(eps), "f32")}
+            inputs["w"] = ((cols,), "f32")
+            mid = [ir.Load(("in1",), "mean_count", (L(0),), F32T), assign("v0", "reciprocal", "in1"),
+                   assign("v2", "multiply", "acc0", "v0"), ir.Load(("inE",), "add_c1", (L(0),), F32T),
+                   assign("v3", "add", "inE", "v2"), assign("v4", "sqrt", "v3"), assign("v5", "reciprocal", "v4")]
+            tail = ir.StridedLoop(axis(a2, cols), V(co), L(T), (
+                ir.Load(("in3",), "x", (V(a0), V(a2)), F32T), assign("v6", "multiply", "in3", "v5"),
+                ir.Load(("in4",), "w", (V(a2),), F32T), assign("v7", "multiply", "in4", "v6"),
+                ir.Write("mul_1", (V(a0), V(a2)), ("v7",), F32T, False, "NONE")), False, None, True)
+            out = "mul_1"
+            code = (f"x = torch.randn({rows}, {cols}); w = torch.rand({cols}) + 0.5; "
+                    f"x / torch.sqrt((x * x).mean(-1, keepdim=True) + {eps}) * w")
+        elif kind == "l2norm":
+            mid = [assign("v1", "sqrt", "acc0"), assign("v2", "reciprocal", "v1")]
+            tail = ir.StridedLoop(axis(a2, cols), V(co), L(T), (
+                ir.Load(("in1",), "x", (V(a0), V(a2)), F32T), assign("v3", "multiply", "in1", "v2"),
+                ir.Write("div", (V(a0), V(a2)), ("v3",), F32T, False, "NONE")), False, None, True)
+            out = "div"
+            code = f"x = torch.randn({rows}, {cols}); x / torch.sqrt((x * x).sum(-1, keepdim=True))"
+        else:
+            mid = []
+            tail = ir.Cond(B("==", V(co), L(0)), (ir.Write("sum_1", (V(a0),), ("acc0",), F32T, False, "NONE"),), ())
+            out = "sum_1"
+            code = f"torch.randn({rows}, {cols}).sum(-1)"
+    else:
+        raise ValueError(f"row op {kind!r}")
+    body = ir.Tile((axis(a0, rows), axis(co, T)),
+                   (l1, *combine_block(states, partners, comb, T), *mid, tail), T, 0, None, None, "m")
+    entry = {"softmax": "k_softmax_rows", "rmsnorm": "k_rmsnorm_rows", "l2norm": "k_l2norm_rows",
+             "rowsum": "k_sum_rows"}[kind]
+    out_shape = (rows,) if kind == "rowsum" else (rows, cols)
+    g = _graph(inputs, consts, out, out_shape, entry, body)
+    args = [{"name": c, "dtype": "f32", "shape": [1], "data": [v]} for c, (v, _) in consts.items()]
+    xrec = {"name": "x", "dtype": "f32", "shape": [rows, cols], "seed": 0}
+    if init:
+        xrec["init"] = init
+    args.append(xrec)
+    if "w" in inputs:
+        wrec = {"name": "w", "dtype": "f32", "shape": [cols], "seed": 1}
+        if w_init:
+            wrec["init"] = w_init
+        args.append(wrec)
+    args.append({"name": out, "dtype": "f32", "shape": list(out_shape), "output": True})
+    kmeta = {"node": out, "arg_order": [a["name"] for a in args], "grid": [rows, 1, 1], "block": [T, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, f"synth_{kind}_{rows}x{cols}", code, entry, g, kmeta, 1e-5, 1e-6)
