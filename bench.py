@@ -143,6 +143,8 @@ class RowOps:
 
     def check(self) -> None:
         torch = self.torch
+        self.step(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
         x, y = self.x["softmax"], self.y["softmax"]
         ref = torch.softmax(x.double(), -1)
         assert torch.allclose(y.double(), ref, rtol=1e-5, atol=1e-6), "softmax mismatch"
@@ -304,9 +306,9 @@ class FullSum:
         return c
 
 
-CONFIGS = {"rowops": lambda r, w, d: RowOps(r, w, d),
-           "sum": lambda r, w, d: FullSum(r, w, d, 1 << 20),
-           "bigsum": lambda r, w, d: FullSum(r, w, d, 1 << 30, sharded=True)}
+CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
+           "sum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 20),
+           "bigsum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True)}
 
 
 def reference_arm(args) -> None:
@@ -359,6 +361,8 @@ def main() -> None:
     ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--size", type=int, default=0,
+                    help="override the workload size (rows for rowops, elements for sums); profiling only")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -377,7 +381,7 @@ def main() -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     runner.init(local)
-    w = CONFIGS[args.config](rank, world, local)
+    w = CONFIGS[args.config](rank, world, local, args.size)
     stream = torch.cuda.current_stream().cuda_stream
     w.check()
     for _ in range(args.warmup):

@@ -131,7 +131,7 @@ class StridedReduce(TunedKernel):
         if not cls._loop_ok(l1, co, T):
             return None
         C = l1.axis.size
-        if C % T or kernel.dynamic_smem_bytes:
+        if (rows and C % T) or kernel.dynamic_smem_bytes:
             return None
         if not cls._simple(pre, kernel, allow_loads="const"):
             return None
