@@ -368,6 +368,12 @@ int thr_release_buffers(void) {
     return THR_OK;
 }
 
+// Lets the allocation-free entry points (noalloc.cu) report through thr_last_error.
+int thr_noalloc_set_error(const char *msg) {
+    g_err = msg ? msg : "";
+    return THR_OK;
+}
+
 int thr_last_error(char *buf, size_t n) {
     if (!buf || !n) return THR_ERR_REQUEST;
     strncpy(buf, g_err.c_str(), n - 1);
