@@ -264,9 +264,17 @@ int thr_launch(uint64_t function, const uint32_t grid[3], const uint32_t block[3
 int thr_run(uint64_t function, const uint32_t grid[3], const uint32_t block[3], uint32_t smem_bytes,
             const thr_arg *args, int nargs, int warmup, int iters, double timeout_s, float *median_us,
             uint64_t stream) {
+    return thr_run_ex(0, function, grid, block, smem_bytes, args, nargs, nullptr, 0, nullptr, warmup, iters,
+                      timeout_s, median_us, stream);
+}
+
+int thr_run_ex(uint64_t module, uint64_t function, const uint32_t grid[3], const uint32_t block[3],
+               uint32_t smem_bytes, const thr_arg *args, int nargs, const thr_tmap_spec *tmaps, int ntmaps,
+               const char *ptr_table, int warmup, int iters, double timeout_s, float *median_us,
+               uint64_t stream) {
     int s = ensure_driver();
     if (s) return s;
-    if (nargs < 0 || (nargs && !args) || warmup < 0 || iters < 0)
+    if (nargs < 0 || (nargs && !args) || warmup < 0 || iters < 0 || ntmaps < 0 || (ntmaps && (!tmaps || !module)))
         return fail(THR_ERR_REQUEST, "thr_run: bad arguments");
     cudaStream_t st = (cudaStream_t)(uintptr_t)stream;
     std::vector<uint64_t> dev(nargs);
@@ -278,6 +286,33 @@ int thr_run(uint64_t function, const uint32_t grid[3], const uint32_t block[3], 
                             ? cudaMemcpyAsync(p, args[i].host, args[i].nbytes, cudaMemcpyHostToDevice, st)
                             : cudaMemsetAsync(p, 0, args[i].nbytes, st);
         if (e != cudaSuccess) return cuda_fail(e, "staging a run argument");
+    }
+    if (ntmaps) {
+        // encode the maps for the staged buffers and place them (and their pointers) in the module
+        std::vector<unsigned char> maps(128 * (size_t)ntmaps);
+        std::vector<uint64_t> ptrs(ntmaps);
+        for (int i = 0; i < ntmaps; ++i) {
+            const thr_tmap_spec &m = tmaps[i];
+            if (m.arg < 0 || m.arg >= nargs || !m.global) return fail(THR_ERR_REQUEST, "tensor map %d: bad argument", i);
+            ptrs[i] = dev[m.arg];
+            if ((s = thr_tensor_map(maps.data() + 128 * i, m.dtype_code, m.rank, dev[m.arg], m.dims, m.strides,
+                                    m.box, m.swizzle)))
+                return s;
+            uint64_t g = 0, n = 0;
+            if ((s = thr_module_global(module, m.global, &g, &n))) return s;
+            if (n < 128) return fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", m.global, (unsigned long long)n);
+            cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, maps.data() + 128 * i, 128, cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "uploading a tensor map");
+        }
+        if (ptr_table) {
+            uint64_t g = 0, n = 0;
+            if ((s = thr_module_global(module, ptr_table, &g, &n))) return s;
+            if (n < 8 * (uint64_t)ntmaps) return fail(THR_ERR_LOOKUP, "pointer table %s is too small", ptr_table);
+            cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, ptrs.data(), 8 * ntmaps, cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "uploading the tensor-map pointers");
+        }
+        cudaError_t e = cudaStreamSynchronize(st);   // the host copies above must not outlive this frame
+        if (e != cudaSuccess) return fail(THR_ERR_RUN, "staging tensor maps: %s", cudaGetErrorString(e));
     }
     auto rezero = [&]() -> int {
         for (int i = 0; i < nargs; ++i)
@@ -354,6 +389,11 @@ int thr_memcpy_htod(uint64_t dst, const void *src, uint64_t nbytes, uint64_t str
     cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)dst, src, nbytes, cudaMemcpyHostToDevice,
                                     (cudaStream_t)(uintptr_t)stream);
     return e == cudaSuccess ? THR_OK : cuda_fail(e, "host to device copy");
+}
+
+int thr_memcpy_dtoh(void *dst, uint64_t src, uint64_t nbytes) {
+    cudaError_t e = cudaMemcpy(dst, (const void *)(uintptr_t)src, nbytes, cudaMemcpyDeviceToHost);
+    return e == cudaSuccess ? THR_OK : cuda_fail(e, "device to host copy");
 }
 
 int thr_synchronize(void) {

@@ -1,0 +1,510 @@
+"""Tuned family: f16 tensor-core matmul on tcgen05 (t01 / t02 / the matmul
+benchmark shapes).
+
+Recognised IR: a Tile whose body stages two f16 operands through shared
+memory with CpAsyncCopy, loads them with LdmatrixLoad (role a from one
+parameter, role b from the other) and accumulates with MmaSyncPtx
+m16n8k16 f16 -> f32, storing the accumulators with RegStore -- the warp-level
+tensor-core schedule of the reference's tests/problems/t01_matmul_f16 and
+t02_matmul_f16_to_f32 (k_to__partial).  What it computes is
+C[M, N] = A[M, K] @ B with B stored [N, K] (b_trans: "column-major") or
+[K, N]; a 3-D output [S, M, N] is the split-K form: slice s holds
+A[:, sK/S:(s+1)K/S] @ B[sK/S:(s+1)K/S, :].
+
+Tuned body (one persistent CTA per SM, 192 threads, warp-specialised):
+
+  warp 0   TMA producer: per K block of 64, waits for the stage to be empty and
+           loads the A tile (128 x 64) and the B tile (BN x 64, or 64 x BN) with
+           cp.async.bulk.tensor into a 128B-swizzled stage, completing on the
+           stage's mbarrier (expect_tx);
+  warp 1   MMA issuer: allocates TMEM (2 accumulators of BN f32 columns), and for
+           each K block issues 4 x tcgen05.mma.cta_group::1.kind::f16 (M=128,
+           N=BN, K=16) from shared-memory descriptors, then tcgen05.commit to the
+           stage's "empty" mbarrier; after the last block, commit to the
+           accumulator's "full" mbarrier;
+  warps 2-5 epilogue: tcgen05.ld 32x32b of their TMEM lane quarter, convert,
+           store to global; arrive on the accumulator's "empty" mbarrier, so the
+           MMA of the next tile (other accumulator) overlaps this epilogue.
+
+Tiles are handed out round-robin (tile = ctaid + i * nctaid), M fastest, so
+the CTAs in flight share B column tiles in L2.  Every mbarrier wait is
+bounded: on expiry the thread records a code in the module's ``thc_error``
+word and leaves through the common exit, which releases TMEM.
+
+Tensor maps live in module ``.global`` variables that the runner fills (the
+tuned launch lists them in the module's sidecar) together with the pointers
+they were encoded for; the kernel takes the tuned path only when its
+``%ntid.x`` is 192 and its A / B pointers are the ones the maps describe,
+otherwise it runs the generic lowering of the IR, which needs nothing but
+meta.json's launch.
+"""
+
+from __future__ import annotations
+
+from thompiler import ir
+from thompiler.families.base import TunedKernel
+from thompiler.lowering.types import F16, F32
+from thompiler.load import KernelInfo
+
+SM_COUNT = 148
+THREADS = 192
+BM, BK = 128, 64
+SMEM_LIMIT = 227 * 1024
+WAIT_LIMIT = 1 << 22          # try_wait rounds before a wait gives up
+
+
+def _desc_hi(sbo: int, layout: int = 2) -> int:
+    """High 32 bits of a tcgen05 shared-memory descriptor: SBO, version 1, layout."""
+    return ((sbo >> 4) & 0x3FFF) | (1 << 14) | (layout << 29)
+
+
+def idesc_f16(n: int, b_mn_major: bool) -> int:
+    """Instruction descriptor, kind::f16: f16 A/B, f32 D, M = 128, N = n."""
+    return (1 << 4) | ((1 if b_mn_major else 0) << 16) | ((n >> 3) << 17) | ((BM >> 4) << 24)
+
+
+class TcMatmul(TunedKernel):
+    family = "tcgen05-matmul"
+
+    def __init__(self, kernel: KernelInfo, a, b, c, M, N, K, S, b_kmajor, static_smem):
+        super().__init__(kernel)
+        self.a, self.b, self.c = a, b, c
+        self.M, self.N, self.K, self.S = M, N, K, S
+        self.Ks = K // S
+        self.b_kmajor = b_kmajor
+        self.BN = self.pick_bn()
+        self.a_bytes = BM * BK * 2
+        self.b_bytes = self.BN * BK * 2
+        stage = self.a_bytes + self.b_bytes
+        room = SMEM_LIMIT - static_smem - 2048
+        self.stages = max(2, min(6, room // stage))
+        self.smem = self.stages * stage + 1024 + 256
+        self.tiles = (M // BM) * (N // self.BN) * S
+        self.ctas = min(self.tiles, SM_COUNT)
+
+    def pick_bn(self) -> int:
+        best, best_score = None, -1.0
+        for bn, pref in ((256, 1.0), (192, 1.0), (128, 0.93), (64, 0.7)):
+            if self.N % bn:
+                continue
+            tiles = (self.M // BM) * (self.N // bn) * self.S
+            waves = -(-tiles // SM_COUNT)
+            score = pref * tiles / (waves * SM_COUNT) if tiles >= SM_COUNT else pref * tiles / SM_COUNT
+            if score > best_score + 1e-9:
+                best, best_score = bn, score
+        return best
+
+    # ---- recognition ------------------------------------------------------------
+
+    @classmethod
+    def match(cls, kernel: KernelInfo):
+        body = kernel.body
+        if len(body) != 1 or not isinstance(body[0], ir.Tile):
+            return None
+        stmts = list(ir.walk_stmts(body[0].body))
+        kinds = {type(s) for s in stmts}
+        if ir.MmaSyncPtx not in kinds or ir.RegStore not in kinds:
+            return None
+        if kinds & {ir.Write, ir.Accum, ir.WarpShuffle, ir.TreeHalve, ir.Opaque, ir.Assign, ir.Load}:
+            return None
+        for s in stmts:
+            if isinstance(s, ir.MmaSyncPtx) and (tuple(s.shape) != (16, 8, 16) or s.ab_dtype != "f16"
+                                                 or s.c_dtype != "f32" or s.b_row_major or s.block_scaled):
+                return None
+        fed = {}
+        for s in stmts:
+            if isinstance(s, ir.CpAsyncCopy):
+                if fed.setdefault(s.smem, s.src) != s.src:
+                    return None
+        roles, trans = {}, set()
+        for s in stmts:
+            if isinstance(s, ir.LdmatrixLoad):
+                src = fed.get(s.src_buffer)
+                if src is None or roles.setdefault(s.role, src) != src:
+                    return None
+                if s.role == "b":
+                    trans.add(bool(s.b_trans))
+        if set(roles) != {"a", "b"} or len(trans) != 1:
+            return None
+        outs = {s.dst_buffer for s in stmts if isinstance(s, ir.RegStore)}
+        if len(outs) != 1:
+            return None
+        a, b, c = kernel.param(roles["a"]), kernel.param(roles["b"]), kernel.param(outs.pop())
+        if a is None or b is None or c is None or len(kernel.params) != 3:
+            return None
+        if a.ty is not F16 or b.ty is not F16 or a.written or b.written or c.ty not in (F32, F16):
+            return None
+        if len(a.shape) != 2 or len(b.shape) != 2:
+            return None
+        M, K = a.shape
+        b_kmajor = trans.pop()
+        N = b.shape[0] if b_kmajor else b.shape[1]
+        if (b.shape[1] if b_kmajor else b.shape[0]) != K:
+            return None
+        if c.shape == (M, N):
+            S = 1
+        elif len(c.shape) == 3 and c.shape[1:] == (M, N) and K % c.shape[0] == 0 and c.ty is F32:
+            S = c.shape[0]
+        else:
+            return None
+        if M % BM or N % 64 or (K // S) % BK:
+            return None
+        # the K loop of the schedule must cover the whole (split) K range
+        loops = [s for s in stmts if isinstance(s, (ir.Loop, ir.StridedLoop))
+                 and any(isinstance(x, ir.MmaSyncPtx) for x in ir.walk_stmts(s.body))]
+        if not any(lp.axis.extent.is_static and lp.axis.size == K // S for lp in loops):
+            return None
+        static = sum(int(__import__("math").prod(s.extents)) * (2 if s.dtype in ("__half", "half") else 4)
+                     for s in stmts if isinstance(s, ir.Smem)) if kernel.dynamic_smem_bytes == 0 else 0
+        return cls(kernel, a, b, c, M, N, K, S, b_kmajor, static)
+
+    # ---- launch ------------------------------------------------------------------
+
+    def sidecar(self) -> dict:
+        a, b = self.a, self.b
+        tm_a = {"global": "thc_tmap_a", "param": a.name, "dtype": "f16", "dims": [self.K, self.M],
+                "strides": [self.K * 2], "box": [BK, BM], "swizzle": 3}
+        if self.b_kmajor:
+            tm_b = {"global": "thc_tmap_b", "param": b.name, "dtype": "f16", "dims": [self.K, self.N],
+                    "strides": [self.K * 2], "box": [BK, self.BN], "swizzle": 3}
+        else:
+            tm_b = {"global": "thc_tmap_b", "param": b.name, "dtype": "f16", "dims": [self.N, self.K],
+                    "strides": [self.N * 2], "box": [64, BK], "swizzle": 3}
+        return {"grid": [self.ctas, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem,
+                "tmaps": [tm_a, tm_b], "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [a.name, b.name]},
+                "error_word": "thc_error", "tile": [BM, self.BN, BK], "stages": self.stages}
+
+    def guard(self, generic: str) -> None:
+        em = self.em
+        em.module(".global .align 64 .b8 thc_tmap_a[128]")
+        em.module(".global .align 64 .b8 thc_tmap_b[128]")
+        em.module(".global .align 8 .u64 thc_tmap_ptr[2]")
+        em.module(".global .align 4 .u32 thc_error")
+        em.module(".extern .shared .align 1024 .b8 smem_pool[]")
+        p = em.tmp("pred")
+        r = self.special("%ntid.x")
+        em.ins(f"setp.ne.u32 {p}, {r}, {THREADS}")
+        em.ins(f"@{p} bra {generic}")
+        for i, prm in enumerate((self.a, self.b)):
+            raw, want = em.tmp("b64"), em.tmp("b64")
+            em.ins(f"ld.param.u64 {raw}, [p_{prm.name}]")
+            em.ins(f"ld.global.u64 {want}, [thc_tmap_ptr+{8 * i}]")
+            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
+            em.ins(f"@{p} bra {generic}")
+
+    # ---- the tuned body -------------------------------------------------------------
+
+    def emit_tuned(self) -> None:  # noqa: C901 - one kernel, written out in order
+        em = self.em
+        t = em.tmp
+        S_, BN, ST = self.S, self.BN, self.stages
+        a_bytes, b_bytes = self.a_bytes, self.b_bytes
+        tiles_m, tiles_n = self.M // BM, self.N // BN
+        kblocks = self.Ks // BK
+        tmem_cols = 512 if 2 * BN > 256 else 256
+        ins, place, lab = em.ins, em.place, em.label
+
+        tid, warp, lane = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {tid}, %tid.x")
+        ins(f"shr.u32 {warp}, {tid}, 5")
+        ins(f"and.b32 {lane}, {tid}, 31")
+        base = t("b32")
+        ins(f"mov.u32 {base}, smem_pool")
+        ins(f"add.u32 {base}, {base}, 1023")
+        ins(f"and.b32 {base}, {base}, -1024")
+        a_st = base
+        b_st = t("b32")
+        ins(f"add.u32 {b_st}, {base}, {ST * a_bytes}")
+        bars = t("b32")
+        ins(f"add.u32 {bars}, {base}, {ST * (a_bytes + b_bytes)}")
+        full = lambda s: f"{bars}+{8 * s}"                  # noqa: E731
+        empty_off, accf_off, acce_off, slot_off = 8 * ST, 16 * ST, 16 * ST + 16, 16 * ST + 32
+        p, q = t("pred"), t("pred")
+        # barriers
+        skip = lab("mm_noinit")
+        ins(f"setp.ne.u32 {p}, {tid}, 0")
+        ins(f"@{p} bra {skip}")
+        for s in range(ST):
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{empty_off + 8 * s}], 1")
+        for b in range(2):
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{accf_off + 8 * b}], 1")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{acce_off + 8 * b}], 128")
+        ins("fence.mbarrier_init.release.cluster")
+        ins("fence.proxy.async.shared::cta")
+        place(skip)
+        # TMEM: warp 1 allocates
+        noalloc = lab("mm_noalloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {noalloc}")
+        slot = t("b32")
+        ins(f"add.u32 {slot}, {bars}, {slot_off}")
+        ins(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{slot}], {tmem_cols}")
+        ins("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned")
+        place(noalloc)
+        ins("tcgen05.fence::before_thread_sync")
+        ins("bar.sync 0")
+        ins("tcgen05.fence::after_thread_sync")
+        tmem = t("b32")
+        ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
+        cta, ncta = self.special("%ctaid.x"), self.special("%nctaid.x")
+        tiles = self.tiles
+
+        # generic addresses of the tensor maps
+        tma, tmb = t("b64"), t("b64")
+        ins(f"mov.u64 {tma}, thc_tmap_a")
+        ins(f"cvta.global.u64 {tma}, {tma}")
+        ins(f"mov.u64 {tmb}, thc_tmap_b")
+        ins(f"cvta.global.u64 {tmb}, {tmb}")
+        errp = t("b64")
+        ins(f"mov.u64 {errp}, thc_error")
+
+        end = lab("mm_end")
+
+        def wait(bar_addr: str, parity: str, code: int) -> None:
+            """Bounded mbarrier wait; on expiry record ``code`` and leave."""
+            top, ok = lab("wait"), lab("waited")
+            n = t("b32")
+            ins(f"mov.u32 {n}, 0")
+            place(top)
+            ins(f"mbarrier.try_wait.parity.shared::cta.b64 {q}, [{bar_addr}], {parity}")
+            ins(f"@{q} bra {ok}")
+            ins(f"add.u32 {n}, {n}, 1")
+            ins(f"setp.lt.u32 {q}, {n}, {WAIT_LIMIT}")
+            ins(f"@{q} bra {top}")
+            ins(f"atom.global.or.b32 {t('b32')}, [{errp}], {1 << code}")
+            ins(f"bra {end}")
+            place(ok)
+
+        def decode(tile: str):
+            tm_, tn_, ts_ = t("b32"), t("b32"), t("b32")
+            r = t("b32")
+            ins(f"rem.u32 {tm_}, {tile}, {tiles_m}")
+            ins(f"div.u32 {r}, {tile}, {tiles_m}")
+            ins(f"rem.u32 {tn_}, {r}, {tiles_n}")
+            ins(f"div.u32 {ts_}, {r}, {tiles_n}")
+            return tm_, tn_, ts_
+
+        role_mma, role_epi = lab("mm_mma"), lab("mm_epi")
+        ins(f"setp.eq.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_mma}")
+        ins(f"setp.gt.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_epi}")
+
+        # ---------------- producer (warp 0) ----------------
+        is0 = t("pred")
+        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        it, tile = t("b32"), t("b32")
+        ins(f"mov.u32 {it}, 0")
+        ins(f"mov.u32 {tile}, {cta}")
+        ptop, pdone = lab("prod_tile"), lab("prod_done")
+        ins(f"setp.ge.u32 {p}, {tile}, {tiles}")
+        ins(f"@{p} bra {pdone}")
+        place(ptop)
+        tm_, tn_, ts_ = decode(tile)
+        m0, n0, k0 = t("b32"), t("b32"), t("b32")
+        ins(f"mul.lo.u32 {m0}, {tm_}, {BM}")
+        ins(f"mul.lo.u32 {n0}, {tn_}, {BN}")
+        ins(f"mul.lo.u32 {k0}, {ts_}, {self.Ks}")
+        kb = t("b32")
+        ins(f"mov.u32 {kb}, 0")
+        ktop = lab("prod_k")
+        place(ktop)
+        stage, ph, par = t("b32"), t("b32"), t("b32")
+        ins(f"rem.u32 {stage}, {it}, {ST}")
+        ins(f"div.u32 {ph}, {it}, {ST}")
+        ins(f"and.b32 {ph}, {ph}, 1")
+        ins(f"xor.b32 {par}, {ph}, 1")
+        eb = t("b32")
+        ins(f"mad.lo.u32 {eb}, {stage}, 8, {bars}")
+        wait(f"{eb}+{empty_off}", par, 0)
+        sa, sb, kc = t("b32"), t("b32"), t("b32")
+        ins(f"mad.lo.u32 {sa}, {stage}, {a_bytes}, {a_st}")
+        ins(f"mad.lo.u32 {sb}, {stage}, {b_bytes}, {b_st}")
+        ins(f"mad.lo.u32 {kc}, {kb}, {BK}, {k0}")
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{eb}], {a_bytes + b_bytes}")
+        ins(f"@{is0} cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+            f"[{sa}], [{tma}, {{{kc}, {m0}}}], [{eb}]")
+        if self.b_kmajor:
+            ins(f"@{is0} cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+                f"[{sb}], [{tmb}, {{{kc}, {n0}}}], [{eb}]")
+        else:
+            for nb in range(BN // 64):
+                nn = t("b32")
+                ins(f"add.u32 {nn}, {n0}, {nb * 64}")
+                ins(f"@{is0} cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+                    f"[{sb}+{nb * 64 * BK * 2}], [{tmb}, {{{nn}, {kc}}}], [{eb}]")
+        ins(f"add.u32 {it}, {it}, 1")
+        ins(f"add.u32 {kb}, {kb}, 1")
+        ins(f"setp.lt.u32 {p}, {kb}, {kblocks}")
+        ins(f"@{p} bra {ktop}")
+        ins(f"add.u32 {tile}, {tile}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {tile}, {tiles}")
+        ins(f"@{p} bra {ptop}")
+        place(pdone)
+        # drain: every stage's last load has landed before the CTA may leave
+        for s in range(ST):
+            used, last, lp = t("pred"), t("b32"), t("b32")
+            skip_s = lab("drain_skip")
+            ins(f"setp.le.u32 {used}, {it}, {s}")
+            ins(f"@{used} bra {skip_s}")
+            ins(f"sub.u32 {last}, {it}, 1")
+            ins(f"sub.u32 {last}, {last}, {s}")
+            ins(f"div.u32 {last}, {last}, {ST}")        # uses of stage s minus one
+            ins(f"and.b32 {lp}, {last}, 1")
+            wait(f"{bars}+{8 * s}", lp, 0)
+            place(skip_s)
+        ins(f"bra {end}")
+
+        # ---------------- MMA issuer (warp 1) ----------------
+        place(role_mma)
+        ism = t("pred")
+        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        it2, tile2, lt = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {it2}, 0")
+        ins(f"mov.u32 {lt}, 0")
+        ins(f"mov.u32 {tile2}, {cta}")
+        mtop, mdone = lab("mma_tile"), lab("mma_done")
+        ins(f"setp.ge.u32 {p}, {tile2}, {tiles}")
+        ins(f"@{p} bra {mdone}")
+        place(mtop)
+        buf, use, upar, apar = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"and.b32 {buf}, {lt}, 1")
+        ins(f"shr.u32 {use}, {lt}, 1")
+        ins(f"and.b32 {upar}, {use}, 1")
+        ins(f"xor.b32 {apar}, {upar}, 1")
+        ab = t("b32")
+        ins(f"mad.lo.u32 {ab}, {buf}, 8, {bars}")
+        wait(f"{ab}+{acce_off}", apar, 1)
+        ins("tcgen05.fence::after_thread_sync")
+        dt = t("b32")
+        ins(f"mad.lo.u32 {dt}, {buf}, {BN}, {tmem}")
+        kb2 = t("b32")
+        ins(f"mov.u32 {kb2}, 0")
+        mk = lab("mma_k")
+        place(mk)
+        st2, ph2 = t("b32"), t("b32")
+        ins(f"rem.u32 {st2}, {it2}, {ST}")
+        ins(f"div.u32 {ph2}, {it2}, {ST}")
+        ins(f"and.b32 {ph2}, {ph2}, 1")
+        fb = t("b32")
+        ins(f"mad.lo.u32 {fb}, {st2}, 8, {bars}")
+        wait(fb, ph2, 1)
+        ins("tcgen05.fence::after_thread_sync")
+        sa2, sb2 = t("b32"), t("b32")
+        ins(f"mad.lo.u32 {sa2}, {st2}, {a_bytes}, {a_st}")
+        ins(f"mad.lo.u32 {sb2}, {st2}, {b_bytes}, {b_st}")
+        # descriptors: low word = start address >> 4 (+ LBO in bits 16..29), high word = SBO | version | layout
+        adesc_lo, bdesc_lo = t("b32"), t("b32")
+        ins(f"shr.u32 {adesc_lo}, {sa2}, 4")
+        ins(f"and.b32 {adesc_lo}, {adesc_lo}, 16383")
+        ins(f"or.b32 {adesc_lo}, {adesc_lo}, {1 << 16}")
+        ins(f"shr.u32 {bdesc_lo}, {sb2}, 4")
+        ins(f"and.b32 {bdesc_lo}, {bdesc_lo}, 16383")
+        b_lbo = 1 if self.b_kmajor else (64 * BK * 2) >> 4
+        ins(f"or.b32 {bdesc_lo}, {bdesc_lo}, {b_lbo << 16}")
+        a_hi = _desc_hi(1024)
+        b_hi = _desc_hi(1024)
+        idesc = idesc_f16(BN, not self.b_kmajor)
+        acc0, always = t("pred"), t("pred")
+        ins(f"setp.ne.u32 {acc0}, {kb2}, 0")          # the tile's first MMA overwrites the accumulator
+        ins(f"setp.eq.u32 {always}, {kb2}, {kb2}")
+        hi_a, hi_b = t("b32"), t("b32")
+        ins(f"mov.u32 {hi_a}, {a_hi}")
+        ins(f"mov.u32 {hi_b}, {b_hi}")
+        for k in range(BK // 16):
+            ad, bd = t("b64"), t("b64")
+            alo, blo = t("b32"), t("b32")
+            ins(f"add.u32 {alo}, {adesc_lo}, {(k * 32) >> 4}")
+            b_step = (k * 32) >> 4 if self.b_kmajor else (k * 16 * 128) >> 4
+            ins(f"add.u32 {blo}, {bdesc_lo}, {b_step}")
+            ins(f"mov.b64 {ad}, {{{alo}, {hi_a}}}")
+            ins(f"mov.b64 {bd}, {{{blo}, {hi_b}}}")
+            ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dt}], {ad}, {bd}, {idesc}, "
+                f"{acc0 if k == 0 else always}")
+        ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{fb}+{empty_off}]")
+        ins(f"add.u32 {it2}, {it2}, 1")
+        ins(f"add.u32 {kb2}, {kb2}, 1")
+        ins(f"setp.lt.u32 {p}, {kb2}, {kblocks}")
+        ins(f"@{p} bra {mk}")
+        ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ab}+{accf_off}]")
+        ins(f"add.u32 {lt}, {lt}, 1")
+        ins(f"add.u32 {tile2}, {tile2}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {tile2}, {tiles}")
+        ins(f"@{p} bra {mtop}")
+        place(mdone)
+        ins(f"bra {end}")
+
+        # ---------------- epilogue (warps 2..5) ----------------
+        place(role_epi)
+        quarter, row = t("b32"), t("b32")
+        ins(f"and.b32 {quarter}, {warp}, 3")
+        ins(f"mad.lo.u32 {row}, {quarter}, 32, {lane}")
+        lane_off = t("b32")
+        ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
+        tile3, lt3 = t("b32"), t("b32")
+        ins(f"mov.u32 {lt3}, 0")
+        ins(f"mov.u32 {tile3}, {cta}")
+        etop, edone = lab("epi_tile"), lab("epi_done")
+        ins(f"setp.ge.u32 {p}, {tile3}, {tiles}")
+        ins(f"@{p} bra {edone}")
+        place(etop)
+        tm3, tn3, ts3 = decode(tile3)
+        buf3, use3, par3 = t("b32"), t("b32"), t("b32")
+        ins(f"and.b32 {buf3}, {lt3}, 1")
+        ins(f"shr.u32 {use3}, {lt3}, 1")
+        ins(f"and.b32 {par3}, {use3}, 1")
+        ab3 = t("b32")
+        ins(f"mad.lo.u32 {ab3}, {buf3}, 8, {bars}")
+        wait(f"{ab3}+{accf_off}", par3, 2)
+        ins("tcgen05.fence::after_thread_sync")
+        taddr = t("b32")
+        ins(f"mad.lo.u32 {taddr}, {buf3}, {BN}, {tmem}")
+        ins(f"add.u32 {taddr}, {taddr}, {lane_off}")
+        # global row address: C + (((s * M) + m0 + row) * N + n0) * esize
+        esz = self.c.ty.nbytes
+        grow, rowp = t("b32"), t("b64")
+        ins(f"mad.lo.u32 {grow}, {ts3}, {self.M}, {row}")
+        ins(f"mad.lo.u32 {grow}, {tm3}, {BM}, {grow}")
+        rowi = t("b64")
+        ins(f"mul.wide.u32 {rowi}, {grow}, {self.N * esz}")
+        ncol = t("b64")
+        ins(f"mul.wide.u32 {ncol}, {tn3}, {BN * esz}")
+        ins(f"add.s64 {rowp}, {rowi}, {ncol}")
+        ins(f"add.s64 {rowp}, {rowp}, {em.buffer_reg(self.c.name)}")
+        for c0 in range(0, BN, 32):
+            v = [t("b32") for _ in range(32)]
+            tc = t("b32")
+            ins(f"add.u32 {tc}, {taddr}, {c0}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(v)}}}, [{tc}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            if esz == 4:
+                for i in range(8):
+                    ins(f"st.global.v4.b32 [{rowp}+{(c0 + 4 * i) * 4}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+            else:
+                h = [t("b32") for _ in range(16)]
+                for i in range(16):
+                    ins(f"cvt.rn.f16x2.f32 {h[i]}, {v[2 * i + 1]}, {v[2 * i]}")
+                for i in range(4):
+                    ins(f"st.global.v4.b32 [{rowp}+{(c0 + 8 * i) * 2}], {{{', '.join(h[4 * i:4 * i + 4])}}}")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{ab3}+{acce_off}]")
+        ins(f"add.u32 {lt3}, {lt3}, 1")
+        ins(f"add.u32 {tile3}, {tile3}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {tile3}, {tiles}")
+        ins(f"@{p} bra {etop}")
+        place(edone)
+
+        # ---------------- common exit ----------------
+        place(end)
+        ins("barrier.sync 0")
+        nodealloc = lab("mm_nodealloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {nodealloc}")
+        ins("tcgen05.fence::after_thread_sync")
+        ins(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, {tmem_cols}")
+        place(nodealloc)
+
+
+def recognise(kernel: KernelInfo):
+    return TcMatmul.match(kernel)

@@ -101,8 +101,6 @@ def run_package(pkg: Package, ptx: dict[str, str], inputs: dict | None = None, h
         try:
             fn = mod.function(k["entry"])
             plan = runner.plan_launch(mod, k, honour_meta=honour_meta)
-            if plan.tmaps:
-                raise runner.RunnerError("request", "tensor-map kernels run through the device-pointer path")
             recs = {a["name"]: a for a in k["args"]}
             args = []
             for name in k["arg_order"]:
@@ -115,7 +113,7 @@ def run_package(pkg: Package, ptx: dict[str, str], inputs: dict | None = None, h
                     args.append({"array": np.ascontiguousarray(produced[name], dtype=dt)})
                 else:
                     args.append({"array": np.ascontiguousarray(inputs[name], dtype=dt)})
-            res = runner.run(fn, plan, args, warmup=warmup, iters=iters)
+            res = runner.run(fn, plan, args, warmup=warmup, iters=iters, arg_order=list(k["arg_order"]))
             if not res["ok"]:
                 raise runner.RunnerError(res["stage"], res["stderr"])
             for name, a in zip(k["arg_order"], args):

@@ -44,6 +44,12 @@ class ThrArg(ctypes.Structure):
                 ("kind", ctypes.c_int32), ("zero_each", ctypes.c_int32)]
 
 
+class ThrTmapSpec(ctypes.Structure):
+    _fields_ = [("global_", ctypes.c_char_p), ("arg", ctypes.c_int32), ("dtype_code", ctypes.c_int32),
+                ("rank", ctypes.c_int32), ("swizzle", ctypes.c_int32), ("dims", ctypes.c_uint64 * 5),
+                ("strides", ctypes.c_uint64 * 4), ("box", ctypes.c_uint32 * 5)]
+
+
 _lib = None
 _inited: set[int] = set()
 
@@ -71,7 +77,11 @@ def library() -> ctypes.CDLL:
                          ctypes.c_double, ctypes.POINTER(ctypes.c_float), u64], i32),
             "thr_tensor_map": ([p, i32, i32, u64, ctypes.POINTER(u64), ctypes.POINTER(u64),
                                 ctypes.POINTER(ctypes.c_uint32), i32], i32),
+            "thr_run_ex": ([u64, u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(ThrArg), i32,
+                            ctypes.POINTER(ThrTmapSpec), i32, ctypes.c_char_p, i32, i32, ctypes.c_double,
+                            ctypes.POINTER(ctypes.c_float), u64], i32),
             "thr_memcpy_htod": ([u64, p, u64, u64], i32),
+            "thr_memcpy_dtoh": ([p, u64, u64], i32),
             "thr_synchronize": ([], i32),
             "thr_release_buffers": ([], i32),
             "thr_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
@@ -201,7 +211,9 @@ class LaunchPlan:
     block: tuple
     smem: int
     tuned: bool
-    tmaps: list = field(default_factory=list)     # [(global name, tensor-map spec)]
+    tmaps: list = field(default_factory=list)       # tensor-map specs the tuned launch reads
+    tmap_ptrs: dict | None = None                   # {"global": name, "params": [...]}
+    error_word: str | None = None                   # module global a kernel records wait time-outs in
 
 
 def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> LaunchPlan:
@@ -210,7 +222,7 @@ def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> Launc
     if side is None or honour_meta:
         return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False)
     return LaunchPlan(tuple(side["grid"]), tuple(side["block"]), int(side.get("smem_bytes", 0)), True,
-                      list(side.get("tmaps", [])))
+                      list(side.get("tmaps", [])), side.get("tmap_ptrs"), side.get("error_word"))
 
 
 def encode_tensor_map(spec: dict, base: int) -> bytes:
@@ -224,22 +236,59 @@ def encode_tensor_map(spec: dict, base: int) -> bytes:
 
 
 def prepare(module: Module, plan: LaunchPlan, arg_order: list[str], ptrs: dict[str, int], stream: int = 0) -> None:
-    """Write the tensor maps a tuned launch reads into the module's globals."""
+    """Write the tensor maps a tuned launch reads, and the pointers they were
+    encoded for, into the module's globals (device-pointer launches)."""
+    lib = library()
     for t in plan.tmaps:
         raw = encode_tensor_map(t, ptrs[t["param"]])
         dst, n = module.global_ptr(t["global"])
         if n < 128:
             raise RunnerError("lookup", f"tensor-map global {t['global']} is {n} bytes")
         buf = ctypes.create_string_buffer(raw, 128)
-        check(library().thr_memcpy_htod(dst, buf, 128, int(stream)), "tensor map upload")
-        # the host buffer must outlive the async copy: synchronise right away
-        check(library().thr_synchronize(), "tensor map upload")
+        check(lib.thr_memcpy_htod(dst, buf, 128, int(stream)), "tensor map upload")
+        check(lib.thr_synchronize(), "tensor map upload")      # the host buffer must outlive the copy
+    if plan.tmap_ptrs:
+        vals = (ctypes.c_uint64 * len(plan.tmap_ptrs["params"]))(*[ptrs[n] for n in plan.tmap_ptrs["params"]])
+        dst, n = module.global_ptr(plan.tmap_ptrs["global"])
+        check(lib.thr_memcpy_htod(dst, vals, ctypes.sizeof(vals), int(stream)), "tensor-map pointer upload")
+        check(lib.thr_synchronize(), "tensor-map pointer upload")
+
+
+def read_error_word(module: Module, plan: LaunchPlan) -> int:
+    """The kernel's wait-time-out record (0: no wait gave up), or 0 if it has none."""
+    if not plan.error_word:
+        return 0
+    dst, _ = module.global_ptr(plan.error_word)
+    v = ctypes.c_uint32()
+    check(library().thr_memcpy_dtoh(ctypes.byref(v), dst, 4), "error word")
+    return v.value
+
+
+def _tmap_specs(plan: LaunchPlan, arg_order: list[str]):
+    specs = (ThrTmapSpec * max(1, len(plan.tmaps)))()
+    names = []
+    for i, t in enumerate(plan.tmaps):
+        names.append(t["global"].encode())
+        specs[i].global_ = names[-1]
+        specs[i].arg = arg_order.index(t["param"])
+        specs[i].dtype_code = DTYPE_CODE[t["dtype"]]
+        specs[i].rank = len(t["dims"])
+        specs[i].swizzle = int(t.get("swizzle", 0))
+        for j, v in enumerate(t["dims"]):
+            specs[i].dims[j] = v
+        for j, v in enumerate(t.get("strides") or []):
+            specs[i].strides[j] = v
+        for j, v in enumerate(t["box"]):
+            specs[i].box[j] = v
+    return specs, names
 
 
 def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0, iters: int = 1,
-        timeout_s: float = 20.0, stream: int = 0) -> dict:
+        timeout_s: float = 20.0, stream: int = 0, arg_order: list[str] | None = None) -> dict:
     """POST /run on host buffers.  ``args``: dicts with ``array`` (numpy; outputs
-    are written back into it), ``output`` (bool) and ``zero_each`` (bool)."""
+    are written back into it), ``output`` (bool) and ``zero_each`` (bool), in
+    the kernel's argument order (``arg_order`` names them; needed for tuned
+    launches that read tensor maps)."""
     arr = (ThrArg * max(1, len(args)))()
     keep = []
     for i, a in enumerate(args):
@@ -250,22 +299,29 @@ def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0,
         arr[i].kind = 1 if a.get("output") else 0
         arr[i].zero_each = 1 if a.get("zero_each") else 0
     med = ctypes.c_float()
-    st = library().thr_run(function.handle, _dims(plan.grid), _dims(plan.block), int(plan.smem), arr, len(args),
-                           int(warmup), int(iters), float(timeout_s), ctypes.byref(med), int(stream))
+    lib = library()
+    if plan.tmaps:
+        if arg_order is None:
+            raise RunnerError("request", "a tuned launch with tensor maps needs the argument names")
+        specs, _names = _tmap_specs(plan, arg_order)
+        table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
+        st = lib.thr_run_ex(function.module.handle, function.handle, _dims(plan.grid), _dims(plan.block),
+                            int(plan.smem), arr, len(args), specs, len(plan.tmaps), table, int(warmup), int(iters),
+                            float(timeout_s), ctypes.byref(med), int(stream))
+    else:
+        st = lib.thr_run(function.handle, _dims(plan.grid), _dims(plan.block), int(plan.smem), arr, len(args),
+                         int(warmup), int(iters), float(timeout_s), ctypes.byref(med), int(stream))
     if st:
         return {"ok": False, "stage": STAGES.get(st, "cuda"), "stderr": last_error()}
     for a, x in zip(args, keep):
         if a.get("output") and x is not a["array"]:
             a["array"][...] = x
+    err = read_error_word(function.module, plan)
+    if err:
+        return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
     return {"ok": True, "median_us": float(med.value)}
 
 
 def release() -> None:
     if _lib is not None:
         _lib.thr_release_buffers()
-
-
-def cdiv(a: int, b: int) -> int:
-    return -(-a // b)
-
-

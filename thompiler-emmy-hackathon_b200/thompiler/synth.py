@@ -166,6 +166,75 @@ def sum_package(outdir, n: int, kind: str = "sum", T: int = 128, init: dict | No
     return _write(outdir, f"synth_{kind}_{n}", code, entry, g, kmeta, 1e-5, 1e-6)
 
 
+def matmul_package(outdir, M: int, N: int, K: int, b_layout: str = "col", out_dtype: str = "f32",
+                   init: dict | None = None) -> Path:
+    """C[M, N] = A[M, K] @ B with f16 inputs on the warp-level tensor cores (mma.sync m16n8k16),
+    in the vocabulary of the reference's t01 / t02 problems.
+
+    B is stored column-major (``b_layout="col"``: a [N, K] buffer, the ``b_trans`` ldmatrix path)
+    or row-major (``"row"``: [K, N]).  Schedule: a 64 x 64 output tile per CTA of 4 warps, each
+    warp a 16 x 64 strip (eight n8 accumulators); K in steps of 64 staged through two 64 x 64
+    f16 slabs in shared memory with 16-byte cp.async copies and the B128 swizzle; per k16 step
+    one ldmatrix.x4 of A, four paired ldmatrix.x4 of B and eight mma.sync."""
+    if M % 64 or N % 64 or K % 64:
+        raise ValueError("matmul_package needs M, N, K multiples of 64")
+    col = b_layout == "col"
+    F16 = F16T
+    a0b, a1b, a0u, ln = "a0_b", "a1_b", "a0_u", "_lane"
+    tid = B("+", B("*", V(a0u), L(32)), V(ln))            # thread index in the CTA (0..127)
+    body = [ir.RegFragment("_a", "a", (16, 8, 16), F16, 1, None),
+            ir.RegFragment("_b", "b", (16, 8, 16), F16, 8, None),
+            ir.RegFragment("_c", "c", (16, 8, 16), F32T, 8, None),
+            ir.Smem("_a_smem", (64, 64), "__half", 1024),
+            ir.Smem("_b_smem", (64, 64), "__half", 1024)]
+    copies = []
+    for i in range(4):
+        chunk = B("+", tid, L(128 * i))                      # 16-byte chunk 0..511 of a 64 x 64 slab
+        row, c8 = B("/", chunk, L(8)), B("*", B("%", chunk, L(8)), L(8))
+        copies.append(ir.CpAsyncCopy("_a_smem", (L(0), L(0)), "x0",
+                                     (B("+", B("*", V(a0b), L(64)), row), B("+", V("_ks"), c8)), 16, "B128",
+                                     (row, c8), None))
+        if col:
+            src = (B("+", B("*", V(a1b), L(64)), row), B("+", V("_ks"), c8))
+        else:
+            src = (B("+", V("_ks"), row), B("+", B("*", V(a1b), L(64)), c8))
+        copies.append(ir.CpAsyncCopy("_b_smem", (L(0), L(0)), "x1", src, 16, "B128", (row, c8), None))
+    inner = [ir.LdmatrixLoad("_a", "_a_smem", (B("*", V(a0u), L(16)), V("_kk")), "a", 64, "B128", True, None,
+                             None, False, None, False, None, (), 0, "m16n8k16", None)]
+    for j in range(4):
+        idx = (L(16 * j), V("_kk")) if col else (V("_kk"), L(16 * j))
+        inner.append(ir.LdmatrixLoad(f"_b[{2 * j}]", "_b_smem", idx, "b", 64, "B128", True, None, None, col,
+                                     f"_b[{2 * j + 1}]", False, None, (), 0, "m16n8k16", None))
+    inner.append(ir.Loop(axis("_r0", 8), (ir.MmaSyncPtx("_c[_r0]", "_a", "_b[_r0]", (16, 8, 16), "f16", "f32",
+                                                       False, None, None),), True, False))
+    ks = ir.StridedLoop(axis("_ks", K), L(0), L(64), (
+        *copies, ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False),
+        ir.StridedLoop(axis("_kk", 64), L(0), L(16), tuple(inner), False, None, False),
+        ir.Sync(0, None, False)), False, None, False)
+    body.append(ks)
+    out = "matmul"
+    for j in range(8):
+        body.append(ir.RegStore(out, (B("+", B("*", V(a0b), L(64)), B("*", V(a0u), L(16))),
+                                      B("+", B("*", V(a1b), L(64)), L(8 * j))), f"_c[{j}]", (16, 8, 16), 0, None,
+                                (), None, None, False, "m16n8k16", False, None, "NONE", None, None))
+    tile = ir.Tile((axis(a0b, M // 64), axis(a1b, N // 64), axis(a0u, 4), axis(ln, 32)), tuple(body), 128, 0,
+                   None, None, "m")
+    entry = "k_matmul_f16"
+    bshape = (N, K) if col else (K, N)
+    g = _graph({"x0": ((M, K), "f16"), "x1": (bshape, "f16")}, {}, out, (M, N), entry, tile, dtype=out_dtype)
+    args = [{"name": "x1", "dtype": "f16", "shape": list(bshape), "seed": 1},
+            {"name": "x0", "dtype": "f16", "shape": [M, K], "seed": 0},
+            {"name": out, "dtype": out_dtype, "shape": [M, N], "output": True}]
+    if init:
+        for a in args[:2]:
+            a["init"] = dict(init, seed=a["seed"])
+    kmeta = {"node": out, "arg_order": ["x1", "x0", out], "grid": [(M // 64) * (N // 64), 1, 1],
+             "block": [128, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
+    bexpr = f"torch.randn({N}, {K}, dtype=torch.float16).T" if col else f"torch.randn({K}, {N}, dtype=torch.float16)"
+    code = f"(torch.randn({M}, {K}, dtype=torch.float16) @ {bexpr})" + (".float()" if out_dtype == "f32" else "")
+    return _write(outdir, f"synth_matmul_{M}x{N}x{K}_{b_layout}", code, entry, g, kmeta, 2e-2, 2e-3)
+
+
 def row_package(outdir, kind: str, rows: int, cols: int, T: int = 128, eps: float = 1e-6,
                 init: dict | None = None, w_init: dict | None = None) -> Path:
     """Row softmax / RMSNorm / L2-normalise / row sum of x[rows, cols], one row per CTA (f01/f02/f03/r04)."""
