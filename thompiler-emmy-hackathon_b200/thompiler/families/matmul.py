@@ -41,6 +41,8 @@ meta.json's launch.
 
 from __future__ import annotations
 
+import os
+
 from thompiler import ir
 from thompiler.families.base import TunedKernel
 from thompiler.lowering.types import F16, F32
@@ -51,6 +53,8 @@ THREADS = 192
 BM, BK = 128, 64
 SMEM_LIMIT = 227 * 1024
 WAIT_LIMIT = 1 << 22          # try_wait rounds before a wait gives up
+EPI_WARPS = 4
+STAGE_TILE = 2048             # one epilogue store box: 32 rows x 64 bytes
 
 
 def _desc_hi(sbo: int, layout: int = 2) -> int:
@@ -76,15 +80,25 @@ class TcMatmul(TunedKernel):
         self.a_bytes = BM * BK * 2
         self.b_bytes = self.BN * BK * 2
         stage = self.a_bytes + self.b_bytes
-        room = SMEM_LIMIT - static_smem - 2048
+        self.staging = EPI_WARPS * 2 * STAGE_TILE        # per-warp double-buffered store staging
+        room = SMEM_LIMIT - static_smem - 2048 - self.staging
         self.stages = max(2, min(6, room // stage))
-        self.smem = self.stages * stage + 1024 + 256
+        forced = int(os.environ.get("THOMPILER_MATMUL_STAGES", "0"))   # tuning knob
+        if 2 <= forced <= room // stage:
+            self.stages = forced
+        self.smem = self.stages * stage + self.staging + 1024 + 256
         self.tiles = (M // BM) * (N // self.BN) * S
         self.ctas = min(self.tiles, SM_COUNT)
 
     def pick_bn(self) -> int:
+        forced = int(os.environ.get("THOMPILER_MATMUL_BN", "0"))     # tuning knob: force the tile width
+        if forced and self.N % forced == 0 and forced % 16 == 0 and 16 <= forced <= 256:
+            return forced
         best, best_score = None, -1.0
-        for bn, pref in ((256, 1.0), (192, 1.0), (128, 0.93), (64, 0.7)):
+        # measured on B200 (cta_group::1, TMA-store epilogue): N = 128 tiles are shared-memory
+        # bound (0.65 of N = 256 at 4096^3); N = 192 trails N = 256 by 7 % even where it
+        # balances the waves better (8192 x 3072 x 1024)
+        for bn, pref in ((256, 1.0), (192, 0.85), (128, 0.65), (64, 0.4)):
             if self.N % bn:
                 continue
             tiles = (self.M // BM) * (self.N // bn) * self.S
@@ -170,22 +184,28 @@ class TcMatmul(TunedKernel):
         else:
             tm_b = {"global": "thc_tmap_b", "param": b.name, "dtype": "f16", "dims": [self.N, self.K],
                     "strides": [self.N * 2], "box": [64, BK], "swizzle": 3}
+        esz = self.c.ty.nbytes
+        tm_c = {"global": "thc_tmap_c", "param": self.c.name, "dtype": "f32" if esz == 4 else "f16",
+                "dims": [self.N, self.S * self.M], "strides": [self.N * esz], "box": [64 // esz, 32],
+                "swizzle": 2}
         return {"grid": [self.ctas, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem,
-                "tmaps": [tm_a, tm_b], "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [a.name, b.name]},
+                "tmaps": [tm_a, tm_b, tm_c],
+                "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [a.name, b.name, self.c.name]},
                 "error_word": "thc_error", "tile": [BM, self.BN, BK], "stages": self.stages}
 
     def guard(self, generic: str) -> None:
         em = self.em
         em.module(".global .align 64 .b8 thc_tmap_a[128]")
         em.module(".global .align 64 .b8 thc_tmap_b[128]")
-        em.module(".global .align 8 .u64 thc_tmap_ptr[2]")
+        em.module(".global .align 64 .b8 thc_tmap_c[128]")
+        em.module(".global .align 8 .u64 thc_tmap_ptr[3]")
         em.module(".global .align 4 .u32 thc_error")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
         em.ins(f"setp.ne.u32 {p}, {r}, {THREADS}")
         em.ins(f"@{p} bra {generic}")
-        for i, prm in enumerate((self.a, self.b)):
+        for i, prm in enumerate((self.a, self.b, self.c)):
             raw, want = em.tmp("b64"), em.tmp("b64")
             em.ins(f"ld.param.u64 {raw}, [p_{prm.name}]")
             em.ins(f"ld.global.u64 {want}, [thc_tmap_ptr+{8 * i}]")
@@ -256,6 +276,9 @@ class TcMatmul(TunedKernel):
         ins(f"cvta.global.u64 {tma}, {tma}")
         ins(f"mov.u64 {tmb}, thc_tmap_b")
         ins(f"cvta.global.u64 {tmb}, {tmb}")
+        tmc = t("b64")
+        ins(f"mov.u64 {tmc}, thc_tmap_c")
+        ins(f"cvta.global.u64 {tmc}, {tmc}")
         errp = t("b64")
         ins(f"mov.u64 {errp}, thc_error")
 
@@ -442,6 +465,24 @@ class TcMatmul(TunedKernel):
         ins(f"mad.lo.u32 {row}, {quarter}, 32, {lane}")
         lane_off = t("b32")
         ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
+        lane0 = t("pred")
+        ins(f"setp.eq.u32 {lane0}, {lane}, 0")
+        ebase = t("b32")
+        ins(f"sub.u32 {ebase}, {warp}, 2")
+        ins(f"mad.lo.u32 {ebase}, {ebase}, {2 * STAGE_TILE}, {b_st}")
+        ins(f"add.u32 {ebase}, {ebase}, {ST * b_bytes}")
+        stage_buf = [ebase, t("b32")]
+        ins(f"add.u32 {stage_buf[1]}, {ebase}, {STAGE_TILE}")
+        sw = t("b32")
+        ins(f"shr.u32 {sw}, {lane}, 1")
+        ins(f"and.b32 {sw}, {sw}, 3")
+        soff = []
+        for i in range(4):
+            o = t("b32")
+            ins(f"xor.b32 {o}, {sw}, {i}")
+            ins(f"shl.b32 {o}, {o}, 4")
+            ins(f"mad.lo.u32 {o}, {lane}, 64, {o}")
+            soff.append(o)
         tile3, lt3 = t("b32"), t("b32")
         ins(f"mov.u32 {lt3}, 0")
         ins(f"mov.u32 {tile3}, {cta}")
@@ -461,32 +502,42 @@ class TcMatmul(TunedKernel):
         taddr = t("b32")
         ins(f"mad.lo.u32 {taddr}, {buf3}, {BN}, {tmem}")
         ins(f"add.u32 {taddr}, {taddr}, {lane_off}")
-        # global row address: C + (((s * M) + m0 + row) * N + n0) * esize
+        # Each warp stages its 32 rows x 64 bytes at a time in its own pair of 2 KB shared
+        # buffers, laid out with the 64-byte swizzle (16-byte chunk i of row r at chunk
+        # i ^ ((r >> 1) & 3)), and writes them with one TMA bulk-tensor store per box:
+        # full, coalesced lines instead of 16-byte pieces of 32 different rows.
         esz = self.c.ty.nbytes
-        grow, rowp = t("b32"), t("b64")
-        ins(f"mad.lo.u32 {grow}, {ts3}, {self.M}, {row}")
-        ins(f"mad.lo.u32 {grow}, {tm3}, {BM}, {grow}")
-        rowi = t("b64")
-        ins(f"mul.wide.u32 {rowi}, {grow}, {self.N * esz}")
-        ncol = t("b64")
-        ins(f"mul.wide.u32 {ncol}, {tn3}, {BN * esz}")
-        ins(f"add.s64 {rowp}, {rowi}, {ncol}")
-        ins(f"add.s64 {rowp}, {rowp}, {em.buffer_reg(self.c.name)}")
-        for c0 in range(0, BN, 32):
-            v = [t("b32") for _ in range(32)]
+        cw = 64 // esz                                   # columns per store box
+        row0, col0 = t("b32"), t("b32")
+        ins(f"mad.lo.u32 {row0}, {ts3}, {self.M}, 0")
+        ins(f"mad.lo.u32 {row0}, {tm3}, {BM}, {row0}")
+        ins(f"mad.lo.u32 {row0}, {quarter}, 32, {row0}")
+        ins(f"mul.lo.u32 {col0}, {tn3}, {BN}")
+        for j, c0 in enumerate(range(0, BN, cw)):
+            sbuf = stage_buf[j % 2]
+            ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
+            ins("bar.warp.sync -1")
+            nv = 16 if esz == 4 else 32
+            v = [t("b32") for _ in range(nv)]
             tc = t("b32")
             ins(f"add.u32 {tc}, {taddr}, {c0}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(v)}}}, [{tc}]")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x{nv}.b32 {{{', '.join(v)}}}, [{tc}]")
             ins("tcgen05.wait::ld.sync.aligned")
-            if esz == 4:
-                for i in range(8):
-                    ins(f"st.global.v4.b32 [{rowp}+{(c0 + 4 * i) * 4}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
-            else:
+            if esz == 2:
                 h = [t("b32") for _ in range(16)]
                 for i in range(16):
                     ins(f"cvt.rn.f16x2.f32 {h[i]}, {v[2 * i + 1]}, {v[2 * i]}")
-                for i in range(4):
-                    ins(f"st.global.v4.b32 [{rowp}+{(c0 + 8 * i) * 2}], {{{', '.join(h[4 * i:4 * i + 4])}}}")
+                v = h
+            for i in range(4):
+                a_ = t("b32")
+                ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
+                ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+            ins("fence.proxy.async.shared::cta")
+            ins("bar.warp.sync -1")
+            cc = t("b32")
+            ins(f"add.u32 {cc}, {col0}, {c0}")
+            ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], [{sbuf}]")
+            ins(f"@{lane0} cp.async.bulk.commit_group")
         ins("tcgen05.fence::before_thread_sync")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{ab3}+{acce_off}]")
         ins(f"add.u32 {lt3}, {lt3}, 1")
@@ -494,6 +545,7 @@ class TcMatmul(TunedKernel):
         ins(f"setp.lt.u32 {p}, {tile3}, {tiles}")
         ins(f"@{p} bra {etop}")
         place(edone)
+        ins(f"@{lane0} cp.async.bulk.wait_group 0")       # stores done before the CTA leaves
 
         # ---------------- common exit ----------------
         place(end)
