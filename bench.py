@@ -432,7 +432,105 @@ class Matmul:
                 "parallelism": f"replicas over {world} GPU(s)"}
 
 
+class Attention:
+    """softmax(Q K^T / sqrt(d)) V, f16 [8, 16, 2048, 128], non-causal; (batch, head) units
+    split over the ranks (strong scaling, no collective)."""
+    name = "attention"
+    metric = "achieved tensor TFLOP/s (attention f16 [8,16,2048,128], non-causal)"
+    unit = "TFLOP/s"
+    dtype = "f16"
+    bound = "tensor"
+    sharded = True
+
+    def __init__(self, rank: int, world: int, dev: int, seq: int = 0):
+        import torch
+        from thompiler import synth
+        from thompiler.device import DeviceKernel
+        self.torch = torch
+        B, H, S, D = 8, 16, seq or 2048, 128
+        if B % world:
+            raise ValueError("the attention workload splits its 8 batches over 1, 2, 4 or 8 GPUs")
+        self.B, self.H, self.S, self.D, self.world = B, H, S, D, world
+        Bl = B // world
+        tmp = Path(tempfile.mkdtemp(prefix=f"bench_att_{rank}_"))
+        d = synth.attention_package(tmp / "att", Bl, H, S, D)
+        self.k = {"attention": DeviceKernel(d / "k_attention.ir.json", device=dev)}
+        g = torch.Generator(device=f"cuda:{dev}").manual_seed(3000 + rank)
+        self.q, self.kk, self.v = (torch.randn(Bl, H, S, D, device=f"cuda:{dev}", generator=g).half()
+                                   for _ in range(3))
+        self.c = torch.tensor([D ** 0.5], device=f"cuda:{dev}")
+        self.o = torch.empty(Bl, H, S, D, device=f"cuda:{dev}", dtype=torch.float16)
+        self.kinds = ("attention",)
+        self.flops = {"attention": 4 * Bl * H * S * S * D}
+        self.kbytes = {"attention": 4 * Bl * H * S * D * 2}
+        self.flops_per_step = 4 * B * H * S * S * D
+        self.bytes_per_step = self.flops_per_step
+        self.launches_per_step = 1
+        self.dominant = "attention"
+
+    def ptrs(self) -> dict:
+        return {"div_c1": self.c.data_ptr(), "q": self.q.data_ptr(), "k": self.kk.data_ptr(),
+                "v": self.v.data_ptr(), "attn": self.o.data_ptr()}
+
+    def step(self, stream: int, events=None) -> None:
+        if events is not None:
+            events["attention"][0].record()
+        self.k["attention"](self.ptrs(), stream)
+        if events is not None:
+            events["attention"][1].record()
+
+    def check(self) -> None:
+        from thompiler import runner
+        torch = self.torch
+        self.step(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        k = self.k["attention"]
+        assert runner.read_error_word(k.module, k.plan) == 0, "kernel wait gave up"
+        s = (self.q[0].float() @ self.kk[0].float().transpose(-1, -2)) / self.D ** 0.5
+        ref = torch.softmax(s, -1) @ self.v[0].float()
+        assert torch.allclose(self.o[0].float(), ref, rtol=2e-2, atol=2e-3), "attention mismatch"
+
+    def e2e(self, steps: int) -> dict:
+        from thompiler import runner
+        torch = self.torch
+        k = self.k["attention"]
+        host = {n: torch.empty_like(x, device="cpu").pin_memory() for n, x in
+                (("q", self.q), ("k", self.kk), ("v", self.v), ("attn", self.o))}
+        for n, x in (("q", self.q), ("k", self.kk), ("v", self.v)):
+            host[n].copy_(x)
+        arrs = {n: h.numpy() for n, h in host.items()}
+        arrs["div_c1"] = self.c.cpu().numpy()
+        args = [{"array": arrs[n], "output": n == "attn"} for n in k.arg_order]
+        runner.run(k.fn, k.plan, args, arg_order=k.arg_order)
+        t = time.perf_counter()
+        for _ in range(steps):
+            r = runner.run(k.fn, k.plan, args, arg_order=k.arg_order)
+            if not r["ok"]:
+                raise RuntimeError(r["stderr"])
+        sec = (time.perf_counter() - t) / steps
+        runner.release()
+        return {"value": self.flops["attention"] / sec / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 3 * self.q.numel() * 2 + 4, "d2h_bytes_per_step": self.o.numel() * 2,
+                "ms_per_step": sec * 1e3}
+
+    def cpu_baseline(self) -> dict:
+        from oracle import cpu_baseline
+        r = cpu_baseline.attention_sample(2, self.S, self.D)
+        fl = 4 * 2 * self.S * self.S * self.D
+        return {"value": fl / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port",
+                "sample": f"torch CPU f16 attention on 2 of the 128 heads ([2, {self.S}, {self.D}]), one run"}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"attention f16 [{self.B}, {self.H}, {self.S}, {self.D}] non-causal, "
+                            "scale 1/sqrt(d), f32 accumulate",
+                "kernels": {"attention": self.k["attention"].family},
+                "tile": self.k["attention"].module.sidecar.get("tile") if self.k["attention"].module.sidecar else None,
+                "l2": "K/V of a head (1 MiB) shared in L2 by its 16 query tiles; no flush",
+                "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective"}
+
+
 CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
+           "attention": lambda r, w, d, n: Attention(r, w, d, n),
            "matmul": lambda r, w, d, n: Matmul(r, w, d, n),
            "sum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 20),
            "bigsum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True)}
@@ -540,8 +638,9 @@ def main() -> None:
         if world > 1:
             v = torch.tensor([e2e["ms_per_step"]], device=f"cuda:{local}")
             dist.all_reduce(v, op=dist.ReduceOp.MAX)
-            e2e["value"] = w.bytes_per_step * world / (float(v.item()) / 1e3) / 1e9 if not \
-                getattr(w, "sharded", False) else w.bytes_per_step / (float(v.item()) / 1e3) / 1e9
+            unit_scale = 1e12 if getattr(w, "bound", "hbm") == "tensor" else 1e9
+            work = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
+            e2e["value"] = work / (float(v.item()) / 1e3) / unit_scale
     if rank == 0:
         pk = peaks()
         dom = w.dominant

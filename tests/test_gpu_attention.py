@@ -1,0 +1,82 @@
+"""GPU parity of the tcgen05 attention family.
+
+* small shapes: the tuned kernel and the same module under meta.json's
+  launch (the generic lowering of the a02-style IR) against the oracle
+  interpreter on the same seeded inputs;
+* the benchmark shape [8, 16, 2048, 128]: against a plain float32 PyTorch
+  evaluation of softmax(Q K^T / sqrt(d)) V on the GPU (all 128 heads), and
+  against the float64 numpy expression on the CPU for two heads;
+* the kernel's wait-time-out word stays 0.
+Tolerance for f16-input attention: rtol 2e-2 / atol 2e-3.
+"""
+
+import numpy as np
+import pytest
+
+from oracle.interp import run_package as oracle_run
+from thompiler import problems, runner, synth
+from thompiler.device import DeviceKernel
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 2e-2, 2e-3
+
+
+def _sdpa64(q, k, v):
+    q, k, v = (x.astype(np.float64) for x in (q, k, v))
+    s = q @ np.swapaxes(k, -1, -2) / np.sqrt(q.shape[-1])
+    p = np.exp(s - s.max(-1, keepdims=True))
+    return (p / p.sum(-1, keepdims=True)) @ v
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 128, 64), (1, 1, 256, 128)])
+def test_attention_small_vs_oracle(tmp_path, shape):
+    d = synth.attention_package(tmp_path / "att", *shape)
+    pkg = problems.load_package(d)
+    ptx = problems.compile_package(pkg)
+    assert "tcgen05.mma" in ptx["k_attention"]
+    tuned = problems.run_package(pkg, ptx)
+    assert tuned["launch"]["k_attention"].tmaps
+    meta = problems.run_package(pkg, ptx, honour_meta=True)
+    want = oracle_run(d)["attn"].astype(np.float64)
+    for res in (tuned, meta):
+        np.testing.assert_allclose(res["outputs"]["attn"].astype(np.float64), want, rtol=RTOL, atol=ATOL)
+    x = problems.make_inputs(pkg)
+    ref = _sdpa64(x["q"], x["k"], x["v"])
+    assert np.max(np.abs(tuned["outputs"]["attn"] - ref)) < 5e-3
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 384, 64), (1, 3, 512, 128)])
+def test_attention_medium_vs_expression(tmp_path, shape):
+    d = synth.attention_package(tmp_path / "att", *shape)
+    pkg = problems.load_package(d)
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    np.testing.assert_allclose(res["outputs"]["attn"].astype(np.float64), _sdpa64(x["q"], x["k"], x["v"]),
+                               rtol=RTOL, atol=ATOL)
+
+
+def test_attention_benchmark_shape(tmp_path):
+    import torch
+    B, H, S, D = 8, 16, 2048, 128
+    k = DeviceKernel(synth.attention_package(tmp_path / "att", B, H, S, D) / "k_attention.ir.json")
+    assert k.plan.tmaps and "tcgen05.mma" in k.ptx
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q, kk, v = (torch.randn(B, H, S, D, device="cuda", generator=g).half() for _ in range(3))
+    c = torch.tensor([D ** 0.5], device="cuda")
+    o = torch.full((B, H, S, D), float("nan"), device="cuda", dtype=torch.float16)
+    k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(), "attn": o.data_ptr()},
+      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert runner.read_error_word(k.module, k.plan) == 0
+    assert not torch.isnan(o).any()
+    worst = 0.0
+    for b in range(B):
+        s = (q[b].float() @ kk[b].float().transpose(-1, -2)) / D ** 0.5
+        ref = torch.softmax(s, -1) @ v[b].float()
+        assert torch.allclose(o[b].float(), ref, rtol=RTOL, atol=ATOL)
+        worst = max(worst, (o[b].float() - ref).abs().max().item())
+    assert worst < 5e-3, worst
+    ref64 = _sdpa64(q[0, :2].cpu().numpy(), kk[0, :2].cpu().numpy(), v[0, :2].cpu().numpy())
+    np.testing.assert_allclose(o[0, :2].float().cpu().numpy(), ref64, rtol=RTOL, atol=ATOL)
+    k.close()

@@ -1,0 +1,569 @@
+"""Tuned family: attention, softmax(Q K^T / c) V, on tcgen05 (the a01 / a02
+family at the benchmark shape [8, 16, 2048, 128], f16 in and out).
+
+Recognised IR: the a02 schedule of the reference's problem set -- one output
+element per thread, a loop over keys holding the QK dot product (an inner
+loop over d), the two-state online softmax (running max, rescaled sum) and
+the V accumulation, then ``acc / sum`` written out (see
+problems/a02_attention_128/k_matmul_softmax_reduce_6f0029.ir.txt of the
+reference).  Q, K, V and the output are f16 [..., S, D] buffers (D = 64 or
+128, S a multiple of 128); ``c`` comes from a one-element constant buffer at
+run time.
+
+Tuned body: one CTA per (head, 128-query tile), 192 threads:
+  warp 0    TMA: the Q tile once, then K and V tiles of 128 keys through a
+            two-stage ring (128B-swizzled, K-major rows of 64 d);
+  warp 1    tcgen05: S_i = Q K_i^T into one of two TMEM score buffers
+            (M = 128 queries, N = 128 keys, K = D), and O += P_{i-1} V_{i-1}
+            (A = P from shared memory, B = V as an MN-major operand, O in TMEM);
+  warps 2-5 softmax: each thread owns one query row; it loads its 128 scores
+            from TMEM, takes the row max, rescales O and the running sum only
+            when the max grew by more than 2^8 (so P <= 256 stays exact in
+            f16 and the rescale is rare), writes P = 2^(s*c' - m) as f16 into
+            a 128B-swizzled shared tile for the next MMA; at the end it
+            normalises O by the row sum and stores the tile with TMA.
+Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
+exactly as the IR's exp lowering; ex2.approx computes the powers.  All
+mbarrier waits are bounded (thompiler.families.kit).
+"""
+
+from __future__ import annotations
+
+import math
+
+from thompiler import ir
+from thompiler.families.base import TunedKernel
+from thompiler.families.kit import Kit, desc_hi, idesc_f16
+from thompiler.lowering.types import F16, F32
+from thompiler.load import KernelInfo
+
+THREADS = 192
+BM = BN = 128
+STAGES = 2
+LOG2E = math.log2(math.e)
+
+
+def _var_tail(index: tuple, names: tuple) -> bool:
+    return len(index) >= 2 and all(isinstance(e, ir.Var) and e.name == n for e, n in zip(index[-2:], names))
+
+
+class TcAttention(TunedKernel):
+    family = "tcgen05-attention"
+
+    def __init__(self, kernel, q, k, v, out, scale, heads, Sq, Sk, D):
+        super().__init__(kernel)
+        self.pq, self.pk, self.pv, self.pout, self.pscale = q, k, v, out, scale
+        self.heads, self.Sq, self.Sk, self.D = heads, Sq, Sk, D
+        self.q_bytes = BM * D * 2
+        self.kv_bytes = BN * D * 2
+        self.p_bytes = BM * BN * 2
+        self.smem = self.q_bytes + STAGES * 2 * self.kv_bytes + 2 * self.p_bytes + 1024 + 256
+        self.tiles = heads * (Sq // BM)
+
+    # ---- recognition -------------------------------------------------------------
+
+    @classmethod
+    def match(cls, kernel: KernelInfo):
+        body = kernel.body
+        if len(body) != 1 or not isinstance(body[0], ir.Tile):
+            return None
+        tile = body[0]
+        if len(tile.axes) < 2:
+            return None
+        a0, a5 = tile.axes[-2].name, tile.axes[-1].name
+        outer = [s for s in tile.body if isinstance(s, ir.Loop)]
+        if len(outer) != 1:
+            return None
+        outer = outer[0]
+        a1 = outer.axis.name
+        inner = [s for s in outer.body if isinstance(s, ir.Loop)]
+        if len(inner) != 1 or not outer.seed or not inner[0].seed:
+            return None
+        inner = inner[0]
+        a2 = inner.axis.name
+        loads = [s for s in ir.walk_stmts(tile.body) if isinstance(s, ir.Load)]
+        qk = {}
+        for s in inner.body:
+            if isinstance(s, ir.Load):
+                if _var_tail(s.index, (a0, a2)):
+                    qk["q"] = s.input
+                elif _var_tail(s.index, (a1, a2)):
+                    qk["k"] = s.input
+                else:
+                    return None
+        vl = [s for s in outer.body if isinstance(s, ir.Load)]
+        if len(vl) != 1 or not _var_tail(vl[0].index, (a1, a5)):
+            return None
+        writes = [s for s in ir.walk_stmts(tile.body) if isinstance(s, ir.Write)]
+        if len(writes) != 1 or not _var_tail(writes[0].index, (a0, a5)) or writes[0].atomic:
+            return None
+        consts = [s for s in loads if all(isinstance(x, ir.Literal) for x in s.index)]
+        if len(consts) != 1 or set(qk) != {"q", "k"}:
+            return None
+        ops = [s.op.name for s in ir.walk_stmts(outer.body) if isinstance(s, ir.Assign)]
+        accs = [(s.op.name, s.base is not None) for s in outer.body if isinstance(s, ir.Accum)]
+        if ops.count("exp") != 2 or sorted(accs) != [("add", True), ("add", True), ("maximum", False)]:
+            return None
+        recips = [s for s in tile.body if isinstance(s, ir.Assign) and s.op.name == "reciprocal"]
+        if len(recips) != 2:
+            return None
+        q, k = kernel.param(qk["q"]), kernel.param(qk["k"])
+        v, out = kernel.param(vl[0].input), kernel.param(writes[0].output)
+        scale = kernel.param(consts[0].input)
+        if None in (q, k, v, out, scale) or len(kernel.params) != 5:
+            return None
+        if any(p.ty is not F16 for p in (q, k, v, out)) or scale.ty is not F32 or scale.nelems != 1:
+            return None
+        if not (q.shape == out.shape and k.shape == v.shape and q.shape[:-2] == k.shape[:-2]):
+            return None
+        Sq, D = q.shape[-2:]
+        Sk = k.shape[-2]
+        if k.shape[-1] != D or D not in (64, 128) or Sq % BM or Sk % BN:
+            return None
+        if tile.extents[-2:] != (Sq, D) or outer.axis.size != Sk or inner.axis.size != D:
+            return None
+        heads = 1
+        for e in q.shape[:-2]:
+            heads *= e
+        if tuple(tile.extents[:-2]) != tuple(q.shape[:-2]):
+            return None
+        return cls(kernel, q, k, v, out, scale, heads, Sq, Sk, D)
+
+    # ---- launch --------------------------------------------------------------------
+
+    def sidecar(self) -> dict:
+        D = self.D
+
+        def tm(name, prm, rows):
+            return {"global": name, "param": prm.name, "dtype": "f16", "dims": [D, rows],
+                    "strides": [D * 2], "box": [64, 128], "swizzle": 3}
+        maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
+                tm("thc_tmap_v", self.pv, self.heads * self.Sk), tm("thc_tmap_o", self.pout, self.heads * self.Sq)]
+        return {"grid": [self.tiles, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem, "tmaps": maps,
+                "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
+                "error_word": "thc_error", "tile": [BM, BN, D], "stages": STAGES}
+
+    def guard(self, generic: str) -> None:
+        em = self.em
+        for n in ("q", "k", "v", "o"):
+            em.module(f".global .align 64 .b8 thc_tmap_{n}[128]")
+        em.module(".global .align 8 .u64 thc_tmap_ptr[4]")
+        em.module(".global .align 4 .u32 thc_error")
+        em.module(".extern .shared .align 1024 .b8 smem_pool[]")
+        p = em.tmp("pred")
+        r = self.special("%ntid.x")
+        em.ins(f"setp.ne.u32 {p}, {r}, {THREADS}")
+        em.ins(f"@{p} bra {generic}")
+        for i, prm in enumerate((self.pq, self.pk, self.pv, self.pout)):
+            raw, want = em.tmp("b64"), em.tmp("b64")
+            em.ins(f"ld.param.u64 {raw}, [p_{prm.name}]")
+            em.ins(f"ld.global.u64 {want}, [thc_tmap_ptr+{8 * i}]")
+            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
+            em.ins(f"@{p} bra {generic}")
+
+    # ---- the tuned body ----------------------------------------------------------------
+
+    def emit_tuned(self) -> None:  # noqa: C901 - one kernel, in order
+        em = self.em
+        t, ins, place, lab = em.tmp, em.ins, em.place, em.label
+        D, n_blk = self.D, self.Sk // BN
+        dblk = D // 64
+        qb, kvb, pb = self.q_bytes, self.kv_bytes, self.p_bytes
+
+        tid, warp, lane = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {tid}, %tid.x")
+        ins(f"shr.u32 {warp}, {tid}, 5")
+        ins(f"and.b32 {lane}, {tid}, 31")
+        base = t("b32")
+        ins(f"mov.u32 {base}, smem_pool")
+        ins(f"add.u32 {base}, {base}, 1023")
+        ins(f"and.b32 {base}, {base}, -1024")
+        q_s = base
+        k_s = [t("b32") for _ in range(STAGES)]
+        v_s = [t("b32") for _ in range(STAGES)]
+        off = qb
+        for s in range(STAGES):
+            ins(f"add.u32 {k_s[s]}, {base}, {off}")
+            ins(f"add.u32 {v_s[s]}, {base}, {off + kvb}")
+            off += 2 * kvb
+        p_s = [t("b32"), t("b32")]
+        ins(f"add.u32 {p_s[0]}, {base}, {off}")
+        ins(f"add.u32 {p_s[1]}, {base}, {off + pb}")
+        off += 2 * pb
+        bars = t("b32")
+        ins(f"add.u32 {bars}, {base}, {off}")
+        nb = 0
+
+        def bar(count: int) -> int:
+            nonlocal nb
+            nb += 1
+            return (nb - 1) * 8
+        q_full = bar(1)
+        kv_full = [bar(1) for _ in range(STAGES)]
+        kv_empty = [bar(1) for _ in range(STAGES)]
+        s_full, s_free = [bar(1), bar(1)], [bar(128), bar(128)]
+        p_full, p_empty = [bar(128), bar(128)], [bar(1), bar(1)]
+        o_done = bar(1)
+        o_staged = bar(128)
+        counts = {q_full: 1, o_done: 1, o_staged: 128, **{o: 1 for o in kv_full + kv_empty + s_full + p_empty},
+                  **{o: 128 for o in s_free + p_full}}
+        slot_off = nb * 8
+        p = t("pred")
+        skip = lab("at_noinit")
+        ins(f"setp.ne.u32 {p}, {tid}, 0")
+        ins(f"@{p} bra {skip}")
+        for o, c in counts.items():
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{o}], {c}")
+        ins("fence.mbarrier_init.release.cluster")
+        ins("fence.proxy.async.shared::cta")
+        place(skip)
+        noalloc = lab("at_noalloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {noalloc}")
+        slot = t("b32")
+        ins(f"add.u32 {slot}, {bars}, {slot_off}")
+        ins(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{slot}], 512")
+        ins("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned")
+        place(noalloc)
+        ins("tcgen05.fence::before_thread_sync")
+        ins("bar.sync 0")
+        ins("tcgen05.fence::after_thread_sync")
+        tmem = t("b32")
+        ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
+        errp = t("b64")
+        ins(f"mov.u64 {errp}, thc_error")
+        end = lab("at_end")
+        kit = Kit(em, errp, end)
+        tmaps = {}
+        for n in ("q", "k", "v", "o"):
+            r = t("b64")
+            ins(f"mov.u64 {r}, thc_tmap_{n}")
+            ins(f"cvta.global.u64 {r}, {r}")
+            tmaps[n] = r
+        cta = self.special("%ctaid.x")
+        qtiles = self.Sq // BM
+        bh, qt = t("b32"), t("b32")
+        ins(f"div.u32 {bh}, {cta}, {qtiles}")
+        ins(f"rem.u32 {qt}, {cta}, {qtiles}")
+        qrow, kvrow = t("b32"), t("b32")
+        ins(f"mul.lo.u32 {qrow}, {bh}, {self.Sq}")
+        ins(f"mad.lo.u32 {qrow}, {qt}, {BM}, {qrow}")
+        ins(f"mul.lo.u32 {kvrow}, {bh}, {self.Sk}")
+        role_mma, role_sm = lab("at_mma"), lab("at_softmax")
+        ins(f"setp.eq.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_mma}")
+        ins(f"setp.gt.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_sm}")
+
+        # ---------------- producer (warp 0) ----------------
+        # ring addresses: stage s holds K at k0 + s*2*kvb and V right after it
+        stage_stride = 2 * kvb
+        is0 = t("pred")
+        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        tma = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {qb}")
+        for db in range(dblk):
+            ins(f"@{is0} {tma} [{q_s}+{db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qrow}}}], [{bars}+{q_full}]")
+        i = t("b32")
+        ins(f"mov.u32 {i}, 0")
+        ptop = lab("at_prod")
+        place(ptop)
+        st, ks, vs, eb, fb, row = t("b32"), t("b32"), t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"rem.u32 {st}, {i}, {STAGES}")
+        ins(f"mad.lo.u32 {ks}, {st}, {stage_stride}, {k_s[0]}")
+        ins(f"add.u32 {vs}, {ks}, {kvb}")
+        ins(f"mad.lo.u32 {eb}, {st}, 8, {bars}")
+        ins(f"add.u32 {fb}, {eb}, {kv_full[0]}")
+        ins(f"add.u32 {eb}, {eb}, {kv_empty[0]}")
+        kit.wait(eb, kit.parity(i, STAGES, flip=True), 0)
+        ins(f"mad.lo.u32 {row}, {i}, {BN}, {kvrow}")
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {2 * kvb}")
+        for db in range(dblk):
+            ins(f"@{is0} {tma} [{ks}+{db * BN * 128}], [{tmaps['k']}, {{{db * 64}, {row}}}], [{fb}]")
+            ins(f"@{is0} {tma} [{vs}+{db * BN * 128}], [{tmaps['v']}, {{{db * 64}, {row}}}], [{fb}]")
+        ins(f"add.u32 {i}, {i}, 1")
+        ins(f"setp.lt.u32 {p}, {i}, {n_blk}")
+        ins(f"@{p} bra {ptop}")
+        for s in range(min(STAGES, n_blk)):               # drain: the last load of each stage landed
+            last_use = (n_blk - 1 - s) // STAGES
+            lp = t("b32")
+            ins(f"mov.u32 {lp}, {last_use & 1}")
+            kit.wait(f"{bars}+{kv_full[s]}", lp, 0)
+        ins(f"bra {end}")
+
+        # ---------------- MMA issuer (warp 1) ----------------
+        place(role_mma)
+        ism = t("pred")
+        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        zero = t("b32")
+        ins(f"mov.u32 {zero}, 0")
+        kit.wait(f"{bars}+{q_full}", zero, 1)
+        ins("tcgen05.fence::after_thread_sync")
+        hi = t("b32")
+        ins(f"mov.u32 {hi}, {desc_hi(1024)}")
+        qdesc = kit.desc(q_s, 16, hi)
+        id_s = idesc_f16(BM, BN)
+        id_o = idesc_f16(BM, D, b_mn_major=True)
+        always, never = t("pred"), t("pred")
+        ins(f"setp.eq.u32 {always}, {zero}, 0")
+        ins(f"setp.ne.u32 {never}, {zero}, 0")
+
+        def issue_s(blk: str) -> None:
+            """S[blk & 1] = Q K_blk^T."""
+            st_, b_, ks_, bar_ = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st_}, {blk}, {STAGES}")
+            ins(f"and.b32 {b_}, {blk}, 1")
+            ins(f"mad.lo.u32 {ks_}, {st_}, {stage_stride}, {k_s[0]}")
+            ins(f"mad.lo.u32 {bar_}, {st_}, 8, {bars}")
+            ins(f"add.u32 {bar_}, {bar_}, {kv_full[0]}")
+            kit.wait(bar_, kit.parity(blk, STAGES), 1)
+            sf = t("b32")
+            ins(f"mad.lo.u32 {sf}, {b_}, 8, {bars}")
+            ins(f"add.u32 {sf}, {sf}, {s_free[0]}")
+            kit.wait(sf, kit.parity(blk, 2, flip=True), 1)
+            ins("tcgen05.fence::after_thread_sync")
+            kd = kit.desc(ks_, 16, hi)
+            dcol = t("b32")
+            ins(f"mad.lo.u32 {dcol}, {b_}, 128, {tmem}")
+            ins(f"add.u32 {dcol}, {dcol}, 128")
+            for kk in range(D // 16):
+                o_ = (kk // 4) * BM * 128 + (kk % 4) * 32
+                a = kit.desc_add(qdesc, o_)
+                bb = kit.desc_add(kd, (kk // 4) * BN * 128 + (kk % 4) * 32)
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {a}, {bb}, {id_s}, "
+                    f"{never if kk == 0 else always}")
+            sb = t("b32")
+            ins(f"mad.lo.u32 {sb}, {b_}, 8, {bars}")
+            ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sb}+{s_full[0]}]")
+
+        def issue_pv(blk: str, first_block: bool) -> None:
+            """O += P[blk & 1] V_blk; the first block's first MMA overwrites O."""
+            st_, b_, vs_, pbuf = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st_}, {blk}, {STAGES}")
+            ins(f"and.b32 {b_}, {blk}, 1")
+            pf = t("b32")
+            ins(f"mad.lo.u32 {pf}, {b_}, 8, {bars}")
+            ins(f"add.u32 {pf}, {pf}, {p_full[0]}")
+            kit.wait(pf, kit.parity(blk, 2), 1)
+            ins("tcgen05.fence::after_thread_sync")
+            ins(f"mad.lo.u32 {vs_}, {st_}, {stage_stride}, {k_s[0]}")
+            ins(f"add.u32 {vs_}, {vs_}, {kvb}")
+            ins(f"mad.lo.u32 {pbuf}, {b_}, {pb}, {p_s[0]}")
+            pd = kit.desc(pbuf, 16, hi)
+            vd = kit.desc(vs_, BN * 128, hi)
+            for kk in range(BN // 16):
+                a = kit.desc_add(pd, (kk // 4) * BM * 128 + (kk % 4) * 32)
+                bb = kit.desc_add(vd, kk * 16 * 128)
+                acc = never if (first_block and kk == 0) else always
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{tmem}], {a}, {bb}, {id_o}, {acc}")
+            ke, pe = t("b32"), t("b32")
+            ins(f"mad.lo.u32 {ke}, {st_}, 8, {bars}")
+            ins(f"mad.lo.u32 {pe}, {b_}, 8, {bars}")
+            commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
+            ins(f"@{ism} {commit} [{ke}+{kv_empty[0]}]")
+            ins(f"@{ism} {commit} [{pe}+{p_empty[0]}]")
+            ins(f"@{ism} {commit} [{bars}+{o_done}]")
+
+        issue_s(zero)
+        if n_blk > 1:
+            one = t("b32")
+            ins(f"mov.u32 {one}, 1")
+            issue_s(one)
+            issue_pv(zero, True)
+            blk = t("b32")
+            ins(f"mov.u32 {blk}, 2")
+            mtop, mdone = lab("at_mma_k"), lab("at_mma_done")
+            ins(f"setp.ge.u32 {p}, {blk}, {n_blk}")
+            ins(f"@{p} bra {mdone}")
+            place(mtop)
+            issue_s(blk)
+            prev = t("b32")
+            ins(f"sub.u32 {prev}, {blk}, 1")
+            issue_pv(prev, False)
+            ins(f"add.u32 {blk}, {blk}, 1")
+            ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
+            ins(f"@{p} bra {mtop}")
+            place(mdone)
+            last = t("b32")
+            ins(f"mov.u32 {last}, {n_blk - 1}")
+            issue_pv(last, False)
+        else:
+            issue_pv(zero, True)
+        ins(f"bra {end}")
+
+        # ---------------- softmax + epilogue (warps 2..5) ----------------
+        place(role_sm)
+        quarter, r = t("b32"), t("b32")
+        ins(f"and.b32 {quarter}, {warp}, 3")
+        ins(f"mad.lo.u32 {r}, {quarter}, 32, {lane}")
+        lane_off = t("b32")
+        ins(f"shl.b32 {lane_off}, {quarter}, 21")
+        trow = t("b32")
+        ins(f"add.u32 {trow}, {tmem}, {lane_off}")
+        # this row's 16-byte chunk offsets in a 128B-swizzled K-major tile: r*128 + ((c ^ (r & 7)) << 4)
+        r7 = t("b32")
+        ins(f"and.b32 {r7}, {r}, 7")
+        choff = []
+        for c in range(8):
+            o = t("b32")
+            ins(f"xor.b32 {o}, {r7}, {c}")
+            ins(f"shl.b32 {o}, {o}, 4")
+            ins(f"mad.lo.u32 {o}, {r}, 128, {o}")
+            choff.append(o)
+        sc = t("f32")
+        ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")
+        ins(f"rcp.rn.f32 {sc}, {sc}")
+        ins(f"mul.rn.f32 {sc}, {sc}, 0f{_f32bits(LOG2E)}")
+        mref, mref8, l = t("f32"), t("f32"), t("f32")
+        ins(f"mov.f32 {mref}, 0fFF800000")
+        ins(f"mov.f32 {mref8}, 0fFF800000")
+        ins(f"mov.f32 {l}, 0f00000000")
+        sv = [t("f32") for _ in range(BN)]
+        blk = t("b32")
+        ins(f"mov.u32 {blk}, 0")
+        stop = lab("at_sm_blk")
+        place(stop)
+        b_, bb8 = t("b32"), t("b32")
+        ins(f"and.b32 {b_}, {blk}, 1")
+        ins(f"mad.lo.u32 {bb8}, {b_}, 8, {bars}")
+        sfull = t("b32")
+        ins(f"add.u32 {sfull}, {bb8}, {s_full[0]}")
+        kit.wait(sfull, kit.parity(blk, 2), 2)
+        ins("tcgen05.fence::after_thread_sync")
+        scol = t("b32")
+        ins(f"mad.lo.u32 {scol}, {b_}, 128, {trow}")
+        for c in range(BN // 32):
+            a = t("b32")
+            ins(f"add.u32 {a}, {scol}, {128 + 32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, [{a}]")
+        ins("tcgen05.wait::ld.sync.aligned")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bb8}+{s_free[0]}]")
+        mx = _tree(em, "max.f32", sv)
+        mnew = t("f32")
+        ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
+        norescale, noowait = lab("at_norescale"), lab("at_first")
+        ins(f"setp.gt.f32 {p}, {mnew}, {mref8}")
+        ins(f"@!{p} bra {norescale}")
+        alpha, dm = t("f32"), t("f32")
+        ins(f"sub.rn.f32 {dm}, {mref}, {mnew}")
+        ins(f"ex2.approx.ftz.f32 {alpha}, {dm}")
+        ins(f"mul.rn.f32 {l}, {l}, {alpha}")
+        ins(f"setp.eq.u32 {p}, {blk}, 0")
+        ins(f"@{p} bra {noowait}")
+        prevb = t("b32")
+        ins(f"sub.u32 {prevb}, {blk}, 1")
+        kit.wait(f"{bars}+{o_done}", kit.parity(prevb, 1), 3)
+        ins("tcgen05.fence::after_thread_sync")
+        for c in range(D // 32):
+            ov = [t("f32") for _ in range(32)]
+            a = t("b32")
+            ins(f"add.u32 {a}, {trow}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            for x in ov:
+                ins(f"mul.rn.f32 {x}, {x}, {alpha}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{a}], {{{', '.join(ov)}}}")
+        ins("tcgen05.wait::st.sync.aligned")
+        place(noowait)
+        ins(f"mov.f32 {mref}, {mnew}")
+        ins(f"add.rn.f32 {mref8}, {mnew}, 0f41000000")
+        place(norescale)
+        negm = t("f32")
+        ins(f"neg.f32 {negm}, {mref}")
+        for x in sv:
+            ins(f"fma.rn.f32 {x}, {x}, {sc}, {negm}")
+            ins(f"ex2.approx.ftz.f32 {x}, {x}")
+        rs = _tree(em, "add.rn.f32", sv)
+        ins(f"add.rn.f32 {l}, {l}, {rs}")
+        hp = [t("b32") for _ in range(BN // 2)]
+        for k in range(BN // 2):
+            ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
+        pe = t("b32")
+        ins(f"add.u32 {pe}, {bb8}, {p_empty[0]}")
+        kit.wait(pe, kit.parity(blk, 2, flip=True), 2)
+        pbuf = t("b32")
+        ins(f"mad.lo.u32 {pbuf}, {b_}, {pb}, {p_s[0]}")
+        for kb in range(BN // 64):
+            for c in range(8):
+                a = t("b32")
+                ins(f"add.u32 {a}, {pbuf}, {choff[c]}")
+                regs = hp[kb * 32 + 4 * c: kb * 32 + 4 * c + 4]
+                ins(f"st.shared.v4.b32 [{a}+{kb * BM * 128}], {{{', '.join(regs)}}}")
+        ins("fence.proxy.async.shared::cta")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bb8}+{p_full[0]}]")
+        ins(f"add.u32 {blk}, {blk}, 1")
+        ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
+        ins(f"@{p} bra {stop}")
+        # epilogue: O / l -> f16 -> swizzled tile in P buffer 0 -> TMA store
+        lastb = t("b32")
+        ins(f"mov.u32 {lastb}, {(n_blk - 1) & 1}")
+        kit.wait(f"{bars}+{o_done}", lastb, 3)
+        ins("tcgen05.fence::after_thread_sync")
+        inv = t("f32")
+        ins(f"rcp.rn.f32 {inv}, {l}")
+        ov = [t("f32") for _ in range(D)]
+        for c in range(D // 32):
+            a = t("b32")
+            ins(f"add.u32 {a}, {trow}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
+        ins("tcgen05.wait::ld.sync.aligned")
+        oh = [t("b32") for _ in range(D // 2)]
+        for k in range(D // 2):
+            ins(f"mul.rn.f32 {ov[2 * k]}, {ov[2 * k]}, {inv}")
+            ins(f"mul.rn.f32 {ov[2 * k + 1]}, {ov[2 * k + 1]}, {inv}")
+            ins(f"cvt.rn.f16x2.f32 {oh[k]}, {ov[2 * k + 1]}, {ov[2 * k]}")
+        for db in range(dblk):
+            for c in range(8):
+                a = t("b32")
+                ins(f"add.u32 {a}, {p_s[0]}, {choff[c]}")
+                ins(f"st.shared.v4.b32 [{a}+{db * BM * 128}], {{{', '.join(oh[db * 32 + 4 * c: db * 32 + 4 * c + 4])}}}")
+        ins("fence.proxy.async.shared::cta")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{o_staged}]")
+        leader = t("pred")
+        ins(f"setp.eq.u32 {leader}, {tid}, 64")
+        skip_store = lab("at_not_leader")
+        ins(f"@!{leader} bra {skip_store}")
+        zb = t("b32")
+        ins(f"mov.u32 {zb}, 0")
+        kit.wait(f"{bars}+{o_staged}", zb, 3)            # every row of the tile is staged
+        for db in range(dblk):
+            ins(f"cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmaps['o']}, "
+                f"{{{db * 64}, {qrow}}}], [{p_s[0]}+{db * BM * 128}]")
+        ins("cp.async.bulk.commit_group")
+        ins("cp.async.bulk.wait_group 0")
+        place(skip_store)
+
+        # ---------------- common exit ----------------
+        place(end)
+        ins("barrier.sync 0")
+        nod = lab("at_nodealloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {nod}")
+        ins("tcgen05.fence::after_thread_sync")
+        ins(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, 512")
+        place(nod)
+
+
+def _f32bits(x: float) -> str:
+    import struct
+    return "%08X" % struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+def _tree(em, op: str, regs: list[str]) -> str:
+    """Pairwise reduction tree of ``regs`` with ``op`` (keeps the inputs)."""
+    cur = list(regs)
+    while len(cur) > 1:
+        nxt = []
+        for i in range(0, len(cur) - 1, 2):
+            d = em.tmp("f32")
+            em.ins(f"{op} {d}, {cur[i]}, {cur[i + 1]}")
+            nxt.append(d)
+        if len(cur) % 2:
+            nxt.append(cur[-1])
+        cur = nxt
+    return cur[0]
+
+
+def recognise(kernel: KernelInfo):
+    return TcAttention.match(kernel)

@@ -1,0 +1,84 @@
+"""Blackwell building blocks shared by the tcgen05 families.
+
+* shared-memory matrix descriptors (64-bit): bits 0-13 start address >> 4,
+  16-29 leading byte offset >> 4, 32-45 stride byte offset >> 4, 46-47
+  version (1 on sm_100), 61-63 layout (2 = 128-byte swizzle) -- the layout
+  CUTLASS documents for sm100 UMMA descriptors;
+* the kind::f16 instruction descriptor (32-bit): D format (f32 = 1) at bit 4,
+  A / B formats at 7 / 10 (f16 = 0), A / B major-ness at 15 / 16 (1 =
+  MN-major), N >> 3 at bit 17, M >> 4 at bit 24;
+* bounded mbarrier waits: every wait gives up after ``WAIT_LIMIT`` rounds of
+  ``mbarrier.try_wait``, records a code in the module's error word and jumps
+  to the kernel's common exit -- no kernel here can hang its GPU.
+"""
+
+from __future__ import annotations
+
+WAIT_LIMIT = 1 << 22
+SWIZZLE_128B = 2
+
+
+def desc_hi(sbo: int, layout: int = SWIZZLE_128B) -> int:
+    """High word: stride byte offset, version 1, layout type."""
+    return ((sbo >> 4) & 0x3FFF) | (1 << 14) | (layout << 29)
+
+
+def idesc_f16(m: int, n: int, a_mn_major: bool = False, b_mn_major: bool = False) -> int:
+    """kind::f16 instruction descriptor: f16 A and B, f32 accumulator."""
+    return ((1 << 4) | ((1 if a_mn_major else 0) << 15) | ((1 if b_mn_major else 0) << 16)
+            | ((n >> 3) << 17) | ((m >> 4) << 24))
+
+
+class Kit:
+    """PTX helpers bound to one emitter, error word and exit label."""
+
+    def __init__(self, em, errp: str, end: str):
+        self.em, self.errp, self.end = em, errp, end
+        self.q = em.tmp("pred")
+
+    def wait(self, bar: str, parity: str, code: int) -> None:
+        em = self.em
+        top, ok = em.label("wait"), em.label("waited")
+        n = em.tmp("b32")
+        em.ins(f"mov.u32 {n}, 0")
+        em.place(top)
+        em.ins(f"mbarrier.try_wait.parity.shared::cta.b64 {self.q}, [{bar}], {parity}")
+        em.ins(f"@{self.q} bra {ok}")
+        em.ins(f"add.u32 {n}, {n}, 1")
+        em.ins(f"setp.lt.u32 {self.q}, {n}, {WAIT_LIMIT}")
+        em.ins(f"@{self.q} bra {top}")
+        em.ins(f"atom.global.or.b32 {em.tmp('b32')}, [{self.errp}], {1 << code}")
+        em.ins(f"bra {self.end}")
+        em.place(ok)
+
+    def desc(self, saddr: str, lbo: int, hi_reg: str) -> str:
+        """A 64-bit descriptor register for the tile at shared address ``saddr``."""
+        em = self.em
+        lo, d = em.tmp("b32"), em.tmp("b64")
+        em.ins(f"shr.u32 {lo}, {saddr}, 4")
+        em.ins(f"and.b32 {lo}, {lo}, 16383")
+        em.ins(f"or.b32 {lo}, {lo}, {(lbo >> 4) << 16}")
+        em.ins(f"mov.b64 {d}, {{{lo}, {hi_reg}}}")
+        return d
+
+    def desc_add(self, d: str, byte_offset: int) -> str:
+        """The descriptor ``d`` advanced by ``byte_offset`` bytes of start address."""
+        if byte_offset == 0:
+            return d
+        em = self.em
+        r = em.tmp("b64")
+        em.ins(f"add.s64 {r}, {d}, {byte_offset >> 4}")
+        return r
+
+    def parity(self, counter: str, period: int, flip: bool = False) -> str:
+        """((counter / period) & 1) [^ 1]: the phase parity of a ring slot's use."""
+        em = self.em
+        r = em.tmp("b32")
+        if period == 1:
+            em.ins(f"and.b32 {r}, {counter}, 1")
+        else:
+            em.ins(f"div.u32 {r}, {counter}, {period}")
+            em.ins(f"and.b32 {r}, {r}, 1")
+        if flip:
+            em.ins(f"xor.b32 {r}, {r}, 1")
+        return r

@@ -235,6 +235,61 @@ def matmul_package(outdir, M: int, N: int, K: int, b_layout: str = "col", out_dt
     return _write(outdir, f"synth_matmul_{M}x{N}x{K}_{b_layout}", code, entry, g, kmeta, 2e-2, 2e-3)
 
 
+def attention_package(outdir, B: int, H: int, S: int, D: int, dtype: str = "f16", T: int = 128) -> Path:
+    """softmax(Q K^T * scale) V over [B, H, S, D] tensors (non-causal), one output element per
+    thread, in the vocabulary and schedule of the reference's a01 / a02 problems (online
+    softmax over the key loop, the QK dot recomputed per output column, ``1/scale`` passed as
+    the constant ``div_c1``).  f16 inputs are widened to f32 with ``copy`` Assigns and the f32
+    result is narrowed to the output dtype -- the only f16 arithmetic the reference lowers."""
+    half = dtype == "f16"
+    DT = F16T if half else F32T
+    b, h, a0, a5, a1, a2 = "a_b", "a_h", "a0", "a5", "a1", "a2"
+
+    def ld(name, buf, idx):
+        if not half:
+            return [ir.Load((name,), buf, idx, F32T)]
+        return [ir.Load((name + "h",), buf, idx, F16T), ir.Assign(name, E("copy"), (name + "h",), F32T)]
+
+    inner = ir.Loop(axis(a2, D), (
+        *ld("in2", "q", (V(b), V(h), V(a0), V(a2))), *ld("in1", "k", (V(b), V(h), V(a1), V(a2))),
+        assign("v3", "multiply", "in1", "in2"),
+        ir.Accum("acc0", "v3", E("add"), F32T, (a2,), None)), False, True)
+    outer = ir.Loop(axis(a1, S), (
+        inner, assign("v4", "multiply", "acc0", "v1"), ir.Let("one", L(1.0, "float"), F32T),
+        assign("v4__gn", "maximum", "acc1", "v4"), assign("v4__dg", "subtract", "acc1", "v4__gn"),
+        assign("v4__alpha", "exp", "v4__dg"), assign("v4__dg_o", "subtract", "v4", "v4__gn"),
+        assign("v4__beta", "exp", "v4__dg_o"), assign("v4__acc3_sa", "multiply", "acc3", "v4__alpha"),
+        assign("v4__acc3_sb", "multiply", "one", "v4__beta"),
+        ir.Accum("acc3", "v4__acc3_sb", E("add"), F32T, (a1,), "v4__acc3_sa"),
+        assign("v4__acc5__sum_sa", "multiply", "acc5__sum", "v4__alpha"),
+        *ld("in7", "v", (V(b), V(h), V(a1), V(a5))),
+        assign("v4__acc5__sum_sb", "multiply", "in7", "v4__beta"),
+        ir.Accum("acc5__sum", "v4__acc5__sum_sb", E("add"), F32T, (a1,), "v4__acc5__sum_sa"),
+        ir.Accum("acc1", "v4", E("maximum"), F32T, (a1,), None)), False, True)
+    tail = [assign("v9", "reciprocal", "acc3"), assign("acc5", "multiply", "acc5__sum", "v9")]
+    if half:
+        tail.append(ir.Assign("out", E("copy"), ("acc5",), F16T))
+    tail.append(ir.Write("attn", (V(b), V(h), V(a0), V(a5)), ("out" if half else "acc5",), DT, False, "NONE"))
+    body = ir.Tile((axis(b, B), axis(h, H), axis(a0, S), axis(a5, D)), (
+        ir.Load(("in0",), "div_c1", (L(0),), F32T), assign("v1", "reciprocal", "in0"), outer, *tail),
+        T, 0, None, None, "m")
+    shape = (B, H, S, D)
+    entry = "k_attention"
+    g = _graph({"q": (shape, dtype), "k": (shape, dtype), "v": (shape, dtype)},
+               {"div_c1": (float(D) ** 0.5, "f32")}, "attn", shape, entry, body, dtype=dtype)
+    args = [{"name": "div_c1", "dtype": "f32", "shape": [1], "data": [float(D) ** 0.5]},
+            {"name": "q", "dtype": dtype, "shape": list(shape), "seed": 0},
+            {"name": "k", "dtype": dtype, "shape": list(shape), "seed": 1},
+            {"name": "v", "dtype": dtype, "shape": list(shape), "seed": 2},
+            {"name": "attn", "dtype": dtype, "shape": list(shape), "output": True}]
+    n = B * H * S * D
+    kmeta = {"node": "attn", "arg_order": [a["name"] for a in args], "grid": [-(-n // T), 1, 1],
+             "block": [T, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
+    code = (f"q, k, v = (torch.randn({B}, {H}, {S}, {D}, dtype=torch.float16) for _ in range(3)); "
+            f"torch.softmax(q @ k.transpose(-1, -2) / {float(D) ** 0.5}, dim=-1) @ v")
+    return _write(outdir, f"synth_attention_{B}x{H}x{S}x{D}", code, entry, g, kmeta, 2e-2, 2e-3)
+
+
 def row_package(outdir, kind: str, rows: int, cols: int, T: int = 128, eps: float = 1e-6,
                 init: dict | None = None, w_init: dict | None = None) -> Path:
     """Row softmax / RMSNorm / L2-normalise / row sum of x[rows, cols], one row per CTA (f01/f02/f03/r04)."""
