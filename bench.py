@@ -27,9 +27,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import signal
 import statistics
-import subprocess
 import sys
 import tempfile
 import time
@@ -66,33 +64,58 @@ def profile_traffic(name: str):
 # ---- clocks ---------------------------------------------------------------------
 
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle reasons sampled every 10 ms from NVML on a background
+    thread while the timed region runs (``nvidia-smi``'s own polling is too coarse
+    for a sub-second region); the first sample is taken before ``start`` returns."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu: int):
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+        self.samples: list[tuple[int, int, int]] = []
+        self.stop_flag = threading.Event()
+        self.error = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpu}", f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.file, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self._physical(gpu))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._sample()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception as e:  # no NVML: report that instead of clocks
+            self.error, self.thread = f"nvml unavailable: {e}", None
+
+    @staticmethod
+    def _physical(gpu: int) -> int:
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x for x in vis.split(",") if x.strip()]
+        return int(ids[gpu]) if gpu < len(ids) and ids[gpu].strip().isdigit() else gpu
+
+    def _sample(self) -> None:
+        nv = self.nv
+        self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetCurrentClocksEventReasons(self.h), 0))
+
+    def _run(self) -> None:
+        while not self.stop_flag.wait(0.01):
+            try:
+                self._sample()
+            except Exception:
+                break
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.send_signal(signal.SIGTERM)
-        self.proc.wait(timeout=10)
-        self.file.flush()
-        rows = [r.split(", ") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
-        os.unlink(self.file.name)
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows if len(r) >= 9 for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        if self.thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error]}
+        self.stop_flag.set()
+        self.thread.join(timeout=5)
+        self._sample()
+        sm = [s[0] for s in self.samples]
+        reasons = sorted({n for s in self.samples for n, bit in self.REASONS.items() if s[1] & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml, 10 ms"}
 
 
 # ---- workloads -----------------------------------------------------------------------
@@ -529,6 +552,9 @@ class Attention:
                 "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective"}
 
 
+# about one second of timed work per workload at one GPU (the clock sampler needs a region that long)
+DEFAULT_STEPS = {"rowops": 6000, "sum": 20000, "bigsum": 1500, "matmul": 5000, "attention": 2500}
+
 CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
            "attention": lambda r, w, d, n: Attention(r, w, d, n),
            "matmul": lambda r, w, d, n: Matmul(r, w, d, n),
@@ -581,7 +607,8 @@ def reference_arm(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=0,
+                    help="timed steps (default: about one second of work for the chosen workload)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -590,6 +617,8 @@ def main() -> None:
                     help="override the workload size (rows for rowops, elements for sums); profiling only")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps <= 0:
+        args.steps = DEFAULT_STEPS[args.config]
     if args.impl == "reference":
         reference_arm(args)
         return

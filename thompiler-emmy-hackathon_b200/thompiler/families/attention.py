@@ -39,7 +39,7 @@ from thompiler.load import KernelInfo
 
 THREADS = 192
 BM = BN = 128
-STAGES = 2
+STAGES = 3                  # K and V rings each
 LOG2E = math.log2(math.e)
 
 
@@ -56,8 +56,7 @@ class TcAttention(TunedKernel):
         self.heads, self.Sq, self.Sk, self.D = heads, Sq, Sk, D
         self.q_bytes = BM * D * 2
         self.kv_bytes = BN * D * 2
-        self.p_bytes = BM * BN * 2
-        self.smem = self.q_bytes + STAGES * 2 * self.kv_bytes + 2 * self.p_bytes + 1024 + 256
+        self.smem = self.q_bytes + STAGES * 2 * self.kv_bytes + 1024 + 256
         self.tiles = heads * (Sq // BM)
 
     # ---- recognition -------------------------------------------------------------
@@ -168,7 +167,8 @@ class TcAttention(TunedKernel):
         t, ins, place, lab = em.tmp, em.ins, em.place, em.label
         D, n_blk = self.D, self.Sk // BN
         dblk = D // 64
-        qb, kvb, pb = self.q_bytes, self.kv_bytes, self.p_bytes
+        qb, kvb = self.q_bytes, self.kv_bytes
+        KS = VS = STAGES
 
         tid, warp, lane = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {tid}, %tid.x")
@@ -178,35 +178,26 @@ class TcAttention(TunedKernel):
         ins(f"mov.u32 {base}, smem_pool")
         ins(f"add.u32 {base}, {base}, 1023")
         ins(f"and.b32 {base}, {base}, -1024")
+        # shared layout: Q tile | K ring | V ring | barriers   (the Q tile stages O at the end)
         q_s = base
-        k_s = [t("b32") for _ in range(STAGES)]
-        v_s = [t("b32") for _ in range(STAGES)]
-        off = qb
-        for s in range(STAGES):
-            ins(f"add.u32 {k_s[s]}, {base}, {off}")
-            ins(f"add.u32 {v_s[s]}, {base}, {off + kvb}")
-            off += 2 * kvb
-        p_s = [t("b32"), t("b32")]
-        ins(f"add.u32 {p_s[0]}, {base}, {off}")
-        ins(f"add.u32 {p_s[1]}, {base}, {off + pb}")
-        off += 2 * pb
-        bars = t("b32")
-        ins(f"add.u32 {bars}, {base}, {off}")
+        k0, v0, bars = t("b32"), t("b32"), t("b32")
+        ins(f"add.u32 {k0}, {base}, {qb}")
+        ins(f"add.u32 {v0}, {base}, {qb + KS * kvb}")
+        ins(f"add.u32 {bars}, {base}, {qb + (KS + VS) * kvb}")
         nb = 0
 
-        def bar(count: int) -> int:
+        def bar() -> int:
             nonlocal nb
             nb += 1
             return (nb - 1) * 8
-        q_full = bar(1)
-        kv_full = [bar(1) for _ in range(STAGES)]
-        kv_empty = [bar(1) for _ in range(STAGES)]
-        s_full, s_free = [bar(1), bar(1)], [bar(128), bar(128)]
-        p_full, p_empty = [bar(128), bar(128)], [bar(1), bar(1)]
-        o_done = bar(1)
-        o_staged = bar(128)
-        counts = {q_full: 1, o_done: 1, o_staged: 128, **{o: 1 for o in kv_full + kv_empty + s_full + p_empty},
-                  **{o: 128 for o in s_free + p_full}}
+        q_full = bar()
+        k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
+        v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
+        s_full, p_full, p_empty = [bar(), bar()], [bar(), bar()], [bar(), bar()]
+        o_done, o_staged = bar(), bar()
+        counts = {o: 1 for o in range(0, nb * 8, 8)}
+        for o in p_full + [o_staged]:
+            counts[o] = 128
         slot_off = nb * 8
         p = t("pred")
         skip = lab("at_noinit")
@@ -230,6 +221,8 @@ class TcAttention(TunedKernel):
         ins("tcgen05.fence::after_thread_sync")
         tmem = t("b32")
         ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
+        # TMEM columns: O [0, 128) | S0 [128, 256) | S1 [256, 384) | P0 [384, 448) | P1 [448, 512)
+        S_COL, P_COL = 128, 384
         errp = t("b64")
         ins(f"mov.u64 {errp}, thc_error")
         end = lab("at_end")
@@ -256,39 +249,41 @@ class TcAttention(TunedKernel):
         ins(f"@{p} bra {role_sm}")
 
         # ---------------- producer (warp 0) ----------------
-        # ring addresses: stage s holds K at k0 + s*2*kvb and V right after it
-        stage_stride = 2 * kvb
         is0 = t("pred")
         ins(f"setp.eq.u32 {is0}, {lane}, 0")
         tma = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
         ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {qb}")
         for db in range(dblk):
             ins(f"@{is0} {tma} [{q_s}+{db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qrow}}}], [{bars}+{q_full}]")
+
+        def ring(i: str, n_st: int, s0: str, full0: int, empty0: int, mapname: str, row: str) -> None:
+            st, buf, fb, eb = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st}, {i}, {n_st}")
+            ins(f"mad.lo.u32 {buf}, {st}, {kvb}, {s0}")
+            ins(f"mad.lo.u32 {fb}, {st}, 8, {bars}")
+            ins(f"add.u32 {eb}, {fb}, {empty0}")
+            ins(f"add.u32 {fb}, {fb}, {full0}")
+            kit.wait(eb, kit.parity(i, n_st, flip=True), 0)
+            ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {kvb}")
+            for db in range(dblk):
+                ins(f"@{is0} {tma} [{buf}+{db * BN * 128}], [{tmaps[mapname]}, {{{db * 64}, {row}}}], [{fb}]")
+
         i = t("b32")
         ins(f"mov.u32 {i}, 0")
         ptop = lab("at_prod")
         place(ptop)
-        st, ks, vs, eb, fb, row = t("b32"), t("b32"), t("b32"), t("b32"), t("b32"), t("b32")
-        ins(f"rem.u32 {st}, {i}, {STAGES}")
-        ins(f"mad.lo.u32 {ks}, {st}, {stage_stride}, {k_s[0]}")
-        ins(f"add.u32 {vs}, {ks}, {kvb}")
-        ins(f"mad.lo.u32 {eb}, {st}, 8, {bars}")
-        ins(f"add.u32 {fb}, {eb}, {kv_full[0]}")
-        ins(f"add.u32 {eb}, {eb}, {kv_empty[0]}")
-        kit.wait(eb, kit.parity(i, STAGES, flip=True), 0)
+        row = t("b32")
         ins(f"mad.lo.u32 {row}, {i}, {BN}, {kvrow}")
-        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {2 * kvb}")
-        for db in range(dblk):
-            ins(f"@{is0} {tma} [{ks}+{db * BN * 128}], [{tmaps['k']}, {{{db * 64}, {row}}}], [{fb}]")
-            ins(f"@{is0} {tma} [{vs}+{db * BN * 128}], [{tmaps['v']}, {{{db * 64}, {row}}}], [{fb}]")
+        ring(i, KS, k0, k_full[0], k_empty[0], "k", row)
+        ring(i, VS, v0, v_full[0], v_empty[0], "v", row)
         ins(f"add.u32 {i}, {i}, 1")
         ins(f"setp.lt.u32 {p}, {i}, {n_blk}")
         ins(f"@{p} bra {ptop}")
-        for s in range(min(STAGES, n_blk)):               # drain: the last load of each stage landed
-            last_use = (n_blk - 1 - s) // STAGES
+        for s in range(min(KS, n_blk)):                   # drain: the last load of each slot landed
             lp = t("b32")
-            ins(f"mov.u32 {lp}, {last_use & 1}")
-            kit.wait(f"{bars}+{kv_full[s]}", lp, 0)
+            ins(f"mov.u32 {lp}, {((n_blk - 1 - s) // KS) & 1}")
+            kit.wait(f"{bars}+{k_full[s]}", lp, 0)
+            kit.wait(f"{bars}+{v_full[s]}", lp, 0)
         ins(f"bra {end}")
 
         # ---------------- MMA issuer (warp 1) ----------------
@@ -307,25 +302,23 @@ class TcAttention(TunedKernel):
         always, never = t("pred"), t("pred")
         ins(f"setp.eq.u32 {always}, {zero}, 0")
         ins(f"setp.ne.u32 {never}, {zero}, 0")
+        commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
 
         def issue_s(blk: str) -> None:
-            """S[blk & 1] = Q K_blk^T."""
-            st_, b_, ks_, bar_ = t("b32"), t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {blk}, {STAGES}")
+            """S[blk & 1] = Q K_blk^T, then release the K slot."""
+            st_, b_, ks_, kb_ = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st_}, {blk}, {KS}")
             ins(f"and.b32 {b_}, {blk}, 1")
-            ins(f"mad.lo.u32 {ks_}, {st_}, {stage_stride}, {k_s[0]}")
-            ins(f"mad.lo.u32 {bar_}, {st_}, 8, {bars}")
-            ins(f"add.u32 {bar_}, {bar_}, {kv_full[0]}")
-            kit.wait(bar_, kit.parity(blk, STAGES), 1)
-            sf = t("b32")
-            ins(f"mad.lo.u32 {sf}, {b_}, 8, {bars}")
-            ins(f"add.u32 {sf}, {sf}, {s_free[0]}")
-            kit.wait(sf, kit.parity(blk, 2, flip=True), 1)
+            ins(f"mad.lo.u32 {ks_}, {st_}, {kvb}, {k0}")
+            ins(f"mad.lo.u32 {kb_}, {st_}, 8, {bars}")
+            kf = t("b32")
+            ins(f"add.u32 {kf}, {kb_}, {k_full[0]}")
+            kit.wait(kf, kit.parity(blk, KS), 1)
             ins("tcgen05.fence::after_thread_sync")
             kd = kit.desc(ks_, 16, hi)
             dcol = t("b32")
             ins(f"mad.lo.u32 {dcol}, {b_}, 128, {tmem}")
-            ins(f"add.u32 {dcol}, {dcol}, 128")
+            ins(f"add.u32 {dcol}, {dcol}, {S_COL}")
             for kk in range(D // 16):
                 o_ = (kk // 4) * BM * 128 + (kk % 4) * 32
                 a = kit.desc_add(qdesc, o_)
@@ -334,33 +327,37 @@ class TcAttention(TunedKernel):
                     f"{never if kk == 0 else always}")
             sb = t("b32")
             ins(f"mad.lo.u32 {sb}, {b_}, 8, {bars}")
-            ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sb}+{s_full[0]}]")
+            ins(f"@{ism} {commit} [{sb}+{s_full[0]}]")
+            ins(f"@{ism} {commit} [{kb_}+{k_empty[0]}]")
 
         def issue_pv(blk: str, first_block: bool) -> None:
-            """O += P[blk & 1] V_blk; the first block's first MMA overwrites O."""
-            st_, b_, vs_, pbuf = t("b32"), t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {blk}, {STAGES}")
+            """O += P[blk & 1] (from TMEM) V_blk; the first block's first MMA overwrites O."""
+            st_, b_, vs_, vb_ = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st_}, {blk}, {VS}")
             ins(f"and.b32 {b_}, {blk}, 1")
             pf = t("b32")
             ins(f"mad.lo.u32 {pf}, {b_}, 8, {bars}")
             ins(f"add.u32 {pf}, {pf}, {p_full[0]}")
             kit.wait(pf, kit.parity(blk, 2), 1)
+            ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
+            vf = t("b32")
+            ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
+            kit.wait(vf, kit.parity(blk, VS), 1)
             ins("tcgen05.fence::after_thread_sync")
-            ins(f"mad.lo.u32 {vs_}, {st_}, {stage_stride}, {k_s[0]}")
-            ins(f"add.u32 {vs_}, {vs_}, {kvb}")
-            ins(f"mad.lo.u32 {pbuf}, {b_}, {pb}, {p_s[0]}")
-            pd = kit.desc(pbuf, 16, hi)
+            ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
             vd = kit.desc(vs_, BN * 128, hi)
+            pcol = t("b32")
+            ins(f"mad.lo.u32 {pcol}, {b_}, 64, {tmem}")
+            ins(f"add.u32 {pcol}, {pcol}, {P_COL}")
             for kk in range(BN // 16):
-                a = kit.desc_add(pd, (kk // 4) * BM * 128 + (kk % 4) * 32)
+                a = t("b32")
+                ins(f"add.u32 {a}, {pcol}, {8 * kk}")
                 bb = kit.desc_add(vd, kk * 16 * 128)
                 acc = never if (first_block and kk == 0) else always
-                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{tmem}], {a}, {bb}, {id_o}, {acc}")
-            ke, pe = t("b32"), t("b32")
-            ins(f"mad.lo.u32 {ke}, {st_}, 8, {bars}")
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{tmem}], [{a}], {bb}, {id_o}, {acc}")
+            pe = t("b32")
             ins(f"mad.lo.u32 {pe}, {b_}, 8, {bars}")
-            commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
-            ins(f"@{ism} {commit} [{ke}+{kv_empty[0]}]")
+            ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
             ins(f"@{ism} {commit} [{pe}+{p_empty[0]}]")
             ins(f"@{ism} {commit} [{bars}+{o_done}]")
 
@@ -400,16 +397,6 @@ class TcAttention(TunedKernel):
         ins(f"shl.b32 {lane_off}, {quarter}, 21")
         trow = t("b32")
         ins(f"add.u32 {trow}, {tmem}, {lane_off}")
-        # this row's 16-byte chunk offsets in a 128B-swizzled K-major tile: r*128 + ((c ^ (r & 7)) << 4)
-        r7 = t("b32")
-        ins(f"and.b32 {r7}, {r}, 7")
-        choff = []
-        for c in range(8):
-            o = t("b32")
-            ins(f"xor.b32 {o}, {r7}, {c}")
-            ins(f"shl.b32 {o}, {o}, 4")
-            ins(f"mad.lo.u32 {o}, {r}, 128, {o}")
-            choff.append(o)
         sc = t("f32")
         ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")
         ins(f"rcp.rn.f32 {sc}, {sc}")
@@ -434,11 +421,9 @@ class TcAttention(TunedKernel):
         ins(f"mad.lo.u32 {scol}, {b_}, 128, {trow}")
         for c in range(BN // 32):
             a = t("b32")
-            ins(f"add.u32 {a}, {scol}, {128 + 32 * c}")
+            ins(f"add.u32 {a}, {scol}, {S_COL + 32 * c}")
             ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, [{a}]")
         ins("tcgen05.wait::ld.sync.aligned")
-        ins("tcgen05.fence::before_thread_sync")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bb8}+{s_free[0]}]")
         mx = _tree(em, "max.f32", sv)
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
@@ -482,20 +467,20 @@ class TcAttention(TunedKernel):
         pe = t("b32")
         ins(f"add.u32 {pe}, {bb8}, {p_empty[0]}")
         kit.wait(pe, kit.parity(blk, 2, flip=True), 2)
-        pbuf = t("b32")
-        ins(f"mad.lo.u32 {pbuf}, {b_}, {pb}, {p_s[0]}")
-        for kb in range(BN // 64):
-            for c in range(8):
-                a = t("b32")
-                ins(f"add.u32 {a}, {pbuf}, {choff[c]}")
-                regs = hp[kb * 32 + 4 * c: kb * 32 + 4 * c + 4]
-                ins(f"st.shared.v4.b32 [{a}+{kb * BM * 128}], {{{', '.join(regs)}}}")
-        ins("fence.proxy.async.shared::cta")
+        ins("tcgen05.fence::after_thread_sync")
+        pcol = t("b32")
+        ins(f"mad.lo.u32 {pcol}, {b_}, 64, {trow}")
+        for c in range(BN // 64):
+            a = t("b32")
+            ins(f"add.u32 {a}, {pcol}, {P_COL + 32 * c}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{a}], {{{', '.join(hp[32 * c:32 * c + 32])}}}")
+        ins("tcgen05.wait::st.sync.aligned")
+        ins("tcgen05.fence::before_thread_sync")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{bb8}+{p_full[0]}]")
         ins(f"add.u32 {blk}, {blk}, 1")
         ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
         ins(f"@{p} bra {stop}")
-        # epilogue: O / l -> f16 -> swizzled tile in P buffer 0 -> TMA store
+        # epilogue: O / l -> f16 -> 128B-swizzled tile in the (now idle) Q buffer -> TMA store
         lastb = t("b32")
         ins(f"mov.u32 {lastb}, {(n_blk - 1) & 1}")
         kit.wait(f"{bars}+{o_done}", lastb, 3)
@@ -513,11 +498,16 @@ class TcAttention(TunedKernel):
             ins(f"mul.rn.f32 {ov[2 * k]}, {ov[2 * k]}, {inv}")
             ins(f"mul.rn.f32 {ov[2 * k + 1]}, {ov[2 * k + 1]}, {inv}")
             ins(f"cvt.rn.f16x2.f32 {oh[k]}, {ov[2 * k + 1]}, {ov[2 * k]}")
+        r7 = t("b32")
+        ins(f"and.b32 {r7}, {r}, 7")
         for db in range(dblk):
             for c in range(8):
-                a = t("b32")
-                ins(f"add.u32 {a}, {p_s[0]}, {choff[c]}")
-                ins(f"st.shared.v4.b32 [{a}+{db * BM * 128}], {{{', '.join(oh[db * 32 + 4 * c: db * 32 + 4 * c + 4])}}}")
+                o = t("b32")
+                ins(f"xor.b32 {o}, {r7}, {c}")
+                ins(f"shl.b32 {o}, {o}, 4")
+                ins(f"mad.lo.u32 {o}, {r}, 128, {o}")
+                ins(f"add.u32 {o}, {o}, {q_s}")
+                ins(f"st.shared.v4.b32 [{o}+{db * BM * 128}], {{{', '.join(oh[db * 32 + 4 * c: db * 32 + 4 * c + 4])}}}")
         ins("fence.proxy.async.shared::cta")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{o_staged}]")
         leader = t("pred")
@@ -529,7 +519,7 @@ class TcAttention(TunedKernel):
         kit.wait(f"{bars}+{o_staged}", zb, 3)            # every row of the tile is staged
         for db in range(dblk):
             ins(f"cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmaps['o']}, "
-                f"{{{db * 64}, {qrow}}}], [{p_s[0]}+{db * BM * 128}]")
+                f"{{{db * 64}, {qrow}}}], [{q_s}+{db * BM * 128}]")
         ins("cp.async.bulk.commit_group")
         ins("cp.async.bulk.wait_group 0")
         place(skip_store)
