@@ -37,7 +37,6 @@ from thompiler.families.kit import Kit, desc_hi, idesc_f16
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
-THREADS = 192
 BM = BN = 128
 STAGES = 3                  # K and V rings each
 LOG2E = math.log2(math.e)
@@ -56,8 +55,12 @@ class TcAttention(TunedKernel):
         self.heads, self.Sq, self.Sk, self.D = heads, Sq, Sk, D
         self.q_bytes = BM * D * 2
         self.kv_bytes = BN * D * 2
-        self.smem = self.q_bytes + STAGES * 2 * self.kv_bytes + 1024 + 256
-        self.tiles = heads * (Sq // BM)
+        # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
+        self.qt = 2 if Sq % (2 * BM) == 0 else 1
+        self.threads = 64 + 128 * self.qt
+        self.ks, self.vs = (3, 2) if (self.qt == 2 and D == 128) else (STAGES, STAGES)
+        self.smem = self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + 1024 + 256
+        self.tiles = heads * (Sq // (BM * self.qt))
 
     # ---- recognition -------------------------------------------------------------
 
@@ -138,9 +141,9 @@ class TcAttention(TunedKernel):
                     "strides": [D * 2], "box": [64, 128], "swizzle": 3}
         maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
                 tm("thc_tmap_v", self.pv, self.heads * self.Sk), tm("thc_tmap_o", self.pout, self.heads * self.Sq)]
-        return {"grid": [self.tiles, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem, "tmaps": maps,
-                "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
-                "error_word": "thc_error", "tile": [BM, BN, D], "stages": STAGES}
+        return {"grid": [self.tiles, 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
+                "tmaps": maps, "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
+                "error_word": "thc_error", "tile": [BM * self.qt, BN, D], "stages": [self.ks, self.vs]}
 
     def guard(self, generic: str) -> None:
         em = self.em
@@ -151,7 +154,7 @@ class TcAttention(TunedKernel):
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
-        em.ins(f"setp.ne.u32 {p}, {r}, {THREADS}")
+        em.ins(f"setp.ne.u32 {p}, {r}, {self.threads}")
         em.ins(f"@{p} bra {generic}")
         for i, prm in enumerate((self.pq, self.pk, self.pv, self.pout)):
             raw, want = em.tmp("b64"), em.tmp("b64")
@@ -165,10 +168,12 @@ class TcAttention(TunedKernel):
     def emit_tuned(self) -> None:  # noqa: C901 - one kernel, in order
         em = self.em
         t, ins, place, lab = em.tmp, em.ins, em.place, em.label
-        D, n_blk = self.D, self.Sk // BN
+        D, n_blk, QT = self.D, self.Sk // BN, self.qt
         dblk = D // 64
         qb, kvb = self.q_bytes, self.kv_bytes
-        KS = VS = STAGES
+        KS, VS = self.ks, self.vs
+        commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
+        tma = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
 
         tid, warp, lane = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {tid}, %tid.x")
@@ -178,12 +183,12 @@ class TcAttention(TunedKernel):
         ins(f"mov.u32 {base}, smem_pool")
         ins(f"add.u32 {base}, {base}, 1023")
         ins(f"and.b32 {base}, {base}, -1024")
-        # shared layout: Q tile | K ring | V ring | barriers   (the Q tile stages O at the end)
+        # shared: Q tiles (QT of them; each later stages its group's O) | K ring | V ring | barriers
         q_s = base
         k0, v0, bars = t("b32"), t("b32"), t("b32")
-        ins(f"add.u32 {k0}, {base}, {qb}")
-        ins(f"add.u32 {v0}, {base}, {qb + KS * kvb}")
-        ins(f"add.u32 {bars}, {base}, {qb + (KS + VS) * kvb}")
+        ins(f"add.u32 {k0}, {base}, {QT * qb}")
+        ins(f"add.u32 {v0}, {base}, {QT * qb + KS * kvb}")
+        ins(f"add.u32 {bars}, {base}, {QT * qb + (KS + VS) * kvb}")
         nb = 0
 
         def bar() -> int:
@@ -193,10 +198,12 @@ class TcAttention(TunedKernel):
         q_full = bar()
         k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
         v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
-        s_full, p_full, p_empty = [bar(), bar()], [bar(), bar()], [bar(), bar()]
-        o_done, o_staged = bar(), bar()
+        s_full = [bar() for _ in range(QT)]
+        p_full = [bar() for _ in range(QT)]
+        o_done = [bar() for _ in range(QT)]
+        o_staged = [bar() for _ in range(QT)]
         counts = {o: 1 for o in range(0, nb * 8, 8)}
-        for o in p_full + [o_staged]:
+        for o in p_full + o_staged:
             counts[o] = 128
         slot_off = nb * 8
         p = t("pred")
@@ -221,8 +228,8 @@ class TcAttention(TunedKernel):
         ins("tcgen05.fence::after_thread_sync")
         tmem = t("b32")
         ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
-        # TMEM columns: O [0, 128) | S0 [128, 256) | S1 [256, 384) | P0 [384, 448) | P1 [448, 512)
-        S_COL, P_COL = 128, 384
+        # TMEM columns: O_g at 128 g, S_g at 256 + 128 g; P_g (f16 pairs) in the first 64 columns of S_g
+        O_COL, S_COL = 0, 256
         errp = t("b64")
         ins(f"mov.u64 {errp}, thc_error")
         end = lab("at_end")
@@ -234,13 +241,13 @@ class TcAttention(TunedKernel):
             ins(f"cvta.global.u64 {r}, {r}")
             tmaps[n] = r
         cta = self.special("%ctaid.x")
-        qtiles = self.Sq // BM
-        bh, qt = t("b32"), t("b32")
-        ins(f"div.u32 {bh}, {cta}, {qtiles}")
-        ins(f"rem.u32 {qt}, {cta}, {qtiles}")
+        groups = self.Sq // (BM * QT)
+        bh, qg = t("b32"), t("b32")
+        ins(f"div.u32 {bh}, {cta}, {groups}")
+        ins(f"rem.u32 {qg}, {cta}, {groups}")
         qrow, kvrow = t("b32"), t("b32")
         ins(f"mul.lo.u32 {qrow}, {bh}, {self.Sq}")
-        ins(f"mad.lo.u32 {qrow}, {qt}, {BM}, {qrow}")
+        ins(f"mad.lo.u32 {qrow}, {qg}, {BM * QT}, {qrow}")
         ins(f"mul.lo.u32 {kvrow}, {bh}, {self.Sk}")
         role_mma, role_sm = lab("at_mma"), lab("at_softmax")
         ins(f"setp.eq.u32 {p}, {warp}, 1")
@@ -251,10 +258,13 @@ class TcAttention(TunedKernel):
         # ---------------- producer (warp 0) ----------------
         is0 = t("pred")
         ins(f"setp.eq.u32 {is0}, {lane}, 0")
-        tma = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {qb}")
-        for db in range(dblk):
-            ins(f"@{is0} {tma} [{q_s}+{db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qrow}}}], [{bars}+{q_full}]")
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {QT * qb}")
+        for g in range(QT):
+            qr = t("b32")
+            ins(f"add.u32 {qr}, {qrow}, {g * BM}")
+            for db in range(dblk):
+                ins(f"@{is0} {tma} [{q_s}+{g * qb + db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qr}}}], "
+                    f"[{bars}+{q_full}]")
 
         def ring(i: str, n_st: int, s0: str, full0: int, empty0: int, mapname: str, row: str) -> None:
             st, buf, fb, eb = t("b32"), t("b32"), t("b32"), t("b32")
@@ -283,6 +293,9 @@ class TcAttention(TunedKernel):
             lp = t("b32")
             ins(f"mov.u32 {lp}, {((n_blk - 1 - s) // KS) & 1}")
             kit.wait(f"{bars}+{k_full[s]}", lp, 0)
+        for s in range(min(VS, n_blk)):
+            lp = t("b32")
+            ins(f"mov.u32 {lp}, {((n_blk - 1 - s) // VS) & 1}")
             kit.wait(f"{bars}+{v_full[s]}", lp, 0)
         ins(f"bra {end}")
 
@@ -296,107 +309,119 @@ class TcAttention(TunedKernel):
         ins("tcgen05.fence::after_thread_sync")
         hi = t("b32")
         ins(f"mov.u32 {hi}, {desc_hi(1024)}")
-        qdesc = kit.desc(q_s, 16, hi)
+        qdesc = [kit.desc_add(kit.desc(q_s, 16, hi), g * qb) for g in range(QT)]
         id_s = idesc_f16(BM, BN)
         id_o = idesc_f16(BM, D, b_mn_major=True)
         always, never = t("pred"), t("pred")
         ins(f"setp.eq.u32 {always}, {zero}, 0")
         ins(f"setp.ne.u32 {never}, {zero}, 0")
-        commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
 
-        def issue_s(blk: str) -> None:
-            """S[blk & 1] = Q K_blk^T, then release the K slot."""
-            st_, b_, ks_, kb_ = t("b32"), t("b32"), t("b32"), t("b32")
+        def k_slot(blk: str):
+            st_, ks_, kb_ = t("b32"), t("b32"), t("b32")
             ins(f"rem.u32 {st_}, {blk}, {KS}")
-            ins(f"and.b32 {b_}, {blk}, 1")
             ins(f"mad.lo.u32 {ks_}, {st_}, {kvb}, {k0}")
             ins(f"mad.lo.u32 {kb_}, {st_}, 8, {bars}")
+            return ks_, kb_
+
+        def issue_s(g: int, blk: str, ks_: str, kb_: str, release_k: bool) -> None:
+            """S_g = Q_g K_blk^T (K slot already waited for)."""
+            kd = kit.desc(ks_, 16, hi)
+            dcol = t("b32")
+            ins(f"add.u32 {dcol}, {tmem}, {S_COL + 128 * g}")
+            for kk in range(D // 16):
+                a = kit.desc_add(qdesc[g], (kk // 4) * BM * 128 + (kk % 4) * 32)
+                bb = kit.desc_add(kd, (kk // 4) * BN * 128 + (kk % 4) * 32)
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {a}, {bb}, {id_s}, "
+                    f"{never if kk == 0 else always}")
+            ins(f"@{ism} {commit} [{bars}+{s_full[g]}]")
+            if release_k:
+                ins(f"@{ism} {commit} [{kb_}+{k_empty[0]}]")
+
+        def wait_k(blk: str):
+            ks_, kb_ = k_slot(blk)
             kf = t("b32")
             ins(f"add.u32 {kf}, {kb_}, {k_full[0]}")
             kit.wait(kf, kit.parity(blk, KS), 1)
             ins("tcgen05.fence::after_thread_sync")
-            kd = kit.desc(ks_, 16, hi)
-            dcol = t("b32")
-            ins(f"mad.lo.u32 {dcol}, {b_}, 128, {tmem}")
-            ins(f"add.u32 {dcol}, {dcol}, {S_COL}")
-            for kk in range(D // 16):
-                o_ = (kk // 4) * BM * 128 + (kk % 4) * 32
-                a = kit.desc_add(qdesc, o_)
-                bb = kit.desc_add(kd, (kk // 4) * BN * 128 + (kk % 4) * 32)
-                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {a}, {bb}, {id_s}, "
-                    f"{never if kk == 0 else always}")
-            sb = t("b32")
-            ins(f"mad.lo.u32 {sb}, {b_}, 8, {bars}")
-            ins(f"@{ism} {commit} [{sb}+{s_full[0]}]")
-            ins(f"@{ism} {commit} [{kb_}+{k_empty[0]}]")
+            return ks_, kb_
 
-        def issue_pv(blk: str, first_block: bool) -> None:
-            """O += P[blk & 1] (from TMEM) V_blk; the first block's first MMA overwrites O."""
-            st_, b_, vs_, vb_ = t("b32"), t("b32"), t("b32"), t("b32")
+        def issue_pv(g: int, blk: str, first_block: bool, release_v: bool) -> None:
+            """O_g += P_g V_blk, P_g read from TMEM (the TS form)."""
+            kit.wait(f"{bars}+{p_full[g]}", kit.parity(blk, 1), 1)
+            st_, vs_, vb_ = t("b32"), t("b32"), t("b32")
             ins(f"rem.u32 {st_}, {blk}, {VS}")
-            ins(f"and.b32 {b_}, {blk}, 1")
-            pf = t("b32")
-            ins(f"mad.lo.u32 {pf}, {b_}, 8, {bars}")
-            ins(f"add.u32 {pf}, {pf}, {p_full[0]}")
-            kit.wait(pf, kit.parity(blk, 2), 1)
             ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
-            vf = t("b32")
-            ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
-            kit.wait(vf, kit.parity(blk, VS), 1)
+            if g == 0:
+                vf = t("b32")
+                ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
+                kit.wait(vf, kit.parity(blk, VS), 1)
             ins("tcgen05.fence::after_thread_sync")
             ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
             vd = kit.desc(vs_, BN * 128, hi)
-            pcol = t("b32")
-            ins(f"mad.lo.u32 {pcol}, {b_}, 64, {tmem}")
-            ins(f"add.u32 {pcol}, {pcol}, {P_COL}")
+            dcol = t("b32")
+            ins(f"add.u32 {dcol}, {tmem}, {O_COL + 128 * g}")
             for kk in range(BN // 16):
                 a = t("b32")
-                ins(f"add.u32 {a}, {pcol}, {8 * kk}")
+                ins(f"add.u32 {a}, {tmem}, {S_COL + 128 * g + 8 * kk}")
                 bb = kit.desc_add(vd, kk * 16 * 128)
                 acc = never if (first_block and kk == 0) else always
-                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{tmem}], [{a}], {bb}, {id_o}, {acc}")
-            pe = t("b32")
-            ins(f"mad.lo.u32 {pe}, {b_}, 8, {bars}")
-            ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
-            ins(f"@{ism} {commit} [{pe}+{p_empty[0]}]")
-            ins(f"@{ism} {commit} [{bars}+{o_done}]")
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{a}], {bb}, {id_o}, {acc}")
+            ins(f"@{ism} {commit} [{bars}+{o_done[g]}]")
+            if release_v:
+                ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
 
-        issue_s(zero)
-        if n_blk > 1:
-            one = t("b32")
-            ins(f"mov.u32 {one}, 1")
-            issue_s(one)
-            issue_pv(zero, True)
-            blk = t("b32")
-            ins(f"mov.u32 {blk}, 2")
-            mtop, mdone = lab("at_mma_k"), lab("at_mma_done")
-            ins(f"setp.ge.u32 {p}, {blk}, {n_blk}")
-            ins(f"@{p} bra {mdone}")
-            place(mtop)
-            issue_s(blk)
-            prev = t("b32")
-            ins(f"sub.u32 {prev}, {blk}, 1")
-            issue_pv(prev, False)
-            ins(f"add.u32 {blk}, {blk}, 1")
-            ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
-            ins(f"@{p} bra {mtop}")
-            place(mdone)
-            last = t("b32")
-            ins(f"mov.u32 {last}, {n_blk - 1}")
-            issue_pv(last, False)
-        else:
-            issue_pv(zero, True)
+        # S_g(0) for every group; then per block: PV_g(i), S_g(i + 1) for each group in turn
+        ks_, kb_ = wait_k(zero)
+        for g in range(QT):
+            issue_s(g, zero, ks_, kb_, g == QT - 1)
+        blk = t("b32")
+        ins(f"mov.u32 {blk}, 0")
+        mtop = lab("at_mma_k")
+        place(mtop)
+        nxt = t("b32")
+        ins(f"add.u32 {nxt}, {blk}, 1")
+        more = t("pred")
+        ins(f"setp.lt.u32 {more}, {nxt}, {n_blk}")
+        first_lab, rest_lab, join_lab = lab("at_pv_first"), lab("at_pv_rest"), lab("at_pv_join")
+        ins(f"setp.eq.u32 {p}, {blk}, 0")
+        ins(f"@!{p} bra {rest_lab}")
+        for first in (True, False):
+            if not first:
+                place(rest_lab)
+            for g in range(QT):
+                issue_pv(g, blk, first, g == QT - 1)
+                if g == 0:
+                    nk = lab("at_nok")
+                    ins(f"@!{more} bra {nk}")
+                    ks2, kb2 = wait_k(nxt)
+                    ins(f"mov.u32 {ks_}, {ks2}")
+                    ins(f"mov.u32 {kb_}, {kb2}")
+                    place(nk)
+                skip_s = lab("at_nos")
+                ins(f"@!{more} bra {skip_s}")
+                issue_s(g, nxt, ks_, kb_, g == QT - 1)
+                place(skip_s)
+            ins(f"bra {join_lab}")
+        place(join_lab)
+        ins(f"mov.u32 {blk}, {nxt}")
+        ins(f"@{more} bra {mtop}")
         ins(f"bra {end}")
 
-        # ---------------- softmax + epilogue (warps 2..5) ----------------
+        # ---------------- softmax + epilogue (warps 2 .. 2 + 4 QT) ----------------
         place(role_sm)
-        quarter, r = t("b32"), t("b32")
+        grp, quarter, r = t("b32"), t("b32"), t("b32")
+        ins(f"sub.u32 {grp}, {warp}, 2")
+        ins(f"shr.u32 {grp}, {grp}, 2")
         ins(f"and.b32 {quarter}, {warp}, 3")
         ins(f"mad.lo.u32 {r}, {quarter}, 32, {lane}")
-        lane_off = t("b32")
-        ins(f"shl.b32 {lane_off}, {quarter}, 21")
         trow = t("b32")
-        ins(f"add.u32 {trow}, {tmem}, {lane_off}")
+        ins(f"shl.b32 {trow}, {quarter}, 21")
+        ins(f"add.u32 {trow}, {trow}, {tmem}")
+        ocol, scol, gb8 = t("b32"), t("b32"), t("b32")
+        ins(f"mad.lo.u32 {ocol}, {grp}, 128, {trow}")
+        ins(f"add.u32 {scol}, {ocol}, {S_COL}")
+        ins(f"add.u32 {ocol}, {ocol}, {O_COL}")
+        ins(f"mad.lo.u32 {gb8}, {grp}, 8, {bars}")
         sc = t("f32")
         ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")
         ins(f"rcp.rn.f32 {sc}, {sc}")
@@ -405,26 +430,23 @@ class TcAttention(TunedKernel):
         ins(f"mov.f32 {mref}, 0fFF800000")
         ins(f"mov.f32 {mref8}, 0fFF800000")
         ins(f"mov.f32 {l}, 0f00000000")
-        sv = [t("f32") for _ in range(BN)]
-        blk = t("b32")
-        ins(f"mov.u32 {blk}, 0")
+        blk2 = t("b32")
+        ins(f"mov.u32 {blk2}, 0")
         stop = lab("at_sm_blk")
         place(stop)
-        b_, bb8 = t("b32"), t("b32")
-        ins(f"and.b32 {b_}, {blk}, 1")
-        ins(f"mad.lo.u32 {bb8}, {b_}, 8, {bars}")
-        sfull = t("b32")
-        ins(f"add.u32 {sfull}, {bb8}, {s_full[0]}")
-        kit.wait(sfull, kit.parity(blk, 2), 2)
+        kit.wait(f"{gb8}+{s_full[0]}", kit.parity(blk2, 1), 2)
         ins("tcgen05.fence::after_thread_sync")
-        scol = t("b32")
-        ins(f"mad.lo.u32 {scol}, {b_}, 128, {trow}")
+        # pass 1: the row max, 32 scores at a time
+        mx = t("f32")
+        ins(f"mov.f32 {mx}, 0fFF800000")
         for c in range(BN // 32):
+            sv = [t("f32") for _ in range(32)]
             a = t("b32")
-            ins(f"add.u32 {a}, {scol}, {S_COL + 32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, [{a}]")
-        ins("tcgen05.wait::ld.sync.aligned")
-        mx = _tree(em, "max.f32", sv)
+            ins(f"add.u32 {a}, {scol}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv)}}}, [{a}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            m = _tree(em, "max.f32", sv)
+            ins(f"max.f32 {mx}, {mx}, {m}")
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
         norescale, noowait = lab("at_norescale"), lab("at_first")
@@ -434,16 +456,16 @@ class TcAttention(TunedKernel):
         ins(f"sub.rn.f32 {dm}, {mref}, {mnew}")
         ins(f"ex2.approx.ftz.f32 {alpha}, {dm}")
         ins(f"mul.rn.f32 {l}, {l}, {alpha}")
-        ins(f"setp.eq.u32 {p}, {blk}, 0")
+        ins(f"setp.eq.u32 {p}, {blk2}, 0")
         ins(f"@{p} bra {noowait}")
         prevb = t("b32")
-        ins(f"sub.u32 {prevb}, {blk}, 1")
-        kit.wait(f"{bars}+{o_done}", kit.parity(prevb, 1), 3)
+        ins(f"sub.u32 {prevb}, {blk2}, 1")
+        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
         for c in range(D // 32):
             ov = [t("f32") for _ in range(32)]
             a = t("b32")
-            ins(f"add.u32 {a}, {trow}, {32 * c}")
+            ins(f"add.u32 {a}, {ocol}, {32 * c}")
             ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
             ins("tcgen05.wait::ld.sync.aligned")
             for x in ov:
@@ -456,70 +478,78 @@ class TcAttention(TunedKernel):
         place(norescale)
         negm = t("f32")
         ins(f"neg.f32 {negm}, {mref}")
-        for x in sv:
-            ins(f"fma.rn.f32 {x}, {x}, {sc}, {negm}")
-            ins(f"ex2.approx.ftz.f32 {x}, {x}")
-        rs = _tree(em, "add.rn.f32", sv)
-        ins(f"add.rn.f32 {l}, {l}, {rs}")
-        hp = [t("b32") for _ in range(BN // 2)]
-        for k in range(BN // 2):
-            ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
-        pe = t("b32")
-        ins(f"add.u32 {pe}, {bb8}, {p_empty[0]}")
-        kit.wait(pe, kit.parity(blk, 2, flip=True), 2)
-        ins("tcgen05.fence::after_thread_sync")
-        pcol = t("b32")
-        ins(f"mad.lo.u32 {pcol}, {b_}, 64, {trow}")
-        for c in range(BN // 64):
+        # pass 2: P = 2^(s c' - m) 32 scores at a time, written back as f16 pairs over S's first columns
+        for c in range(BN // 32):
+            sv = [t("f32") for _ in range(32)]
             a = t("b32")
-            ins(f"add.u32 {a}, {pcol}, {P_COL + 32 * c}")
-            ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{a}], {{{', '.join(hp[32 * c:32 * c + 32])}}}")
+            ins(f"add.u32 {a}, {scol}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv)}}}, [{a}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            for x in sv:
+                ins(f"fma.rn.f32 {x}, {x}, {sc}, {negm}")
+                ins(f"ex2.approx.ftz.f32 {x}, {x}")
+            s_ = _tree(em, "add.rn.f32", sv)
+            ins(f"add.rn.f32 {l}, {l}, {s_}")
+            hp = [t("b32") for _ in range(16)]
+            for k in range(16):
+                ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
+            a2 = t("b32")
+            ins(f"add.u32 {a2}, {scol}, {16 * c}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{a2}], {{{', '.join(hp)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         ins("tcgen05.fence::before_thread_sync")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bb8}+{p_full[0]}]")
-        ins(f"add.u32 {blk}, {blk}, 1")
-        ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[0]}]")
+        ins(f"add.u32 {blk2}, {blk2}, 1")
+        ins(f"setp.lt.u32 {p}, {blk2}, {n_blk}")
         ins(f"@{p} bra {stop}")
-        # epilogue: O / l -> f16 -> 128B-swizzled tile in the (now idle) Q buffer -> TMA store
+        # epilogue: O_g / l -> f16 -> 128B-swizzled tile over Q_g (idle now) -> TMA store
         lastb = t("b32")
         ins(f"mov.u32 {lastb}, {(n_blk - 1) & 1}")
-        kit.wait(f"{bars}+{o_done}", lastb, 3)
+        kit.wait(f"{gb8}+{o_done[0]}", lastb, 3)
         ins("tcgen05.fence::after_thread_sync")
         inv = t("f32")
         ins(f"rcp.rn.f32 {inv}, {l}")
-        ov = [t("f32") for _ in range(D)]
-        for c in range(D // 32):
-            a = t("b32")
-            ins(f"add.u32 {a}, {trow}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
-        ins("tcgen05.wait::ld.sync.aligned")
-        oh = [t("b32") for _ in range(D // 2)]
-        for k in range(D // 2):
-            ins(f"mul.rn.f32 {ov[2 * k]}, {ov[2 * k]}, {inv}")
-            ins(f"mul.rn.f32 {ov[2 * k + 1]}, {ov[2 * k + 1]}, {inv}")
-            ins(f"cvt.rn.f16x2.f32 {oh[k]}, {ov[2 * k + 1]}, {ov[2 * k]}")
-        r7 = t("b32")
+        stg, r7 = t("b32"), t("b32")
+        ins(f"mad.lo.u32 {stg}, {grp}, {qb}, {q_s}")
         ins(f"and.b32 {r7}, {r}, 7")
-        for db in range(dblk):
-            for c in range(8):
+        for c in range(D // 32):
+            ov = [t("f32") for _ in range(32)]
+            a = t("b32")
+            ins(f"add.u32 {a}, {ocol}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            oh = [t("b32") for _ in range(16)]
+            for k in range(16):
+                ins(f"mul.rn.f32 {ov[2 * k]}, {ov[2 * k]}, {inv}")
+                ins(f"mul.rn.f32 {ov[2 * k + 1]}, {ov[2 * k + 1]}, {inv}")
+                ins(f"cvt.rn.f16x2.f32 {oh[k]}, {ov[2 * k + 1]}, {ov[2 * k]}")
+            # columns 32c .. 32c+31 are 16-byte chunks 4c' .. 4c'+3 of 64-column block c // 2
+            db, cc = c // 2, (c % 2) * 4
+            for j in range(4):
                 o = t("b32")
-                ins(f"xor.b32 {o}, {r7}, {c}")
+                ins(f"xor.b32 {o}, {r7}, {cc + j}")
                 ins(f"shl.b32 {o}, {o}, 4")
                 ins(f"mad.lo.u32 {o}, {r}, 128, {o}")
-                ins(f"add.u32 {o}, {o}, {q_s}")
-                ins(f"st.shared.v4.b32 [{o}+{db * BM * 128}], {{{', '.join(oh[db * 32 + 4 * c: db * 32 + 4 * c + 4])}}}")
+                ins(f"add.u32 {o}, {o}, {stg}")
+                ins(f"st.shared.v4.b32 [{o}+{db * BM * 128}], {{{', '.join(oh[4 * j:4 * j + 4])}}}")
         ins("fence.proxy.async.shared::cta")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{o_staged}]")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_staged[0]}]")
         leader = t("pred")
-        ins(f"setp.eq.u32 {leader}, {tid}, 64")
+        lt_ = t("b32")
+        ins(f"sub.u32 {lt_}, {warp}, 2")
+        ins(f"and.b32 {lt_}, {lt_}, 3")
+        ins(f"or.b32 {lt_}, {lt_}, {lane}")
+        ins(f"setp.eq.u32 {leader}, {lt_}, 0")          # lane 0 of each group's first warp
         skip_store = lab("at_not_leader")
         ins(f"@!{leader} bra {skip_store}")
         zb = t("b32")
         ins(f"mov.u32 {zb}, 0")
-        kit.wait(f"{bars}+{o_staged}", zb, 3)            # every row of the tile is staged
+        kit.wait(f"{gb8}+{o_staged[0]}", zb, 3)           # every row of this group's tile is staged
+        orow = t("b32")
+        ins(f"mad.lo.u32 {orow}, {grp}, {BM}, {qrow}")
         for db in range(dblk):
             ins(f"cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmaps['o']}, "
-                f"{{{db * 64}, {qrow}}}], [{q_s}+{db * BM * 128}]")
+                f"{{{db * 64}, {orow}}}], [{stg}+{db * BM * 128}]")
         ins("cp.async.bulk.commit_group")
         ins("cp.async.bulk.wait_group 0")
         place(skip_store)
