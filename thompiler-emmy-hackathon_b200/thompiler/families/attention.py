@@ -30,6 +30,7 @@ mbarrier waits are bounded (thompiler.families.kit).
 from __future__ import annotations
 
 import math
+import os
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
@@ -40,6 +41,7 @@ from thompiler.load import KernelInfo
 BM = BN = 128
 STAGES = 3                  # K and V rings each
 LOG2E = math.log2(math.e)
+POLY_PAIRS = int(os.environ.get("THOMPILER_ATTN_POLY", "0"))    # of every 8 score pairs (0 .. 8)
 
 
 def _var_tail(index: tuple, names: tuple) -> bool:
@@ -57,7 +59,12 @@ class TcAttention(TunedKernel):
         self.kv_bytes = BN * D * 2
         # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
         self.qt = 2 if Sq % (2 * BM) == 0 else 1
-        self.threads = 64 + 128 * self.qt
+        # warps 0 .. 4 qt - 1 softmax (warp w reads TMEM lanes 32 (w % 4) ..), then the TMA warp and
+        # the MMA warp; with two groups they fill a third warpgroup (two warps idle) whose registers
+        # go to the softmax warpgroups (setmaxnreg: 168 at launch -> 224 / 56)
+        self.w_tma, self.w_mma = 4 * self.qt, 4 * self.qt + 1
+        self.threads = 128 * (self.qt + 1) if self.qt == 2 else 192
+        self.reg_split = (224, 56) if self.qt == 2 else None
         self.ks, self.vs = (3, 2) if (self.qt == 2 and D == 128) else (STAGES, STAGES)
         self.smem = self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + 1024 + 256
         self.tiles = heads * (Sq // (BM * self.qt))
@@ -152,6 +159,10 @@ class TcAttention(TunedKernel):
         em.module(".global .align 8 .u64 thc_tmap_ptr[4]")
         em.module(".global .align 4 .u32 thc_error")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
+        # the softmax rows live in registers: cap them so the tuned CTA (and meta.json's) can launch.
+        # Each of the SM's four sub-partitions holds 16384 registers and ceil(warps / 4) of the warps.
+        warps = -(-max(self.threads, self.k.threads_per_cta) // 32)
+        em.entry_attrs.append(f".maxnreg {min(255, 16384 // (32 * -(-warps // 4)) // 8 * 8)}")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
         em.ins(f"setp.ne.u32 {p}, {r}, {self.threads}")
@@ -216,7 +227,7 @@ class TcAttention(TunedKernel):
         ins("fence.proxy.async.shared::cta")
         place(skip)
         noalloc = lab("at_noalloc")
-        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"setp.ne.u32 {p}, {warp}, {self.w_mma}")
         ins(f"@{p} bra {noalloc}")
         slot = t("b32")
         ins(f"add.u32 {slot}, {bars}, {slot_off}")
@@ -250,12 +261,19 @@ class TcAttention(TunedKernel):
         ins(f"mad.lo.u32 {qrow}, {qg}, {BM * QT}, {qrow}")
         ins(f"mul.lo.u32 {kvrow}, {bh}, {self.Sk}")
         role_mma, role_sm = lab("at_mma"), lab("at_softmax")
-        ins(f"setp.eq.u32 {p}, {warp}, 1")
-        ins(f"@{p} bra {role_mma}")
-        ins(f"setp.gt.u32 {p}, {warp}, 1")
+        ins(f"setp.lt.u32 {p}, {warp}, {4 * QT}")
         ins(f"@{p} bra {role_sm}")
+        if self.reg_split:
+            # the producer warpgroup hands registers to the softmax warpgroups (each warpgroup runs
+            # its own setmaxnreg before its warps part): per sub-partition 2 inc + dec <= 512 per
+            # thread, and over the CTA the split is exactly what it launched with
+            ins(f"setmaxnreg.dec.sync.aligned.u32 {self.reg_split[1]}")
+        ins(f"setp.eq.u32 {p}, {warp}, {self.w_mma}")
+        ins(f"@{p} bra {role_mma}")
+        ins(f"setp.ne.u32 {p}, {warp}, {self.w_tma}")
+        ins(f"@{p} bra {end}")                           # the warpgroup's idle warps
 
-        # ---------------- producer (warp 0) ----------------
+        # ---------------- producer (one warp) ----------------
         is0 = t("pred")
         ins(f"setp.eq.u32 {is0}, {lane}, 0")
         ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {QT * qb}")
@@ -299,7 +317,7 @@ class TcAttention(TunedKernel):
             kit.wait(f"{bars}+{v_full[s]}", lp, 0)
         ins(f"bra {end}")
 
-        # ---------------- MMA issuer (warp 1) ----------------
+        # ---------------- MMA issuer (one warp) ----------------
         place(role_mma)
         ism = t("pred")
         ins(f"setp.eq.u32 {ism}, {lane}, 0")
@@ -407,11 +425,12 @@ class TcAttention(TunedKernel):
         ins(f"@{more} bra {mtop}")
         ins(f"bra {end}")
 
-        # ---------------- softmax + epilogue (warps 2 .. 2 + 4 QT) ----------------
+        # ---------------- softmax + epilogue (warps 0 .. 4 QT - 1) ----------------
         place(role_sm)
+        if self.reg_split:
+            ins(f"setmaxnreg.inc.sync.aligned.u32 {self.reg_split[0]}")
         grp, quarter, r = t("b32"), t("b32"), t("b32")
-        ins(f"sub.u32 {grp}, {warp}, 2")
-        ins(f"shr.u32 {grp}, {grp}, 2")
+        ins(f"shr.u32 {grp}, {warp}, 2")
         ins(f"and.b32 {quarter}, {warp}, 3")
         ins(f"mad.lo.u32 {r}, {quarter}, 32, {lane}")
         trow = t("b32")
@@ -436,17 +455,14 @@ class TcAttention(TunedKernel):
         place(stop)
         kit.wait(f"{gb8}+{s_full[0]}", kit.parity(blk2, 1), 2)
         ins("tcgen05.fence::after_thread_sync")
-        # pass 1: the row max, 32 scores at a time
-        mx = t("f32")
-        ins(f"mov.f32 {mx}, 0fFF800000")
+        # the row's 128 scores into registers: four loads in flight, one wait
+        srow = [t("f32") for _ in range(BN)]
         for c in range(BN // 32):
-            sv = [t("f32") for _ in range(32)]
             a = t("b32")
             ins(f"add.u32 {a}, {scol}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv)}}}, [{a}]")
-            ins("tcgen05.wait::ld.sync.aligned")
-            m = _tree(em, "max.f32", sv)
-            ins(f"max.f32 {mx}, {mx}, {m}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(srow[32 * c:32 * c + 32])}}}, [{a}]")
+        ins("tcgen05.wait::ld.sync.aligned")
+        mx = _tree(em, "max.f32", srow, arity=3)
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
         norescale, noowait = lab("at_norescale"), lab("at_first")
@@ -462,15 +478,15 @@ class TcAttention(TunedKernel):
         ins(f"sub.u32 {prevb}, {blk2}, 1")
         kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
-        for c in range(D // 32):
-            ov = [t("f32") for _ in range(32)]
+        for c in range(D // 16):            # 16 columns at a time: the scores hold 128 registers
+            ov = [t("f32") for _ in range(16)]
             a = t("b32")
-            ins(f"add.u32 {a}, {ocol}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
+            ins(f"add.u32 {a}, {ocol}, {16 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x16.b32 {{{', '.join(ov)}}}, [{a}]")
             ins("tcgen05.wait::ld.sync.aligned")
             for x in ov:
                 ins(f"mul.rn.f32 {x}, {x}, {alpha}")
-            ins(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{a}], {{{', '.join(ov)}}}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{a}], {{{', '.join(ov)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         place(noowait)
         ins(f"mov.f32 {mref}, {mnew}")
@@ -478,24 +494,42 @@ class TcAttention(TunedKernel):
         place(norescale)
         negm = t("f32")
         ins(f"neg.f32 {negm}, {mref}")
-        # pass 2: P = 2^(s c' - m) 32 scores at a time, written back as f16 pairs over S's first columns
-        for c in range(BN // 32):
-            sv = [t("f32") for _ in range(32)]
-            a = t("b32")
-            ins(f"add.u32 {a}, {scol}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv)}}}, [{a}]")
-            ins("tcgen05.wait::ld.sync.aligned")
-            for x in sv:
-                ins(f"fma.rn.f32 {x}, {x}, {sc}, {negm}")
-                ins(f"ex2.approx.ftz.f32 {x}, {x}")
-            s_ = _tree(em, "add.rn.f32", sv)
-            ins(f"add.rn.f32 {l}, {l}, {s_}")
-            hp = [t("b32") for _ in range(16)]
-            for k in range(16):
+        # P = 2^(s c' - m), 16 scores at a time, written back as f16 pairs over S's first 64 columns
+        # (every score is already in registers, so the stores cannot overtake a load).  Pairs of
+        # scores go through the packed f32x2 FMA pipe; POLY_PAIRS of every 8 pairs take 2^x from
+        # a polynomial on that pipe instead of the MUFU unit, which would otherwise bound the step.
+        pair = t("b64"), t("b64")
+        ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
+        ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
+        ex2 = _Exp2(em) if POLY_PAIRS else None
+        for c in range(BN // 16):
+            sv = srow[16 * c:16 * c + 16]
+            packs = []
+            for k in range(8):
+                x0, x1 = sv[2 * k], sv[2 * k + 1]
+                d = t("b64")
+                ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
+                ins(f"fma.rn.ftz.f32x2 {d}, {d}, {pair[0]}, {pair[1]}")
+                if k < POLY_PAIRS:
+                    d = ex2.pair(d, x0, x1)
+                else:
+                    ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
+                    ins(f"ex2.approx.ftz.f32 {x0}, {x0}")
+                    ins(f"ex2.approx.ftz.f32 {x1}, {x1}")
+                    d = t("b64")
+                    ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
+                packs.append(d)
+            sp = _tree(em, "add.rn.f32x2", packs, kind="b64")
+            lo, hi = t("f32"), t("f32")
+            ins(f"mov.b64 {{{lo}, {hi}}}, {sp}")
+            ins(f"add.rn.f32 {lo}, {lo}, {hi}")
+            ins(f"add.rn.f32 {l}, {l}, {lo}")
+            hp = [t("b32") for _ in range(8)]
+            for k in range(8):
                 ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
             a2 = t("b32")
-            ins(f"add.u32 {a2}, {scol}, {16 * c}")
-            ins(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{a2}], {{{', '.join(hp)}}}")
+            ins(f"add.u32 {a2}, {scol}, {8 * c}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x8.b32 [{a2}], {{{', '.join(hp)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         ins("tcgen05.fence::before_thread_sync")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[0]}]")
@@ -536,8 +570,7 @@ class TcAttention(TunedKernel):
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_staged[0]}]")
         leader = t("pred")
         lt_ = t("b32")
-        ins(f"sub.u32 {lt_}, {warp}, 2")
-        ins(f"and.b32 {lt_}, {lt_}, 3")
+        ins(f"and.b32 {lt_}, {warp}, 3")
         ins(f"or.b32 {lt_}, {lt_}, {lane}")
         ins(f"setp.eq.u32 {leader}, {lt_}, 0")          # lane 0 of each group's first warp
         skip_store = lab("at_not_leader")
@@ -558,7 +591,7 @@ class TcAttention(TunedKernel):
         place(end)
         ins("barrier.sync 0")
         nod = lab("at_nodealloc")
-        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"setp.ne.u32 {p}, {warp}, {self.w_mma}")
         ins(f"@{p} bra {nod}")
         ins("tcgen05.fence::after_thread_sync")
         ins(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, 512")
@@ -570,17 +603,68 @@ def _f32bits(x: float) -> str:
     return "%08X" % struct.unpack("<I", struct.pack("<f", x))[0]
 
 
-def _tree(em, op: str, regs: list[str]) -> str:
-    """Pairwise reduction tree of ``regs`` with ``op`` (keeps the inputs)."""
+class _Exp2:
+    """2^x for a pair of f32 lanes on the FMA pipe (packed f32x2), in place of ex2.approx.
+
+    x is clamped to >= -125 (below that the result is ~2^-125, which rounds to 0 in the
+    f16 P tile), split as x = j + f with j = round(x) (adding and subtracting 1.5 * 2^23)
+    and |f| <= 1/2; 2^f comes from a degree-3 polynomial fitted here for least maximum
+    relative error on [-1/2, 1/2] (7.5e-5 evaluated in f32, below f16's 2^-11 rounding),
+    and j is added into the exponent field as an integer (j << 23).
+    """
+
+    COEF = (0.9999280727914258, 0.6932609870112008, 0.24261113509452387, 0.055171666814684134)
+
+    def __init__(self, em):
+        self.em = em
+        self.k = []
+        for v in (12582912.0,) + self.COEF:
+            r = em.tmp("b64")
+            h = _f32bits(v)
+            em.ins(f"mov.b64 {r}, 0x{h}{h}")
+            self.k.append(r)
+
+    def pair(self, d: str, x0: str, x1: str) -> str:
+        em, ins = self.em, self.em.ins
+        mag, c0, c1, c2, c3 = self.k
+        ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
+        ins(f"max.f32 {x0}, {x0}, 0fC2FA0000")
+        ins(f"max.f32 {x1}, {x1}, 0fC2FA0000")
+        x, tj, f, p = em.tmp("b64"), em.tmp("b64"), em.tmp("b64"), em.tmp("b64")
+        ins(f"mov.b64 {x}, {{{x0}, {x1}}}")
+        ins(f"add.rn.f32x2 {tj}, {x}, {mag}")
+        ins(f"sub.rn.f32x2 {f}, {tj}, {mag}")
+        ins(f"sub.rn.f32x2 {f}, {x}, {f}")
+        ins(f"fma.rn.f32x2 {p}, {f}, {c3}, {c2}")
+        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c1}")
+        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c0}")
+        j0, j1, p0, p1 = (em.tmp("b32") for _ in range(4))
+        ins(f"mov.b64 {{{j0}, {j1}}}, {tj}")
+        ins(f"mov.b64 {{{p0}, {p1}}}, {p}")
+        for j, q, x_ in ((j0, p0, x0), (j1, p1, x1)):
+            ins(f"shl.b32 {j}, {j}, 23")
+            ins(f"add.s32 {q}, {q}, {j}")
+            ins(f"mov.b32 {x_}, {q}")
+        r = em.tmp("b64")
+        ins(f"mov.b64 {r}, {{{x0}, {x1}}}")
+        return r
+
+
+def _tree(em, op: str, regs: list[str], arity: int = 2, kind: str = "f32") -> str:
+    """Reduction tree of ``regs`` with ``op`` (keeps the inputs); ``arity`` 3 uses
+    the three-source form sm_100 has for max / min."""
     cur = list(regs)
     while len(cur) > 1:
-        nxt = []
-        for i in range(0, len(cur) - 1, 2):
-            d = em.tmp("f32")
-            em.ins(f"{op} {d}, {cur[i]}, {cur[i + 1]}")
-            nxt.append(d)
-        if len(cur) % 2:
-            nxt.append(cur[-1])
+        nxt, i = [], 0
+        while i < len(cur):
+            n = min(arity, len(cur) - i)
+            if n == 1:
+                nxt.append(cur[i])
+            else:
+                d = em.tmp(kind)
+                em.ins(f"{op} {d}, {', '.join(cur[i:i + n])}")
+                nxt.append(d)
+            i += n
         cur = nxt
     return cur[0]
 
