@@ -1,7 +1,7 @@
 """Benchmark: emitted sm_100a kernels on the benchmark workloads.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config rowops|sum|bigsum]
-    python bench.py --impl reference ...       # the reference's CPU path
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config rowops|sum|bigsum|matmul|attention]
+    python bench.py --impl reference ...       # the reference's CPU path (bounded sample, <= ~90 s)
 
 A step is one pass of the hot path over one batch of synthetic input:
 
@@ -15,6 +15,10 @@ A step is one pass of the hot path over one batch of synthetic input:
   bigsum  f32[2^30] U[-1, 1) split into contiguous slices over N GPUs: one
           two-pass grid-reduction kernel per GPU, then an NCCL all-reduce of
           the per-GPU partials.
+  matmul  f16 C = A B (B column-major), f32 out: 4096^3 and 8192x3072x1024 on
+          the tcgen05 matmul family; N GPUs run replicas (weak scaling).
+  attention  softmax(Q K^T / sqrt(d)) V, f16 [8, 16, 2048, 128] on the tcgen05
+          attention family; the 128 (batch, head) units split over N GPUs.
 
 value is the whole-job algorithmic HBM bandwidth (bytes the workload must
 move / max-over-ranks device time of the K steps, CUDA events on the launch
@@ -250,8 +254,10 @@ class FullSum:
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
+        from thompiler.shard import slice_bounds
         self.torch, self.rank, self.world, self.sharded = torch, rank, world, sharded
-        self.n = n_total // world if sharded else n_total
+        lo, hi = slice_bounds(n_total, rank, world) if sharded else (0, n_total)
+        self.n = hi - lo
         self.n_total = n_total
         self.metric = ("achieved HBM GB/s (sharded sum + NCCL all-reduce)" if sharded
                        else "achieved HBM GB/s (single-kernel array sum)")
@@ -469,23 +475,23 @@ class Attention:
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
+        from thompiler.shard import unit_range
         self.torch = torch
         B, H, S, D = 8, 16, seq or 2048, 128
-        if B % world:
-            raise ValueError("the attention workload splits its 8 batches over 1, 2, 4 or 8 GPUs")
         self.B, self.H, self.S, self.D, self.world = B, H, S, D, world
-        Bl = B // world
+        u0, u1 = unit_range(B * H, rank, world)          # this rank's (batch, head) units
+        Ul = u1 - u0
         tmp = Path(tempfile.mkdtemp(prefix=f"bench_att_{rank}_"))
-        d = synth.attention_package(tmp / "att", Bl, H, S, D)
+        d = synth.attention_package(tmp / "att", Ul, 1, S, D)
         self.k = {"attention": DeviceKernel(d / "k_attention.ir.json", device=dev)}
         g = torch.Generator(device=f"cuda:{dev}").manual_seed(3000 + rank)
-        self.q, self.kk, self.v = (torch.randn(Bl, H, S, D, device=f"cuda:{dev}", generator=g).half()
+        self.q, self.kk, self.v = (torch.randn(Ul, 1, S, D, device=f"cuda:{dev}", generator=g).half()
                                    for _ in range(3))
         self.c = torch.tensor([D ** 0.5], device=f"cuda:{dev}")
-        self.o = torch.empty(Bl, H, S, D, device=f"cuda:{dev}", dtype=torch.float16)
+        self.o = torch.empty(Ul, 1, S, D, device=f"cuda:{dev}", dtype=torch.float16)
         self.kinds = ("attention",)
-        self.flops = {"attention": 4 * Bl * H * S * S * D}
-        self.kbytes = {"attention": 4 * Bl * H * S * D * 2}
+        self.flops = {"attention": 4 * Ul * S * S * D}
+        self.kbytes = {"attention": 4 * Ul * S * D * 2}
         self.flops_per_step = 4 * B * H * S * S * D
         self.bytes_per_step = self.flops_per_step
         self.launches_per_step = 1
@@ -562,8 +568,12 @@ CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
            "bigsum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True)}
 
 
-def reference_arm(args) -> None:
-    """The reference's CPU path on this host's cores, same metric and config."""
+REFERENCE_BUDGET_S = 90.0      # wall-time cap on the reference arm's timed samples
+
+
+def reference_arm(args, out=None) -> None:
+    """The reference's CPU path (the torch expression each problem was generated from, evaluated on
+    this host's cores) on a bounded sample of the same workload, same metric and config."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -571,40 +581,65 @@ def reference_arm(args) -> None:
     cfg = args.config
     if cfg == "rowops":
         rows, cols = 1024, 4096
-        samples = []
-        for _ in range(args.warmup):
-            cpu_baseline.rowops_sample(rows, cols)
-        for _ in range(args.steps):
-            samples.append(cpu_baseline.rowops_sample(rows, cols)["seconds"])
-        sec = statistics.median(samples)
-        nbytes = 3 * 2 * rows * cols * 4 + cols * 4
-        value, cores = nbytes / sec / 1e9, cpu_baseline.threads()
+        run = lambda: cpu_baseline.rowops_sample(rows, cols)             # noqa: E731
+        work, unit, scale, dtype = 3 * 2 * rows * cols * 4 + cols * 4, "GB/s", 1e9, "f32"
         sample = f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {cols}] (1/8 of a [8192, 4096] step)"
-        metric = RowOps.metric
+        metric, scaling = RowOps.metric, "weak"
         config = {"workload": "fused row ops f32[8192, 4096] x3 (softmax, rmsnorm eps=1e-6, l2norm)",
                   "sample_rows": rows}
+    elif cfg == "matmul":
+        m = n = k = 1024
+        run = lambda: cpu_baseline.matmul_sample(m, n, k)                # noqa: E731
+        work, unit, scale, dtype = 2 * m * n * k, "TFLOP/s", 1e12, "f16"
+        sample = f"torch CPU f16 matmul {m}x{n}x{k} (B column-major, f32 result)"
+        metric, scaling = Matmul.metric, "weak"
+        config = {"workload": "f16 matmul, f32 accumulate/out, A row-major, B column-major: "
+                              "4096x4096x4096, 8192x3072x1024", "sample": f"{m}x{n}x{k}"}
+    elif cfg == "attention":
+        bh, sq, d = 2, 2048, 128
+        run = lambda: cpu_baseline.attention_sample(bh, sq, d)           # noqa: E731
+        work, unit, scale, dtype = 4 * bh * sq * sq * d, "TFLOP/s", 1e12, "f16"
+        sample = f"torch CPU f16 attention on {bh} of the 128 heads ([{bh}, {sq}, {d}])"
+        metric, scaling = Attention.metric, "strong"
+        config = {"workload": "attention f16 [8, 16, 2048, 128] non-causal, scale 1/sqrt(d), f32 accumulate",
+                  "sample_heads": bh}
     else:
         n = 1 << 26
-        samples = []
-        for _ in range(args.warmup):
-            cpu_baseline.sum_sample(n)
-        for _ in range(args.steps):
-            samples.append(cpu_baseline.sum_sample(n)["seconds"])
-        sec = statistics.median(samples)
-        value, cores = n * 4 / sec / 1e9, cpu_baseline.threads()
+        run = lambda: cpu_baseline.sum_sample(n)                         # noqa: E731
+        work, unit, scale, dtype = n * 4, "GB/s", 1e9, "f32"
         sample = f"torch CPU sum of f32[{n}]"
         metric = "achieved HBM GB/s (single-kernel array sum)" if cfg == "sum" else \
             "achieved HBM GB/s (sharded sum + NCCL all-reduce)"
+        scaling = "weak" if cfg == "sum" else "strong"
         config = {"workload": f"{cfg} (CPU sample of {n} elements)"}
-    line = {"impl": "reference", "metric": metric, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+    for _ in range(min(args.warmup, 3)):
+        run()
+    samples, t0 = [], time.perf_counter()
+    while len(samples) < args.steps and (not samples or time.perf_counter() - t0 < REFERENCE_BUDGET_S):
+        samples.append(run()["seconds"])
+    sec = statistics.median(samples)
+    value, cores = work / sec / scale, cpu_baseline.threads()
+    config["samples_timed"] = len(samples)
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config,
-            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
-            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+            "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), file=out or sys.stdout, flush=True)
+
+
+def _result_stream():
+    """The JSON line is the only thing this program writes to its standard output: native
+    libraries (NCCL's version banner, driver JIT messages) print to file descriptor 1 too, so
+    that descriptor is pointed at stderr and the line goes to a private copy of the original."""
+    out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    return out
 
 
 def main() -> None:
+    out = _result_stream()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=0,
@@ -620,7 +655,7 @@ def main() -> None:
     if args.steps <= 0:
         args.steps = DEFAULT_STEPS[args.config]
     if args.impl == "reference":
-        reference_arm(args)
+        reference_arm(args, out)
         return
 
     import torch
@@ -703,7 +738,7 @@ def main() -> None:
             "cpu_baseline": w.cpu_baseline() if world == 1 else None,
             "e2e": e2e, "gpu_launches": w.launches_per_step * args.steps, "clocks": clk,
         }
-        print(json.dumps(line))
+        print(json.dumps(line), file=out, flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
