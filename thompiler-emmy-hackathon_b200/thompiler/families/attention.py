@@ -10,21 +10,28 @@ reference).  Q, K, V and the output are f16 [..., S, D] buffers (D = 64 or
 128, S a multiple of 128); ``c`` comes from a one-element constant buffer at
 run time.
 
-Tuned body: one CTA per (head, 128-query tile), 192 threads:
-  warp 0    TMA: the Q tile once, then K and V tiles of 128 keys through a
-            two-stage ring (128B-swizzled, K-major rows of 64 d);
-  warp 1    tcgen05: S_i = Q K_i^T into one of two TMEM score buffers
-            (M = 128 queries, N = 128 keys, K = D), and O += P_{i-1} V_{i-1}
-            (A = P from shared memory, B = V as an MN-major operand, O in TMEM);
-  warps 2-5 softmax: each thread owns one query row; it loads its 128 scores
-            from TMEM, takes the row max, rescales O and the running sum only
-            when the max grew by more than 2^8 (so P <= 256 stays exact in
-            f16 and the rescale is rare), writes P = 2^(s*c' - m) as f16 into
-            a 128B-swizzled shared tile for the next MMA; at the end it
-            normalises O by the row sum and stores the tile with TMA.
+Tuned body: one CTA per (head, QT query tiles of 128), QT = 2 when S allows
+(384 threads), else 1 (192 threads):
+  warps 0 .. 4QT-1  softmax, one warpgroup per query tile g; thread = query row,
+            warp w reads TMEM lanes 32 (w % 4) ..;
+  warp 4QT  TMA: the Q tiles once, then K and V tiles of 128 keys through
+            their own rings (128B-swizzled rows of 64 d);
+  warp 4QT+1  tcgen05 issuer: S_g = Q_g K_i^T (SS form, M = 128 queries,
+            N = 128 keys, K = D) and O_g += P_g V_i (TS form: A = P_g from
+            TMEM, B = V as an MN-major shared operand), ordered PV_0, S_0(next),
+            PV_1, S_1(next) so each group's softmax overlaps the other's MMAs;
+  with QT = 2 warps 10-11 fill the third warpgroup, which hands registers to
+  the softmax warpgroups (setmaxnreg 168 -> 224 / 56).
+TMEM (512 columns): O_g at 128 g, S_g at 256 + 128 g; P_g (f16 pairs) is
+written over the first 64 columns of S_g.  Softmax per row and key block: the
+128 scores in registers (four loads, one wait), a three-input max tree, O and
+the running sum rescaled only when the max grew by more than 2^8 (P <= 256
+stays exact in f16, the rescale is rare), P = 2^(s c' - m) with packed f32x2
+FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  Epilogue:
+O / l as f16 staged over the group's Q tile, one TMA store per group.
 Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
-exactly as the IR's exp lowering; ex2.approx computes the powers.  All
-mbarrier waits are bounded (thompiler.families.kit).
+exactly as the IR's exp lowering.  All mbarrier waits are bounded
+(thompiler.families.kit).
 """
 
 from __future__ import annotations

@@ -23,8 +23,10 @@ Tuned body (one persistent CTA per SM, 192 threads, warp-specialised):
            stage's "empty" mbarrier; after the last block, commit to the
            accumulator's "full" mbarrier;
   warps 2-5 epilogue: tcgen05.ld 32x32b of their TMEM lane quarter, convert,
-           store to global; arrive on the accumulator's "empty" mbarrier, so the
-           MMA of the next tile (other accumulator) overlaps this epilogue.
+           stage 32-row x 64-byte boxes in per-warp 64B-swizzled shared buffers
+           and store them with cp.async.bulk.tensor (bulk groups); arrive on the
+           accumulator's "empty" mbarrier, so the MMA of the next tile (other
+           accumulator) overlaps this epilogue.
 
 Tiles are handed out round-robin (tile = ctaid + i * nctaid), M fastest, so
 the CTAs in flight share B column tiles in L2.  Every mbarrier wait is
