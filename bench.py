@@ -245,22 +245,26 @@ class RowOps:
                 "parallelism": f"weak: {world} GPU(s), one matrix set each, no collective"}
 
 
+BIGSUM_METRIC = "achieved HBM GB/s (sharded sum: per-GPU reduction + cross-GPU combine)"
+
+
 class FullSum:
     name = "sum"
     unit = "GB/s"
     dtype = "f32"
 
-    def __init__(self, rank: int, world: int, dev: int, n_total: int = 1 << 20, sharded: bool = False):
+    def __init__(self, rank: int, world: int, dev: int, n_total: int = 1 << 20, sharded: bool = False,
+                 collective: str = "peer"):
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
-        from thompiler.shard import slice_bounds
+        from thompiler.shard import PeerCombine, slice_bounds
         self.torch, self.rank, self.world, self.sharded = torch, rank, world, sharded
         lo, hi = slice_bounds(n_total, rank, world) if sharded else (0, n_total)
         self.n = hi - lo
         self.n_total = n_total
-        self.metric = ("achieved HBM GB/s (sharded sum + NCCL all-reduce)" if sharded
-                       else "achieved HBM GB/s (single-kernel array sum)")
+        self.collective = collective if (sharded and world > 1) else None
+        self.metric = (BIGSUM_METRIC if sharded else "achieved HBM GB/s (single-kernel array sum)")
         tmp = Path(tempfile.mkdtemp(prefix=f"bench_sum_{rank}_"))
         d = synth.sum_package(tmp / "sum", self.n)
         self.k = DeviceKernel(d / "k_sum_1_reduce.ir.json", device=dev)
@@ -272,6 +276,7 @@ class FullSum:
         self.launches_per_step = 1
         self.dominant = "sum"
         self.kinds = ("sum",)
+        self.peer = PeerCombine(self.k.module, rank, world) if self.collective == "peer" else None
 
     def step(self, stream: int, events=None) -> None:
         if events is not None:
@@ -279,22 +284,28 @@ class FullSum:
         self.k({"x": self.x.data_ptr(), "sum_1": self.out.data_ptr()}, stream)
         if events is not None:
             events["sum"][1].record()
-        if self.sharded and self.world > 1:
+        if self.collective == "nccl":
             import torch.distributed as dist
             dist.all_reduce(self.out)
 
     def check(self) -> None:
+        from thompiler import runner
         torch = self.torch
         want = self.x.double().sum()
-        if self.sharded and self.world > 1:
+        if self.collective is not None:
             import torch.distributed as dist
             dist.all_reduce(want)
-            self.step(self.torch.cuda.current_stream().cuda_stream)
-        else:
-            self.step(self.torch.cuda.current_stream().cuda_stream)
+        self.step(self.torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         got = float(self.out.item())
+        if self.k.plan.error_word:
+            assert runner.read_error_word(self.k.module, self.k.plan) == 0, "peer combine gave up"
         assert abs(got - float(want)) <= 1e-5 * max(1.0, abs(float(want))) + 1e-3, f"sum mismatch {got} vs {want}"
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def e2e(self, steps: int) -> dict:
         from thompiler import runner
@@ -309,7 +320,7 @@ class FullSum:
             r = runner.run(self.k.fn, self.k.plan, args)
             if not r["ok"]:
                 raise RuntimeError(r["stderr"])
-            if self.sharded and self.world > 1:
+            if self.collective == "nccl":          # the peer combine already left the total in ho
                 import torch.distributed as dist
                 v = torch.tensor([float(ho[0])], device=self.x.device)
                 dist.all_reduce(v)
@@ -327,8 +338,10 @@ class FullSum:
                 "sample": f"torch CPU sum of f32[{n}], best of 3"}
 
     def config(self, world: int) -> dict:
+        how = {"peer": "in-kernel combine over NVLink peer memory (no NCCL in the step)",
+               "nccl": "NCCL all-reduce of the per-GPU results", None: "no exchange (one GPU)"}
         c = {"workload": (f"sharded sum f32[2^{self.n_total.bit_length() - 1}] -> per-GPU two-pass reduction "
-                          "+ NCCL all-reduce" if self.sharded else f"array sum f32[{self.n}] U[-1,1)"),
+                          f"+ {how[self.collective]}" if self.sharded else f"array sum f32[{self.n}] U[-1,1)"),
              "elements_per_gpu": self.n, "kernel": self.k.family,
              "launch": {"grid": list(self.k.plan.grid), "block": list(self.k.plan.block)},
              "l2": ("inputs larger than L2" if self.n * 4 > 126e6 else
@@ -565,7 +578,8 @@ CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
            "attention": lambda r, w, d, n: Attention(r, w, d, n),
            "matmul": lambda r, w, d, n: Matmul(r, w, d, n),
            "sum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 20),
-           "bigsum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True)}
+           "bigsum": lambda r, w, d, n, coll="peer": FullSum(r, w, d, n or 1 << 30, sharded=True,
+                                                             collective=coll)}
 
 
 REFERENCE_BUDGET_S = 90.0      # wall-time cap on the reference arm's timed samples
@@ -608,8 +622,7 @@ def reference_arm(args, out=None) -> None:
         run = lambda: cpu_baseline.sum_sample(n)                         # noqa: E731
         work, unit, scale, dtype = n * 4, "GB/s", 1e9, "f32"
         sample = f"torch CPU sum of f32[{n}]"
-        metric = "achieved HBM GB/s (single-kernel array sum)" if cfg == "sum" else \
-            "achieved HBM GB/s (sharded sum + NCCL all-reduce)"
+        metric = "achieved HBM GB/s (single-kernel array sum)" if cfg == "sum" else BIGSUM_METRIC
         scaling = "weak" if cfg == "sum" else "strong"
         config = {"workload": f"{cfg} (CPU sample of {n} elements)"}
     for _ in range(min(args.warmup, 3)):
@@ -648,6 +661,8 @@ def main() -> None:
     ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--collective", default="peer", choices=["peer", "nccl"],
+                    help="bigsum's exchange step: in-kernel peer combine (default) or an NCCL all-reduce")
     ap.add_argument("--size", type=int, default=0,
                     help="override the workload size (rows for rowops, elements for sums); profiling only")
     args = ap.parse_args()
@@ -670,7 +685,10 @@ def main() -> None:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     runner.init(local)
-    w = CONFIGS[args.config](rank, world, local, args.size)
+    if args.config == "bigsum":
+        w = CONFIGS[args.config](rank, world, local, args.size, args.collective)
+    else:
+        w = CONFIGS[args.config](rank, world, local, args.size)
     stream = torch.cuda.current_stream().cuda_stream
     w.check()
     for _ in range(args.warmup):
@@ -739,6 +757,8 @@ def main() -> None:
             "e2e": e2e, "gpu_launches": w.launches_per_step * args.steps, "clocks": clk,
         }
         print(json.dumps(line), file=out, flush=True)
+    if hasattr(w, "close"):
+        w.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -408,6 +408,47 @@ int thr_release_buffers(void) {
     return THR_OK;
 }
 
+// ---- peer mailboxes (CUDA IPC; no multicast objects) ----------------------------------
+
+int thr_peer_alloc(uint64_t bytes, uint64_t *dptr, unsigned char handle[THR_IPC_HANDLE_BYTES]) {
+    if (!dptr || !handle || bytes == 0) return fail(THR_ERR_REQUEST, "thr_peer_alloc: bad arguments");
+    static_assert(sizeof(cudaIpcMemHandle_t) == THR_IPC_HANDLE_BYTES, "IPC handle size");
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "peer mailbox cudaMalloc");
+    e = cudaMemset(p, 0, bytes);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "peer mailbox handle");
+    }
+    memcpy(handle, &h, sizeof h);
+    *dptr = (uint64_t)(uintptr_t)p;
+    return THR_OK;
+}
+
+int thr_peer_open(const unsigned char handle[THR_IPC_HANDLE_BYTES], uint64_t *dptr) {
+    if (!dptr || !handle) return fail(THR_ERR_REQUEST, "thr_peer_open: bad arguments");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void *p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    *dptr = (uint64_t)(uintptr_t)p;
+    return THR_OK;
+}
+
+int thr_peer_close(uint64_t dptr) {
+    cudaError_t e = cudaIpcCloseMemHandle((void *)(uintptr_t)dptr);
+    return e == cudaSuccess ? THR_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int thr_peer_free(uint64_t dptr) {
+    cudaError_t e = cudaFree((void *)(uintptr_t)dptr);
+    return e == cudaSuccess ? THR_OK : cuda_fail(e, "peer mailbox cudaFree");
+}
+
 // Lets the allocation-free entry points (noalloc.cu) report through thr_last_error.
 int thr_noalloc_set_error(const char *msg) {
     g_err = msg ? msg : "";

@@ -32,7 +32,10 @@ deterministic second pass: each CTA stores its state to a module-scope
 partials in CTA order with the IR's ``combine_states`` and runs the IR's
 epilogue.  Under meta.json's single-CTA launch the second pass is skipped.
 The tuned launch (recorded in the sidecar) is ``ctas_per_sm`` CTAs of T
-threads per SM.
+threads per SM.  A single f32 sum also carries an in-kernel combine across
+GPUs (off unless the host binds the module to its peers): the finishing CTA
+adds the other ranks' results over NVLink before the epilogue, replacing a
+separate all-reduce of the per-GPU partials.
 """
 
 from __future__ import annotations
@@ -50,6 +53,8 @@ MAX_PARTIALS = 8192         # CTAs the full-mode second pass supports
 SM_COUNT = 148
 CTAS_PER_SM = 8
 UNROLL = 4                  # v4 chunks in flight per thread (full mode)
+MAX_PEERS = 8               # GPUs the in-kernel combine of a sharded sum supports
+PEER_WAIT_LIMIT = 1 << 20   # polling rounds before the peer combine gives up
 
 
 def _is_var(e, name: str) -> bool:
@@ -252,7 +257,12 @@ class StridedReduce(TunedKernel):
             return None
         chunks = -(-self.C // self.V)
         ctas = min(MAX_PARTIALS, SM_COUNT * CTAS_PER_SM, max(1, -(-chunks // (self.T * UNROLL))))
-        return {"grid": [ctas, 1, 1], "block": [self.T, 1, 1], "smem_bytes": 0}
+        side = {"grid": [ctas, 1, 1], "block": [self.T, 1, 1], "smem_bytes": 0}
+        if self._peer_capable():
+            side.update(error_word="thc_error",
+                        peer={"table": "thc_peer_ptr", "world": "thc_world", "rank": "thc_rank",
+                              "max_ranks": MAX_PEERS})
+        return side
 
     # ---- hooks -------------------------------------------------------------------
 
@@ -470,8 +480,103 @@ class StridedReduce(TunedKernel):
         em.ins(f"@{p} bra {final}")
         self._second_pass(cta, tid, nct)
         em.place(final)
+        if self._peer_capable():
+            self._peer_combine(tid)
         w.body(self.mid)
         w.body((self.tail,))
+
+    def _peer_capable(self) -> bool:
+        """A single f32 sum state: the result the ranks of a sharded sum add up."""
+        accs = [s for s in self.l1.body if isinstance(s, ir.Accum)]
+        return (not self.row_mode and len(self.states) == 1 and len(accs) == 1
+                and accs[0].op.name == "add" and dtype_of(accs[0].dtype, "Accum") is F32)
+
+    def _peer_combine(self, tid: str) -> None:
+        """Add the other GPUs' results to this one over peer memory, inside the kernel.
+
+        Off unless the host sets ``thc_world`` > 1 (``thompiler.shard.PeerCombine``), which
+        also fills ``thc_peer_ptr[r]`` with rank r's mailbox (8 slots of 8 bytes, CUDA IPC
+        mapped) and ``thc_rank``.  Thread 0 of the finishing CTA bumps the module's launch
+        counter ``thc_epoch``, publishes (epoch << 32 | f32 bits) into slot ``rank`` of every
+        rank's mailbox -- one 64-bit store carries both, so relaxed system-scope stores and loads
+        suffice (no release fence per peer) -- then polls all of its own mailbox's slots in one
+        round until each carries this epoch and adds the values in rank order: every rank gets
+        the same total.  The wait gives up after PEER_WAIT_LIMIT rounds (tens of nanoseconds
+        apart), sets bit 0 of ``thc_error`` and adds only the values that arrived, so a rank that
+        never arrives costs at most about a second and no hang.  The ranks run the same sequence
+        of launches, so their epochs agree.
+        """
+        em = self.em
+        em.module(f".global .align 8 .u64 thc_peer_ptr[{MAX_PEERS}]")
+        em.module(".global .align 4 .u32 thc_world = 1")
+        em.module(".global .align 4 .u32 thc_rank = 0")
+        em.module(".global .align 4 .u32 thc_epoch = 0")
+        em.module(".global .align 4 .u32 thc_error = 0")
+        em.module(".shared .align 4 .f32 thc_peer_total")
+        acc = em.get(self.states[0])
+        p, q = em.tmp("pred"), em.tmp("pred")
+        world, rank, e = em.tmp("b32"), em.tmp("b32"), em.tmp("b32")
+        skip, bar = em.label("no_peer"), em.label("peer_bar")
+        em.ins(f"ld.global.u32 {world}, [thc_world]")
+        em.ins(f"setp.le.u32 {p}, {world}, 1")
+        em.ins(f"@{p} bra {skip}")
+        em.ins(f"setp.ne.u32 {p}, {tid}, 0")
+        em.ins(f"@{p} bra {bar}")
+        em.ins(f"ld.global.u32 {rank}, [thc_rank]")
+        em.ins(f"ld.global.u32 {e}, [thc_epoch]")
+        em.ins(f"add.u32 {e}, {e}, 1")
+        em.ins(f"st.global.u32 [thc_epoch], {e}")
+        vb, pack, off = em.tmp("b32"), em.tmp("b64"), em.tmp("b64")
+        em.ins(f"mov.b32 {vb}, {acc}")
+        em.ins(f"mov.b64 {pack}, {{{vb}, {e}}}")
+        em.ins(f"mul.wide.u32 {off}, {rank}, 8")
+        for r in range(MAX_PEERS):                        # publish into slot `rank` of every mailbox
+            base = em.tmp("b64")
+            em.ins(f"setp.gt.u32 {q}, {world}, {r}")
+            em.ins(f"@{q} ld.global.u64 {base}, [thc_peer_ptr+{8 * r}]")
+            em.ins(f"@{q} add.u64 {base}, {base}, {off}")
+            em.ins(f"@{q} st.relaxed.sys.global.u64 [{base}], {pack}")
+        own, tab = em.tmp("b64"), em.tmp("b64")
+        em.ins(f"mov.u64 {tab}, thc_peer_ptr")
+        em.ins(f"add.u64 {tab}, {tab}, {off}")
+        em.ins(f"ld.global.u64 {own}, [{tab}]")
+        total, n = em.tmp("f32"), em.tmp("b32")
+        em.ins(f"mov.f32 {total}, 0f00000000")
+        # poll every slot in one round until all carry this epoch, then add them in rank order
+        top, done = em.label("peer_wait"), em.label("peer_done")
+        live = [em.tmp("pred") for _ in range(MAX_PEERS)]
+        got = [em.tmp("pred") for _ in range(MAX_PEERS)]
+        los = [em.tmp("b32") for _ in range(MAX_PEERS)]
+        for r in range(MAX_PEERS):
+            em.ins(f"setp.gt.u32 {live[r]}, {world}, {r}")
+        em.ins(f"mov.u32 {n}, 0")
+        em.place(top)
+        allin = em.tmp("pred")
+        em.ins(f"setp.eq.u32 {allin}, {n}, {n}")
+        for r in range(MAX_PEERS):
+            x, hi = em.tmp("b64"), em.tmp("b32")
+            em.ins(f"mov.u32 {hi}, {e}")
+            em.ins(f"@{live[r]} ld.relaxed.sys.global.u64 {x}, [{own}+{8 * r}]")
+            em.ins(f"@{live[r]} mov.b64 {{{los[r]}, {hi}}}, {x}")
+            em.ins(f"setp.eq.u32 {got[r]}, {hi}, {e}")
+            em.ins(f"and.pred {allin}, {allin}, {got[r]}")
+        em.ins(f"@{allin} bra {done}")
+        em.ins(f"add.u32 {n}, {n}, 1")
+        em.ins(f"setp.lt.u32 {q}, {n}, {PEER_WAIT_LIMIT}")
+        em.ins(f"@{q} nanosleep.u32 32")
+        em.ins(f"@{q} bra {top}")
+        em.ins(f"atom.global.or.b32 {em.tmp('b32')}, [thc_error], 1")   # gave up: add what arrived
+        em.place(done)
+        for r in range(MAX_PEERS):
+            vf = em.tmp("f32")
+            em.ins(f"and.pred {got[r]}, {got[r]}, {live[r]}")
+            em.ins(f"mov.b32 {vf}, {los[r]}")
+            em.ins(f"@{got[r]} add.rn.f32 {total}, {total}, {vf}")
+        em.ins(f"st.shared.f32 [thc_peer_total], {total}")
+        em.place(bar)
+        em.ins("bar.sync 0")
+        em.ins(f"ld.shared.f32 {acc}, [thc_peer_total]")
+        em.place(skip)
 
     def _second_pass(self, cta: str, tid: str, nct: str) -> None:
         """Store the CTA's state; the last CTA to arrive folds all states in CTA order."""

@@ -85,6 +85,10 @@ def library() -> ctypes.CDLL:
             "thr_synchronize": ([], i32),
             "thr_release_buffers": ([], i32),
             "thr_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
+            "thr_peer_alloc": ([u64, ctypes.POINTER(u64), ctypes.c_char_p], i32),
+            "thr_peer_open": ([ctypes.c_char_p, ctypes.POINTER(u64)], i32),
+            "thr_peer_close": ([u64], i32),
+            "thr_peer_free": ([u64], i32),
         }
         for name, (args, res) in sig.items():
             f = getattr(lib, name)

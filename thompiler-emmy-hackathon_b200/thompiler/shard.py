@@ -43,3 +43,73 @@ def combine_partials(partial, group=None):
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=group)
     return partial
+
+
+def peer_table(module, rank: int, world: int, pointers: list[int]) -> None:
+    """Write a full-sum module's peer globals: ``thc_peer_ptr[r]`` = rank r's mailbox (as this
+    process addresses it), ``thc_rank``, ``thc_world`` (1 switches the combine off)."""
+    import ctypes
+    from thompiler import runner
+    side = module.sidecar or {}
+    peer = side.get("peer")
+    if peer is None:
+        raise ValueError("this module has no in-kernel peer combine")
+    if not 1 <= world <= peer["max_ranks"] or len(pointers) != world:
+        raise ValueError(f"world {world} with {len(pointers)} mailboxes (at most {peer['max_ranks']})")
+    lib = runner.library()
+    tab = (ctypes.c_uint64 * peer["max_ranks"])(*(pointers + [0] * (peer["max_ranks"] - world)))
+    for name, buf in ((peer["table"], tab), (peer["rank"], ctypes.c_uint32(rank)),
+                      (peer["world"], ctypes.c_uint32(world))):
+        dst, size = module.global_ptr(name)
+        runner.check(lib.thr_memcpy_htod(dst, ctypes.byref(buf), ctypes.sizeof(buf), 0), f"write {name}")
+    runner.check(lib.thr_synchronize(), "synchronise")
+
+
+class PeerCombine:
+    """Bind a compiled full-sum module to the other ranks' copies of it, so its finishing CTA
+    adds the per-GPU results over NVLink (see ``families.strided``) -- the sharded sum's
+    exchange step without a separate collective launch.
+
+    Every rank allocates a zeroed mailbox (CUDA IPC-exportable), the handles travel once through
+    ``torch.distributed.all_gather_object``, and each rank maps the others' mailboxes.  Call
+    ``close`` on every rank (it switches the combine off and unmaps)."""
+
+    SLOT_BYTES = 8
+
+    def __init__(self, module, rank: int, world: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from thompiler import runner
+        self.module, self.rank, self.world = module, rank, world
+        lib = runner.library()
+        mine, handle = ctypes.c_uint64(), ctypes.create_string_buffer(64)
+        slots = (module.sidecar or {}).get("peer", {}).get("max_ranks", 8)
+        runner.check(lib.thr_peer_alloc(slots * self.SLOT_BYTES, ctypes.byref(mine), handle), "mailbox")
+        self.mine, self.opened = mine.value, []
+        handles = [None] * world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        pointers = []
+        for r, h in enumerate(handles):
+            if r == rank:
+                pointers.append(self.mine)
+                continue
+            q = ctypes.c_uint64()
+            runner.check(lib.thr_peer_open(h, ctypes.byref(q)), f"map rank {r}'s mailbox")
+            self.opened.append(q.value)
+            pointers.append(q.value)
+        peer_table(module, rank, world, pointers)
+        dist.barrier(group=group)            # every rank's table is in place before any launch
+
+    def close(self, group=None) -> None:
+        """Switch the combine off, then unmap and free -- after every rank's kernels have
+        finished (device synchronise + barrier), so no rank still writes into a mailbox."""
+        import torch.distributed as dist
+        from thompiler import runner
+        lib = runner.library()
+        runner.check(lib.thr_synchronize(), "synchronise")
+        dist.barrier(group=group)
+        peer_table(self.module, 0, 1, [self.mine])
+        for q in self.opened:
+            lib.thr_peer_close(q)
+        lib.thr_peer_free(self.mine)
+        self.opened = []
