@@ -56,6 +56,28 @@ def test_attention_medium_vs_expression(tmp_path, shape):
                                rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("shape,grid", [((2, 3, 512, 128), 1), ((2, 3, 512, 128), 5), ((1, 2, 384, 64), 4)])
+def test_attention_persistent_tiles(tmp_path, shape, grid):
+    """Fewer CTAs than (head, query-tile) tiles: each CTA walks several tiles, carrying its
+    K / V rings, barrier phases and TMEM accumulators from one tile to the next."""
+    import torch
+    d = synth.attention_package(tmp_path / "att", *shape)
+    k = DeviceKernel(d / "k_attention.ir.json")
+    k.plan.grid = (grid, 1, 1)
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q, kk, v = (torch.randn(*shape, device="cuda", generator=g).half() for _ in range(3))
+    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
+    o = torch.full(shape, float("nan"), device="cuda", dtype=torch.float16)
+    for _ in range(2):                                 # a second launch starts from the first's phases
+        k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(),
+           "attn": o.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert runner.read_error_word(k.module, k.plan) == 0
+    ref = _sdpa64(q.cpu().numpy(), kk.cpu().numpy(), v.cpu().numpy())
+    np.testing.assert_allclose(o.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
+    k.close()
+
+
 def test_attention_benchmark_shape(tmp_path):
     import torch
     B, H, S, D = 8, 16, 2048, 128

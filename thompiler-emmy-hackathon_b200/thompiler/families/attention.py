@@ -46,6 +46,7 @@ from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
 BM = BN = 128
+SM_COUNT = 148
 STAGES = 3                  # K and V rings each
 LOG2E = math.log2(math.e)
 POLY_PAIRS = int(os.environ.get("THOMPILER_ATTN_POLY", "0"))    # of every 8 score pairs (0 .. 8)
@@ -72,8 +73,11 @@ class TcAttention(TunedKernel):
         self.w_tma, self.w_mma = 4 * self.qt, 4 * self.qt + 1
         self.threads = 128 * (self.qt + 1) if self.qt == 2 else 192
         self.reg_split = (224, 56) if self.qt == 2 else None
-        self.ks, self.vs = (3, 2) if (self.qt == 2 and D == 128) else (STAGES, STAGES)
-        self.smem = self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + 1024 + 256
+        self.ks, self.vs = ((2, 2) if self.qt == 2 else (3, 2)) if D == 128 else (STAGES, STAGES)
+        # per softmax warp: a 32-row x 128-byte staging box for the output's TMA stores
+        self.stage_bytes = 4 * self.qt * 32 * 128
+        self.smem = (self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + self.stage_bytes
+                     + 1024 + 256)
         self.tiles = heads * (Sq // (BM * self.qt))
 
     # ---- recognition -------------------------------------------------------------
@@ -150,12 +154,12 @@ class TcAttention(TunedKernel):
     def sidecar(self) -> dict:
         D = self.D
 
-        def tm(name, prm, rows):
+        def tm(name, prm, rows, box_rows=128):
             return {"global": name, "param": prm.name, "dtype": "f16", "dims": [D, rows],
-                    "strides": [D * 2], "box": [64, 128], "swizzle": 3}
+                    "strides": [D * 2], "box": [64, box_rows], "swizzle": 3}
         maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
-                tm("thc_tmap_v", self.pv, self.heads * self.Sk), tm("thc_tmap_o", self.pout, self.heads * self.Sq)]
-        return {"grid": [self.tiles, 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
+                tm("thc_tmap_v", self.pv, self.heads * self.Sk), tm("thc_tmap_o", self.pout, self.heads * self.Sq, 32)]
+        return {"grid": [min(self.tiles, SM_COUNT), 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
                 "tmaps": maps, "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
                 "error_word": "thc_error", "tile": [BM * self.qt, BN, D], "stages": [self.ks, self.vs]}
 
@@ -201,29 +205,32 @@ class TcAttention(TunedKernel):
         ins(f"mov.u32 {base}, smem_pool")
         ins(f"add.u32 {base}, {base}, 1023")
         ins(f"and.b32 {base}, {base}, -1024")
-        # shared: Q tiles (QT of them; each later stages its group's O) | K ring | V ring | barriers
+        # shared: Q tiles (QT of them) | K ring | V ring | output staging (32 x 128 B per softmax
+        # warp) | barriers
         q_s = base
-        k0, v0, bars = t("b32"), t("b32"), t("b32")
+        k0, v0, stage0, bars = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"add.u32 {k0}, {base}, {QT * qb}")
         ins(f"add.u32 {v0}, {base}, {QT * qb + KS * kvb}")
-        ins(f"add.u32 {bars}, {base}, {QT * qb + (KS + VS) * kvb}")
+        ins(f"add.u32 {stage0}, {base}, {QT * qb + (KS + VS) * kvb}")
+        ins(f"add.u32 {bars}, {base}, {QT * qb + (KS + VS) * kvb + self.stage_bytes}")
         nb = 0
 
         def bar() -> int:
             nonlocal nb
             nb += 1
             return (nb - 1) * 8
-        q_full = bar()
+        q_full, q_free = bar(), bar()
         k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
         v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
         s_full = [bar() for _ in range(QT)]
         p_full = [bar() for _ in range(QT)]
         o_done = [bar() for _ in range(QT)]
-        o_staged = [bar() for _ in range(QT)]
+        o_free = [bar() for _ in range(QT)]
         counts = {o: 1 for o in range(0, nb * 8, 8)}
-        for o in p_full + o_staged:
+        for o in p_full + o_free:
             counts[o] = 128
         slot_off = nb * 8
+        assert slot_off + 8 <= 256, "barriers outgrow their shared-memory slot"
         p = t("pred")
         skip = lab("at_noinit")
         ins(f"setp.ne.u32 {p}, {tid}, 0")
@@ -253,20 +260,32 @@ class TcAttention(TunedKernel):
         end = lab("at_end")
         kit = Kit(em, errp, end)
         tmaps = {}
-        for n in ("q", "k", "v", "o"):
+        for n in ("q", "k", "v"):
             r = t("b64")
             ins(f"mov.u64 {r}, thc_tmap_{n}")
             ins(f"cvta.global.u64 {r}, {r}")
             tmaps[n] = r
-        cta = self.special("%ctaid.x")
+        # persistent: CTA c takes tiles c, c + nctaid, ...; nt of them, nt * n_blk key blocks in all
+        cta, ncta = self.special("%ctaid.x"), self.special("%nctaid.x")
+        nt, total = t("b32"), t("b32")
+        ins(f"setp.ge.u32 {p}, {cta}, {self.tiles}")
+        ins(f"@{p} bra {end}")
+        ins(f"sub.u32 {nt}, {self.tiles - 1}, {cta}")
+        ins(f"div.u32 {nt}, {nt}, {ncta}")
+        ins(f"add.u32 {nt}, {nt}, 1")
+        ins(f"mul.lo.u32 {total}, {nt}, {n_blk}")
         groups = self.Sq // (BM * QT)
-        bh, qg = t("b32"), t("b32")
-        ins(f"div.u32 {bh}, {cta}, {groups}")
-        ins(f"rem.u32 {qg}, {cta}, {groups}")
-        qrow, kvrow = t("b32"), t("b32")
-        ins(f"mul.lo.u32 {qrow}, {bh}, {self.Sq}")
-        ins(f"mad.lo.u32 {qrow}, {qg}, {BM * QT}, {qrow}")
-        ins(f"mul.lo.u32 {kvrow}, {bh}, {self.Sk}")
+
+        def tile_rows(tile: str) -> tuple[str, str]:
+            """First query row and first key row of ``tile`` in the flattened [heads * S] views."""
+            bh, qg, qrow, kvrow = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"div.u32 {bh}, {tile}, {groups}")
+            ins(f"rem.u32 {qg}, {tile}, {groups}")
+            ins(f"mul.lo.u32 {qrow}, {bh}, {self.Sq}")
+            ins(f"mad.lo.u32 {qrow}, {qg}, {BM * QT}, {qrow}")
+            ins(f"mul.lo.u32 {kvrow}, {bh}, {self.Sk}")
+            return qrow, kvrow
+
         role_mma, role_sm = lab("at_mma"), lab("at_softmax")
         ins(f"setp.lt.u32 {p}, {warp}, {4 * QT}")
         ins(f"@{p} bra {role_sm}")
@@ -283,13 +302,6 @@ class TcAttention(TunedKernel):
         # ---------------- producer (one warp) ----------------
         is0 = t("pred")
         ins(f"setp.eq.u32 {is0}, {lane}, 0")
-        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {QT * qb}")
-        for g in range(QT):
-            qr = t("b32")
-            ins(f"add.u32 {qr}, {qrow}, {g * BM}")
-            for db in range(dblk):
-                ins(f"@{is0} {tma} [{q_s}+{g * qb + db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qr}}}], "
-                    f"[{bars}+{q_full}]")
 
         def ring(i: str, n_st: int, s0: str, full0: int, empty0: int, mapname: str, row: str) -> None:
             st, buf, fb, eb = t("b32"), t("b32"), t("b32"), t("b32")
@@ -303,25 +315,41 @@ class TcAttention(TunedKernel):
             for db in range(dblk):
                 ins(f"@{is0} {tma} [{buf}+{db * BN * 128}], [{tmaps[mapname]}, {{{db * 64}, {row}}}], [{fb}]")
 
-        i = t("b32")
-        ins(f"mov.u32 {i}, 0")
-        ptop = lab("at_prod")
-        place(ptop)
+        ti, tile, j, blk = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {ti}, 0")
+        ins(f"mov.u32 {tile}, {cta}")
+        ins(f"mov.u32 {j}, 0")
+        ptile, pblk = lab("at_prod_tile"), lab("at_prod_blk")
+        place(ptile)
+        qrow, kvrow = tile_rows(tile)
+        first_tile = lab("at_prod_q")
+        ins(f"setp.eq.u32 {p}, {ti}, 0")
+        ins(f"@{p} bra {first_tile}")
+        prev = t("b32")
+        ins(f"sub.u32 {prev}, {ti}, 1")
+        kit.wait(f"{bars}+{q_free}", kit.parity(prev, 1), 0)      # the last S of the previous tile is done
+        place(first_tile)
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {QT * qb}")
+        for g in range(QT):
+            qr = t("b32")
+            ins(f"add.u32 {qr}, {qrow}, {g * BM}")
+            for db in range(dblk):
+                ins(f"@{is0} {tma} [{q_s}+{g * qb + db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qr}}}], "
+                    f"[{bars}+{q_full}]")
+        ins(f"mov.u32 {blk}, 0")
+        place(pblk)
         row = t("b32")
-        ins(f"mad.lo.u32 {row}, {i}, {BN}, {kvrow}")
-        ring(i, KS, k0, k_full[0], k_empty[0], "k", row)
-        ring(i, VS, v0, v_full[0], v_empty[0], "v", row)
-        ins(f"add.u32 {i}, {i}, 1")
-        ins(f"setp.lt.u32 {p}, {i}, {n_blk}")
-        ins(f"@{p} bra {ptop}")
-        for s in range(min(KS, n_blk)):                   # drain: the last load of each slot landed
-            lp = t("b32")
-            ins(f"mov.u32 {lp}, {((n_blk - 1 - s) // KS) & 1}")
-            kit.wait(f"{bars}+{k_full[s]}", lp, 0)
-        for s in range(min(VS, n_blk)):
-            lp = t("b32")
-            ins(f"mov.u32 {lp}, {((n_blk - 1 - s) // VS) & 1}")
-            kit.wait(f"{bars}+{v_full[s]}", lp, 0)
+        ins(f"mad.lo.u32 {row}, {blk}, {BN}, {kvrow}")
+        ring(j, KS, k0, k_full[0], k_empty[0], "k", row)
+        ring(j, VS, v0, v_full[0], v_empty[0], "v", row)
+        ins(f"add.u32 {j}, {j}, 1")
+        ins(f"add.u32 {blk}, {blk}, 1")
+        ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
+        ins(f"@{p} bra {pblk}")
+        ins(f"add.u32 {ti}, {ti}, 1")
+        ins(f"add.u32 {tile}, {tile}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {ti}, {nt}")
+        ins(f"@{p} bra {ptile}")
         ins(f"bra {end}")
 
         # ---------------- MMA issuer (one warp) ----------------
@@ -330,8 +358,6 @@ class TcAttention(TunedKernel):
         ins(f"setp.eq.u32 {ism}, {lane}, 0")
         zero = t("b32")
         ins(f"mov.u32 {zero}, 0")
-        kit.wait(f"{bars}+{q_full}", zero, 1)
-        ins("tcgen05.fence::after_thread_sync")
         hi = t("b32")
         ins(f"mov.u32 {hi}, {desc_hi(1024)}")
         qdesc = [kit.desc_add(kit.desc(q_s, 16, hi), g * qb) for g in range(QT)]
@@ -341,15 +367,8 @@ class TcAttention(TunedKernel):
         ins(f"setp.eq.u32 {always}, {zero}, 0")
         ins(f"setp.ne.u32 {never}, {zero}, 0")
 
-        def k_slot(blk: str):
-            st_, ks_, kb_ = t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {blk}, {KS}")
-            ins(f"mad.lo.u32 {ks_}, {st_}, {kvb}, {k0}")
-            ins(f"mad.lo.u32 {kb_}, {st_}, 8, {bars}")
-            return ks_, kb_
-
-        def issue_s(g: int, blk: str, ks_: str, kb_: str, release_k: bool) -> None:
-            """S_g = Q_g K_blk^T (K slot already waited for)."""
+        def issue_s(g: int, ks_: str, kb_: str, release_k: bool) -> None:
+            """S_g = Q_g K^T for the K tile in slot ks_ (already waited for)."""
             kd = kit.desc(ks_, 16, hi)
             dcol = t("b32")
             ins(f"add.u32 {dcol}, {tmem}, {S_COL + 128 * g}")
@@ -362,24 +381,25 @@ class TcAttention(TunedKernel):
             if release_k:
                 ins(f"@{ism} {commit} [{kb_}+{k_empty[0]}]")
 
-        def wait_k(blk: str):
-            ks_, kb_ = k_slot(blk)
-            kf = t("b32")
+        def wait_k(jj: str):
+            st_, ks_, kb_, kf = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {st_}, {jj}, {KS}")
+            ins(f"mad.lo.u32 {ks_}, {st_}, {kvb}, {k0}")
+            ins(f"mad.lo.u32 {kb_}, {st_}, 8, {bars}")
             ins(f"add.u32 {kf}, {kb_}, {k_full[0]}")
-            kit.wait(kf, kit.parity(blk, KS), 1)
+            kit.wait(kf, kit.parity(jj, KS), 1)
             ins("tcgen05.fence::after_thread_sync")
             return ks_, kb_
 
-        def issue_pv(g: int, blk: str, first_block: bool, release_v: bool) -> None:
-            """O_g += P_g V_blk, P_g read from TMEM (the TS form)."""
-            kit.wait(f"{bars}+{p_full[g]}", kit.parity(blk, 1), 1)
+        def issue_pv(g: int, jj: str, acc0: str, release_v: bool) -> None:
+            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile."""
             st_, vs_, vb_ = t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {blk}, {VS}")
+            ins(f"rem.u32 {st_}, {jj}, {VS}")
             ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
             if g == 0:
                 vf = t("b32")
                 ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
-                kit.wait(vf, kit.parity(blk, VS), 1)
+                kit.wait(vf, kit.parity(jj, VS), 1)
             ins("tcgen05.fence::after_thread_sync")
             ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
             vd = kit.desc(vs_, BN * 128, hi)
@@ -389,46 +409,81 @@ class TcAttention(TunedKernel):
                 a = t("b32")
                 ins(f"add.u32 {a}, {tmem}, {S_COL + 128 * g + 8 * kk}")
                 bb = kit.desc_add(vd, kk * 16 * 128)
-                acc = never if (first_block and kk == 0) else always
-                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{a}], {bb}, {id_o}, {acc}")
+                ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{a}], {bb}, {id_o}, "
+                    f"{acc0 if kk == 0 else always}")
             ins(f"@{ism} {commit} [{bars}+{o_done[g]}]")
             if release_v:
                 ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
 
-        # S_g(0) for every group; then per block: PV_g(i), S_g(i + 1) for each group in turn
+        def q_released(jj: str) -> None:
+            """After the S of a tile's last key block: its Q tiles may be overwritten."""
+            if n_blk == 1:
+                ins(f"@{ism} {commit} [{bars}+{q_free}]")
+                return
+            r_, skipq = t("b32"), lab("at_q_keep")
+            ins(f"rem.u32 {r_}, {jj}, {n_blk}")
+            ins(f"setp.ne.u32 {p}, {r_}, {n_blk - 1}")
+            ins(f"@{p} bra {skipq}")
+            ins(f"@{ism} {commit} [{bars}+{q_free}]")
+            place(skipq)
+
+        # S_g(0) of the first tile; then per key block j: PV_g(j) and S_g(j + 1) for each group in
+        # turn -- S_g(j + 1) may already belong to the next tile (its Q is loaded once q_free fires)
+        kit.wait(f"{bars}+{q_full}", zero, 1)
+        ins("tcgen05.fence::after_thread_sync")
         ks_, kb_ = wait_k(zero)
         for g in range(QT):
-            issue_s(g, zero, ks_, kb_, g == QT - 1)
-        blk = t("b32")
-        ins(f"mov.u32 {blk}, 0")
+            issue_s(g, ks_, kb_, g == QT - 1)
+        q_released(zero)
+        mj, mblk, mti = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {mj}, 0")
+        ins(f"mov.u32 {mblk}, 0")
+        ins(f"mov.u32 {mti}, 0")
         mtop = lab("at_mma_k")
         place(mtop)
         nxt = t("b32")
-        ins(f"add.u32 {nxt}, {blk}, 1")
-        more = t("pred")
-        ins(f"setp.lt.u32 {more}, {nxt}, {n_blk}")
-        first_lab, rest_lab, join_lab = lab("at_pv_first"), lab("at_pv_rest"), lab("at_pv_join")
-        ins(f"setp.eq.u32 {p}, {blk}, 0")
-        ins(f"@!{p} bra {rest_lab}")
-        for first in (True, False):
-            if not first:
-                place(rest_lab)
-            for g in range(QT):
-                issue_pv(g, blk, first, g == QT - 1)
-                if g == 0:
-                    nk = lab("at_nok")
-                    ins(f"@!{more} bra {nk}")
-                    ks2, kb2 = wait_k(nxt)
-                    ins(f"mov.u32 {ks_}, {ks2}")
-                    ins(f"mov.u32 {kb_}, {kb2}")
-                    place(nk)
-                skip_s = lab("at_nos")
-                ins(f"@!{more} bra {skip_s}")
-                issue_s(g, nxt, ks_, kb_, g == QT - 1)
-                place(skip_s)
-            ins(f"bra {join_lab}")
-        place(join_lab)
-        ins(f"mov.u32 {blk}, {nxt}")
+        ins(f"add.u32 {nxt}, {mj}, 1")
+        more, acc0, newtile = t("pred"), t("pred"), t("pred")
+        ins(f"setp.lt.u32 {more}, {nxt}, {total}")
+        ins(f"setp.ne.u32 {acc0}, {mblk}, 0")
+        ins(f"setp.eq.u32 {newtile}, {mblk}, {n_blk - 1}")           # S(j + 1) opens the next tile
+        for g in range(QT):
+            kit.wait(f"{bars}+{p_full[g]}", kit.parity(mj, 1), 1)
+            nowait = lab("at_o_ready")
+            ins(f"@{acc0} bra {nowait}")
+            ins(f"setp.eq.u32 {p}, {mti}, 0")
+            ins(f"@{p} bra {nowait}")
+            pt = t("b32")
+            ins(f"sub.u32 {pt}, {mti}, 1")
+            kit.wait(f"{bars}+{o_free[g]}", kit.parity(pt, 1), 1)     # the previous tile's O_g was read
+            place(nowait)
+            issue_pv(g, mj, acc0, g == QT - 1)
+            if g == 0:
+                nk = lab("at_nok")
+                ins(f"@!{more} bra {nk}")
+                sameq = lab("at_same_q")
+                ins(f"@!{newtile} bra {sameq}")
+                nq = t("b32")
+                ins(f"add.u32 {nq}, {mti}, 1")
+                kit.wait(f"{bars}+{q_full}", kit.parity(nq, 1), 1)    # the next tile's Q landed
+                place(sameq)
+                ks2, kb2 = wait_k(nxt)
+                ins(f"mov.u32 {ks_}, {ks2}")
+                ins(f"mov.u32 {kb_}, {kb2}")
+                place(nk)
+            skip_s = lab("at_nos")
+            ins(f"@!{more} bra {skip_s}")
+            issue_s(g, ks_, kb_, g == QT - 1)
+            place(skip_s)
+        noq = lab("at_noq")
+        ins(f"@!{more} bra {noq}")
+        q_released(nxt)
+        place(noq)
+        ins(f"mov.u32 {mj}, {nxt}")
+        ins(f"add.u32 {mblk}, {mblk}, 1")
+        ins(f"setp.eq.u32 {p}, {mblk}, {n_blk}")
+        ins(f"@{p} add.u32 {mti}, {mti}, 1")
+        ins(f"@{p} mov.u32 {mblk}, 0")
         ins(f"@{more} bra {mtop}")
         ins(f"bra {end}")
 
@@ -448,19 +503,35 @@ class TcAttention(TunedKernel):
         ins(f"add.u32 {scol}, {ocol}, {S_COL}")
         ins(f"add.u32 {ocol}, {ocol}, {O_COL}")
         ins(f"mad.lo.u32 {gb8}, {grp}, 8, {bars}")
+        rowoff = t("b32")                                  # this thread's query row within the tile pair
+        ins(f"mad.lo.u32 {rowoff}, {grp}, {BM}, {r}")
+        wstage, srowa, r7 = t("b32"), t("b32"), t("b32")    # the warp's staging box and this row in it
+        ins(f"mad.lo.u32 {wstage}, {warp}, {32 * 128}, {stage0}")
+        ins(f"mad.lo.u32 {srowa}, {lane}, 128, {wstage}")
+        ins(f"and.b32 {r7}, {lane}, 7")
+        lead = t("pred")
+        ins(f"setp.eq.u32 {lead}, {lane}, 0")
+        tmap_o = t("b64")
+        ins("mov.u64 " + tmap_o + ", thc_tmap_o")
+        ins(f"cvta.global.u64 {tmap_o}, {tmap_o}")
         sc = t("f32")
         ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")
         ins(f"rcp.rn.f32 {sc}, {sc}")
         ins(f"mul.rn.f32 {sc}, {sc}, 0f{_f32bits(LOG2E)}")
         mref, mref8, l = t("f32"), t("f32"), t("f32")
+        sti, stile, sj, blk2 = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {sti}, 0")
+        ins(f"mov.u32 {stile}, {cta}")
+        ins(f"mov.u32 {sj}, 0")
+        stile_top = lab("at_sm_tile")
+        place(stile_top)
         ins(f"mov.f32 {mref}, 0fFF800000")
         ins(f"mov.f32 {mref8}, 0fFF800000")
         ins(f"mov.f32 {l}, 0f00000000")
-        blk2 = t("b32")
         ins(f"mov.u32 {blk2}, 0")
         stop = lab("at_sm_blk")
         place(stop)
-        kit.wait(f"{gb8}+{s_full[0]}", kit.parity(blk2, 1), 2)
+        kit.wait(f"{gb8}+{s_full[0]}", kit.parity(sj, 1), 2)
         ins("tcgen05.fence::after_thread_sync")
         # the row's 128 scores into registers: four loads in flight, one wait
         srow = [t("f32") for _ in range(BN)]
@@ -482,7 +553,7 @@ class TcAttention(TunedKernel):
         ins(f"setp.eq.u32 {p}, {blk2}, 0")
         ins(f"@{p} bra {noowait}")
         prevb = t("b32")
-        ins(f"sub.u32 {prevb}, {blk2}, 1")
+        ins(f"sub.u32 {prevb}, {sj}, 1")
         kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
         for c in range(D // 16):            # 16 columns at a time: the scores hold 128 registers
@@ -504,7 +575,7 @@ class TcAttention(TunedKernel):
         # P = 2^(s c' - m), 16 scores at a time, written back as f16 pairs over S's first 64 columns
         # (every score is already in registers, so the stores cannot overtake a load).  Pairs of
         # scores go through the packed f32x2 FMA pipe; POLY_PAIRS of every 8 pairs take 2^x from
-        # a polynomial on that pipe instead of the MUFU unit, which would otherwise bound the step.
+        # a polynomial on that pipe instead of the MUFU unit.
         pair = t("b64"), t("b64")
         ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
         ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
@@ -527,9 +598,9 @@ class TcAttention(TunedKernel):
                     ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
                 packs.append(d)
             sp = _tree(em, "add.rn.f32x2", packs, kind="b64")
-            lo, hi = t("f32"), t("f32")
-            ins(f"mov.b64 {{{lo}, {hi}}}, {sp}")
-            ins(f"add.rn.f32 {lo}, {lo}, {hi}")
+            lo, hi2 = t("f32"), t("f32")
+            ins(f"mov.b64 {{{lo}, {hi2}}}, {sp}")
+            ins(f"add.rn.f32 {lo}, {lo}, {hi2}")
             ins(f"add.rn.f32 {l}, {l}, {lo}")
             hp = [t("b32") for _ in range(8)]
             for k in range(8):
@@ -540,59 +611,57 @@ class TcAttention(TunedKernel):
         ins("tcgen05.wait::st.sync.aligned")
         ins("tcgen05.fence::before_thread_sync")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[0]}]")
+        ins(f"add.u32 {sj}, {sj}, 1")
         ins(f"add.u32 {blk2}, {blk2}, 1")
         ins(f"setp.lt.u32 {p}, {blk2}, {n_blk}")
         ins(f"@{p} bra {stop}")
-        # epilogue: O_g / l -> f16 -> 128B-swizzled tile over Q_g (idle now) -> TMA store
+        # epilogue: read O_g, hand its TMEM back to the MMA warp, then O / l -> f16 -> this row of
+        # the output with 16-byte stores (the TMEM and shared memory go on to the next tile)
         lastb = t("b32")
-        ins(f"mov.u32 {lastb}, {(n_blk - 1) & 1}")
-        kit.wait(f"{gb8}+{o_done[0]}", lastb, 3)
+        ins(f"sub.u32 {lastb}, {sj}, 1")
+        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
-        inv = t("f32")
-        ins(f"rcp.rn.f32 {inv}, {l}")
-        stg, r7 = t("b32"), t("b32")
-        ins(f"mad.lo.u32 {stg}, {grp}, {qb}, {q_s}")
-        ins(f"and.b32 {r7}, {r}, 7")
+        ov = [t("f32") for _ in range(D)]
         for c in range(D // 32):
-            ov = [t("f32") for _ in range(32)]
             a = t("b32")
             ins(f"add.u32 {a}, {ocol}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
-            ins("tcgen05.wait::ld.sync.aligned")
-            oh = [t("b32") for _ in range(16)]
-            for k in range(16):
-                ins(f"mul.rn.f32 {ov[2 * k]}, {ov[2 * k]}, {inv}")
-                ins(f"mul.rn.f32 {ov[2 * k + 1]}, {ov[2 * k + 1]}, {inv}")
-                ins(f"cvt.rn.f16x2.f32 {oh[k]}, {ov[2 * k + 1]}, {ov[2 * k]}")
-            # columns 32c .. 32c+31 are 16-byte chunks 4c' .. 4c'+3 of 64-column block c // 2
-            db, cc = c // 2, (c % 2) * 4
-            for j in range(4):
-                o = t("b32")
-                ins(f"xor.b32 {o}, {r7}, {cc + j}")
-                ins(f"shl.b32 {o}, {o}, 4")
-                ins(f"mad.lo.u32 {o}, {r}, 128, {o}")
-                ins(f"add.u32 {o}, {o}, {stg}")
-                ins(f"st.shared.v4.b32 [{o}+{db * BM * 128}], {{{', '.join(oh[4 * j:4 * j + 4])}}}")
-        ins("fence.proxy.async.shared::cta")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_staged[0]}]")
-        leader = t("pred")
-        lt_ = t("b32")
-        ins(f"and.b32 {lt_}, {warp}, 3")
-        ins(f"or.b32 {lt_}, {lt_}, {lane}")
-        ins(f"setp.eq.u32 {leader}, {lt_}, 0")          # lane 0 of each group's first warp
-        skip_store = lab("at_not_leader")
-        ins(f"@!{leader} bra {skip_store}")
-        zb = t("b32")
-        ins(f"mov.u32 {zb}, 0")
-        kit.wait(f"{gb8}+{o_staged[0]}", zb, 3)           # every row of this group's tile is staged
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
+        ins("tcgen05.wait::ld.sync.aligned")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
+        inv = t("f32")
+        ins(f"rcp.rn.f32 {inv}, {l}")
+        # 64 columns at a time: this row's 128 bytes into the warp's 32 x 128 B box (16-byte chunk c
+        # of row r at chunk c ^ (r % 8): the 128-byte swizzle, conflict-free), then lane 0 stores the
+        # box with TMA; the box is reused only after that store has read it
+        qrow_s, _ = tile_rows(stile)
         orow = t("b32")
-        ins(f"mad.lo.u32 {orow}, {grp}, {BM}, {qrow}")
-        for db in range(dblk):
-            ins(f"cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmaps['o']}, "
-                f"{{{db * 64}, {orow}}}], [{stg}+{db * BM * 128}]")
-        ins("cp.async.bulk.commit_group")
-        ins("cp.async.bulk.wait_group 0")
-        place(skip_store)
+        ins(f"add.u32 {orow}, {qrow_s}, {rowoff}")
+        ins(f"sub.u32 {orow}, {orow}, {lane}")                    # the warp's first row
+        for half in range(D // 64):
+            ins(f"@{lead} cp.async.bulk.wait_group.read 0")
+            ins("bar.warp.sync -1")
+            for c in range(8):
+                oh = [t("b32") for _ in range(4)]
+                for k in range(4):
+                    x0, x1 = ov[64 * half + 8 * c + 2 * k], ov[64 * half + 8 * c + 2 * k + 1]
+                    ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
+                    ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
+                    ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
+                ch = t("b32")
+                ins(f"xor.b32 {ch}, {r7}, {c}")
+                ins(f"mad.lo.u32 {ch}, {ch}, 16, {srowa}")
+                ins(f"st.shared.v4.b32 [{ch}], {{{', '.join(oh)}}}")
+            ins("fence.proxy.async.shared::cta")
+            ins("bar.warp.sync -1")
+            ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
+                f"{{{64 * half}, {orow}}}], [{wstage}]")
+            ins(f"@{lead} cp.async.bulk.commit_group")
+        ins(f"add.u32 {sti}, {sti}, 1")
+        ins(f"add.u32 {stile}, {stile}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {sti}, {nt}")
+        ins(f"@{p} bra {stile_top}")
+        ins(f"@{lead} cp.async.bulk.wait_group 0")               # the output stores are complete
 
         # ---------------- common exit ----------------
         place(end)
