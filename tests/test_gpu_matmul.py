@@ -80,3 +80,32 @@ def test_matmul_benchmark_shapes(tmp_path, M, N, K):
     assert torch.equal(c1, c1b)
     tuned.close()
     generic.close()
+
+
+@pytest.mark.parametrize("grid", [0, 5])
+def test_matmul_split_tail(tmp_path, grid):
+    """More tiles than SMs with a partial last wave (2048 x 2560 x 2048: 160 tiles of 128 x 256,
+    12 left over): those are cut along K into parts whose partials meet in the module's
+    workspace, the last part to arrive adding them in part order.  grid 5 puts several whole
+    tiles and several parts on each CTA (the arrival barriers' phases carry over)."""
+    import torch
+    M, N, K = 2048, 2560, 2048
+    d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
+    k = DeviceKernel(d / "k_matmul_f16.ir.json")
+    assert "thc_tail_ws" in k.ptx
+    if grid:
+        k.plan.grid = (grid, 1, 1)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    outs = []
+    for _ in range(2):
+        c = torch.full((M, N), float("nan"), device="cuda")
+        k({"x0": a.data_ptr(), "x1": b.data_ptr(), "matmul": c.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        outs.append(c)
+    assert runner.read_error_word(k.module, k.plan) == 0
+    ref = a.double() @ b.double().t()
+    assert (outs[0].double() - ref).abs().max().item() < 1e-4
+    assert torch.equal(outs[0], outs[1])                 # the part order fixes the rounding
+    k.close()

@@ -91,6 +91,18 @@ class TcMatmul(TunedKernel):
         self.smem = self.stages * stage + self.staging + 1024 + 256
         self.tiles = (M // BM) * (N // self.BN) * S
         self.ctas = min(self.tiles, SM_COUNT)
+        # the last, partial wave: its `rem` tiles are cut along K into `parts` units each, so one
+        # round of 1/parts of a tile replaces a round of whole tiles on `rem` of the SMs
+        kblocks = self.Ks // BK
+        rem = self.tiles % SM_COUNT if self.tiles > SM_COUNT else 0
+        # a part must be long enough to pay for its partial's round trip through L2: the last part
+        # to arrive reads all `parts` partials (128 KB each at N = 256), so at least 16 K blocks
+        parts = min(kblocks // 16, SM_COUNT // rem) if rem else 1
+        if S != 1 or c.ty is not F32 or parts < 2 or os.environ.get("THOMPILER_MATMUL_SPLIT_TAIL") == "0":
+            rem, parts = 0, 1
+        self.rem, self.parts = rem, parts
+        self.full_tiles = self.tiles - rem
+        self.units = self.full_tiles + rem * parts
 
     def pick_bn(self) -> int:
         forced = int(os.environ.get("THOMPILER_MATMUL_BN", "0"))     # tuning knob: force the tile width
@@ -202,6 +214,9 @@ class TcMatmul(TunedKernel):
         em.module(".global .align 64 .b8 thc_tmap_c[128]")
         em.module(".global .align 8 .u64 thc_tmap_ptr[3]")
         em.module(".global .align 4 .u32 thc_error")
+        if self.rem:
+            em.module(f".global .align 4 .u32 thc_tile_arrivals[{self.rem}]")
+            em.module(f".global .align 16 .b8 thc_tail_ws[{self.rem * self.parts * BM * self.BN * 4}]")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
@@ -237,8 +252,9 @@ class TcMatmul(TunedKernel):
         a_st = base
         b_st = t("b32")
         ins(f"add.u32 {b_st}, {base}, {ST * a_bytes}")
+        # shared: A stages | B stages | epilogue staging (2 x 2 KB per epilogue warp) | barriers
         bars = t("b32")
-        ins(f"add.u32 {bars}, {base}, {ST * (a_bytes + b_bytes)}")
+        ins(f"add.u32 {bars}, {base}, {ST * (a_bytes + b_bytes) + self.staging}")
         full = lambda s: f"{bars}+{8 * s}"                  # noqa: E731
         empty_off, accf_off, acce_off, slot_off = 8 * ST, 16 * ST, 16 * ST + 16, 16 * ST + 32
         p, q = t("pred"), t("pred")
@@ -252,6 +268,10 @@ class TcMatmul(TunedKernel):
         for b in range(2):
             ins(f"mbarrier.init.shared::cta.b64 [{bars}+{accf_off + 8 * b}], 1")
             ins(f"mbarrier.init.shared::cta.b64 [{bars}+{acce_off + 8 * b}], 128")
+        tail_done_off, tail_last_off, tail_flag_off = 16 * ST + 40, 16 * ST + 48, 16 * ST + 56
+        if self.rem:
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{tail_done_off}], 128")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{tail_last_off}], 1")
         ins("fence.mbarrier_init.release.cluster")
         ins("fence.proxy.async.shared::cta")
         place(skip)
@@ -310,6 +330,28 @@ class TcMatmul(TunedKernel):
             ins(f"div.u32 {ts_}, {r}, {tiles_n}")
             return tm_, tn_, ts_
 
+        units, full_tiles, parts = self.units, self.full_tiles, self.parts
+
+        def unit(u: str):
+            """Work unit u -> (tile, first and end K block, is-whole-tile predicate, part):
+            units below full_tiles are whole tiles, the rest cut the last tiles along K."""
+            tile_, lo, hi_, part, v, whole = t("b32"), t("b32"), t("b32"), t("b32"), t("b32"), t("pred")
+            ins(f"setp.lt.u32 {whole}, {u}, {full_tiles}")
+            ins(f"mov.u32 {tile_}, {u}")
+            ins(f"mov.u32 {lo}, 0")
+            ins(f"mov.u32 {hi_}, {kblocks}")
+            ins(f"mov.u32 {part}, 0")
+            if self.rem:
+                ins(f"sub.u32 {v}, {u}, {full_tiles}")
+                ins(f"@!{whole} div.u32 {tile_}, {v}, {parts}")
+                ins(f"@!{whole} add.u32 {tile_}, {tile_}, {full_tiles}")
+                ins(f"@!{whole} rem.u32 {part}, {v}, {parts}")
+                ins(f"@!{whole} mul.lo.u32 {lo}, {part}, {kblocks}")
+                ins(f"@!{whole} div.u32 {lo}, {lo}, {parts}")
+                ins(f"@!{whole} mad.lo.u32 {hi_}, {part}, {kblocks}, {kblocks}")
+                ins(f"@!{whole} div.u32 {hi_}, {hi_}, {parts}")
+            return tile_, lo, hi_, whole, part
+
         role_mma, role_epi = lab("mm_mma"), lab("mm_epi")
         ins(f"setp.eq.u32 {p}, {warp}, 1")
         ins(f"@{p} bra {role_mma}")
@@ -319,20 +361,19 @@ class TcMatmul(TunedKernel):
         # ---------------- producer (warp 0) ----------------
         is0 = t("pred")
         ins(f"setp.eq.u32 {is0}, {lane}, 0")
-        it, tile = t("b32"), t("b32")
+        it, pu = t("b32"), t("b32")
         ins(f"mov.u32 {it}, 0")
-        ins(f"mov.u32 {tile}, {cta}")
+        ins(f"mov.u32 {pu}, {cta}")
         ptop, pdone = lab("prod_tile"), lab("prod_done")
-        ins(f"setp.ge.u32 {p}, {tile}, {tiles}")
+        ins(f"setp.ge.u32 {p}, {pu}, {units}")
         ins(f"@{p} bra {pdone}")
         place(ptop)
+        tile, kb, kend, _, _ = unit(pu)
         tm_, tn_, ts_ = decode(tile)
         m0, n0, k0 = t("b32"), t("b32"), t("b32")
         ins(f"mul.lo.u32 {m0}, {tm_}, {BM}")
         ins(f"mul.lo.u32 {n0}, {tn_}, {BN}")
         ins(f"mul.lo.u32 {k0}, {ts_}, {self.Ks}")
-        kb = t("b32")
-        ins(f"mov.u32 {kb}, 0")
         ktop = lab("prod_k")
         place(ktop)
         stage, ph, par = t("b32"), t("b32"), t("b32")
@@ -361,10 +402,10 @@ class TcMatmul(TunedKernel):
                     f"[{sb}+{nb * 64 * BK * 2}], [{tmb}, {{{nn}, {kc}}}], [{eb}]")
         ins(f"add.u32 {it}, {it}, 1")
         ins(f"add.u32 {kb}, {kb}, 1")
-        ins(f"setp.lt.u32 {p}, {kb}, {kblocks}")
+        ins(f"setp.lt.u32 {p}, {kb}, {kend}")
         ins(f"@{p} bra {ktop}")
-        ins(f"add.u32 {tile}, {tile}, {ncta}")
-        ins(f"setp.lt.u32 {p}, {tile}, {tiles}")
+        ins(f"add.u32 {pu}, {pu}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {pu}, {units}")
         ins(f"@{p} bra {ptop}")
         place(pdone)
         # drain: every stage's last load has landed before the CTA may leave
@@ -385,14 +426,17 @@ class TcMatmul(TunedKernel):
         place(role_mma)
         ism = t("pred")
         ins(f"setp.eq.u32 {ism}, {lane}, 0")
-        it2, tile2, lt = t("b32"), t("b32"), t("b32")
+        it2, mu, lt = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {it2}, 0")
         ins(f"mov.u32 {lt}, 0")
-        ins(f"mov.u32 {tile2}, {cta}")
+        ins(f"mov.u32 {mu}, {cta}")
         mtop, mdone = lab("mma_tile"), lab("mma_done")
-        ins(f"setp.ge.u32 {p}, {tile2}, {tiles}")
+        ins(f"setp.ge.u32 {p}, {mu}, {units}")
         ins(f"@{p} bra {mdone}")
         place(mtop)
+        _, kb2, kend2, _, _ = unit(mu)
+        kfirst = t("b32")
+        ins(f"mov.u32 {kfirst}, {kb2}")
         buf, use, upar, apar = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"and.b32 {buf}, {lt}, 1")
         ins(f"shr.u32 {use}, {lt}, 1")
@@ -404,8 +448,6 @@ class TcMatmul(TunedKernel):
         ins("tcgen05.fence::after_thread_sync")
         dt = t("b32")
         ins(f"mad.lo.u32 {dt}, {buf}, {BN}, {tmem}")
-        kb2 = t("b32")
-        ins(f"mov.u32 {kb2}, 0")
         mk = lab("mma_k")
         place(mk)
         st2, ph2 = t("b32"), t("b32")
@@ -432,7 +474,7 @@ class TcMatmul(TunedKernel):
         b_hi = _desc_hi(1024)
         idesc = idesc_f16(BN, not self.b_kmajor)
         acc0, always = t("pred"), t("pred")
-        ins(f"setp.ne.u32 {acc0}, {kb2}, 0")          # the tile's first MMA overwrites the accumulator
+        ins(f"setp.ne.u32 {acc0}, {kb2}, {kfirst}")   # the unit's first MMA overwrites the accumulator
         ins(f"setp.eq.u32 {always}, {kb2}, {kb2}")
         hi_a, hi_b = t("b32"), t("b32")
         ins(f"mov.u32 {hi_a}, {a_hi}")
@@ -450,12 +492,12 @@ class TcMatmul(TunedKernel):
         ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{fb}+{empty_off}]")
         ins(f"add.u32 {it2}, {it2}, 1")
         ins(f"add.u32 {kb2}, {kb2}, 1")
-        ins(f"setp.lt.u32 {p}, {kb2}, {kblocks}")
+        ins(f"setp.lt.u32 {p}, {kb2}, {kend2}")
         ins(f"@{p} bra {mk}")
         ins(f"@{ism} tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ab}+{accf_off}]")
         ins(f"add.u32 {lt}, {lt}, 1")
-        ins(f"add.u32 {tile2}, {tile2}, {ncta}")
-        ins(f"setp.lt.u32 {p}, {tile2}, {tiles}")
+        ins(f"add.u32 {mu}, {mu}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {mu}, {units}")
         ins(f"@{p} bra {mtop}")
         place(mdone)
         ins(f"bra {end}")
@@ -485,13 +527,15 @@ class TcMatmul(TunedKernel):
             ins(f"shl.b32 {o}, {o}, 4")
             ins(f"mad.lo.u32 {o}, {lane}, 64, {o}")
             soff.append(o)
-        tile3, lt3 = t("b32"), t("b32")
+        eu, lt3, ls = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {lt3}, 0")
-        ins(f"mov.u32 {tile3}, {cta}")
-        etop, edone = lab("epi_tile"), lab("epi_done")
-        ins(f"setp.ge.u32 {p}, {tile3}, {tiles}")
+        ins(f"mov.u32 {ls}, 0")
+        ins(f"mov.u32 {eu}, {cta}")
+        etop, edone, enext = lab("epi_tile"), lab("epi_done"), lab("epi_next")
+        ins(f"setp.ge.u32 {p}, {eu}, {units}")
         ins(f"@{p} bra {edone}")
         place(etop)
+        tile3, _, _, whole3, part3 = unit(eu)
         tm3, tn3, ts3 = decode(tile3)
         buf3, use3, par3 = t("b32"), t("b32"), t("b32")
         ins(f"and.b32 {buf3}, {lt3}, 1")
@@ -515,10 +559,28 @@ class TcMatmul(TunedKernel):
         ins(f"mad.lo.u32 {row0}, {tm3}, {BM}, {row0}")
         ins(f"mad.lo.u32 {row0}, {quarter}, 32, {row0}")
         ins(f"mul.lo.u32 {col0}, {tn3}, {BN}")
-        for j, c0 in enumerate(range(0, BN, cw)):
-            sbuf = stage_buf[j % 2]
-            ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
-            ins("bar.warp.sync -1")
+
+        def store_boxes(values) -> None:
+            """Columns c0 .. c0 + cw of this warp's 32 rows, for each c0: ``values(c0)`` gives the
+            row's cw values as b32 registers (f32, or f16 pairs), staged and stored with TMA."""
+            for j, c0 in enumerate(range(0, BN, cw)):
+                sbuf = stage_buf[j % 2]
+                ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
+                ins("bar.warp.sync -1")
+                v = values(c0)
+                for i in range(4):
+                    a_ = t("b32")
+                    ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
+                    ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+                ins("fence.proxy.async.shared::cta")
+                ins("bar.warp.sync -1")
+                cc = t("b32")
+                ins(f"add.u32 {cc}, {col0}, {c0}")
+                ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], "
+                    f"[{sbuf}]")
+                ins(f"@{lane0} cp.async.bulk.commit_group")
+
+        def from_tmem(c0):
             nv = 16 if esz == 4 else 32
             v = [t("b32") for _ in range(nv)]
             tc = t("b32")
@@ -530,21 +592,22 @@ class TcMatmul(TunedKernel):
                 for i in range(16):
                     ins(f"cvt.rn.f16x2.f32 {h[i]}, {v[2 * i + 1]}, {v[2 * i]}")
                 v = h
-            for i in range(4):
-                a_ = t("b32")
-                ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
-                ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
-            ins("fence.proxy.async.shared::cta")
-            ins("bar.warp.sync -1")
-            cc = t("b32")
-            ins(f"add.u32 {cc}, {col0}, {c0}")
-            ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], [{sbuf}]")
-            ins(f"@{lane0} cp.async.bulk.commit_group")
+            return v
+
+        tail = lab("epi_tail")
+        if self.rem:
+            ins(f"@!{whole3} bra {tail}")
+        store_boxes(from_tmem)
         ins("tcgen05.fence::before_thread_sync")
         ins(f"mbarrier.arrive.shared::cta.b64 _, [{ab3}+{acce_off}]")
+        if self.rem:
+            ins(f"bra {enext}")
+            self._tail_epilogue(tail, enext, tile3, part3, taddr, ab3, row, lane, bars, ls, store_boxes,
+                                acce_off, tail_done_off, tail_last_off, tail_flag_off, wait, p)
+        place(enext)
         ins(f"add.u32 {lt3}, {lt3}, 1")
-        ins(f"add.u32 {tile3}, {tile3}, {ncta}")
-        ins(f"setp.lt.u32 {p}, {tile3}, {tiles}")
+        ins(f"add.u32 {eu}, {eu}, {ncta}")
+        ins(f"setp.lt.u32 {p}, {eu}, {units}")
         ins(f"@{p} bra {etop}")
         place(edone)
         ins(f"@{lane0} cp.async.bulk.wait_group 0")       # stores done before the CTA leaves
@@ -558,6 +621,85 @@ class TcMatmul(TunedKernel):
         ins("tcgen05.fence::after_thread_sync")
         ins(f"tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tmem}, {tmem_cols}")
         place(nodealloc)
+
+
+    def _tail_epilogue(self, tail, enext, tile3, part3, taddr, ab3, row, lane, bars, ls, store_boxes,
+                       acce_off, done_off, last_off, flag_off, wait, p) -> None:
+        """A K part of one of the last tiles: its partial goes to the module workspace, and the
+        part that arrives last adds all parts in part order (deterministic) and stores C.
+
+        Workspace layout, per (tile, part) slot: [BN / 4 chunks][128 rows] of 16-byte chunks, so a
+        warp's store or load of one chunk index touches 512 contiguous bytes.  Arrival: every
+        epilogue thread fences its stores and arrives on a CTA mbarrier; thread 0 then bumps the
+        tile's counter (``atom.acq_rel.gpu.inc`` wrapping at parts - 1: self-resetting) and
+        publishes whether it was the last through shared memory.  No CTA waits for another."""
+        em, ins, t, place = self.em, self.em.ins, self.em.tmp, self.em.place
+        BN, parts = self.BN, self.parts
+        place(tail)
+        slot, ws, cnt = t("b32"), t("b64"), t("b64")
+        ins(f"sub.u32 {slot}, {tile3}, {self.full_tiles}")
+        ins(f"mov.u64 {cnt}, thc_tile_arrivals")
+        ins(f"mad.wide.u32 {cnt}, {slot}, 4, {cnt}")
+        ins(f"mad.lo.u32 {slot}, {slot}, {parts}, {part3}")
+        ins("mov.u64 " + ws + ", thc_tail_ws")
+        rowb = t("b64")                                   # this row's first chunk, 16 bytes apart per row
+        ins(f"mul.wide.u32 {rowb}, {row}, 16")
+        ins(f"add.u64 {rowb}, {rowb}, {ws}")
+        mine = t("b64")
+        ins(f"mul.wide.u32 {mine}, {slot}, {BN // 4 * 128 * 16}")
+        ins(f"add.u64 {mine}, {mine}, {rowb}")
+        for c0 in range(0, BN, 16):
+            v = [t("b32") for _ in range(16)]
+            tc = t("b32")
+            ins(f"add.u32 {tc}, {taddr}, {c0}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x16.b32 {{{', '.join(v)}}}, [{tc}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            for i in range(4):
+                ins(f"st.global.v4.b32 [{mine}+{(c0 // 4 + i) * 128 * 16}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{ab3}+{acce_off}]")      # the accumulator is free
+        ins("fence.acq_rel.gpu")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{done_off}]")
+        par, lead, flag = t("b32"), t("pred"), t("b32")
+        ins(f"and.b32 {par}, {ls}, 1")
+        ins(f"add.u32 {ls}, {ls}, 1")
+        ins(f"setp.eq.u32 {lead}, {row}, 0")
+        notlead = em.label("tail_notlead")
+        ins(f"@!{lead} bra {notlead}")
+        wait(f"{bars}+{done_off}", par, 3)                 # all 128 rows of the partial are stored
+        old = t("b32")
+        ins(f"atom.acq_rel.gpu.global.inc.u32 {old}, [{cnt}], {parts - 1}")
+        ins(f"setp.eq.u32 {p}, {old}, {parts - 1}")
+        ins(f"selp.u32 {flag}, 1, 0, {p}")
+        ins(f"st.shared.u32 [{bars}+{flag_off}], {flag}")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{last_off}]")
+        place(notlead)
+        wait(f"{bars}+{last_off}", par, 3)
+        ins(f"ld.shared.u32 {flag}, [{bars}+{flag_off}]")
+        ins(f"setp.eq.u32 {p}, {flag}, 0")
+        ins(f"@{p} bra {enext}")
+        ins("fence.acq_rel.gpu")
+        first = t("b64")                                   # part 0 of this tile
+        ins(f"sub.u32 {slot}, {slot}, {part3}")
+        ins(f"mul.wide.u32 {first}, {slot}, {BN // 4 * 128 * 16}")
+        ins(f"add.u64 {first}, {first}, {rowb}")
+
+        def summed(c0):
+            acc = [t("f32") for _ in range(16)]
+            for pp in range(parts):
+                for i in range(4):
+                    off = pp * (BN // 4 * 128 * 16) + (c0 // 4 + i) * 128 * 16
+                    v = acc[4 * i:4 * i + 4] if pp == 0 else [t("f32") for _ in range(4)]
+                    ins(f"ld.global.cg.v4.f32 {{{', '.join(v)}}}, [{first}+{off}]")
+                    if pp:
+                        for a_, b_ in zip(acc[4 * i:4 * i + 4], v):
+                            ins(f"add.rn.f32 {a_}, {a_}, {b_}")
+            out = [t("b32") for _ in range(16)]
+            for o_, a_ in zip(out, acc):
+                ins(f"mov.b32 {o_}, {a_}")
+            return out
+
+        store_boxes(summed)
 
 
 def recognise(kernel: KernelInfo):
