@@ -661,6 +661,8 @@ def main() -> None:
     ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the timed steps one by one instead of replaying CUDA graphs")
     ap.add_argument("--collective", default="peer", choices=["peer", "nccl"],
                     help="bigsum's exchange step: in-kernel peer combine (default) or an NCCL all-reduce")
     ap.add_argument("--size", type=int, default=0,
@@ -693,27 +695,55 @@ def main() -> None:
     w.check()
     for _ in range(args.warmup):
         w.step(stream)
+    # per-kernel durations: CUDA events around every launch of an untimed pass on the launch stream
+    n_ev = min(args.steps, 200)
     events = {k: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(args.steps)] for k in w.kinds}
+                  for _ in range(n_ev)] for k in w.kinds}
+    for i in range(n_ev):
+        w.step(stream, {k: events[k][i] for k in w.kinds})
+    torch.cuda.synchronize()
+    per_kernel = {k: statistics.mean(a.elapsed_time(b) for a, b in events[k]) for k in w.kinds}
+    # the timed region: the K steps replayed from CUDA graphs of G steps each (no host launch
+    # overhead between kernels), or launched one by one when a step holds an NCCL collective
+    use_graph = not args.no_graph and getattr(w, "collective", None) != "nccl"
+    graph, G = None, 1
+    if use_graph:
+        G = next(g for g in range(min(args.steps, 500), 0, -1) if args.steps % g == 0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            cap = torch.cuda.current_stream().cuda_stream
+            for _ in range(G):
+                w.step(cap)
+        graph.replay()
+        torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     start.record()
-    for i in range(args.steps):
-        w.step(stream, {k: events[k][i] for k in w.kinds})
+    if graph is not None:
+        for _ in range(args.steps // G):
+            graph.replay()
+    else:
+        for _ in range(args.steps):
+            w.step(stream)
     end.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
     if world > 1:
         dist.barrier()
     ms = start.elapsed_time(end) / args.steps
+    if graph is not None:
+        # kernels run back to back inside the graphs: share the timed step among them in the
+        # proportions of their event-timed durations (one kernel per step: the step itself)
+        tot = sum(per_kernel.values())
+        per_kernel = {k: ms * v / tot for k, v in per_kernel.items()}
+    del graph
     t = torch.tensor([ms], device=f"cuda:{local}")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    per_kernel = {k: statistics.mean(a.elapsed_time(b) for a, b in events[k]) for k in w.kinds}
     e2e = None
     if not args.no_e2e:
         e2e = w.e2e(max(1, min(args.steps, 5)))
@@ -745,6 +775,9 @@ def main() -> None:
                     "frac": achieved / pk["hbm_gbs"], "traffic": traffic}
         roof.update(kernel=kernel_name, peak_source=pk["source"], kernel_ms=kms, per_kernel_ms=per_kernel)
         cfg = w.config(world)
+        how = f"{args.steps // G} replays of a CUDA graph of {G} steps" if use_graph else "steps launched one by one"
+        cfg["timing"] = how + ("; per-kernel times: the timed step shared in the proportions of per-launch "
+                               "CUDA events" if use_graph else "; per-kernel times from per-launch CUDA events")
         if hasattr(w, "reference_lowering"):
             cfg["reference_lowering"] = w.reference_lowering()
         line = {
