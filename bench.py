@@ -1,6 +1,6 @@
 """Benchmark: emitted sm_100a kernels on the benchmark workloads.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config rowops|sum|bigsum|matmul|attention]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config rowops|sum|bigsum|matmul|attention|pointwise]
     python bench.py --impl reference ...       # the reference's CPU path (bounded sample, <= ~90 s)
 
 A step is one pass of the hot path over one batch of synthetic input:
@@ -19,6 +19,8 @@ A step is one pass of the hot path over one batch of synthetic input:
           the tcgen05 matmul family; N GPUs run replicas (weak scaling).
   attention  softmax(Q K^T / sqrt(d)) V, f16 [8, 16, 2048, 128] on the tcgen05
           attention family; the 128 (batch, head) units split over N GPUs.
+  pointwise  relu(x0) * x1 on f32[2^28] in the p03 schedule (vectorised
+          pointwise family); N GPUs run replicas.
 
 value is the whole-job algorithmic HBM bandwidth (bytes the workload must
 move / max-over-ranks device time of the K steps, CUDA events on the launch
@@ -243,6 +245,101 @@ class RowOps:
                 "kernels": {k: self.k[k].family for k in self.kinds},
                 "l2": "inputs larger than L2 (3 x 128 MiB distinct input matrices per GPU)",
                 "parallelism": f"weak: {world} GPU(s), one matrix set each, no collective"}
+
+
+class Pointwise:
+    """relu(x0) * x1 over f32[2^28] (the p03 schedule: 4 elements per thread, 1 GiB per operand,
+    3 GiB per step, larger than L2); N GPUs run replicas."""
+    name = "pointwise"
+    metric = "achieved HBM GB/s (pointwise relu(x0) * x1, f32)"
+    unit = "GB/s"
+    dtype = "f32"
+
+    def __init__(self, rank: int, world: int, dev: int, n: int = 0):
+        import torch
+        from thompiler import synth
+        from thompiler.device import DeviceKernel
+        self.torch, self.n = torch, n or 1 << 28
+        d = synth.pointwise_package(Path(tempfile.mkdtemp(prefix=f"bench_pw_{rank}_")) / "pw", self.n, "relu_mul")
+        self.k = DeviceKernel(d / "k_mul_pointwise.ir.json", device=dev)
+        g = torch.Generator(device=f"cuda:{dev}").manual_seed(4000 + rank)
+        self.x0 = torch.randn(self.n, device=f"cuda:{dev}", generator=g)
+        self.x1 = torch.randn(self.n, device=f"cuda:{dev}", generator=g)
+        self.y = torch.empty(self.n, device=f"cuda:{dev}")
+        self.kinds = ("pointwise",)
+        self.kbytes = {"pointwise": 12 * self.n}
+        self.bytes_per_step = 12 * self.n
+        self.launches_per_step = 1
+        self.dominant = "pointwise"
+
+    def ptrs(self) -> dict:
+        return {"x0": self.x0.data_ptr(), "x1": self.x1.data_ptr(), "mul": self.y.data_ptr()}
+
+    def step(self, stream: int, events=None) -> None:
+        if events is not None:
+            events["pointwise"][0].record()
+        self.k(self.ptrs(), stream)
+        if events is not None:
+            events["pointwise"][1].record()
+
+    def check(self) -> None:
+        torch = self.torch
+        self.step(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert torch.equal(self.y, torch.relu(self.x0) * self.x1), "pointwise mismatch"
+
+    def e2e(self, steps: int) -> dict:
+        from thompiler import runner
+        torch = self.torch
+        m = min(self.n, 1 << 26)                   # host copies of 3 x 256 MiB per step
+        h = [torch.empty(m, pin_memory=True) for _ in range(3)]
+        h[0].copy_(self.x0[:m])
+        h[1].copy_(self.x1[:m])
+        from thompiler import synth
+        d = synth.pointwise_package(Path(tempfile.mkdtemp(prefix="bench_pw_e2e_")) / "pw", m, "relu_mul")
+        from thompiler.device import DeviceKernel
+        k = DeviceKernel(d / "k_mul_pointwise.ir.json")
+        args = [{"array": h[0].numpy()}, {"array": h[1].numpy()}, {"array": h[2].numpy(), "output": True}]
+        runner.run(k.fn, k.plan, args, arg_order=k.arg_order)
+        t = time.perf_counter()
+        for _ in range(steps):
+            r = runner.run(k.fn, k.plan, args, arg_order=k.arg_order)
+            if not r["ok"]:
+                raise RuntimeError(r["stderr"])
+        sec = (time.perf_counter() - t) / steps
+        runner.release()
+        k.close()
+        return {"value": 12 * m / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 8 * m,
+                "d2h_bytes_per_step": 4 * m, "ms_per_step": sec * 1e3, "elements": m}
+
+    def cpu_baseline(self) -> dict:
+        from oracle import cpu_baseline
+        r = cpu_baseline.pointwise_sample(1 << 24)
+        return {"value": 12 * (1 << 24) / r["seconds"] / 1e9, "unit": "GB/s", "cores": r["cores"],
+                "kind": "port", "sample": "torch CPU relu(x0) * x1 on f32[2^24], best of 3"}
+
+    def reference_lowering(self) -> dict:
+        """The same IR through the statement-by-statement lowering (scalar 4-byte accesses)."""
+        from thompiler.device import DeviceKernel
+        torch = self.torch
+        gk = DeviceKernel(self.k.ir_path, tuned=False)
+        s = torch.cuda.current_stream().cuda_stream
+        for _ in range(3):
+            gk(self.ptrs(), s)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            gk(self.ptrs(), s)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        gk.close()
+        return {"ms": ms, "gbs": 12 * self.n / ms / 1e6}
+
+    def config(self, world: int) -> dict:
+        return {"workload": f"pointwise relu(x0) * x1, f32[{self.n}] N(0,1), p03 schedule (4 per thread)",
+                "kernel": self.k.family, "l2": "operands (3 GiB per step) far exceed L2; no flush",
+                "parallelism": f"replicas over {world} GPU(s)"}
 
 
 BIGSUM_METRIC = "achieved HBM GB/s (sharded sum: per-GPU reduction + cross-GPU combine)"
@@ -572,9 +669,11 @@ class Attention:
 
 
 # about one second of timed work per workload at one GPU (the clock sampler needs a region that long)
-DEFAULT_STEPS = {"rowops": 6000, "sum": 20000, "bigsum": 1500, "matmul": 5000, "attention": 2500}
+DEFAULT_STEPS = {"rowops": 6000, "sum": 20000, "bigsum": 1500, "matmul": 5000, "attention": 2500,
+                 "pointwise": 2000}
 
 CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
+           "pointwise": lambda r, w, d, n: Pointwise(r, w, d, n),
            "attention": lambda r, w, d, n: Attention(r, w, d, n),
            "matmul": lambda r, w, d, n: Matmul(r, w, d, n),
            "sum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 20),
@@ -601,6 +700,14 @@ def reference_arm(args, out=None) -> None:
         metric, scaling = RowOps.metric, "weak"
         config = {"workload": "fused row ops f32[8192, 4096] x3 (softmax, rmsnorm eps=1e-6, l2norm)",
                   "sample_rows": rows}
+    elif cfg == "pointwise":
+        m_ = 1 << 24
+        run = lambda: cpu_baseline.pointwise_sample(m_)                  # noqa: E731
+        work, unit, scale, dtype = 12 * m_, "GB/s", 1e9, "f32"
+        sample = f"torch CPU relu(x0) * x1 on f32[{m_}] (1/16 of a step)"
+        metric, scaling = Pointwise.metric, "weak"
+        config = {"workload": "pointwise relu(x0) * x1, f32[268435456] N(0,1), p03 schedule (4 per thread)",
+                  "sample_elements": m_}
     elif cfg == "matmul":
         m = n = k = 1024
         run = lambda: cpu_baseline.matmul_sample(m, n, k)                # noqa: E731

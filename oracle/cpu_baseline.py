@@ -72,6 +72,15 @@ def sum_sample(n_elems: int, seed: int = 0) -> dict:
     return {"seconds": sec, "elements": n_elems, "cores": n}
 
 
+def pointwise_sample(n_elems: int, seed: int = 0) -> dict:
+    """relu(x0) * x1 (problems/p03_relu_mul's expression) on f32[n_elems]."""
+    c = threads()
+    g = torch.Generator().manual_seed(seed)
+    x0, x1 = torch.randn(n_elems, generator=g), torch.randn(n_elems, generator=g)
+    sec = time_call(lambda: torch.relu(x0) * x1)
+    return {"seconds": sec, "elements": n_elems, "cores": c}
+
+
 def matmul_sample(m: int, n: int, k: int, seed: int = 0) -> dict:
     c = threads()
     g = torch.Generator().manual_seed(seed)

@@ -13,6 +13,7 @@ pointer changes.
 from __future__ import annotations
 
 import json
+import re
 from pathlib import Path
 
 from thompiler import runner
@@ -23,7 +24,7 @@ from thompiler.load import load
 class DeviceKernel:
     def __init__(self, ir_path: str | Path, device: int = 0, honour_meta: bool = False, tuned: bool = True,
                  ptx: str | None = None):
-        ir_path = Path(ir_path)
+        ir_path = self.ir_path = Path(ir_path)
         meta = json.loads((ir_path.parent / "meta.json").read_text())
         self.info = load(ir_path, meta)
         self.kmeta = next(k for k in meta["kernels"] if k["entry"] == self.info.name)
@@ -37,7 +38,10 @@ class DeviceKernel:
     @property
     def family(self) -> str:
         side = self.module.sidecar or {}
-        return side.get("family", "generic") if side else ("tuned" if "family:" in self.ptx else "generic")
+        if side.get("family"):
+            return side["family"]
+        m = re.search(r"// family: ([\w-]+)", self.ptx)
+        return m.group(1) if m else "generic"
 
     def __call__(self, ptrs: dict[str, int], stream: int = 0) -> None:
         if self.plan.tmaps and ptrs != self._tmap_ptrs:

@@ -166,6 +166,43 @@ def sum_package(outdir, n: int, kind: str = "sum", T: int = 128, init: dict | No
     return _write(outdir, f"synth_{kind}_{n}", code, entry, g, kmeta, 1e-5, 1e-6)
 
 
+def pointwise_package(outdir, n: int, kind: str = "relu_mul", U: int = 4, T: int = 256) -> Path:
+    """Pointwise f32 kernel over n elements in the schedule of the reference's p01 / p03
+    problems: one thread per U consecutive elements (``a0 * U + u``), each element's Loads and
+    Assigns in turn, one Write of the U results.  kind: "add" (x0 + x1, p01) or "relu_mul"
+    (relu(x0) * x1, p03)."""
+    if n % U or (n // U) % T:
+        raise ValueError("pointwise_package needs n a multiple of U * T")
+    a0 = "a0"
+    body = []
+    outs = []
+    for u in range(U):
+        idx = (B("+", B("*", V(a0), L(U)), L(u)),)
+        body.append(ir.Load((f"in0__u{u}",), "x0", idx, F32T))
+        if kind == "relu_mul":
+            body.append(assign(f"v0__u{u}", "relu", f"in0__u{u}"))
+            body.append(ir.Load((f"in1__u{u}",), "x1", idx, F32T))
+            body.append(assign(f"v1__u{u}", "multiply", f"v0__u{u}", f"in1__u{u}"))
+            outs.append(f"v1__u{u}")
+        else:
+            body.append(ir.Load((f"in1__u{u}",), "x1", idx, F32T))
+            body.append(assign(f"v0__u{u}", "add", f"in0__u{u}", f"in1__u{u}"))
+            outs.append(f"v0__u{u}")
+    out = "mul" if kind == "relu_mul" else "add"
+    body.append(ir.Write(out, (B("+", B("*", V(a0), L(U)), L(0)),), tuple(outs), F32T, False, "NONE"))
+    tile = ir.Tile((axis(a0, n // U),), tuple(body), T, 0, None, None, "m")
+    entry = f"k_{out}_pointwise"
+    g = _graph({"x0": ((n,), "f32"), "x1": ((n,), "f32")}, {}, out, (n,), entry, tile)
+    args = [{"name": "x0", "dtype": "f32", "shape": [n], "seed": 0},
+            {"name": "x1", "dtype": "f32", "shape": [n], "seed": 1},
+            {"name": out, "dtype": "f32", "shape": [n], "output": True}]
+    kmeta = {"node": out, "arg_order": ["x0", "x1", out], "grid": [n // U // T, 1, 1], "block": [T, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    code = (f"torch.relu(torch.randn({n})) * torch.randn({n})" if kind == "relu_mul"
+            else f"torch.randn({n}) + torch.randn({n})")
+    return _write(outdir, f"synth_{kind}_{n}", code, entry, g, kmeta, 0, 0)
+
+
 def matmul_package(outdir, M: int, N: int, K: int, b_layout: str = "col", out_dtype: str = "f32",
                    init: dict | None = None) -> Path:
     """C[M, N] = A[M, K] @ B with f16 inputs on the warp-level tensor cores (mma.sync m16n8k16),
