@@ -408,7 +408,7 @@ int thr_release_buffers(void) {
     return THR_OK;
 }
 
-// ---- peer mailboxes (CUDA IPC; no multicast objects) ----------------------------------
+// ---- peer mailboxes (CUDA IPC, plain device memory) -----------------------------------
 
 int thr_peer_alloc(uint64_t bytes, uint64_t *dptr, unsigned char handle[THR_IPC_HANDLE_BYTES]) {
     if (!dptr || !handle || bytes == 0) return fail(THR_ERR_REQUEST, "thr_peer_alloc: bad arguments");
