@@ -136,7 +136,7 @@ class RowOps:
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
-        self.torch, self.rows, self.cols, self.eps = torch, rows, cols, 1e-6
+        self.torch, self.rows, self.cols, self.eps, self.dev = torch, rows, cols, 1e-6, dev
         tmp = Path(tempfile.mkdtemp(prefix=f"bench_rowops_{rank}_"))
         self.kinds = ("softmax", "rmsnorm", "l2norm")
         self.k = {}
@@ -247,7 +247,7 @@ class RowOps:
         for kind in self.kinds:
             d = synth.row_package(tmp / kind, kind, chunk_rows, self.cols, eps=self.eps)
             meta = json.loads((d / "meta.json").read_text())
-            kch[kind] = DeviceKernel(d / f"{meta['kernels'][0]['entry']}.ir.json")
+            kch[kind] = DeviceKernel(d / f"{meta['kernels'][0]['entry']}.ir.json", device=self.dev)
         xh = {k: torch.empty(self.rows, self.cols, pin_memory=True) for k in self.kinds}
         yh = {k: torch.empty(self.rows, self.cols, pin_memory=True) for k in self.kinds}
         for k in self.kinds:
@@ -336,7 +336,7 @@ class Pointwise:
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
-        self.torch, self.n = torch, n or 1 << 28
+        self.torch, self.n, self.dev = torch, n or 1 << 28, dev
         d = synth.pointwise_package(Path(tempfile.mkdtemp(prefix=f"bench_pw_{rank}_")) / "pw", self.n, "relu_mul")
         self.k = DeviceKernel(d / "k_mul_pointwise.ir.json", device=dev)
         g = torch.Generator(device=f"cuda:{dev}").manual_seed(4000 + rank)
@@ -375,7 +375,7 @@ class Pointwise:
         from thompiler import synth
         d = synth.pointwise_package(Path(tempfile.mkdtemp(prefix="bench_pw_e2e_")) / "pw", m, "relu_mul")
         from thompiler.device import DeviceKernel
-        k = DeviceKernel(d / "k_mul_pointwise.ir.json")
+        k = DeviceKernel(d / "k_mul_pointwise.ir.json", device=self.dev)
         args = [{"array": h[0].numpy()}, {"array": h[1].numpy()}, {"array": h[2].numpy(), "output": True}]
         runner.run(k.fn, k.plan, args, arg_order=k.arg_order)
         t = time.perf_counter()
@@ -399,7 +399,7 @@ class Pointwise:
         """The same IR through the statement-by-statement lowering (scalar 4-byte accesses)."""
         from thompiler.device import DeviceKernel
         torch = self.torch
-        gk = DeviceKernel(self.k.ir_path, tuned=False)
+        gk = DeviceKernel(self.k.ir_path, device=self.dev, tuned=False)
         s = torch.cuda.current_stream().cuda_stream
         for _ in range(3):
             gk(self.ptrs(), s)

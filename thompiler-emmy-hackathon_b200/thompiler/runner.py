@@ -109,9 +109,10 @@ def check(status: int, what: str) -> None:
 
 
 def init(device: int = 0) -> None:
-    if device not in _inited:
-        check(library().thr_init(device), f"thr_init({device})")
-        _inited.add(device)
+    """Make ``device`` current in this thread (every call: modules load into the current
+    device's context, so a caller switching devices must not be left on the previous one)."""
+    check(library().thr_init(device), f"thr_init({device})")
+    _inited.add(device)
 
 
 def device_info(device: int = 0) -> dict:
