@@ -46,7 +46,7 @@ def test_attention_small_vs_oracle(tmp_path, shape):
     assert np.max(np.abs(tuned["outputs"]["attn"] - ref)) < 5e-3
 
 
-@pytest.mark.parametrize("shape", [(2, 2, 384, 64), (1, 3, 512, 128)])
+@pytest.mark.parametrize("shape", [(2, 2, 384, 64), (1, 3, 512, 128), (2, 2, 512, 64)])
 def test_attention_medium_vs_expression(tmp_path, shape):
     d = synth.attention_package(tmp_path / "att", *shape)
     pkg = problems.load_package(d)
