@@ -227,13 +227,16 @@ class RowOps:
         runner.release()
         h2d = sum(h[0].nbytes for h in host.values()) + hw.numel() * 4 + 8
         d2h = sum(h[1].nbytes for h in host.values())
-        sync = {"value": self.bytes_per_step / sec / 1e9, "ms_per_step": sec * 1e3}
         streamed = self.e2e_streamed(steps)
-        return {"value": streamed["value"], "unit": "GB/s", "h2d_bytes_per_step": streamed["h2d"],
-                "d2h_bytes_per_step": streamed["d2h"], "ms_per_step": streamed["ms_per_step"],
-                "how": "pinned host buffers; per 1024-row chunk: host->device copy, kernel, device->host "
-                       "copy on three streams, so the two copy directions and the kernels overlap",
-                "blocking_thr_run": sync}
+        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3,
+                "how": "one thr_run per kernel on pinned host buffers (the C-ABI call: copy in, launch, "
+                       "copy out)",
+                "streamed_device_api": {
+                    "value": streamed["value"], "ms_per_step": streamed["ms_per_step"],
+                    "how": "DeviceKernel launches on device buffers; per 1024-row chunk a host->device copy, "
+                           "the kernel and a device->host copy on three streams, so both copy directions "
+                           "and the kernels overlap"}}
 
     def e2e_streamed(self, steps: int, chunk_rows: int = 1024) -> dict:
         """The same three row ops on host data, chunked by rows and pipelined on three streams
