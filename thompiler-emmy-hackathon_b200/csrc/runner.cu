@@ -358,6 +358,127 @@ int thr_run_ex(uint64_t module, uint64_t function, const uint32_t grid[3], const
     return rc;
 }
 
+int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
+    int s = ensure_driver();
+    if (s) return s;
+    if (nruns < 0 || (nruns && !runs)) return fail(THR_ERR_REQUEST, "thr_run_batch: bad arguments");
+    for (int r = 0; r < nruns; ++r) {
+        const thr_run_desc &d = runs[r];
+        if (d.nargs < 0 || (d.nargs && !d.args) || d.ntmaps < 0 || (d.ntmaps && (!d.tmaps || !d.module)))
+            return fail(THR_ERR_REQUEST, "thr_run_batch: request %d has bad arguments", r);
+        for (int q = 0; q < r; ++q)
+            if (d.ntmaps && runs[q].ntmaps && runs[q].module == d.module)
+                return fail(THR_ERR_REQUEST, "thr_run_batch: requests %d and %d need tensor maps in one module", q, r);
+    }
+    cudaStream_t sin = nullptr, scmp = nullptr, sout = nullptr;
+    std::vector<cudaEvent_t> evs;
+    std::vector<std::vector<unsigned char>> host_maps(nruns);   // alive until the batch is done
+    std::vector<std::vector<uint64_t>> host_ptrs(nruns);
+    auto event = [&](cudaEvent_t *e) -> bool {
+        if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return false;
+        evs.push_back(*e);
+        return true;
+    };
+    int rc = THR_OK;
+    if (cudaStreamCreateWithFlags(&sin, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&scmp, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&sout, cudaStreamNonBlocking) != cudaSuccess)
+        rc = fail(THR_ERR_CUDA, "thr_run_batch: creating streams");
+    // the batch's buffers sit after the slots thr_run uses for one request's arguments
+    size_t slot = 4096;
+    for (int r = 0; r < nruns && rc == THR_OK; ++r) {
+        const thr_run_desc &d = runs[r];
+        std::vector<uint64_t> dev(d.nargs);
+        for (int i = 0; i < d.nargs && rc == THR_OK; ++i) {
+            void *p = nullptr;
+            if ((rc = slot_buffer(slot++, d.args[i].nbytes, &p))) break;
+            dev[i] = (uint64_t)(uintptr_t)p;
+            cudaError_t e = d.args[i].kind == THR_ARG_INPUT
+                                ? cudaMemcpyAsync(p, d.args[i].host, d.args[i].nbytes, cudaMemcpyHostToDevice, sin)
+                                : cudaMemsetAsync(p, 0, d.args[i].nbytes, sin);
+            if (e != cudaSuccess) rc = cuda_fail(e, "staging a batch argument");
+        }
+        if (rc) break;
+        if (d.ntmaps) {
+            host_maps[r].resize(128 * (size_t)d.ntmaps);
+            host_ptrs[r].resize(d.ntmaps);
+            for (int i = 0; i < d.ntmaps && rc == THR_OK; ++i) {
+                const thr_tmap_spec &m = d.tmaps[i];
+                if (m.arg < 0 || m.arg >= d.nargs || !m.global) {
+                    rc = fail(THR_ERR_REQUEST, "request %d tensor map %d: bad argument", r, i);
+                    break;
+                }
+                host_ptrs[r][i] = dev[m.arg];
+                if ((rc = thr_tensor_map(host_maps[r].data() + 128 * i, m.dtype_code, m.rank, dev[m.arg], m.dims,
+                                         m.strides, m.box, m.swizzle)))
+                    break;
+                uint64_t g = 0, n = 0;
+                if ((rc = thr_module_global(d.module, m.global, &g, &n))) break;
+                if (n < 128) {
+                    rc = fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", m.global, (unsigned long long)n);
+                    break;
+                }
+                cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, host_maps[r].data() + 128 * i, 128,
+                                                cudaMemcpyHostToDevice, sin);
+                if (e != cudaSuccess) rc = cuda_fail(e, "uploading a tensor map");
+            }
+            if (rc == THR_OK && d.ptr_table) {
+                uint64_t g = 0, n = 0;
+                if ((rc = thr_module_global(d.module, d.ptr_table, &g, &n)) == THR_OK) {
+                    if (n < 8 * (uint64_t)d.ntmaps) {
+                        rc = fail(THR_ERR_LOOKUP, "pointer table %s is too small", d.ptr_table);
+                    } else {
+                        cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, host_ptrs[r].data(), 8 * d.ntmaps,
+                                                        cudaMemcpyHostToDevice, sin);
+                        if (e != cudaSuccess) rc = cuda_fail(e, "uploading the tensor-map pointers");
+                    }
+                }
+            }
+            if (rc) break;
+        }
+        cudaEvent_t staged, ran;
+        if (!event(&staged) || !event(&ran)) {
+            rc = fail(THR_ERR_CUDA, "cudaEventCreate");
+            break;
+        }
+        cudaEventRecord(staged, sin);
+        cudaStreamWaitEvent(scmp, staged, 0);
+        if ((rc = thr_launch(d.function, d.grid, d.block, d.smem_bytes, dev.data(), d.nargs,
+                             (uint64_t)(uintptr_t)scmp)))
+            break;
+        cudaEventRecord(ran, scmp);
+        cudaStreamWaitEvent(sout, ran, 0);
+        for (int i = 0; i < d.nargs && rc == THR_OK; ++i)
+            if (d.args[i].kind == THR_ARG_OUTPUT) {
+                cudaError_t e = cudaMemcpyAsync(d.args[i].host, (void *)(uintptr_t)dev[i], d.args[i].nbytes,
+                                                cudaMemcpyDeviceToHost, sout);
+                if (e != cudaSuccess) rc = cuda_fail(e, "copying an output back");
+            }
+    }
+    if (sout) {
+        // every request's copies and launch are ordered before this point of the copy-out stream
+        cudaEvent_t done;
+        if (event(&done)) {
+            cudaEventRecord(done, sout);
+            int w = wait_event(done, timeout_s);
+            if (rc == THR_OK) rc = w;
+        } else if (rc == THR_OK) {
+            rc = fail(THR_ERR_CUDA, "cudaEventCreate");
+        }
+    }
+    if (rc != THR_OK) {
+        // leave nothing in flight that reads the caller's host buffers
+        if (sin) cudaStreamSynchronize(sin);
+        if (scmp) cudaStreamSynchronize(scmp);
+        if (sout) cudaStreamSynchronize(sout);
+    }
+    for (auto e : evs) cudaEventDestroy(e);
+    if (sin) cudaStreamDestroy(sin);
+    if (scmp) cudaStreamDestroy(scmp);
+    if (sout) cudaStreamDestroy(sout);
+    return rc;
+}
+
 int thr_tensor_map(void *out128, int dtype_code, int rank, uint64_t base, const uint64_t *dims,
                    const uint64_t *strides_bytes, const uint32_t *box, int swizzle) {
     int s = ensure_driver();

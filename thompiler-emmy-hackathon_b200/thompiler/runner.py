@@ -50,6 +50,13 @@ class ThrTmapSpec(ctypes.Structure):
                 ("strides", ctypes.c_uint64 * 4), ("box", ctypes.c_uint32 * 5)]
 
 
+class ThrRunDesc(ctypes.Structure):
+    _fields_ = [("module", ctypes.c_uint64), ("function", ctypes.c_uint64), ("grid", ctypes.c_uint32 * 3),
+                ("block", ctypes.c_uint32 * 3), ("smem_bytes", ctypes.c_uint32), ("nargs", ctypes.c_int32),
+                ("args", ctypes.POINTER(ThrArg)), ("tmaps", ctypes.POINTER(ThrTmapSpec)), ("ntmaps", ctypes.c_int32),
+                ("ptr_table", ctypes.c_char_p)]
+
+
 _lib = None
 _inited: set[int] = set()
 
@@ -85,6 +92,7 @@ def library() -> ctypes.CDLL:
             "thr_synchronize": ([], i32),
             "thr_release_buffers": ([], i32),
             "thr_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
+            "thr_run_batch": ([ctypes.POINTER(ThrRunDesc), i32, ctypes.c_double], i32),
             "thr_peer_alloc": ([u64, ctypes.POINTER(u64), ctypes.c_char_p], i32),
             "thr_peer_open": ([ctypes.c_char_p, ctypes.POINTER(u64)], i32),
             "thr_peer_close": ([u64], i32),
@@ -325,6 +333,46 @@ def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0,
     if err:
         return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
     return {"ok": True, "median_us": float(med.value)}
+
+
+def run_batch(requests: list, timeout_s: float = 60.0) -> dict:
+    """Several independent POST /run requests with their copies and launches overlapped
+    (thr_run_batch).  ``requests``: (function, plan, args, arg_order) tuples, ``args`` as for
+    ``run``; pass pinned host arrays for the copies to overlap."""
+    descs = (ThrRunDesc * max(1, len(requests)))()
+    keep = []
+    for r, (function, plan, args, arg_order) in enumerate(requests):
+        arr = (ThrArg * max(1, len(args)))()
+        xs = []
+        for i, a in enumerate(args):
+            x = np.ascontiguousarray(a["array"])
+            xs.append(x)
+            arr[i].host = x.ctypes.data
+            arr[i].nbytes = x.nbytes
+            arr[i].kind = 1 if a.get("output") else 0
+            arr[i].zero_each = 1 if a.get("zero_each") else 0
+        d = descs[r]
+        d.module, d.function = function.module.handle, function.handle
+        d.grid, d.block = _dims(plan.grid), _dims(plan.block)
+        d.smem_bytes, d.nargs, d.args = int(plan.smem), len(args), arr
+        specs, table, names = None, None, None
+        if plan.tmaps:
+            specs, names = _tmap_specs(plan, arg_order)
+            table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
+            d.tmaps, d.ntmaps, d.ptr_table = specs, len(plan.tmaps), table
+        keep.append((arr, xs, (specs, names, table), args))
+    st = library().thr_run_batch(descs, len(requests), float(timeout_s))
+    if st:
+        return {"ok": False, "stage": STAGES.get(st, "cuda"), "stderr": last_error()}
+    for arr, xs, _, args in keep:
+        for a, x in zip(args, xs):
+            if a.get("output") and x is not a["array"]:
+                a["array"][...] = x
+    for (function, plan, _, _) in requests:
+        err = read_error_word(function.module, plan)
+        if err:
+            return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
+    return {"ok": True}
 
 
 def release() -> None:
