@@ -58,7 +58,6 @@ class ThrRunDesc(ctypes.Structure):
 
 
 _lib = None
-_inited: set[int] = set()
 
 
 def library() -> ctypes.CDLL:
@@ -120,7 +119,6 @@ def init(device: int = 0) -> None:
     """Make ``device`` current in this thread (every call: modules load into the current
     device's context, so a caller switching devices must not be left on the previous one)."""
     check(library().thr_init(device), f"thr_init({device})")
-    _inited.add(device)
 
 
 def device_info(device: int = 0) -> dict:
