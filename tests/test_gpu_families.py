@@ -160,3 +160,35 @@ def test_pointwise_vectorised(tmp_path, kind):
         want = np.maximum(a, 0) * b if kind == "relu_mul" else a + b
         assert np.array_equal(y.cpu().numpy(), want.astype(np.float32)), off
     k.close()
+
+
+def test_past_2_31_elements(tmp_path):
+    """Buffers longer than 2^31 elements (8.6 GB of f32 each): the pointwise family's 64-bit
+    addressing (bit-exact at the far end of the range) and the full-mode sum's chunk indexing
+    (within 1e-4 of the data's l2 norm of the float64 sum)."""
+    import torch
+    from thompiler.device import DeviceKernel
+    n = (1 << 31) + (1 << 20)
+    d = synth.pointwise_package(tmp_path / "pw", n, "relu_mul")
+    k = DeviceKernel(d / "k_mul_pointwise.ir.json")
+    g = torch.Generator(device="cuda").manual_seed(31)
+    x0 = torch.randn(n, device="cuda", generator=g)
+    x1 = torch.randn(n, device="cuda", generator=g)
+    y = torch.full((n,), float("nan"), device="cuda")
+    k({"x0": x0.data_ptr(), "x1": x1.data_ptr(), "mul": y.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for lo in (0, (1 << 31) - 4096, n - 4096):
+        want = torch.relu(x0[lo:lo + 4096]) * x1[lo:lo + 4096]
+        assert torch.equal(y[lo:lo + 4096], want), lo
+    assert not torch.isnan(y).any()
+    k.close()
+    del x1, y
+    d2 = synth.sum_package(tmp_path / "s", n)
+    ks = DeviceKernel(d2 / "k_sum_1_reduce.ir.json")
+    out = torch.zeros(1, device="cuda")
+    ks({"x": x0.data_ptr(), "sum_1": out.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    want = float(x0.double().sum())
+    l2 = float(x0.double().norm())                       # f32 summation error scales with it
+    assert abs(float(out.item()) - want) <= 1e-4 * l2, (float(out.item()), want)
+    ks.close()
