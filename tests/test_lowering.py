@@ -32,3 +32,17 @@ def test_immediates():
     assert F64.imm(1.0) == "0d3FF0000000000000"
     assert F16.imm(1.0) == "0x3C00"
     assert I32.imm(7) == "7"
+
+
+def test_wide_buffer_index_expressions_are_64_bit(tmp_path):
+    """A buffer of 2^31 or more elements: the whole index expression (a0 * 4 + u) is evaluated
+    in 64-bit arithmetic, not widened after a 32-bit product that would wrap past 2^31."""
+    from thompiler import compiler, load, synth
+    n = (1 << 31) + (1 << 20)
+    d = synth.pointwise_package(tmp_path / "pw", n, "relu_mul")
+    ptx = compiler.compile_kernel(load.load(str(d / "k_mul_pointwise.ir.json")))
+    assert "mul.lo.s64" in ptx
+    assert "mul.lo.s32" not in ptx                       # no 32-bit index product anywhere
+    small = synth.pointwise_package(tmp_path / "pw_small", 1 << 20, "relu_mul")
+    ptx_small = compiler.compile_kernel(load.load(str(small / "k_mul_pointwise.ir.json")))
+    assert "mul.lo.s64" not in ptx_small                 # small buffers keep the 32-bit form

@@ -28,7 +28,7 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import TYPE_CHECKING
 
-from thompiler.lowering.expr import int_operand, is_imm
+from thompiler.lowering.expr import int_operand, int_operand_wide, is_imm
 from thompiler.lowering.types import Ty
 
 if TYPE_CHECKING:
@@ -95,12 +95,7 @@ def _flat_index_wide(w: "Walker", shape: tuple[int, ...], index: tuple) -> str:
     em = w.em
     flat = None
     for k, (size, e) in enumerate(zip(shape, index)):
-        i = int_operand(w, e)
-        if is_imm(i):
-            iw = i
-        else:
-            iw = em.tmp("b64")
-            em.ins(f"cvt.s64.s32 {iw}, {i}")
+        iw = int_operand_wide(w, e)
         if flat is None:
             flat = iw
         elif is_imm(flat) and is_imm(iw):

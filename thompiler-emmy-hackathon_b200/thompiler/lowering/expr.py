@@ -89,6 +89,43 @@ def int_operand(w: "Walker", e: object) -> str:
     raise NotImplementedError(f"index expression {type(e).__name__}")
 
 
+WIDE_OPS = {"+": "add.s64", "-": "sub.s64", "*": "mul.lo.s64", "/": "div.s64", "%": "rem.s64"}
+
+
+def int_operand_wide(w: "Walker", e: object) -> str:
+    """An index expression evaluated in signed 64-bit arithmetic (b64 register or immediate):
+    the form an offset into a buffer of 2^31 or more elements needs, where an intermediate
+    such as ``a0 * 4`` may pass 2^31 although every axis value fits in 32 bits."""
+    em = w.em
+    if isinstance(e, ir.BinaryExpr):
+        if e.op not in WIDE_OPS:
+            raise NotImplementedError(f"integer operator {e.op!r}")
+        a, b = int_operand_wide(w, e.left), int_operand_wide(w, e.right)
+        if is_imm(a) and is_imm(b):
+            return str(fold(e.op, int(a), int(b)))
+        if e.op in ("+", "-") and b == "0":
+            return a
+        if e.op == "+" and a == "0":
+            return b
+        if e.op in ("*", "/") and b == "1":
+            return a
+        out = em.tmp("b64")
+        em.ins(f"{WIDE_OPS[e.op]} {out}, {a}, {b}")
+        return out
+    if isinstance(e, ir.TernaryExpr):
+        p = pred_operand(w, e.cond)
+        a, b = int_operand_wide(w, e.if_true), int_operand_wide(w, e.if_false)
+        out = em.tmp("b64")
+        em.ins(f"selp.b64 {out}, {a}, {b}, {p}")
+        return out
+    v = int_operand(w, e)                 # a variable or a literal: a 32-bit value
+    if is_imm(v):
+        return v
+    out = em.tmp("b64")
+    em.ins(f"cvt.s64.s32 {out}, {v}")
+    return out
+
+
 def value_type(w: "Walker", e: object) -> Ty:
     """Type of an expression (I32 for indices, the register's type for
     IR values, F32 for float literals)."""
