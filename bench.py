@@ -136,7 +136,7 @@ class RowOps:
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
-        self.torch, self.rows, self.cols, self.eps, self.dev = torch, rows, cols, 1e-6, dev
+        self.torch, self.rows, self.cols, self.eps, self.dev, self.world = torch, rows, cols, 1e-6, dev, world
         tmp = Path(tempfile.mkdtemp(prefix=f"bench_rowops_{rank}_"))
         self.kinds = ("softmax", "rmsnorm", "l2norm")
         self.k = {}
@@ -240,18 +240,21 @@ class RowOps:
         runner.release()
         h2d = sum(h[0].nbytes for h in host.values()) + hw.numel() * 4 + 8
         d2h = sum(h[1].nbytes for h in host.values())
-        streamed = self.e2e_streamed(steps)
-        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3,
-                "how": "one thr_run_batch per step on pinned host buffers (the C-ABI host-buffer call: the "
-                       "three requests' copies in, kernels and copies out overlap on three streams)",
-                "one_thr_run_per_kernel": {"value": self.bytes_per_step / sec_single / 1e9,
-                                           "ms_per_step": sec_single * 1e3},
-                "streamed_device_api": {
-                    "value": streamed["value"], "ms_per_step": streamed["ms_per_step"],
-                    "how": "DeviceKernel launches on device buffers; per 1024-row chunk a host->device copy, "
-                           "the kernel and a device->host copy on three streams, so both copy directions "
-                           "and the kernels overlap"}}
+        # the device-API pipeline for comparison (one GPU only: it pins another 768 MB of host memory)
+        streamed = self.e2e_streamed(steps) if self.world == 1 else None
+        out = {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3,
+               "how": "one thr_run_batch per step on pinned host buffers (the C-ABI host-buffer call: the "
+                      "three requests' copies in, kernels and copies out overlap on three streams)",
+               "one_thr_run_per_kernel": {"value": self.bytes_per_step / sec_single / 1e9,
+                                          "ms_per_step": sec_single * 1e3}}
+        if streamed is not None:
+            out["streamed_device_api"] = {
+                "value": streamed["value"], "ms_per_step": streamed["ms_per_step"],
+                "how": "DeviceKernel launches on device buffers; per 1024-row chunk a host->device copy, "
+                       "the kernel and a device->host copy on three streams, so both copy directions "
+                       "and the kernels overlap"}
+        return out
 
     def e2e_streamed(self, steps: int, chunk_rows: int = 1024) -> dict:
         """The same three row ops on host data, chunked by rows and pipelined on three streams
