@@ -1,0 +1,77 @@
+"""The tuned families' launch plans, on the CPU: which family a package gets, its tuned launch,
+its shared-memory layout and the work split -- the numbers the GPU kernels are built around."""
+
+import re
+
+import pytest
+
+from conftest import GOLDEN
+from thompiler import load, synth
+from thompiler.families import recognise
+from thompiler.families.attention import TcAttention
+from thompiler.families.matmul import TcMatmul
+from thompiler.families.pointwise import Pointwise
+from thompiler.families.strided import StridedReduce
+
+
+def _kernel(path):
+    return load.load(str(path))
+
+
+def _ir(d):
+    return next(d.glob("*.ir.json"))
+
+
+@pytest.mark.parametrize("M,N,K,rem,parts", [(4096, 4096, 4096, 68, 2), (8192, 3072, 1024, 0, 1),
+                                            (2048, 2560, 2048, 12, 2), (256, 256, 512, 0, 1)])
+def test_matmul_split_tail_plan(tmp_path, M, N, K, rem, parts):
+    fam = recognise(_kernel(_ir(synth.matmul_package(tmp_path / "mm", M, N, K))))
+    assert isinstance(fam, TcMatmul)
+    assert (fam.rem, fam.parts) == (rem, parts)
+    assert fam.units == fam.tiles - rem + rem * parts
+    assert fam.units - (fam.tiles - rem) <= 148                 # the split tail is one round at most
+    # shared memory: stages | staging | barriers, all inside the dynamic allocation
+    assert fam.stages * (fam.a_bytes + fam.b_bytes) + fam.staging + 1024 + 256 == fam.smem <= 227 * 1024
+
+
+def test_attention_plan_benchmark_shape(tmp_path):
+    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
+    assert isinstance(fam, TcAttention)
+    assert (fam.qt, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 384, 2, 2, 1024)
+    assert fam.reg_split == (224, 56)
+    # per sub-partition: 2 softmax warps at 224 + 1 producer warp at 56 registers <= 512 per thread,
+    # and the split hands over exactly what the launch holds (168 per thread)
+    assert 2 * 224 + 56 <= 512 and 256 * 224 + 128 * 56 == 384 * 168
+    assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + 1024 + 256 <= 227 * 1024
+    ptx = fam.emit()
+    assert ".maxnreg 168" in ptx and "setmaxnreg.inc.sync.aligned.u32 224" in ptx
+    assert '"grid":[148,1,1]' in ptx                            # persistent: one CTA per SM
+
+
+@pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 192), ((2, 2, 384, 64), 1, 192),
+                                              ((2, 2, 512, 64), 2, 384), ((1, 3, 512, 128), 2, 384)])
+def test_attention_plan_small(tmp_path, shape, qt, threads):
+    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", *shape))))
+    assert (fam.qt, fam.threads) == (qt, threads)
+    assert fam.smem <= 227 * 1024
+    assert (fam.reg_split is not None) == (qt == 2)
+
+
+def test_pointwise_plan_on_shipped_packages():
+    for name, align in (("p01_vector_add", 8), ("p03_relu_mul", 16), ("x01_f64_relu_mul_add", 16)):
+        fam = recognise(_kernel(_ir(GOLDEN / name)))
+        assert isinstance(fam, Pointwise), name
+        assert set(fam.vparams.values()) == {align}, (name, fam.vparams)
+        ptx = fam.emit()
+        assert "and.b64" in ptx and re.search(r"ld\.global\.nc\.v[24]\.", ptx)
+
+
+def test_strided_sum_plans():
+    r01 = recognise(_kernel(_ir(GOLDEN / "r01_array_sum")))
+    assert isinstance(r01, StridedReduce) and not r01.row_mode
+    side = r01.sidecar()
+    assert side["peer"]["max_ranks"] == 8 and side["error_word"] == "thc_error"
+    f02 = recognise(_kernel(_ir(GOLDEN / "f02_row_softmax")))
+    assert isinstance(f02, StridedReduce) and f02.row_mode and f02.sidecar() is None
+    r03 = recognise(_kernel(_ir(GOLDEN / "r03_mean")))
+    assert "peer" not in (r03.sidecar() or {})                 # a mean is not combined across GPUs

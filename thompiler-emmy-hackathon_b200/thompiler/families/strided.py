@@ -486,10 +486,17 @@ class StridedReduce(TunedKernel):
         w.body((self.tail,))
 
     def _peer_capable(self) -> bool:
-        """A single f32 sum state: the result the ranks of a sharded sum add up."""
+        """A plain f32 sum: one add state written out as it is (r01 / r02) -- the result the
+        ranks of a sharded sum add up.  A mean (r03) divides by its count and is left alone."""
         accs = [s for s in self.l1.body if isinstance(s, ir.Accum)]
-        return (not self.row_mode and len(self.states) == 1 and len(accs) == 1
-                and accs[0].op.name == "add" and dtype_of(accs[0].dtype, "Accum") is F32)
+        if self.row_mode or len(self.states) != 1 or len(accs) != 1:
+            return False
+        if accs[0].op.name != "add" or dtype_of(accs[0].dtype, "Accum") is not F32:
+            return False
+        tail = self.tail.body if isinstance(self.tail, ir.Cond) else ()
+        writes = [s for s in tail if isinstance(s, ir.Write)]
+        return (not any(isinstance(s, ir.Assign) for s in tuple(self.mid) + tuple(tail))
+                and len(writes) == 1 and tuple(writes[0].values) == (self.states[0],))
 
     def _peer_combine(self, tid: str) -> None:
         """Add the other GPUs' results to this one over peer memory, inside the kernel.
