@@ -34,18 +34,36 @@ def test_matmul_split_tail_plan(tmp_path, M, N, K, rem, parts):
     assert fam.stages * (fam.a_bytes + fam.b_bytes) + fam.staging + 1024 + 256 == fam.smem <= 227 * 1024
 
 
-def test_attention_plan_benchmark_shape(tmp_path):
+def test_attention_plan_two_threads_per_row(tmp_path, monkeypatch):
+    monkeypatch.setenv("THOMPILER_ATTN_SPLIT", "2")         # 16 softmax warps, 640 threads
     fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
     assert isinstance(fam, TcAttention)
-    assert (fam.qt, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 384, 2, 2, 1024)
-    assert fam.reg_split == (224, 56)
+    assert (fam.qt, fam.h, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 2, 640, 2, 2, 1024)
+    assert (fam.maxnreg, fam.reg_split) == (96, (104, 56))
+    # per sub-partition (5 warps): 4 softmax warps at 104 + 1 producer warp at 56 registers fit its
+    # 16384, and the split never asks for more than the launch holds (96 per thread)
+    assert 32 * (4 * 104 + 56) <= 16384 and 512 * 104 + 128 * 56 <= 640 * 96
+    assert fam.stage_bytes == 16 * 32 * 32 and fam.xchg_bytes == 2 * 2 * 2 * 128 * 4
+    assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + fam.xchg_bytes + 1024 + 256 <= 227 * 1024
+    ptx = fam.emit()
+    assert ".maxnreg 96" in ptx and "setmaxnreg.inc.sync.aligned.u32 104" in ptx
+    assert '"grid":[148,1,1]' in ptx                            # persistent: one CTA per SM
+    assert '"box":[16,32]' in ptx.replace(" ", "")              # the output's 32 x 32 B staging boxes
+
+
+def test_attention_plan_benchmark_shape(tmp_path, monkeypatch):
+    monkeypatch.delenv("THOMPILER_ATTN_SPLIT", raising=False)    # default: one thread per query row
+    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
+    assert isinstance(fam, TcAttention)
+    assert (fam.qt, fam.h, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 1, 384, 2, 2, 1024)
+    assert (fam.maxnreg, fam.reg_split) == (168, (224, 56))
     # per sub-partition: 2 softmax warps at 224 + 1 producer warp at 56 registers <= 512 per thread,
     # and the split hands over exactly what the launch holds (168 per thread)
     assert 2 * 224 + 56 <= 512 and 256 * 224 + 128 * 56 == 384 * 168
+    assert fam.xchg_bytes == 0
     assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + 1024 + 256 <= 227 * 1024
     ptx = fam.emit()
     assert ".maxnreg 168" in ptx and "setmaxnreg.inc.sync.aligned.u32 224" in ptx
-    assert '"grid":[148,1,1]' in ptx                            # persistent: one CTA per SM
 
 
 @pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 192), ((2, 2, 384, 64), 1, 192),

@@ -28,7 +28,11 @@ written over the first 64 columns of S_g.  Softmax per row and key block: the
 the running sum rescaled only when the max grew by more than 2^8 (P <= 256
 stays exact in f16, the rescale is rare), P = 2^(s c' - m) with packed f32x2
 FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  Epilogue:
-O / l as f16 staged over the group's Q tile, one TMA store per group.
+O / l as f16 through each warp's own 32-row staging box (128B-swizzled), one
+TMA store per box.  THOMPILER_ATTN_SPLIT=2 (two query tiles only) runs two
+threads per query row instead: 640 threads, each with half of the row's keys
+and half of O's columns, the row max and row sum exchanged through shared
+memory under their own mbarriers, 32-byte unswizzled staging boxes.
 Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
 exactly as the IR's exp lowering.  All mbarrier waits are bounded
 (thompiler.families.kit).
@@ -67,17 +71,40 @@ class TcAttention(TunedKernel):
         self.kv_bytes = BN * D * 2
         # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
         self.qt = 2 if Sq % (2 * BM) == 0 else 1
-        # warps 0 .. 4 qt - 1 softmax (warp w reads TMEM lanes 32 (w % 4) ..), then the TMA warp and
-        # the MMA warp; with two groups they fill a third warpgroup (two warps idle) whose registers
-        # go to the softmax warpgroups (setmaxnreg: 168 at launch -> 224 / 56)
-        self.w_tma, self.w_mma = 4 * self.qt, 4 * self.qt + 1
-        self.threads = 128 * (self.qt + 1) if self.qt == 2 else 192
-        self.reg_split = (224, 56) if self.qt == 2 else None
+        # h threads per query row: one by default; with two query tiles THOMPILER_ATTN_SPLIT=2 gives
+        # two (each takes half of the row's keys and half of O's columns, the row max and the row
+        # sum exchanged through shared memory), two softmax warps per tile on each SM
+        # sub-partition.  Measured on B200 at [8, 16, 2048 | 4096, 128] it is about 1% slower
+        # than one thread per row (the exponentials' latency is hidden already)
+        self.h = int(os.environ.get("THOMPILER_ATTN_SPLIT", "1")) if self.qt == 2 else 1
+        self.h = self.h if self.h in (1, 2) else 1
+        # warps 0 .. 4 qt h - 1 softmax (warp w reads TMEM lanes 32 (w % 4) ..), then the TMA warp and
+        # the MMA warp; with two query tiles they fill one more warpgroup (two warps idle) whose
+        # registers go to the softmax warpgroups through setmaxnreg
+        sm_warps = 4 * self.qt * self.h
+        self.sm_threads = 32 * sm_warps
+        self.w_tma, self.w_mma = sm_warps, sm_warps + 1
+        self.threads = 32 * sm_warps + 128 if self.qt == 2 else 192
+        # each of the SM's four sub-partitions holds 16384 registers and ceil(warps / 4) of the warps
+        # (of the tuned CTA or of meta.json's, whichever is larger: the module serves both)
+        warps = -(-max(self.threads, kernel.threads_per_cta) // 32)
+        self.maxnreg = min(255, 16384 // (32 * -(-warps // 4)) // 8 * 8)
+        if self.qt == 2:
+            dec = 56
+            inc = min(248, self.maxnreg + ((self.maxnreg - dec) * 128 // self.sm_threads) // 8 * 8)
+            assert self.qt * self.h * inc + dec <= 512, "setmaxnreg split over one sub-partition's file"
+            self.reg_split = (inc, dec)
+        else:
+            self.reg_split = None
         self.ks, self.vs = ((2, 2) if self.qt == 2 else (3, 2)) if D == 128 else (STAGES, STAGES)
-        # per softmax warp: a 32-row x 128-byte staging box for the output's TMA stores
-        self.stage_bytes = 4 * self.qt * 32 * 128
+        # per softmax warp: a 32-row staging box for the output's TMA stores, 128 bytes wide
+        # (128B swizzle) with one thread per row, 32 bytes wide (no swizzle) with two
+        self.box_bytes = 128 if self.h == 1 else 32
+        self.stage_bytes = sm_warps * 32 * self.box_bytes
+        # with two threads per row: the partial row maxima and row sums they exchange
+        self.xchg_bytes = 2 * self.qt * self.h * BM * 4 if self.h == 2 else 0
         self.smem = (self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + self.stage_bytes
-                     + 1024 + 256)
+                     + self.xchg_bytes + 1024 + 256)
         self.tiles = heads * (Sq // (BM * self.qt))
 
     # ---- recognition -------------------------------------------------------------
@@ -154,11 +181,13 @@ class TcAttention(TunedKernel):
     def sidecar(self) -> dict:
         D = self.D
 
-        def tm(name, prm, rows, box_rows=128):
+        def tm(name, prm, rows, box=(64, 128), swizzle=3):
             return {"global": name, "param": prm.name, "dtype": "f16", "dims": [D, rows],
-                    "strides": [D * 2], "box": [64, box_rows], "swizzle": 3}
+                    "strides": [D * 2], "box": list(box), "swizzle": swizzle}
+        o_box = (self.box_bytes // 2, 32)                 # one warp's staging box of the output
         maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
-                tm("thc_tmap_v", self.pv, self.heads * self.Sk), tm("thc_tmap_o", self.pout, self.heads * self.Sq, 32)]
+                tm("thc_tmap_v", self.pv, self.heads * self.Sk),
+                tm("thc_tmap_o", self.pout, self.heads * self.Sq, o_box, 3 if self.h == 1 else 0)]
         return {"grid": [min(self.tiles, SM_COUNT), 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
                 "tmaps": maps, "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
                 "error_word": "thc_error", "tile": [BM * self.qt, BN, D], "stages": [self.ks, self.vs]}
@@ -170,10 +199,8 @@ class TcAttention(TunedKernel):
         em.module(".global .align 8 .u64 thc_tmap_ptr[4]")
         em.module(".global .align 4 .u32 thc_error")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
-        # the softmax rows live in registers: cap them so the tuned CTA (and meta.json's) can launch.
-        # Each of the SM's four sub-partitions holds 16384 registers and ceil(warps / 4) of the warps.
-        warps = -(-max(self.threads, self.k.threads_per_cta) // 32)
-        em.entry_attrs.append(f".maxnreg {min(255, 16384 // (32 * -(-warps // 4)) // 8 * 8)}")
+        # the softmax rows live in registers: cap them so the tuned CTA (and meta.json's) can launch
+        em.entry_attrs.append(f".maxnreg {self.maxnreg}")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
         em.ins(f"setp.ne.u32 {p}, {r}, {self.threads}")
@@ -205,14 +232,16 @@ class TcAttention(TunedKernel):
         ins(f"mov.u32 {base}, smem_pool")
         ins(f"add.u32 {base}, {base}, 1023")
         ins(f"and.b32 {base}, {base}, -1024")
-        # shared: Q tiles (QT of them) | K ring | V ring | output staging (32 x 128 B per softmax
-        # warp) | barriers
+        # shared: Q tiles (QT of them) | K ring | V ring | output staging (one 32-row box per
+        # softmax warp) | exchanged row maxima and sums (two threads per row) | barriers
+        H = self.h
         q_s = base
-        k0, v0, stage0, bars = t("b32"), t("b32"), t("b32"), t("b32")
+        k0, v0, stage0, xchg, bars = t("b32"), t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"add.u32 {k0}, {base}, {QT * qb}")
         ins(f"add.u32 {v0}, {base}, {QT * qb + KS * kvb}")
         ins(f"add.u32 {stage0}, {base}, {QT * qb + (KS + VS) * kvb}")
-        ins(f"add.u32 {bars}, {base}, {QT * qb + (KS + VS) * kvb + self.stage_bytes}")
+        ins(f"add.u32 {xchg}, {stage0}, {self.stage_bytes}")
+        ins(f"add.u32 {bars}, {xchg}, {self.xchg_bytes}")
         nb = 0
 
         def bar() -> int:
@@ -226,9 +255,11 @@ class TcAttention(TunedKernel):
         p_full = [bar() for _ in range(QT)]
         o_done = [bar() for _ in range(QT)]
         o_free = [bar() for _ in range(QT)]
+        mx_full = [bar() for _ in range(QT)] if H == 2 else []     # both halves' row maxima written
+        l_full = [bar() for _ in range(QT)] if H == 2 else []      # both halves' row sums written
         counts = {o: 1 for o in range(0, nb * 8, 8)}
-        for o in p_full + o_free:
-            counts[o] = 128
+        for o in p_full + o_free + mx_full + l_full:
+            counts[o] = 128 * H
         slot_off = nb * 8
         assert slot_off + 8 <= 256, "barriers outgrow their shared-memory slot"
         p = t("pred")
@@ -287,7 +318,7 @@ class TcAttention(TunedKernel):
             return qrow, kvrow
 
         role_mma, role_sm = lab("at_mma"), lab("at_softmax")
-        ins(f"setp.lt.u32 {p}, {warp}, {4 * QT}")
+        ins(f"setp.lt.u32 {p}, {warp}, {self.w_tma}")                # the softmax warps
         ins(f"@{p} bra {role_sm}")
         if self.reg_split:
             # the producer warpgroup hands registers to the softmax warpgroups (each warpgroup runs
@@ -487,28 +518,48 @@ class TcAttention(TunedKernel):
         ins(f"@{more} bra {mtop}")
         ins(f"bra {end}")
 
-        # ---------------- softmax + epilogue (warps 0 .. 4 QT - 1) ----------------
+        # ---------------- softmax + epilogue (warps 0 .. 4 QT H - 1) ----------------
+        # warp w: query tile g = w / 4H, half h = (w / 4) % H of the row's keys and of O's columns,
+        # TMEM lanes 32 (w % 4) .. (= the tile's rows of this thread)
+        KH, DH = BN // H, D // H                       # keys and O columns per thread
         place(role_sm)
         if self.reg_split:
             ins(f"setmaxnreg.inc.sync.aligned.u32 {self.reg_split[0]}")
-        grp, quarter, r = t("b32"), t("b32"), t("b32")
-        ins(f"shr.u32 {grp}, {warp}, 2")
+        grp, half, quarter, r = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"shr.u32 {grp}, {warp}, {2 + (H - 1)}")
+        ins(f"shr.u32 {half}, {warp}, 2")
+        ins(f"and.b32 {half}, {half}, {H - 1}")
         ins(f"and.b32 {quarter}, {warp}, 3")
         ins(f"mad.lo.u32 {r}, {quarter}, 32, {lane}")
         trow = t("b32")
         ins(f"shl.b32 {trow}, {quarter}, 21")
         ins(f"add.u32 {trow}, {trow}, {tmem}")
-        ocol, scol, gb8 = t("b32"), t("b32"), t("b32")
+        ocol, scol, pcol, gb8 = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"mad.lo.u32 {ocol}, {grp}, 128, {trow}")
-        ins(f"add.u32 {scol}, {ocol}, {S_COL}")
+        ins(f"mad.lo.u32 {scol}, {half}, {KH}, {ocol}")           # this half's keys' scores
+        ins(f"add.u32 {scol}, {scol}, {S_COL}")
+        ins(f"mad.lo.u32 {pcol}, {half}, {KH // 2}, {ocol}")      # their P (key k in column k / 2)
+        ins(f"add.u32 {pcol}, {pcol}, {S_COL}")
+        ins(f"mad.lo.u32 {ocol}, {half}, {DH}, {ocol}")           # this half's O columns
         ins(f"add.u32 {ocol}, {ocol}, {O_COL}")
         ins(f"mad.lo.u32 {gb8}, {grp}, 8, {bars}")
         rowoff = t("b32")                                  # this thread's query row within the tile pair
         ins(f"mad.lo.u32 {rowoff}, {grp}, {BM}, {r}")
         wstage, srowa, r7 = t("b32"), t("b32"), t("b32")    # the warp's staging box and this row in it
-        ins(f"mad.lo.u32 {wstage}, {warp}, {32 * 128}, {stage0}")
-        ins(f"mad.lo.u32 {srowa}, {lane}, 128, {wstage}")
+        ins(f"mad.lo.u32 {wstage}, {warp}, {32 * self.box_bytes}, {stage0}")
+        ins(f"mad.lo.u32 {srowa}, {lane}, {self.box_bytes}, {wstage}")
         ins(f"and.b32 {r7}, {lane}, 7")
+        if H == 2:
+            # exchange slots: [max | sum][group][half][row] f32
+            xmine, xpart, xi = t("b32"), t("b32"), t("b32")
+            ins(f"mad.lo.u32 {xi}, {grp}, 2, {half}")
+            ins(f"mad.lo.u32 {xi}, {xi}, {BM}, {r}")
+            ins(f"mad.lo.u32 {xmine}, {xi}, 4, {xchg}")
+            ins(f"xor.b32 {xi}, {half}, 1")
+            ins(f"mad.lo.u32 {xpart}, {grp}, 2, {xi}")
+            ins(f"mad.lo.u32 {xpart}, {xpart}, {BM}, {r}")
+            ins(f"mad.lo.u32 {xpart}, {xpart}, 4, {xchg}")
+            sum_off = QT * 2 * BM * 4
         lead = t("pred")
         ins(f"setp.eq.u32 {lead}, {lane}, 0")
         tmap_o = t("b64")
@@ -533,14 +584,25 @@ class TcAttention(TunedKernel):
         place(stop)
         kit.wait(f"{gb8}+{s_full[0]}", kit.parity(sj, 1), 2)
         ins("tcgen05.fence::after_thread_sync")
-        # the row's 128 scores into registers: four loads in flight, one wait
-        srow = [t("f32") for _ in range(BN)]
-        for c in range(BN // 32):
+        # this thread's 128 / H scores of the row into registers: all loads in flight, one wait
+        srow = [t("f32") for _ in range(KH)]
+        for c in range(KH // 32):
             a = t("b32")
             ins(f"add.u32 {a}, {scol}, {32 * c}")
             ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(srow[32 * c:32 * c + 32])}}}, [{a}]")
         ins("tcgen05.wait::ld.sync.aligned")
         mx = _tree(em, "max.f32", srow, arity=3)
+        if H == 2:
+            # the two halves' maxima through shared memory; the barrier also orders both halves'
+            # score loads before either half's P stores (half 1's P columns are half 0's scores)
+            ins(f"st.shared.f32 [{xmine}], {mx}")
+            ins("tcgen05.fence::before_thread_sync")
+            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{mx_full[0]}]")
+            kit.wait(f"{gb8}+{mx_full[0]}", kit.parity(sj, 1), 4)
+            ins("tcgen05.fence::after_thread_sync")
+            other = t("f32")
+            ins(f"ld.shared.f32 {other}, [{xpart}]")
+            ins(f"max.f32 {mx}, {mx}, {other}")
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
         norescale, noowait = lab("at_norescale"), lab("at_first")
@@ -556,15 +618,16 @@ class TcAttention(TunedKernel):
         ins(f"sub.u32 {prevb}, {sj}, 1")
         kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
-        for c in range(D // 16):            # 16 columns at a time: the scores hold 128 registers
-            ov = [t("f32") for _ in range(16)]
+        rw = 16 if H == 1 else 8            # columns at a time: the scores hold the registers
+        for c in range(DH // rw):
+            ov = [t("f32") for _ in range(rw)]
             a = t("b32")
-            ins(f"add.u32 {a}, {ocol}, {16 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x16.b32 {{{', '.join(ov)}}}, [{a}]")
+            ins(f"add.u32 {a}, {ocol}, {rw * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x{rw}.b32 {{{', '.join(ov)}}}, [{a}]")
             ins("tcgen05.wait::ld.sync.aligned")
             for x in ov:
                 ins(f"mul.rn.f32 {x}, {x}, {alpha}")
-            ins(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{a}], {{{', '.join(ov)}}}")
+            ins(f"tcgen05.st.sync.aligned.32x32b.x{rw}.b32 [{a}], {{{', '.join(ov)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         place(noowait)
         ins(f"mov.f32 {mref}, {mnew}")
@@ -573,14 +636,14 @@ class TcAttention(TunedKernel):
         negm = t("f32")
         ins(f"neg.f32 {negm}, {mref}")
         # P = 2^(s c' - m), 16 scores at a time, written back as f16 pairs over S's first 64 columns
-        # (every score is already in registers, so the stores cannot overtake a load).  Pairs of
+        # (every score of the row is already in registers, so the stores cannot overtake a load).  Pairs of
         # scores go through the packed f32x2 FMA pipe; POLY_PAIRS of every 8 pairs take 2^x from
         # a polynomial on that pipe instead of the MUFU unit.
         pair = t("b64"), t("b64")
         ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
         ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
         ex2 = _Exp2(em) if POLY_PAIRS else None
-        for c in range(BN // 16):
+        for c in range(KH // 16):
             sv = srow[16 * c:16 * c + 16]
             packs = []
             for k in range(8):
@@ -606,7 +669,7 @@ class TcAttention(TunedKernel):
             for k in range(8):
                 ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
             a2 = t("b32")
-            ins(f"add.u32 {a2}, {scol}, {8 * c}")
+            ins(f"add.u32 {a2}, {pcol}, {8 * c}")
             ins(f"tcgen05.st.sync.aligned.32x32b.x8.b32 [{a2}], {{{', '.join(hp)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         ins("tcgen05.fence::before_thread_sync")
@@ -615,48 +678,92 @@ class TcAttention(TunedKernel):
         ins(f"add.u32 {blk2}, {blk2}, 1")
         ins(f"setp.lt.u32 {p}, {blk2}, {n_blk}")
         ins(f"@{p} bra {stop}")
-        # epilogue: read O_g, hand its TMEM back to the MMA warp, then O / l -> f16 -> this row of
-        # the output with 16-byte stores (the TMEM and shared memory go on to the next tile)
-        lastb = t("b32")
-        ins(f"sub.u32 {lastb}, {sj}, 1")
-        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
-        ins("tcgen05.fence::after_thread_sync")
-        ov = [t("f32") for _ in range(D)]
-        for c in range(D // 32):
-            a = t("b32")
-            ins(f"add.u32 {a}, {ocol}, {32 * c}")
-            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
-        ins("tcgen05.wait::ld.sync.aligned")
-        ins("tcgen05.fence::before_thread_sync")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
-        inv = t("f32")
-        ins(f"rcp.rn.f32 {inv}, {l}")
-        # 64 columns at a time: this row's 128 bytes into the warp's 32 x 128 B box (16-byte chunk c
-        # of row r at chunk c ^ (r % 8): the 128-byte swizzle, conflict-free), then lane 0 stores the
-        # box with TMA; the box is reused only after that store has read it
+        # epilogue: O / l -> f16 -> this row of the output through the warp's staging box and TMA
+        # stores; O_g's TMEM goes back to the MMA warp once read (the TMEM and shared memory go on
+        # to the next tile), the box is reused only after the previous store has read it
         qrow_s, _ = tile_rows(stile)
         orow = t("b32")
         ins(f"add.u32 {orow}, {qrow_s}, {rowoff}")
         ins(f"sub.u32 {orow}, {orow}, {lane}")                    # the warp's first row
-        for half in range(D // 64):
-            ins(f"@{lead} cp.async.bulk.wait_group.read 0")
-            ins("bar.warp.sync -1")
-            for c in range(8):
-                oh = [t("b32") for _ in range(4)]
-                for k in range(4):
-                    x0, x1 = ov[64 * half + 8 * c + 2 * k], ov[64 * half + 8 * c + 2 * k + 1]
-                    ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
-                    ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
-                    ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
-                ch = t("b32")
-                ins(f"xor.b32 {ch}, {r7}, {c}")
-                ins(f"mad.lo.u32 {ch}, {ch}, 16, {srowa}")
-                ins(f"st.shared.v4.b32 [{ch}], {{{', '.join(oh)}}}")
-            ins("fence.proxy.async.shared::cta")
-            ins("bar.warp.sync -1")
-            ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
-                f"{{{64 * half}, {orow}}}], [{wstage}]")
-            ins(f"@{lead} cp.async.bulk.commit_group")
+        lastb = t("b32")
+        ins(f"sub.u32 {lastb}, {sj}, 1")
+        if H == 2:
+            # the row sum is the two halves' partial sums (f32 addition commutes: both halves get
+            # the same bits); then O 32 columns at a time, 16 per box (32 x 32 B, unswizzled), lane
+            # 0 storing the box at columns D/2 h + 16 b
+            ins(f"st.shared.f32 [{xmine}+{sum_off}], {l}")
+            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{l_full[0]}]")
+            kit.wait(f"{gb8}+{l_full[0]}", kit.parity(sti, 1), 5)
+            other = t("f32")
+            ins(f"ld.shared.f32 {other}, [{xpart}+{sum_off}]")
+            ins(f"add.rn.f32 {l}, {l}, {other}")
+            inv = t("f32")
+            ins(f"rcp.rn.f32 {inv}, {l}")
+            ocol0 = t("b32")
+            ins(f"mul.lo.u32 {ocol0}, {half}, {DH}")
+            kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
+            ins("tcgen05.fence::after_thread_sync")
+            for c in range(DH // 32):
+                ov = [t("f32") for _ in range(32)]
+                a = t("b32")
+                ins(f"add.u32 {a}, {ocol}, {32 * c}")
+                ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
+                ins("tcgen05.wait::ld.sync.aligned")
+                if c == DH // 32 - 1:
+                    ins("tcgen05.fence::before_thread_sync")
+                    ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
+                for b in range(2):
+                    ins(f"@{lead} cp.async.bulk.wait_group.read 0")
+                    ins("bar.warp.sync -1")
+                    oh = [t("b32") for _ in range(8)]
+                    for k in range(8):
+                        x0, x1 = ov[16 * b + 2 * k], ov[16 * b + 2 * k + 1]
+                        ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
+                        ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
+                        ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
+                    ins(f"st.shared.v4.b32 [{srowa}], {{{', '.join(oh[:4])}}}")
+                    ins(f"st.shared.v4.b32 [{srowa}+16], {{{', '.join(oh[4:])}}}")
+                    ins("fence.proxy.async.shared::cta")
+                    ins("bar.warp.sync -1")
+                    oc = t("b32")
+                    ins(f"add.u32 {oc}, {ocol0}, {32 * c + 16 * b}")
+                    ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
+                        f"{{{oc}, {orow}}}], [{wstage}]")
+                    ins(f"@{lead} cp.async.bulk.commit_group")
+        else:
+            kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
+            ins("tcgen05.fence::after_thread_sync")
+            ov = [t("f32") for _ in range(D)]
+            for c in range(D // 32):
+                a = t("b32")
+                ins(f"add.u32 {a}, {ocol}, {32 * c}")
+                ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            ins("tcgen05.fence::before_thread_sync")
+            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
+            inv = t("f32")
+            ins(f"rcp.rn.f32 {inv}, {l}")
+            # 64 columns at a time: this row's 128 bytes into the warp's 32 x 128 B box (16-byte chunk
+            # c of row r at chunk c ^ (r % 8): the 128-byte swizzle, conflict-free)
+            for hb in range(D // 64):
+                ins(f"@{lead} cp.async.bulk.wait_group.read 0")
+                ins("bar.warp.sync -1")
+                for c in range(8):
+                    oh = [t("b32") for _ in range(4)]
+                    for k in range(4):
+                        x0, x1 = ov[64 * hb + 8 * c + 2 * k], ov[64 * hb + 8 * c + 2 * k + 1]
+                        ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
+                        ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
+                        ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
+                    ch = t("b32")
+                    ins(f"xor.b32 {ch}, {r7}, {c}")
+                    ins(f"mad.lo.u32 {ch}, {ch}, 16, {srowa}")
+                    ins(f"st.shared.v4.b32 [{ch}], {{{', '.join(oh)}}}")
+                ins("fence.proxy.async.shared::cta")
+                ins("bar.warp.sync -1")
+                ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
+                    f"{{{64 * hb}, {orow}}}], [{wstage}]")
+                ins(f"@{lead} cp.async.bulk.commit_group")
         ins(f"add.u32 {sti}, {sti}, 1")
         ins(f"add.u32 {stile}, {stile}, {ncta}")
         ins(f"setp.lt.u32 {p}, {sti}, {nt}")
