@@ -93,3 +93,32 @@ def test_strided_sum_plans():
     assert isinstance(f02, StridedReduce) and f02.row_mode and f02.sidecar() is None
     r03 = recognise(_kernel(_ir(GOLDEN / "r03_mean")))
     assert "peer" not in (r03.sidecar() or {})                 # a mean is not combined across GPUs
+
+
+@pytest.mark.parametrize("split,threads,box", [("1", 192, 64), ("2", 320, 64), ("4", 576, 32)])
+def test_attention_pair_plan(tmp_path, monkeypatch, split, threads, box):
+    """The opt-in 2-SM attention: CTA pairs (.reqnctapercluster 2), an even grid of at most 74
+    pairs, the leader-signalled TMA of each CTA's halves, tcgen05 cta_group::2 throughout."""
+    from thompiler.families.attention_pair import TcAttentionPair
+    monkeypatch.setenv("THOMPILER_ATTN_PAIR", "1")
+    monkeypatch.setenv("THOMPILER_ATTN_PAIR_SPLIT", split)
+    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
+    assert isinstance(fam, TcAttentionPair)
+    assert (fam.threads, fam.box_cols, fam.pair_tiles, fam.pairs) == (threads, box, 1024, 74)
+    assert fam.smem <= 227 * 1024 and fam.ks >= 4
+    ptx = fam.emit()
+    assert ".reqnctapercluster 2, 1, 1" in ptx and '"grid":[148,1,1]' in ptx
+    assert "tcgen05.mma.cta_group::1" not in ptx and "tcgen05.cp.cta_group::2.128x256b" in ptx
+    assert "cp.async.bulk.tensor.2d.cta_group::2" in ptx and "mapa.shared::cluster" in ptx
+    assert not re.search(r"cp\.async\.bulk[^\n]*multicast", ptx)     # no load is multicast
+
+
+def test_attention_pair_needs_opt_in_and_shape(tmp_path, monkeypatch):
+    from thompiler.families.attention_pair import TcAttentionPair
+    monkeypatch.delenv("THOMPILER_ATTN_PAIR", raising=False)
+    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 1, 2, 256, 128))))
+    assert isinstance(fam, TcAttention) and not isinstance(fam, TcAttentionPair)
+    monkeypatch.setenv("THOMPILER_ATTN_PAIR", "1")
+    for shape in ((1, 2, 384, 128), (2, 2, 512, 64)):         # S not a multiple of 256, or d = 64
+        fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / f"b{shape[2]}{shape[3]}", *shape))))
+        assert not isinstance(fam, TcAttentionPair)

@@ -36,13 +36,16 @@ class Kit:
         self.em, self.errp, self.end = em, errp, end
         self.q = em.tmp("pred")
 
-    def wait(self, bar: str, parity: str, code: int) -> None:
+    def wait(self, bar: str, parity: str, code: int, cluster: bool = False) -> None:
+        """Bounded wait for the phase of parity ``parity`` of the barrier at ``bar``; ``cluster``
+        acquires at cluster scope (the barrier's arrivals come from the other CTA of a pair)."""
         em = self.em
+        sem = ".acquire.cluster" if cluster else ""
         top, ok = em.label("wait"), em.label("waited")
         n = em.tmp("b32")
         em.ins(f"mov.u32 {n}, 0")
         em.place(top)
-        em.ins(f"mbarrier.try_wait.parity.shared::cta.b64 {self.q}, [{bar}], {parity}")
+        em.ins(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {self.q}, [{bar}], {parity}")
         em.ins(f"@{self.q} bra {ok}")
         em.ins(f"add.u32 {n}, {n}, 1")
         em.ins(f"setp.lt.u32 {self.q}, {n}, {WAIT_LIMIT}")
