@@ -236,16 +236,57 @@ class RowOps:
             r = runner.run_batch(batch)
             if not r["ok"]:
                 raise RuntimeError(r["stderr"])
+        sec_three = (time.perf_counter() - t) / steps
+        runner.release()
+        # the same step as 1024-row requests (the same row kernels compiled for 1024 rows), prepared
+        # once: one thr_run_batch of 3 x 8 requests per step, so each direction's copies stream back
+        # to back while the kernels run
+        chunk = self.E2E_CHUNK_ROWS
+        kch = self._chunk_kernels(chunk)
+        creqs = []
+        for kind in self.kinds:
+            for r0 in range(0, self.rows, chunk):
+                a = []
+                for n in kch[kind].arg_order:
+                    if n == "x":
+                        a.append({"array": host[kind][0][r0:r0 + chunk]})
+                    elif n == "w":
+                        a.append({"array": hw.numpy()})
+                    elif n in consts:
+                        a.append({"array": consts[n]})
+                    else:
+                        a.append({"array": host[kind][1][r0:r0 + chunk], "output": True})
+                creqs.append((kch[kind].fn, kch[kind].plan, a, kch[kind].arg_order))
+        for kind in self.kinds:
+            host[kind][1][...] = 0
+        prepared = runner.PreparedBatch(creqs)
+        r = prepared.run()
+        if not r["ok"]:
+            raise RuntimeError(r["stderr"])
+        for kind, fn in (("softmax", lambda x: torch.softmax(x, -1)),
+                         ("l2norm", lambda x: x / torch.sqrt((x * x).sum(-1, keepdim=True)))):
+            rows = [0, chunk - 1, chunk, self.rows - 1]
+            xr = torch.from_numpy(host[kind][0][rows]).double()
+            assert torch.allclose(torch.from_numpy(host[kind][1][rows]).double(), fn(xr), rtol=1e-5, atol=1e-6), kind
+        t = time.perf_counter()
+        for _ in range(steps):
+            r = prepared.run()
+            if not r["ok"]:
+                raise RuntimeError(r["stderr"])
         sec = (time.perf_counter() - t) / steps
         runner.release()
+        for k in kch.values():
+            k.close()
         h2d = sum(h[0].nbytes for h in host.values()) + hw.numel() * 4 + 8
         d2h = sum(h[1].nbytes for h in host.values())
         # the device-API pipeline for comparison (one GPU only: it pins another 768 MB of host memory)
         streamed = self.e2e_streamed(steps) if self.world == 1 else None
         out = {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3,
-               "how": "one thr_run_batch per step on pinned host buffers (the C-ABI host-buffer call: the "
-                      "three requests' copies in, kernels and copies out overlap on three streams)",
+               "how": f"one thr_run_batch per step on pinned host buffers (the C-ABI host-buffer call, its "
+                      f"descriptors prepared once), the three row ops as {3 * self.rows // chunk} requests of "
+                      f"{chunk} rows each: copies in, kernels and copies out overlap on three streams",
+               "three_requests": {"value": self.bytes_per_step / sec_three / 1e9, "ms_per_step": sec_three * 1e3},
                "one_thr_run_per_kernel": {"value": self.bytes_per_step / sec_single / 1e9,
                                           "ms_per_step": sec_single * 1e3}}
         if streamed is not None:
@@ -256,19 +297,26 @@ class RowOps:
                        "and the kernels overlap"}
         return out
 
-    def e2e_streamed(self, steps: int, chunk_rows: int = 1024) -> dict:
-        """The same three row ops on host data, chunked by rows and pipelined on three streams
-        (copy in, compute, copy out); each step copies every input in and every result out."""
+    E2E_CHUNK_ROWS = 1024
+
+    def _chunk_kernels(self, chunk_rows: int) -> dict:
+        """The three row kernels compiled for [chunk_rows, cols] (one CTA per row, as the full ones)."""
         from thompiler import synth
         from thompiler.device import DeviceKernel
-        torch = self.torch
-        nch = self.rows // chunk_rows
-        tmp = Path(tempfile.mkdtemp(prefix="bench_rowops_e2e_"))
+        tmp = Path(tempfile.mkdtemp(prefix="bench_rowops_chunk_"))
         kch = {}
         for kind in self.kinds:
             d = synth.row_package(tmp / kind, kind, chunk_rows, self.cols, eps=self.eps)
             meta = json.loads((d / "meta.json").read_text())
             kch[kind] = DeviceKernel(d / f"{meta['kernels'][0]['entry']}.ir.json", device=self.dev)
+        return kch
+
+    def e2e_streamed(self, steps: int, chunk_rows: int = 1024) -> dict:
+        """The same three row ops on host data, chunked by rows and pipelined on three streams
+        (copy in, compute, copy out); each step copies every input in and every result out."""
+        torch = self.torch
+        nch = self.rows // chunk_rows
+        kch = self._chunk_kernels(chunk_rows)
         xh = {k: torch.empty(self.rows, self.cols, pin_memory=True) for k in self.kinds}
         yh = {k: torch.empty(self.rows, self.cols, pin_memory=True) for k in self.kinds}
         for k in self.kinds:

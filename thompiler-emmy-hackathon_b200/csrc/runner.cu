@@ -137,6 +137,53 @@ int slot_buffer(size_t i, uint64_t nbytes, void **out) {
     return THR_OK;
 }
 
+// thr_run_batch's copy-in, compute and copy-out streams and its events, per device, created on
+// first use and kept (a serving loop calls the batch repeatedly); every batch waits for all of its
+// work before returning, so the next one can reuse them
+struct BatchRes {
+    cudaStream_t s[3] = {nullptr, nullptr, nullptr};
+    std::vector<cudaEvent_t> events;
+};
+std::vector<BatchRes> g_batch;
+
+int batch_resources(BatchRes **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if ((int)g_batch.size() <= dev) g_batch.resize(dev + 1);
+    BatchRes &b = g_batch[dev];
+    for (auto &st : b.s)
+        if (!st && (e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess)
+            return cuda_fail(e, "thr_run_batch: creating streams");
+    *out = &b;
+    return THR_OK;
+}
+
+int batch_event(BatchRes &b, size_t i, cudaEvent_t *ev) {
+    while (b.events.size() <= i) {
+        cudaEvent_t e = nullptr;
+        cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+        if (r != cudaSuccess) return cuda_fail(r, "cudaEventCreate");
+        b.events.push_back(e);
+    }
+    *ev = b.events[i];
+    return THR_OK;
+}
+
+void release_batch_resources() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || (int)g_batch.size() <= dev) return;
+    BatchRes &b = g_batch[dev];
+    for (auto &st : b.s)
+        if (st) {
+            cudaStreamSynchronize(st);
+            cudaStreamDestroy(st);
+            st = nullptr;
+        }
+    for (auto e : b.events) cudaEventDestroy(e);
+    b.events.clear();
+}
+
 int wait_event(cudaEvent_t ev, double timeout_s) {
     auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -370,20 +417,14 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
             if (d.ntmaps && runs[q].ntmaps && runs[q].module == d.module)
                 return fail(THR_ERR_REQUEST, "thr_run_batch: requests %d and %d need tensor maps in one module", q, r);
     }
-    cudaStream_t sin = nullptr, scmp = nullptr, sout = nullptr;
-    std::vector<cudaEvent_t> evs;
+    BatchRes *res = nullptr;
+    int rc = batch_resources(&res);
+    if (rc) return rc;
+    cudaStream_t sin = res->s[0], scmp = res->s[1], sout = res->s[2];
     std::vector<std::vector<unsigned char>> host_maps(nruns);   // alive until the batch is done
     std::vector<std::vector<uint64_t>> host_ptrs(nruns);
-    auto event = [&](cudaEvent_t *e) -> bool {
-        if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return false;
-        evs.push_back(*e);
-        return true;
-    };
-    int rc = THR_OK;
-    if (cudaStreamCreateWithFlags(&sin, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&scmp, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaStreamCreateWithFlags(&sout, cudaStreamNonBlocking) != cudaSuccess)
-        rc = fail(THR_ERR_CUDA, "thr_run_batch: creating streams");
+    size_t nev = 0;
+    auto event = [&](cudaEvent_t *e) -> bool { return batch_event(*res, nev++, e) == THR_OK; };
     // the batch's buffers sit after the slots thr_run uses for one request's arguments
     size_t slot = 4096;
     for (int r = 0; r < nruns && rc == THR_OK; ++r) {
@@ -467,15 +508,11 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
         }
     }
     if (rc != THR_OK) {
-        // leave nothing in flight that reads the caller's host buffers
-        if (sin) cudaStreamSynchronize(sin);
-        if (scmp) cudaStreamSynchronize(scmp);
-        if (sout) cudaStreamSynchronize(sout);
+        // leave nothing in flight that reads the caller's host buffers (or the reused events)
+        cudaStreamSynchronize(sin);
+        cudaStreamSynchronize(scmp);
+        cudaStreamSynchronize(sout);
     }
-    for (auto e : evs) cudaEventDestroy(e);
-    if (sin) cudaStreamDestroy(sin);
-    if (scmp) cudaStreamDestroy(scmp);
-    if (sout) cudaStreamDestroy(sout);
     return rc;
 }
 
@@ -523,6 +560,7 @@ int thr_synchronize(void) {
 }
 
 int thr_release_buffers(void) {
+    release_batch_resources();
     for (auto &s : g_slots)
         if (s.ptr) cudaFree(s.ptr);
     g_slots.clear();

@@ -333,44 +333,67 @@ def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0,
     return {"ok": True, "median_us": float(med.value)}
 
 
+class PreparedBatch:
+    """Independent POST /run requests for thr_run_batch with their C descriptors built once, so a
+    caller that repeats a batch (a serving loop, the e2e benchmark) pays no per-call Python setup.
+    ``requests``: (function, plan, args, arg_order) tuples, ``args`` as for ``run``; pass pinned,
+    C-contiguous host arrays for the copies to overlap and to be read and written in place (others
+    are staged through private copies, refreshed on every run)."""
+
+    def __init__(self, requests: list) -> None:
+        self.n = len(requests)
+        self.descs = (ThrRunDesc * max(1, self.n))()
+        self._keep = []
+        self._staged = []                       # (caller's array, private copy, is output)
+        for r, (function, plan, args, arg_order) in enumerate(requests):
+            arr = (ThrArg * max(1, len(args)))()
+            for i, a in enumerate(args):
+                x = np.ascontiguousarray(a["array"])
+                if x is not a["array"]:
+                    self._staged.append((a["array"], x, bool(a.get("output"))))
+                self._keep.append(x)
+                arr[i].host = x.ctypes.data
+                arr[i].nbytes = x.nbytes
+                arr[i].kind = 1 if a.get("output") else 0
+                arr[i].zero_each = 1 if a.get("zero_each") else 0
+            d = self.descs[r]
+            d.module, d.function = function.module.handle, function.handle
+            d.grid, d.block = _dims(plan.grid), _dims(plan.block)
+            d.smem_bytes, d.nargs, d.args = int(plan.smem), len(args), arr
+            if plan.tmaps:
+                specs, names = _tmap_specs(plan, arg_order)
+                table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
+                d.tmaps, d.ntmaps, d.ptr_table = specs, len(plan.tmaps), table
+                self._keep.append((specs, names, table))
+            self._keep.append(arr)
+        # one error-word read per module that has one
+        seen, self._checks = set(), []
+        for function, plan, _, _ in requests:
+            if plan.error_word and function.module.handle not in seen:
+                seen.add(function.module.handle)
+                self._checks.append((function.module, plan))
+
+    def run(self, timeout_s: float = 60.0) -> dict:
+        for src, x, out in self._staged:
+            if not out:
+                x[...] = src
+        st = library().thr_run_batch(self.descs, self.n, float(timeout_s))
+        if st:
+            return {"ok": False, "stage": STAGES.get(st, "cuda"), "stderr": last_error()}
+        for src, x, out in self._staged:
+            if out:
+                src[...] = x
+        for module, plan in self._checks:
+            err = read_error_word(module, plan)
+            if err:
+                return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
+        return {"ok": True}
+
+
 def run_batch(requests: list, timeout_s: float = 60.0) -> dict:
     """Several independent POST /run requests with their copies and launches overlapped
-    (thr_run_batch).  ``requests``: (function, plan, args, arg_order) tuples, ``args`` as for
-    ``run``; pass pinned host arrays for the copies to overlap."""
-    descs = (ThrRunDesc * max(1, len(requests)))()
-    keep = []
-    for r, (function, plan, args, arg_order) in enumerate(requests):
-        arr = (ThrArg * max(1, len(args)))()
-        xs = []
-        for i, a in enumerate(args):
-            x = np.ascontiguousarray(a["array"])
-            xs.append(x)
-            arr[i].host = x.ctypes.data
-            arr[i].nbytes = x.nbytes
-            arr[i].kind = 1 if a.get("output") else 0
-            arr[i].zero_each = 1 if a.get("zero_each") else 0
-        d = descs[r]
-        d.module, d.function = function.module.handle, function.handle
-        d.grid, d.block = _dims(plan.grid), _dims(plan.block)
-        d.smem_bytes, d.nargs, d.args = int(plan.smem), len(args), arr
-        specs, table, names = None, None, None
-        if plan.tmaps:
-            specs, names = _tmap_specs(plan, arg_order)
-            table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
-            d.tmaps, d.ntmaps, d.ptr_table = specs, len(plan.tmaps), table
-        keep.append((arr, xs, (specs, names, table), args))
-    st = library().thr_run_batch(descs, len(requests), float(timeout_s))
-    if st:
-        return {"ok": False, "stage": STAGES.get(st, "cuda"), "stderr": last_error()}
-    for arr, xs, _, args in keep:
-        for a, x in zip(args, xs):
-            if a.get("output") and x is not a["array"]:
-                a["array"][...] = x
-    for (function, plan, _, _) in requests:
-        err = read_error_word(function.module, plan)
-        if err:
-            return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
-    return {"ok": True}
+    (thr_run_batch), prepared and run once; see ``PreparedBatch``."""
+    return PreparedBatch(requests).run(timeout_s)
 
 
 def release() -> None:
