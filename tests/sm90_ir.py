@@ -1,0 +1,76 @@
+"""Test packages in the IR vocabulary the reference compiler does not lower (the statements
+marked * in its TASK.md: TMA copies, mbarriers, Select, ZeroPrologue, built-in and call
+expressions).  No emmy-generated sample of these exists, so the packages are written here from
+the IR reference's field lists, in the repr format of the shipped kernels."""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+from thompiler import ir
+from thompiler.synth import B, F32T, L, V, _graph, _write, assign, axis
+
+N, TILE, T = 256, 64, 256            # x[N, N] f32, one CTA per TILE x TILE tile, T threads
+
+
+def tma_transpose_package(outdir: Path, swizzle=None) -> Path:
+    """y = x^T: each CTA loads its 64 x 64 tile of x into shared memory with one TMA box copy
+    (TmaDescriptor / MbarrierInit / MbarrierArriveExpectTx / TmaLoad / MbarrierWait), then
+    each thread writes 16 elements of the transposed tile."""
+    tiles = (N // TILE) ** 2
+    per = TILE * TILE // T
+    ty = B("/", V("t"), L(N // TILE))
+    tx = B("%", V("t"), L(N // TILE))
+    e = B("+", B("*", V("lane"), L(per)), V("j"))          # this thread's j-th element of the tile
+    r, c = B("/", e, L(TILE)), B("%", e, L(TILE))
+    body = (
+        ir.Smem("buf", (TILE, TILE), "float", 1024),
+        ir.Smem("bar", (1,), "uint64_t", 8),
+        ir.TmaDescriptor("dx", "x", (N, N), (TILE, TILE), swizzle, F32T),
+        ir.MbarrierInit("bar", L(1), L(0)),
+        ir.Sync(0, None, False),
+        ir.Cond(B("==", V("lane"), L(0)), (
+            ir.MbarrierArriveExpectTx("bar", L(TILE * TILE * 4), L(0)),
+            ir.TmaLoad("buf", (L(0), L(0)), "dx", (B("*", ty, L(TILE)), B("*", tx, L(TILE))), "bar", L(0)),
+        ), ()),
+        ir.MbarrierWait("bar", L(0), L(0)),
+        ir.Loop(axis("j", per), (
+            ir.Load(("v",), "buf", (r, c), F32T),
+            ir.Write("y", (B("+", B("*", tx, L(TILE)), c), B("+", B("*", ty, L(TILE)), r)), ("v",), F32T,
+                     False, "NONE"),
+        ), False, False),
+    )
+    tile = ir.Tile((axis("t", tiles), axis("lane", T)), body, T, 0, None, None, "m")
+    g = _graph({"x": ((N, N), "f32")}, {}, "y", (N, N), "k_tma_transpose", tile)
+    args = [{"name": "x", "dtype": "f32", "shape": [N, N], "seed": 0},
+            {"name": "y", "dtype": "f32", "shape": [N, N], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x", "y"], "grid": [tiles, 1, 1], "block": [T, 1, 1], "smem_bytes": 0,
+             "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_tma_transpose", "x.t()", "k_tma_transpose", g, kmeta, 0, 0)
+
+
+M = 4096                             # elements of the Select kernel
+
+
+def select_package(outdir: Path) -> Path:
+    """y[i] = x[min(i, 99)] if i < 100 else x[i]^2, with i read back from the built-ins, the flat
+    offset of y from a FlatIndex, int casts; and ZeroPrologue clearing the first 64 words of z."""
+    i = B("+", B("*", ir.Builtin("blockIdx.x"), L(T)), ir.Builtin("threadIdx.x"))
+    body = (
+        ir.ZeroPrologue("z", L(64)),
+        ir.Let("i", ir.CastExpr("int", i), ir.DataType("i32", "int32", 4)),
+        ir.Let("f", ir.FlatIndex("y", (V("a0"),)), ir.DataType("i32", "int32", 4)),
+        ir.Load(("lo",), "x", (ir.FuncCallExpr("min", (V("i"), L(99))),), F32T),
+        ir.Load(("v",), "x", (V("a0"),), F32T),
+        assign("sq", "multiply", "v", "v"),
+        ir.Select("s", (ir.Branch("lo", B("<", V("i"), L(100))), ir.Branch("sq", None))),
+        ir.Write("y", (V("f"),), ("s",), F32T, False, "NONE"),
+    )
+    tile = ir.Tile((axis("a0", M),), body, T, 0, None, None, "m")
+    g = _graph({"x": ((M,), "f32"), "z": ((M,), "f32")}, {}, "y", (M,), "k_select", tile)
+    args = [{"name": "x", "dtype": "f32", "shape": [M], "seed": 0},
+            {"name": "z", "dtype": "f32", "shape": [M], "seed": 1},
+            {"name": "y", "dtype": "f32", "shape": [M], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x", "z", "y"], "grid": [M // T, 1, 1], "block": [T, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_select", "select", "k_select", g, kmeta, 0, 0)

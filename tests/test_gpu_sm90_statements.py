@@ -1,0 +1,53 @@
+"""GPU checks of the IR statements the reference compiler does not lower (TMA box copies with
+mbarriers, Select, ZeroPrologue, built-in / call / cast index expressions, FlatIndex): the
+kernels of tests/sm90_ir.py against numpy, through the device-pointer launch (tensor maps
+encoded from the launch's pointers) and the host-buffer C-ABI run (tensor maps per request).
+The reference has no lowering of these statements to compare with, so numpy is the check."""
+
+import numpy as np
+import pytest
+
+from sm90_ir import M, N, select_package, tma_transpose_package
+from thompiler import problems, runner
+from thompiler.device import DeviceKernel
+
+pytestmark = pytest.mark.gpu
+
+
+def test_tma_transpose_device_pointers(tmp_path):
+    import torch
+    d = tma_transpose_package(tmp_path / "t")
+    k = DeviceKernel(d / "k_tma_transpose.ir.json")
+    assert k.plan.tmaps and not k.plan.tuned
+    x = torch.randn(N, N, device="cuda")
+    for trial in range(2):                          # new pointers: the tensor map is re-encoded
+        x = x + trial
+        y = torch.full((N, N), float("nan"), device="cuda")
+        k({"x": x.data_ptr(), "y": y.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert runner.read_error_word(k.module, k.plan) == 0
+        assert torch.equal(y, x.t())
+    k.close()
+
+
+def test_tma_transpose_host_buffers(tmp_path):
+    pkg = problems.load_package(tma_transpose_package(tmp_path / "t"))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)["x"]
+    np.testing.assert_array_equal(res["outputs"]["y"], x.T)
+
+
+def test_select_zero_prologue(tmp_path):
+    import torch
+    d = select_package(tmp_path / "s")
+    k = DeviceKernel(d / "k_select.ir.json")
+    x = torch.randn(M, device="cuda")
+    z = torch.ones(M, device="cuda")
+    y = torch.full((M,), float("nan"), device="cuda")
+    k({"x": x.data_ptr(), "z": z.data_ptr(), "y": y.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    i = torch.arange(M, device="cuda")
+    want = torch.where(i < 100, x[torch.clamp(i, max=99)], x * x)
+    assert torch.equal(y, want)
+    assert torch.all(z[:64] == 0) and torch.all(z[64:] == 1)
+    k.close()

@@ -33,8 +33,9 @@ def test_kernel_info_follows_arg_order():
 
 
 def test_unknown_constructor_is_kept_opaque():
-    s = ir.parse_stmt("TmaLoad(smem='a', coords=(Var(name='i'),), mbar='m')")
-    assert isinstance(s, ir.Opaque) and s.kind == "TmaLoad"
+    s = ir.parse_stmt("WgmmaMma(c_frags=('c0',), b_desc='bd', shape=(64, 128, 16), scale_d=Var(name='i'))")
+    assert isinstance(s, ir.Opaque) and s.kind == "WgmmaMma"
+    assert dict(s.fields)["b_desc"] == "bd"
 
 
 def test_rejects_non_constructor_syntax():

@@ -1,0 +1,104 @@
+"""The IR statements the reference compiler does not lower (TASK.md's * entries), on the CPU:
+they parse, lower to PTX that ptxas accepts for sm_100a, record their tensor maps in the
+launch sidecar, and refuse at compile time the tensor maps the TMA unit would reject."""
+
+import re
+import shutil
+import subprocess
+
+import pytest
+
+from sm90_ir import N, TILE, select_package, tma_transpose_package
+from thompiler import ir, load, synth
+from thompiler.compiler import compile_kernel
+from thompiler.emitter import read_sidecar
+
+
+def _ptx(d):
+    return compile_kernel(load.load(str(next(d.glob("*.ir.json")))))
+
+
+def _ptxas(ptx, tmp_path):
+    if shutil.which("ptxas") is None:
+        pytest.skip("ptxas not on PATH")
+    f = tmp_path / "k.ptx"
+    f.write_text(ptx)
+    r = subprocess.run(["ptxas", "-arch=sm_100a", str(f), "-o", str(tmp_path / "k.cubin")],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+
+
+def test_statements_parse_from_repr():
+    stmts = [ir.TmaDescriptor("d", "x", (8, 16), (8, 16), "B64", synth.F32T),
+             ir.TmaLoad("buf", (synth.L(0),), "d", (synth.L(0), synth.L(0)), "bar", synth.L(1)),
+             ir.MbarrierInit("bar", synth.L(1), synth.L(0)), ir.MbarrierArriveExpectTx("bar", synth.L(512), None),
+             ir.MbarrierArrive("bar", None), ir.MbarrierWait("bar", synth.V("ph"), None), ir.SetMaxNReg(232, "inc"),
+             ir.Select("s", (ir.Branch("a", synth.B("<", synth.V("i"), synth.L(3))), ir.Branch("b", None))),
+             ir.ZeroPrologue("z", synth.L(8)), ir.Pre("p", "c", (synth.L(0),)),
+             ir.Carry("c", "v", (synth.L(0),), synth.L(0), synth.F32T)]
+    for s in stmts:
+        assert ir.parse_stmt(synth.to_repr(s)) == s
+    # an arm written with another constructor name keeps its fields
+    sel = ir.parse_stmt("Select(name='s', branches=(SelectBranch(value='a', select=None),))")
+    assert isinstance(sel, ir.Select) and isinstance(sel.branches[0], ir.Opaque)
+
+
+def test_tma_transpose_lowers(tmp_path):
+    ptx = _ptx(tma_transpose_package(tmp_path / "t"))
+    side = read_sidecar(ptx)
+    assert side["error_word"] == "thc_error" and "grid" not in side          # meta.json's launch
+    (m,) = side["ir_tmaps"]
+    assert m == {"global": "thc_tmap_dx", "param": "x", "dtype": "f32", "dims": [N, N], "strides": [N * 4],
+                 "box": [TILE, TILE], "swizzle": 0}
+    assert "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes" in ptx
+    assert "mbarrier.init.shared::cta.b64" in ptx and "fence.mbarrier_init.release.cluster" in ptx
+    assert "mbarrier.arrive.expect_tx.shared::cta.b64" in ptx and "mbarrier.try_wait.parity" in ptx
+    assert re.search(r"setp\.lt\.u32 [^,]+, [^,]+, 4194304", ptx)                # the wait is bounded
+    _ptxas(ptx, tmp_path)
+
+
+def test_select_zero_prologue_builtins_lower(tmp_path):
+    ptx = _ptx(select_package(tmp_path / "s"))
+    for s in ("%ctaid.x", "%tid.x", "min.s32", "selp.f32", "st.global.u32"):
+        assert s in ptx, s
+    _ptxas(ptx, tmp_path)
+
+
+@pytest.mark.parametrize("box,swizzle,why", [((64, 2), None, "not a multiple of 16"),
+                                            ((300, 64), None, "outside 1..256"),
+                                            ((64, 64), "B128", "wider than the 128-byte swizzle"),
+                                            ((64, 32), "B7", "swizzle")])
+def test_bad_tensor_maps_refused(tmp_path, box, swizzle, why):
+    d = tma_transpose_package(tmp_path / "t")
+    f = next(d.glob("*.ir.json"))
+    txt = f.read_text().replace("box_extents=(64, 64)", f"box_extents={box}")
+    txt = txt.replace("swizzle=None, dtype=DataType", f"swizzle={swizzle!r}, dtype=DataType")
+    f.write_text(txt)
+    with pytest.raises((ValueError, NotImplementedError), match=why):
+        _ptx(d)
+
+
+def test_set_max_nreg_and_checks(tmp_path):
+    from thompiler.emitter import Emitter
+    from thompiler.handlers.async_copy import emit_set_max_nreg
+    from thompiler.walk import Walker
+    k = load.load(str(next(select_package(tmp_path / "s").glob("*.ir.json"))))
+    w = Walker(Emitter(), k)
+    emit_set_max_nreg(w, ir.SetMaxNReg(232, "inc"))
+    emit_set_max_nreg(w, ir.SetMaxNReg(40, "dec"))
+    text = "\n".join(w.em.lines)
+    assert "setmaxnreg.inc.sync.aligned.u32 232" in text and "setmaxnreg.dec.sync.aligned.u32 40" in text
+    for bad in (ir.SetMaxNReg(230, "inc"), ir.SetMaxNReg(16, "dec"), ir.SetMaxNReg(64, "sideways")):
+        with pytest.raises(ValueError):
+            emit_set_max_nreg(w, bad)
+
+
+def test_unbuilt_vocabulary_fails_loudly(tmp_path):
+    """Wgmma* (Hopper-only instructions), Fragment* and carried state still fail at lowering,
+    naming the statement, as the reference does for every statement it lacks."""
+    d = select_package(tmp_path / "s")
+    f = next(d.glob("*.ir.json"))
+    f.write_text(f.read_text().replace("ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))",
+                                       "WgmmaFence()"))
+    with pytest.raises(NotImplementedError, match="WgmmaFence"):
+        _ptx(d)

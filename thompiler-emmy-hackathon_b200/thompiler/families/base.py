@@ -59,8 +59,9 @@ class TunedKernel:
         em.ins("ret")
         side = self.sidecar()
         if side is not None:
-            side = dict(side, family=self.family)
-        em.sidecar = side
+            # keep what the generic path's statements recorded (IR-level tensor maps)
+            side = dict(em.sidecar or {}, **side, family=self.family)
+        em.sidecar = side if side is not None else em.sidecar
         return em.render(prologue.header(), self.k.name, prologue.params(self.k))
 
     # helpers ----------------------------------------------------------------

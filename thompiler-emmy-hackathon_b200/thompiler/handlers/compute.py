@@ -141,7 +141,16 @@ def emit_let(w: "Walker", let: ir.Let) -> None:
     em.note(let.pretty())
     v = let.value
     if isinstance(v, ir.FlatIndex):
-        raise NotImplementedError(f"Let {let.name} of a FlatIndex")
+        # the row-major element offset of a coordinate, against the buffer's (or Smem array's) shape
+        p = w.kernel.param(v.buffer)
+        shape = tuple(p.shape) if p is not None else (w.smem[v.buffer].extents if v.buffer in w.smem else None)
+        if shape is None:
+            raise ValueError(f"Let {let.name}: FlatIndex of unknown buffer {v.buffer}")
+        if not shape:
+            shape = (1,)
+        off = address.flat_index(w, tuple(int(x) for x in shape), tuple(v.index), v.buffer)
+        em.ins(f"mov.s32 {em.value(let.name, 'b32')}, {off}")
+        return
     if isinstance(v, ir.Literal) and v.dtype == "float":
         ty = dtype_of(let.dtype, f"Let {let.name}")
         em.ins(f"mov.{ty.mov} {em.value(let.name, ty.reg)}, {ty.imm(float(v.value))}")
@@ -153,3 +162,84 @@ def emit_let(w: "Walker", let: ir.Let) -> None:
         em.ins(f"mov.s32 {em.value(let.name, 'b32')}, {val}")
         return
     raise NotImplementedError(f"Let {let.name} = {ir.pretty(v)}")
+
+
+def _branch_fields(b) -> tuple:
+    """(value, select) of a Select arm: a Branch, any constructor with those fields, or a pair."""
+    if isinstance(b, ir.Branch):
+        return b.value, b.select
+    if isinstance(b, ir.Opaque):
+        f = {k: v for k, v in b.fields if isinstance(k, str)}
+        if "value" in f:
+            return f["value"], f.get("select")
+    if isinstance(b, tuple) and len(b) == 2:
+        return b
+    raise NotImplementedError(f"Select branch {b!r}")
+
+
+def emit_select(w: "Walker", s: ir.Select) -> None:
+    """``name`` = the value of the first branch whose predicate holds (the last branch when
+    none does): a chain of ``selp`` from the last branch back to the first."""
+    em = w.em
+    em.note(s.pretty())
+    arms = [_branch_fields(b) for b in s.branches]
+    if not arms:
+        raise ValueError(f"Select {s.name} has no branches")
+
+    def operand(v):
+        if isinstance(v, str):
+            return em.get(v), arg_type(w, v)
+        if isinstance(v, ir.Var) and v.name not in w.consts:
+            return em.get(v.name), arg_type(w, v.name)
+        if isinstance(v, ir.Literal) and v.dtype == "float":
+            return F32.imm(float(v.value)), F32
+        return expr.int_operand(w, v), I32
+
+    vals = [operand(v) for v, _ in arms]
+    tys = {t for _, t in vals}
+    if len(tys) != 1:
+        raise TypeError(f"Select {s.name}: branches of mixed types {sorted(t.name for t in tys)}")
+    (ty,) = tys
+    cur = vals[-1][0]
+    for (v, sel), (op, _) in zip(reversed(arms[:-1]), reversed(vals[:-1])):
+        if sel is None:
+            cur = op
+            continue
+        pr = expr.pred_operand(w, sel)
+        nxt = em.tmp(ty.reg)
+        em.ins(f"selp.{ty.reg} {nxt}, {op}, {cur}, {pr}")
+        cur = nxt
+    dst = em.value(s.name, ty.reg)
+    em.ins(f"mov.{ty.mov} {dst}, {cur}")
+
+
+def emit_zero_prologue(w: "Walker", z: ir.ZeroPrologue) -> None:
+    """Zero ``words`` 32-bit words of buffer ``dst`` (another kernel's atomic accumulator) with a
+    grid-stride loop over every thread of the launch."""
+    em = w.em
+    em.note(z.pretty())
+    p = w.kernel.param(z.dst)
+    if p is None:
+        raise ValueError(f"ZeroPrologue: {z.dst} is not a kernel buffer")
+    words = expr.int_operand(w, z.words)
+    if expr.is_imm(words) and int(words) * 4 > p.nelems * p.ty.nbytes:
+        raise ValueError(f"ZeroPrologue: {words} words overrun {z.dst} ({p.nelems * p.ty.nbytes} bytes)")
+    gid, stride, a = em.tmp("b32"), em.tmp("b32"), em.tmp("b32")
+    em.ins(f"mov.u32 {gid}, %ctaid.x")
+    em.ins(f"mov.u32 {a}, %ntid.x")
+    t = em.tmp("b32")
+    em.ins(f"mov.u32 {t}, %tid.x")
+    em.ins(f"mad.lo.u32 {gid}, {gid}, {a}, {t}")
+    em.ins(f"mov.u32 {stride}, %nctaid.x")
+    em.ins(f"mul.lo.u32 {stride}, {stride}, {a}")
+    top, done = em.label("zp"), em.label("zp_done")
+    q = em.tmp("pred")
+    em.place(top)
+    em.ins(f"setp.ge.u32 {q}, {gid}, {words}")
+    em.ins(f"@{q} bra {done}")
+    ad = em.tmp("b64")
+    em.ins(f"mad.wide.u32 {ad}, {gid}, 4, {em.buffer_reg(z.dst)}")
+    em.ins(f"st.global.u32 [{ad}], 0")
+    em.ins(f"add.u32 {gid}, {gid}, {stride}")
+    em.ins(f"bra {top}")
+    em.place(done)

@@ -86,7 +86,44 @@ def int_operand(w: "Walker", e: object) -> str:
         out = em.tmp("b32")
         em.ins(f"selp.s32 {out}, {a}, {b}, {p}")
         return out
+    if isinstance(e, ir.Builtin):
+        sreg = BUILTINS.get(e.name)
+        if sreg is None:
+            raise NotImplementedError(f"built-in variable {e.name!r}")
+        out = em.tmp("b32")
+        em.ins(f"mov.u32 {out}, {sreg}")
+        return out
+    if isinstance(e, ir.CastExpr):
+        name = getattr(e.dtype, "name", e.dtype)
+        if name not in INT_NAMES:
+            raise NotImplementedError(f"cast to {name!r} in an integer expression")
+        inner = e.expr
+        if isinstance(inner, ir.Var) and inner.name not in w.consts and em.cls_of(inner.name) in ("f32", "f64"):
+            out = em.tmp("b32")             # C's float -> int conversion truncates toward zero
+            em.ins(f"cvt.rzi.s32.{em.cls_of(inner.name)} {out}, {em.get(inner.name)}")
+            return out
+        return int_operand(w, inner)
+    if isinstance(e, ir.FuncCallExpr):
+        fn = INT_FUNCS.get(e.name)
+        if fn is None or len(e.args) != fn[1]:
+            raise NotImplementedError(f"integer function {e.name}({len(e.args)} args)")
+        args = [int_operand(w, a) for a in e.args]
+        if all(is_imm(a) for a in args):
+            return str(fn[2](*[int(a) for a in args]))
+        out = em.tmp("b32")
+        em.ins(f"{fn[0]} {out}, {', '.join(args)}")
+        return out
     raise NotImplementedError(f"index expression {type(e).__name__}")
+
+
+# Builtin names (CUDA spelling) -> PTX special registers
+BUILTINS = {f"{v}.{c}": f"%{r}.{c}" for v, r in (("threadIdx", "tid"), ("blockIdx", "ctaid"),
+                                                 ("blockDim", "ntid"), ("gridDim", "nctaid")) for c in "xyz"}
+BUILTINS.update({"laneid": "%laneid", "warpid": "%warpid", "smid": "%smid"})
+INT_NAMES = ("int", "int32", "i32", "s32")
+# integer functions of index expressions: PTX instruction, arity, compile-time value
+INT_FUNCS = {"min": ("min.s32", 2, min), "minimum": ("min.s32", 2, min), "max": ("max.s32", 2, max),
+             "maximum": ("max.s32", 2, max), "abs": ("abs.s32", 1, abs)}
 
 
 WIDE_OPS = {"+": "add.s64", "-": "sub.s64", "*": "mul.lo.s64", "/": "div.s64", "%": "rem.s64"}
@@ -148,6 +185,10 @@ def value_type(w: "Walker", e: object) -> Ty:
         if a != b:
             raise TypeError(f"conditional with mixed branch types: {e.pretty()}")
         return a
+    if isinstance(e, (ir.Builtin, ir.FuncCallExpr)):
+        return I32
+    if isinstance(e, ir.CastExpr) and getattr(e.dtype, "name", e.dtype) in INT_NAMES:
+        return I32
     raise NotImplementedError(f"expression {type(e).__name__}")
 
 

@@ -60,7 +60,10 @@ PRED = Ty("pred", "int", "pred", "pred", "pred", 0)
 BUFFER_TYPES: dict[str, Ty] = {"f16": F16, "f32": F32, "f64": F64}
 
 # Smem.dtype is the C element type emmy renders, not an IR dtype.
-SMEM_TYPES: dict[str, Ty] = {"__half": F16, "half": F16, "float": F32, "double": F64}
+SMEM_TYPES: dict[str, Ty] = {"__half": F16, "half": F16, "float": F32, "double": F64,
+                             # 8-byte words: the mbarrier arrays of the TMA statements
+                             "uint64_t": I64, "int64_t": I64, "unsigned long long": I64, "long long": I64,
+                             "u64": I64, "i64": I64}
 
 # Literal.dtype -> type of the literal.
 LITERAL_TYPES: dict[str, Ty] = {"int": I32, "float": F32}

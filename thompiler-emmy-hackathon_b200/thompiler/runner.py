@@ -228,12 +228,16 @@ class LaunchPlan:
 
 
 def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> LaunchPlan:
-    """meta.json's geometry, or the tuned launch recorded in the PTX."""
-    side = module.sidecar
-    if side is None or honour_meta:
-        return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False)
+    """meta.json's geometry, or the tuned launch recorded in the PTX.  Tensor maps the IR itself
+    declares (TmaDescriptor statements: the sidecar's ``ir_tmaps``) belong to every launch."""
+    side = module.sidecar or {}
+    ir_maps = list(side.get("ir_tmaps", []))
+    if "grid" not in side or honour_meta:
+        err = side.get("error_word") if "grid" not in side else None
+        return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False,
+                          ir_maps, None, err)
     return LaunchPlan(tuple(side["grid"]), tuple(side["block"]), int(side.get("smem_bytes", 0)), True,
-                      list(side.get("tmaps", [])), side.get("tmap_ptrs"), side.get("error_word"))
+                      list(side.get("tmaps", [])) + ir_maps, side.get("tmap_ptrs"), side.get("error_word"))
 
 
 def encode_tensor_map(spec: dict, base: int) -> bytes:

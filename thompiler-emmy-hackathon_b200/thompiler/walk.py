@@ -21,7 +21,9 @@ from typing import Any, Callable
 from thompiler import ir
 from thompiler.emitter import Emitter
 from thompiler.handlers.blocks import emit_cond, emit_loop, emit_strided_loop, emit_tile
-from thompiler.handlers.compute import emit_assign, emit_let, emit_load, emit_write
+from thompiler.handlers.async_copy import (emit_mbarrier_arrive, emit_mbarrier_arrive_expect_tx, emit_mbarrier_init,
+                                           emit_mbarrier_wait, emit_set_max_nreg, emit_tma_descriptor, emit_tma_load)
+from thompiler.handlers.compute import emit_assign, emit_let, emit_load, emit_select, emit_write, emit_zero_prologue
 from thompiler.handlers.cp_async import emit_cp_async_commit, emit_cp_async_copy, emit_cp_async_wait
 from thompiler.handlers.memory import emit_smem, emit_sync
 from thompiler.handlers.mma import emit_ldmatrix_load, emit_mma_sync, emit_reg_fragment, emit_reg_store
@@ -78,4 +80,13 @@ HANDLERS: dict[type, Callable[[Walker, Any], None]] = {
     ir.LdmatrixLoad: emit_ldmatrix_load,
     ir.MmaSyncPtx: emit_mma_sync,
     ir.RegStore: emit_reg_store,
+    ir.Select: emit_select,
+    ir.ZeroPrologue: emit_zero_prologue,
+    ir.TmaDescriptor: emit_tma_descriptor,
+    ir.TmaLoad: emit_tma_load,
+    ir.MbarrierInit: emit_mbarrier_init,
+    ir.MbarrierArriveExpectTx: emit_mbarrier_arrive_expect_tx,
+    ir.MbarrierArrive: emit_mbarrier_arrive,
+    ir.MbarrierWait: emit_mbarrier_wait,
+    ir.SetMaxNReg: emit_set_max_nreg,
 }
