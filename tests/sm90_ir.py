@@ -74,3 +74,23 @@ def select_package(outdir: Path) -> Path:
     kmeta = {"node": "y", "arg_order": ["x", "z", "y"], "grid": [M // T, 1, 1], "block": [T, 1, 1],
              "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_select", "select", "k_select", g, kmeta, 0, 0)
+
+
+def stuck_wait_package(outdir: Path, n: int = 64) -> Path:
+    """y = x after an MbarrierWait that nothing completes (count 1, no arrival): the bounded wait
+    must give up, record its bit in the error word and let the kernel finish."""
+    body = (
+        ir.Smem("bar", (1,), "uint64_t", 8),
+        ir.MbarrierInit("bar", L(1), L(0)),
+        ir.Sync(0, None, False),
+        ir.MbarrierWait("bar", L(0), L(0)),
+        ir.Load(("v",), "x", (V("a0"),), F32T),
+        ir.Write("y", (V("a0"),), ("v",), F32T, False, "NONE"),
+    )
+    tile = ir.Tile((axis("a0", n),), body, n, 0, None, None, "m")
+    g = _graph({"x": ((n,), "f32")}, {}, "y", (n,), "k_stuck_wait", tile)
+    args = [{"name": "x", "dtype": "f32", "shape": [n], "seed": 0},
+            {"name": "y", "dtype": "f32", "shape": [n], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x", "y"], "grid": [1, 1, 1], "block": [n, 1, 1], "smem_bytes": 0,
+             "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_stuck_wait", "x", "k_stuck_wait", g, kmeta, 0, 0)

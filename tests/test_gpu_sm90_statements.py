@@ -7,7 +7,7 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import M, N, select_package, tma_transpose_package
+from sm90_ir import M, N, select_package, stuck_wait_package, tma_transpose_package
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -50,4 +50,27 @@ def test_select_zero_prologue(tmp_path):
     want = torch.where(i < 100, x[torch.clamp(i, max=99)], x * x)
     assert torch.equal(y, want)
     assert torch.all(z[:64] == 0) and torch.all(z[64:] == 1)
+    k.close()
+
+
+def test_wait_that_never_completes_gives_up(tmp_path):
+    """A wait on an mbarrier nothing arrives on: every thread's bounded wait runs out (2^18
+    polls, about a second), sets bit 1 of the kernel's error word and carries on, so the launch
+    finishes and the statements after the wait still run -- the failure is reported, the GPU
+    never hangs."""
+    import time
+
+    import torch
+    d = stuck_wait_package(tmp_path / "w")
+    k = DeviceKernel(d / "k_stuck_wait.ir.json")
+    x = torch.randn(64, device="cuda")
+    y = torch.zeros(64, device="cuda")
+    t0 = time.perf_counter()
+    k({"x": x.data_ptr(), "y": y.data_ptr()}, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert runner.read_error_word(k.module, k.plan) == 2
+    assert torch.equal(y, x)
+    assert elapsed < 10, elapsed
+    print(f"bounded wait gave up after {elapsed:.2f} s")
     k.close()

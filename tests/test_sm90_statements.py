@@ -53,7 +53,7 @@ def test_tma_transpose_lowers(tmp_path):
     assert "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes" in ptx
     assert "mbarrier.init.shared::cta.b64" in ptx and "fence.mbarrier_init.release.cluster" in ptx
     assert "mbarrier.arrive.expect_tx.shared::cta.b64" in ptx and "mbarrier.try_wait.parity" in ptx
-    assert re.search(r"setp\.lt\.u32 [^,]+, [^,]+, 4194304", ptx)                # the wait is bounded
+    assert re.search(r"setp\.lt\.u32 [^,]+, [^,]+, 262144", ptx)                 # the wait is bounded
     _ptxas(ptx, tmp_path)
 
 

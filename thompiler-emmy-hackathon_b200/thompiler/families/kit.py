@@ -14,7 +14,7 @@
 
 from __future__ import annotations
 
-WAIT_LIMIT = 1 << 22
+WAIT_LIMIT = 1 << 18          # try_wait rounds (~4 us each while the phase is open): ~1 s
 SWIZZLE_128B = 2
 
 

@@ -54,7 +54,7 @@ SM_COUNT = 148
 THREADS = 192
 BM, BK = 128, 64
 SMEM_LIMIT = 227 * 1024
-WAIT_LIMIT = 1 << 22          # try_wait rounds before a wait gives up
+WAIT_LIMIT = 1 << 18          # try_wait rounds before a wait gives up (~4 us each while open: ~1 s)
 EPI_WARPS = 4
 STAGE_TILE = 2048             # one epilogue store box: 32 rows x 64 bytes
 

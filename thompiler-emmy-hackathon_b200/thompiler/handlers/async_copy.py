@@ -39,7 +39,7 @@ from thompiler.lowering.types import dtype_of
 if TYPE_CHECKING:
     from thompiler.walk import Walker
 
-WAIT_LIMIT = 1 << 22
+WAIT_LIMIT = 1 << 18          # try_wait rounds (~4 us each while the phase is open): ~1 s
 ERROR_WORD = "thc_error"
 ERR_TMA_SKIPPED = 1
 ERR_WAIT_TIMEOUT = 2
