@@ -113,3 +113,51 @@ class PeerCombine:
             lib.thr_peer_close(q)
         lib.thr_peer_free(self.mine)
         self.opened = []
+
+
+class RankFailure(RuntimeError):
+    """Some ranks did not reach a step in time: ``missing`` lists them."""
+
+    def __init__(self, step: int, missing: list[int], timeout_s: float):
+        super().__init__(f"ranks {missing} did not reach step {step} within {timeout_s:.1f} s")
+        self.step, self.missing = step, missing
+
+
+class StepMonitor:
+    """Host-side failure detection between steps: before launching step ``s`` (its kernels and
+    collectives), each rank posts ``s`` to a shared key-value store (a ``torch.distributed``
+    Store) and waits, with a time limit, for every other rank's post.  A rank that raised,
+    exited or stopped is named in a ``RankFailure`` on the others before they launch anything
+    that would wait for it -- no kernel or collective is left waiting on a rank that is gone.
+    Keys are namespaced by ``tag`` so several monitors can share one store."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, tag: str = "step"):
+        if world < 1 or not 0 <= rank < world:
+            raise ValueError(f"rank {rank} of world {world}")
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.tag = float(timeout_s), tag
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.tag}/{step}/{rank}"
+
+    def arrive(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), "1")
+
+    def wait_all(self, step: int) -> None:
+        import time
+        from datetime import timedelta
+        deadline = time.monotonic() + self.timeout_s
+        missing = []
+        for r in range(self.world):
+            left = max(0.0, deadline - time.monotonic())
+            try:
+                self.store.wait([self._key(step, r)], timedelta(seconds=max(left, 0.001)))
+            except Exception:                  # the store's timeout (a RuntimeError / DistStoreError)
+                missing.append(r)
+        if missing:
+            raise RankFailure(step, missing, self.timeout_s)
+
+    def step(self, step: int) -> None:
+        """Post this rank's arrival at ``step`` and wait for all the others'."""
+        self.arrive(step)
+        self.wait_all(step)
