@@ -94,3 +94,45 @@ def stuck_wait_package(outdir: Path, n: int = 64) -> Path:
     kmeta = {"node": "y", "arg_order": ["x", "y"], "grid": [1, 1, 1], "block": [n, 1, 1], "smem_bytes": 0,
              "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_stuck_wait", "x", "k_stuck_wait", g, kmeta, 0, 0)
+
+
+ROWS, COLS = 256, 24
+
+
+def scan_package(outdir: Path) -> Path:
+    """Carried state (Carry, Pre), one thread per row of x[ROWS, COLS]:
+    y[r, j] = x[r, 0] + ... + x[r, j] and t[r] = the row total (read after the loop), and f[r] =
+    the (COLS + 1)-th Fibonacci number from a two-cell carrier whose step reads cell 0 after
+    setting it (a read within a step sees the previous state)."""
+    f32 = F32T
+    step = (
+        ir.Pre("prev", "acc", ()),
+        ir.Load(("v",), "x", (V("r"), V("j")), f32),
+        assign("s", "add", "prev", "v"),
+        ir.Carry("acc", "s", (), L(0.0, "float"), f32),
+        ir.Write("y", (V("r"), V("j")), ("s",), f32, False, "NONE"),
+        ir.Pre("fb", "fib", (L(1),)),
+        ir.Carry("fib", "fb", (L(0),), L(0.0, "float"), f32),
+        ir.Pre("fa", "fib", (L(0),)),                    # the previous step's cell 0, not fb
+        assign("fs", "add", "fa", "fb"),
+        ir.Carry("fib", "fs", (L(1),), L(1.0, "float"), f32),
+    )
+    body = (
+        ir.Loop(axis("j", COLS), step, False, False),
+        ir.Pre("tot", "acc", ()),
+        ir.Write("t", (V("r"),), ("tot",), f32, False, "NONE"),
+        ir.Pre("fn", "fib", (L(1),)),
+        ir.Write("f", (V("r"),), ("fn",), f32, False, "NONE"),
+    )
+    tile = ir.Tile((axis("r", ROWS),), body, 128, 0, None, None, "m")
+    g = _graph({"x": ((ROWS, COLS), "f32")}, {}, "y", (ROWS, COLS), "k_scan", tile)
+    g["nodes"]["y"]["outputs"] += [{"name": "t", "shape": [ROWS], "dtype": "f32"},
+                                   {"name": "f", "shape": [ROWS], "dtype": "f32"}]
+    g["outputs"] = ["y", "t", "f"]
+    args = [{"name": "x", "dtype": "f32", "shape": [ROWS, COLS], "seed": 0},
+            {"name": "y", "dtype": "f32", "shape": [ROWS, COLS], "output": True},
+            {"name": "t", "dtype": "f32", "shape": [ROWS], "output": True},
+            {"name": "f", "dtype": "f32", "shape": [ROWS], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x", "y", "t", "f"], "grid": [ROWS // 128, 1, 1], "block": [128, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_scan", "x.cumsum(-1)", "k_scan", g, kmeta, 1e-5, 1e-5)

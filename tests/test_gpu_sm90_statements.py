@@ -7,7 +7,7 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import M, N, select_package, stuck_wait_package, tma_transpose_package
+from sm90_ir import COLS, M, N, ROWS, scan_package, select_package, stuck_wait_package, tma_transpose_package
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -74,3 +74,19 @@ def test_wait_that_never_completes_gives_up(tmp_path):
     assert elapsed < 10, elapsed
     print(f"bounded wait gave up after {elapsed:.2f} s")
     k.close()
+
+
+def test_carried_state_scan(tmp_path):
+    """Carry / Pre on the GPU: a per-row prefix sum (sequential f32 adds, so bit-exact against
+    numpy's float32 cumsum), its total after the loop, and the Fibonacci carrier whose step reads
+    cell 0 after setting it -- F(COLS + 1) only if that read sees the previous state."""
+    pkg = problems.load_package(scan_package(tmp_path / "c"))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)["x"]
+    want = np.cumsum(x, axis=1, dtype=np.float32)
+    np.testing.assert_array_equal(res["outputs"]["y"], want)
+    np.testing.assert_array_equal(res["outputs"]["t"].reshape(ROWS), want[:, -1])
+    fib = [0, 1]
+    for _ in range(COLS):
+        fib = [fib[1], fib[0] + fib[1]]
+    assert np.all(res["outputs"]["f"] == fib[1]) and fib[1] == 75025

@@ -8,7 +8,7 @@ import subprocess
 
 import pytest
 
-from sm90_ir import N, TILE, select_package, tma_transpose_package
+from sm90_ir import N, TILE, scan_package, select_package, tma_transpose_package
 from thompiler import ir, load, synth
 from thompiler.compiler import compile_kernel
 from thompiler.emitter import read_sidecar
@@ -101,4 +101,26 @@ def test_unbuilt_vocabulary_fails_loudly(tmp_path):
     f.write_text(f.read_text().replace("ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))",
                                        "WgmmaFence()"))
     with pytest.raises(NotImplementedError, match="WgmmaFence"):
+        _ptx(d)
+
+
+def test_carried_state_lowers(tmp_path):
+    """Carry / Pre: each cell is seeded before its loop, copied at each step's start, replaced at
+    its end; a Pre inside the loop reads the previous step's value, after the loop the final one."""
+    ptx = _ptx(scan_package(tmp_path / "c"))
+    for cell, seed in (("acc__cell_s", "0f00000000"), ("fib__cell_0", "0f00000000"), ("fib__cell_1", "0f3F800000")):
+        assert f"mov.f32 %n_{cell}, {seed};" in ptx, cell
+    loop = ptx[ptx.index("$L_loop_2:"):ptx.index("$L_loop_end_3:")]
+    assert "mov.f32 %n_fa, %n_fib__cell_0;" in loop            # cell 0 as the step began
+    tail = ptx[ptx.index("$L_loop_end_3:"):]
+    assert "mov.f32 %n_tot, %n_acc__cell_s;" in tail
+    _ptxas(ptx, tmp_path)
+
+
+def test_carried_state_needs_constant_cells(tmp_path):
+    d = scan_package(tmp_path / "c")
+    f = next(d.glob("*.ir.json"))
+    f.write_text(f.read_text().replace("Carry(name='fib', value='fs', index=(Literal(value=1, dtype='int'),)",
+                                       "Carry(name='fib', value='fs', index=(Var(name='r'),)"))
+    with pytest.raises(NotImplementedError, match="compile-time constant"):
         _ptx(d)

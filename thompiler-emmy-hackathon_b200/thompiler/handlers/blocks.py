@@ -104,21 +104,30 @@ def static_extent(axis: ir.Axis) -> str:
 
 def emit_loop(w: "Walker", loop: ir.Loop) -> None:
     w.em.note(loop.pretty())
-    if loop.carries:
-        raise NotImplementedError(f"Loop over {loop.axis.name} carrying {list(loop.carries)}")
+    body = _with_carried_state(w, loop)
     if loop.seed:
         seed_accumulators(w, loop.body)
-    counted_loop(w, loop.axis.name, "0", static_extent(loop.axis), "1", loop.body, loop.unroll)
+    counted_loop(w, loop.axis.name, "0", static_extent(loop.axis), "1", body, loop.unroll)
+
+
+def _with_carried_state(w: "Walker", loop) -> tuple:
+    """The loop's body, bracketed per step when it sets carried state (handlers/carry.py)."""
+    from thompiler.handlers.carry import carries_in, open_cells
+    if not carries_in(loop.body) and not getattr(loop, "carries", ()):
+        return loop.body
+    begin, end = open_cells(w, loop)
+    return (begin, *loop.body, end)
 
 
 def emit_strided_loop(w: "Walker", loop: ir.StridedLoop) -> None:
     w.em.note(loop.pretty())
     if loop.seed:
         seed_accumulators(w, loop.body)
+    body = _with_carried_state(w, loop)
     start = expr.int_operand(w, loop.start)
     bound = expr.int_operand(w, loop.end) if loop.end is not None else static_extent(loop.axis)
     step = expr.int_operand(w, loop.step) if isinstance(loop.step, ir.Expr) else str(int(loop.step))
-    counted_loop(w, loop.axis.name, start, bound, step, loop.body, loop.unroll)
+    counted_loop(w, loop.axis.name, start, bound, step, body, loop.unroll)
 
 
 def counted_loop(w: "Walker", var: str, start: str, bound: str, step: str, body: tuple,

@@ -21,6 +21,7 @@ from typing import Any, Callable
 from thompiler import ir
 from thompiler.emitter import Emitter
 from thompiler.handlers.blocks import emit_cond, emit_loop, emit_strided_loop, emit_tile
+from thompiler.handlers.carry import StepBegin, StepEnd, emit_carry, emit_pre, emit_step_begin, emit_step_end
 from thompiler.handlers.async_copy import (emit_mbarrier_arrive, emit_mbarrier_arrive_expect_tx, emit_mbarrier_init,
                                            emit_mbarrier_wait, emit_set_max_nreg, emit_tma_descriptor, emit_tma_load)
 from thompiler.handlers.compute import emit_assign, emit_let, emit_load, emit_select, emit_write, emit_zero_prologue
@@ -89,4 +90,8 @@ HANDLERS: dict[type, Callable[[Walker, Any], None]] = {
     ir.MbarrierArrive: emit_mbarrier_arrive,
     ir.MbarrierWait: emit_mbarrier_wait,
     ir.SetMaxNReg: emit_set_max_nreg,
+    ir.Carry: emit_carry,
+    ir.Pre: emit_pre,
+    StepBegin: emit_step_begin,
+    StepEnd: emit_step_end,
 }
