@@ -5,7 +5,6 @@ tiles than SMs.  Each launch's wait-time-out word stays 0.
 Tolerances: f32-out matmul 1e-3 absolute (f16 products summed in f32); f16-out and attention
 rtol 2e-2 / atol 2e-3."""
 
-import numpy as np
 import pytest
 
 from thompiler import runner, synth
