@@ -1,7 +1,7 @@
 """Build the golden fixtures under tests/golden/packages/ from the reference.
 
-Run in a container that has the reference checkout (it is not needed
-afterwards: the GPU box never reads it):
+Run where the reference checkout is present (the fixtures it writes are
+all the tests need; nothing reads the checkout at test time):
 
     python tests/golden/make_golden.py [--reference /root/reference]
 

@@ -1,5 +1,5 @@
-"""Out-of-bounds writes, caught with guard bands (compute-sanitizer is not available on this
-GPU pool): every buffer of a package is placed between two 64 KiB bands of a known byte
+"""Out-of-bounds writes, caught with guard bands (no memory-checking tool runs beside these
+tests): every buffer of a package is placed between two 64 KiB bands of a known byte
 pattern, the package's kernels run through their tuned launches on the interior pointers
 (device-pointer path, tensor maps encoded for those pointers), and afterwards every band
 must be intact and the outputs must match the oracle."""

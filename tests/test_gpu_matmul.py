@@ -5,8 +5,8 @@
   oracle interpreter on the same seeded inputs;
 * the benchmark shapes (4096^3 and M=8192, N=3072, K=1024, f16 in, f32 out,
   B column-major): against the reference compiler's own PTX for the same IR
-  (mma.sync, committed nowhere: generated here from the IR through the emmy
-  stand-in is not possible on the GPU box, so the generic lowering -- which is
+  (mma.sync, committed nowhere: the emmy stand-in that generates it needs the
+  reference checkout, absent where the GPU tests run, so the generic lowering -- which is
   bit-identical to the reference PTX on every shipped package -- stands in),
   and against a float64 checksum: C @ 1 == A @ (B^T @ 1) row by row.
 Every tuned launch also checks the kernel's wait-time-out word stays 0.
