@@ -124,3 +124,62 @@ def test_carried_state_needs_constant_cells(tmp_path):
                                        "Carry(name='fib', value='fs', index=(Var(name='r'),)"))
     with pytest.raises(NotImplementedError, match="compile-time constant"):
         _ptx(d)
+
+
+def _lower_body(tmp_path, stmts, inputs=(("x", (1024,)),), out=("y", (1024,)), T=128):
+    """Lower a one-axis Tile of ``stmts`` (a ragged probe kernel) and assemble it."""
+    from sm90_ir import _graph, _write, axis
+    tile = ir.Tile((axis("a0", out[1][0]),), tuple(stmts), T, 0, None, None, "m")
+    g = _graph({n: (s, "f32") for n, s in inputs}, {}, out[0], out[1], "k_probe", tile)
+    args = [{"name": n, "dtype": "f32", "shape": list(s), "seed": i} for i, (n, s) in enumerate(inputs)]
+    args.append({"name": out[0], "dtype": "f32", "shape": list(out[1]), "output": True})
+    kmeta = {"node": out[0], "arg_order": [n for n, _ in inputs] + [out[0]], "grid": [out[1][0] // T, 1, 1],
+             "block": [T, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
+    d = _write(tmp_path / "k", "probe", "probe", "k_probe", g, kmeta, 0, 0)
+    ptx = _ptx(d)
+    _ptxas(ptx, tmp_path)
+    return ptx
+
+
+def test_runtime_forms_lower(tmp_path):
+    """Run-time operands take the checked paths: a TMA destination chosen at run time gets the
+    bound check that skips an overrunning box, a wait takes its phase from a register, a
+    ZeroPrologue its word count from an index expression, a Select mixes literal and named arms."""
+    L, V, B = synth.L, synth.V, synth.B
+    stmts = [
+        ir.Smem("buf", (4, 32, 32), "float", 1024),
+        ir.Smem("bar", (2,), "uint64_t", 8),
+        ir.TmaDescriptor("dx", "x", (32, 32), (32, 32), None, synth.F32T),
+        ir.MbarrierInit("bar", L(1), B("%", V("a0"), L(2))),
+        ir.Sync(0, None, False),
+        ir.Let("slot", B("/", V("a0"), L(256)), ir.DataType("i32", "int32", 4)),
+        ir.Cond(B("==", B("%", V("a0"), L(128)), L(0)), (
+            ir.MbarrierArriveExpectTx("bar", L(4096), B("%", V("slot"), L(2))),
+            ir.TmaLoad("buf", (V("slot"), L(0), L(0)), "dx", (L(0), L(0)), "bar", B("%", V("slot"), L(2))),
+        ), ()),
+        ir.MbarrierWait("bar", V("slot"), B("%", V("slot"), L(2))),
+        ir.ZeroPrologue("z", B("*", V("slot"), L(0))),
+        ir.Load(("v",), "x", (V("a0"),), synth.F32T),
+        ir.Select("s", (ir.Branch(L(2.5, "float"), B(">", V("a0"), L(1000))), ir.Branch("v", None))),
+        ir.Write("y", (V("a0"),), ("s",), synth.F32T, False, "NONE"),
+    ]
+    ptx = _lower_body(tmp_path, stmts, inputs=(("x", (1024,)), ("z", (1024,))))
+    assert "setp.gt.u32" in ptx                        # the run-time destination bound
+    assert "mbarrier.try_wait.parity.shared::cta.b64" in ptx and "selp.f32" in ptx
+
+
+def test_carried_state_in_unrolled_inner_loop(tmp_path):
+    """A carrier owned by an unrolled inner loop, its cells indexed by the outer unrolled
+    variable -- cell indices fold to constants."""
+    L, V = synth.L, synth.V
+    inner = ir.Loop(synth.axis("k", 4), (
+        ir.Pre("p", "acc", (V("c"),)),
+        ir.Load(("v",), "x", (V("a0"),), synth.F32T),
+        synth.assign("s", "add", "p", "v"),
+        ir.Carry("acc", "s", (V("c"),), L(0.0, "float"), synth.F32T),
+    ), True, False)
+    outer = ir.Loop(synth.axis("c", 2), (inner, ir.Pre("fin", "acc", (V("c"),)),
+                                         ir.Write("y", (V("a0"),), ("fin",), synth.F32T, False, "NONE")),
+                    True, False)
+    ptx = _lower_body(tmp_path, [outer])
+    assert "%n_acc__cell_0" in ptx and "%n_acc__cell_1" in ptx
