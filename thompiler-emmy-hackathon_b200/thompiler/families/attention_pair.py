@@ -32,6 +32,12 @@ p_full, s_full and o_done come in pairs indexed by the key block's parity,
 so every parity wait is at most one phase away from its barrier.  All waits
 are bounded (thompiler.families.kit); the CTAs meet at a cluster barrier
 before exit, so neither leaves while the other can still signal it.
+
+Measured at [8, 16, 2048, 128] it runs at 687 TFLOP/s (h = 1, 2 or 4 alike)
+against the single-CTA kernel's 1064, hence opt-in.  S and PV MMAs issued
+alternately average ~128 cycles per 2-SM instruction (74 for either form
+alone), and with only two key blocks in flight the cross-SM round trip
+(commit -> softmax -> remote arrive -> issue) stays exposed.
 """
 
 from __future__ import annotations
