@@ -8,7 +8,7 @@ from __future__ import annotations
 from pathlib import Path
 
 from thompiler import ir
-from thompiler.synth import B, F32T, L, V, _graph, _write, assign, axis
+from thompiler.synth import B, F16T, F32T, L, V, _graph, _write, assign, axis
 
 N, TILE, T = 256, 64, 256            # x[N, N] f32, one CTA per TILE x TILE tile, T threads
 
@@ -136,3 +136,79 @@ def scan_package(outdir: Path) -> Path:
     kmeta = {"node": "y", "arg_order": ["x", "y", "t", "f"], "grid": [ROWS // 128, 1, 1], "block": [128, 1, 1],
              "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_scan", "x.cumsum(-1)", "k_scan", g, kmeta, 1e-5, 1e-5)
+
+
+def wgmma_gemm_package(outdir: Path, M: int, N: int, K: int, BN: int = 128, n_wg: int = 1,
+                       trans_b: bool = False, tail_overwrite: bool = False) -> Path:
+    """y[M, N] = x0[M, K] @ B (f16 in, f32 out) in the warpgroup vocabulary of sm_90 kernels:
+    WgmmaDescriptor / WgmmaFence / WgmmaMma / WgmmaCommit / WgmmaWait with an m64 accumulator
+    RegFragment and a RegStore of it, the operands staged by TMA with the 128-byte swizzle.
+
+    B is x1[N, K] (K-major) or, with ``trans_b``, x1[K, N] (MN-major, loaded as 64 x 64 boxes).
+    A CTA of ``n_wg`` warpgroups computes a (64 n_wg) x BN tile, warpgroup g its rows
+    64g..64g+63; K runs in blocks of 64, four k16 MMAs per block, the first of them
+    overwriting the accumulator (``scale_d`` false at kb = kk = 0).  With ``tail_overwrite``
+    one more MMA after the loop, with ``scale_d`` 0, replaces the result by the product of
+    the last 16 columns of K alone: y = x0[:, K-16:] @ B[K-16:, :]."""
+    if M % (64 * n_wg) or N % BN or K % 64 or BN % 64:
+        raise ValueError("wgmma_gemm_package: M, N, K and BN must be whole tiles")
+    F16 = F16T
+    rows = 64 * n_wg
+    t, wg = V("t"), B("/", V("t"), L(128))
+    if trans_b:
+        bshape, b_s = (K, N), ir.Smem("b_s", (BN // 64, 64, 64), "__half", 1024)
+        db = ir.TmaDescriptor("db", "x1", bshape, (64, 64), "B128", F16)
+        b_loads = tuple(ir.TmaLoad("b_s", (L(j), L(0), L(0)), "db", (V("kb"), B("+", B("*", V("tn"), L(BN)), L(64 * j))),
+                                   "bar", L(0)) for j in range(BN // 64))
+    else:
+        bshape, b_s = (N, K), ir.Smem("b_s", (BN, 64), "__half", 1024)
+        db = ir.TmaDescriptor("db", "x1", bshape, (BN, 64), "B128", F16)
+        b_loads = (ir.TmaLoad("b_s", (L(0), L(0)), "db", (B("*", V("tn"), L(BN)), V("kb")), "bar", L(0)),)
+
+    def descs(k0):
+        """Descriptors of the k16 slice starting at column k0 of the staged 64-wide K block."""
+        a = ir.WgmmaDescriptor("ad", "a_s", (B("*", wg, L(64)), k0), "B128", L(16), L(1024))
+        if trans_b:      # MN-major: the slice is rows k0..k0+15 of each 64 x 64 box, boxes 8 KiB apart
+            b = ir.WgmmaDescriptor("bd", "b_s", (L(0), k0, L(0)), "B128", L(8192), L(1024))
+        else:
+            b = ir.WgmmaDescriptor("bd", "b_s", (L(0), k0), "B128", L(16), L(1024))
+        return a, b
+
+    def mma(scale):
+        return ir.WgmmaMma(("acc",), "bd", (64, BN, 16), "f16", "ad", None, scale, False, trans_b)
+
+    kstep = (*descs(B("*", V("kk"), L(16))), ir.WgmmaFence(),
+             mma(B("||", B("!=", V("kb"), L(0)), B("!=", V("kk"), L(0)))))
+    body = [
+        ir.Smem("a_s", (rows, 64), "__half", 1024), b_s,
+        ir.Smem("bar", (1,), "uint64_t", 8),
+        ir.TmaDescriptor("da", "x0", (M, K), (rows, 64), "B128", F16), db,
+        ir.MbarrierInit("bar", L(1), L(0)),
+        ir.Sync(0, None, False),
+        ir.RegFragment("acc", "c", (64, BN, 16), F32T, 1, None),
+        ir.StridedLoop(axis("kb", K), L(0), L(64), (
+            ir.Cond(B("==", t, L(0)), (
+                ir.MbarrierArriveExpectTx("bar", L((rows + BN) * 64 * 2), L(0)),
+                ir.TmaLoad("a_s", (L(0), L(0)), "da", (B("*", V("tm"), L(rows)), V("kb")), "bar", L(0)),
+                *b_loads), ()),
+            ir.MbarrierWait("bar", B("/", V("kb"), L(64)), L(0)),
+            ir.Loop(axis("kk", 4), kstep, True, False),
+            ir.WgmmaCommit(),
+            ir.WgmmaWait(L(0)),
+            ir.Sync(0, None, False)), False, None, False),
+    ]
+    if tail_overwrite:
+        body += [*descs(L(3 * 16)), ir.WgmmaFence(), mma(L(0)), ir.WgmmaCommit(), ir.WgmmaWait(L(0))]
+    body.append(ir.RegStore("y", (B("+", B("*", V("tm"), L(rows)), B("*", wg, L(64))), B("*", V("tn"), L(BN))),
+                            "acc", (64, BN, 16), 0, None, (), None, None, False, "m64nNk16", False, None, "NONE",
+                            None, None))
+    tile = ir.Tile((axis("tm", M // rows), axis("tn", N // BN), axis("t", 128 * n_wg)), tuple(body), 128 * n_wg, 0,
+                   None, None, "m")
+    entry = "k_wgmma_gemm"
+    g = _graph({"x0": ((M, K), "f16"), "x1": (bshape, "f16")}, {}, "y", (M, N), entry, tile)
+    args = [{"name": "x0", "dtype": "f16", "shape": [M, K], "seed": 0},
+            {"name": "x1", "dtype": "f16", "shape": list(bshape), "seed": 1},
+            {"name": "y", "dtype": "f32", "shape": [M, N], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x0", "x1", "y"], "grid": [(M // rows) * (N // BN), 1, 1],
+             "block": [128 * n_wg, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_wgmma_gemm", "x0 @ x1", entry, g, kmeta, 1e-3, 1e-3)

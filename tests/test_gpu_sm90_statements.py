@@ -7,7 +7,8 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import COLS, M, N, ROWS, scan_package, select_package, stuck_wait_package, tma_transpose_package
+from sm90_ir import (COLS, M, N, ROWS, scan_package, select_package, stuck_wait_package, tma_transpose_package,
+                     wgmma_gemm_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -90,3 +91,25 @@ def test_carried_state_scan(tmp_path):
     for _ in range(COLS):
         fib = [fib[1], fib[0] + fib[1]]
     assert np.all(res["outputs"]["f"] == fib[1]) and fib[1] == 75025
+
+
+WGMMA_CASES = [{}, {"n_wg": 2}, {"trans_b": True}, {"tail_overwrite": True}, {"BN": 64}, {"BN": 256}]
+
+
+@pytest.mark.parametrize("kw", WGMMA_CASES, ids=[",".join(f"{k}={v}" for k, v in c.items()) or "base"
+                                                  for c in WGMMA_CASES])
+def test_wgmma_gemm(tmp_path, kw):
+    """The sm_90-style GEMM (Wgmma* statements, m64 accumulator fragments) on tcgen05: y = x0 @ B
+    against float64 numpy on the same f16 inputs, through the host-buffer run (TMA maps encoded
+    per request; a non-zero error word -- a wait that gave up, a skipped copy or MMA -- fails the
+    run).  The tolerance covers f32 accumulation over K = 512 products of N(0, 1) halves (|y| ~ 23)."""
+    M_, N_, K_ = 256, 512, 512
+    pkg = problems.load_package(wgmma_gemm_package(tmp_path / "g", M_, N_, K_, **kw))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    a = x["x0"].astype(np.float64)
+    b = x["x1"].astype(np.float64)
+    bk = b if kw.get("trans_b") else b.T                      # [K, N]
+    if kw.get("tail_overwrite"):
+        a, bk = a[:, K_ - 16:], bk[K_ - 16:, :]
+    np.testing.assert_allclose(res["outputs"]["y"], a @ bk, rtol=1e-3, atol=2e-3)

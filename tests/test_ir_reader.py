@@ -33,9 +33,10 @@ def test_kernel_info_follows_arg_order():
 
 
 def test_unknown_constructor_is_kept_opaque():
-    s = ir.parse_stmt("WgmmaMma(c_frags=('c0',), b_desc='bd', shape=(64, 128, 16), scale_d=Var(name='i'))")
-    assert isinstance(s, ir.Opaque) and s.kind == "WgmmaMma"
-    assert dict(s.fields)["b_desc"] == "bd"
+    s = ir.parse_stmt("FragmentApply(out='c0', op=ElementwiseImpl('exp'), args=('c0',), kinds=('frag',), "
+                      "row_base=Var(name='i'))")
+    assert isinstance(s, ir.Opaque) and s.kind == "FragmentApply"
+    assert dict(s.fields)["out"] == "c0"
 
 
 def test_rejects_non_constructor_syntax():

@@ -94,13 +94,17 @@ def test_set_max_nreg_and_checks(tmp_path):
 
 
 def test_unbuilt_vocabulary_fails_loudly(tmp_path):
-    """Wgmma* (Hopper-only instructions), Fragment* and carried state still fail at lowering,
-    naming the statement, as the reference does for every statement it lacks."""
+    """Fragment* statements still fail at lowering, naming the statement, as the reference does
+    for every statement it lacks; a Wgmma statement in a kernel with no WgmmaMma is refused."""
     d = select_package(tmp_path / "s")
     f = next(d.glob("*.ir.json"))
-    f.write_text(f.read_text().replace("ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))",
-                                       "WgmmaFence()"))
-    with pytest.raises(NotImplementedError, match="WgmmaFence"):
+    text = f.read_text()
+    zp = "ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))"
+    f.write_text(text.replace(zp, "FragmentPromote(dst='c', src='c16')"))
+    with pytest.raises(NotImplementedError, match="FragmentPromote"):
+        _ptx(d)
+    f.write_text(text.replace(zp, "WgmmaFence()"))
+    with pytest.raises(ValueError, match="WgmmaFence in a kernel without a WgmmaMma"):
         _ptx(d)
 
 

@@ -24,9 +24,16 @@ from thompiler.walk import Walker
 
 
 def compile_generic(kernel: KernelInfo) -> str:
+    from thompiler.handlers import wgmma
     em = Emitter()
     prologue.emit_param_loads(em, kernel)
-    Walker(em, kernel).body(kernel.body)
+    w = Walker(em, kernel)
+    w.wgmma = wgmma.plan(kernel)
+    if w.wgmma is not None:
+        wgmma.prologue(w, w.wgmma)
+    w.body(kernel.body)
+    if w.wgmma is not None:
+        wgmma.epilogue(w, w.wgmma)
     em.ins("ret")
     return em.render(prologue.header(), kernel.name, prologue.params(kernel))
 

@@ -1,6 +1,9 @@
 """Warp-level tensor-core statements: RegFragment, LdmatrixLoad, MmaSyncPtx,
 RegStore (the generic lowering; the tuned matmul family replaces whole
-kernels of these by tcgen05).
+kernels of these by tcgen05).  RegFragment and RegStore also take the m64
+warpgroup accumulators of the Wgmma* statements (handlers/wgmma.py): N/2
+f32 registers per thread, warp q of the group holding rows 16q + g and
+16q + g + 8, registers 4i..4i+3 at columns 8i + 2t, 8i + 2t + 1.
 
 A fragment family is ``count`` members of ``nregs`` registers each, named
 ``%fr_<frag>_<member>_<slot>``.  The IR indexes families by expressions of
@@ -63,7 +66,8 @@ def operand_regs(role: str, shape: tuple, ty: Ty) -> int:
             raise NotImplementedError(f"mma operand {role} of {ty.name}")
         return (m * k if role == "a" else k * n) // 64
     if role == "c":
-        return (m * n) // (64 if ty.nbytes == 2 else 32)
+        threads = 128 if m == 64 else 32          # an m64 accumulator spans a warpgroup (wgmma)
+        return (m * n) // (threads * (2 if ty.nbytes == 2 else 1))
     raise ValueError(f"mma role {role!r}")
 
 
@@ -83,6 +87,9 @@ def emit_reg_fragment(w: "Walker", f: ir.RegFragment) -> None:
             em.declare(r, cls)
             if f.role == "c":
                 em.ins(f"mov.{'f32' if cls == 'f32' else 'b32'} {r}, {'0f00000000' if cls == 'f32' else '0'}")
+    if f.role == "c":
+        from thompiler.handlers.wgmma import fragment_written
+        fragment_written(w, f.name)
 
 
 def _const_index(w: "Walker", text: str, ref: str) -> int:
@@ -197,11 +204,13 @@ def emit_mma_sync(w: "Walker", mma: ir.MmaSyncPtx) -> None:
 def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
     em = w.em
     em.note(f"RegStore {st.dst_buffer} <- {st.frag}")
-    if (st.fragment_layout != "m16n8k16" or st.volta_interleaved or st.epilogue is not None
+    if (st.fragment_layout not in ("m16n8k16", "m64nNk16") or st.volta_interleaved or st.epilogue is not None
             or st.extra_frags or st.m_guard is not None or st.n_guard is not None or st.atomic
             or st.swizzle not in ("NONE", None)):
         raise NotImplementedError("RegStore form: epilogue, guards, atomics, swizzle or Volta layout")
-    if tuple(int(x) for x in st.shape) != (16, 8, 16):
+    shape = tuple(int(x) for x in st.shape)
+    wide = len(shape) == 3 and shape[0] == 64 and shape[2] == 16 and shape[1] % 8 == 0
+    if shape != (16, 8, 16) and not wide:
         raise NotImplementedError(f"RegStore of shape {st.shape}")
     p = w.kernel.param(st.dst_buffer)
     if p is None:
@@ -209,8 +218,9 @@ def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
     if p.ty not in (F32, F16):
         raise NotImplementedError(f"RegStore to a {p.ty.name} buffer")
     frag, regs = fragment_regs(w, st.frag)
-    if frag.role != "c" or frag.ty is not F32 or len(regs) != 4:
-        raise ValueError(f"RegStore of {st.frag}: not an f32 accumulator of 4 registers")
+    want = shape[1] // 2 if wide else 4
+    if frag.role != "c" or frag.ty is not F32 or len(regs) != want:
+        raise ValueError(f"RegStore of {st.frag}: not an f32 accumulator of {want} registers")
     index = list(st.dst_index)
     if len(index) < 2:
         raise ValueError(f"RegStore to {st.dst_buffer}: {len(index)}-d index")
@@ -225,11 +235,14 @@ def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
         raise NotImplementedError(f"RegStore ldm={st.ldm}, but the row stride is {row_stride}")
     lane = ir.Var("lane")
     g = _lane_expr("/", lane, 4)
+    if wide:                     # a warpgroup accumulator: warp q of the group holds rows 16q..16q+15
+        g = ir.BinaryExpr("+", g, _lane_expr("*", _lane_expr("%", ir.Var("warp"), 4), 16))
     col = _lane_expr("*", _lane_expr("%", lane, 4), 2)
-    for dr, (lo, hi) in ((0, regs[0:2]), (8, regs[2:4])):
+    for dr, dc, (lo, hi) in ((dr, 8 * i, regs[4 * i + (2 if dr else 0):4 * i + (4 if dr else 2)])
+                             for i in range(len(regs) // 4) for dr in (0, 8)):
         idx = list(index)
         idx[rdim] = ir.BinaryExpr("+", st.dst_index[rdim], g if dr == 0 else _lane_expr("+", g, dr))
-        idx[cdim] = ir.BinaryExpr("+", st.dst_index[cdim], col)
+        idx[cdim] = ir.BinaryExpr("+", st.dst_index[cdim], col if dc == 0 else _lane_expr("+", col, dc))
         addr = address.global_address(w, p, tuple(idx))
         if p.ty is F32:
             em.ins(f"st.global.v2.f32 [{addr}], {{{lo}, {hi}}}")

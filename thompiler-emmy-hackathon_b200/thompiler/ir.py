@@ -472,9 +472,10 @@ class RegStore(Stmt):
 
 
 # Statements of the IR reference that the reference compiler does not lower (the entries marked
-# * in its TASK.md:95-160) and no shipped kernel uses.  Field names follow that table; the
+# * in its TASK.md:95-180) and no shipped kernel uses.  Field names follow that table; the
 # handlers in thompiler/handlers/async_copy.py and compute.py lower the TMA / mbarrier /
-# register-budget subset, Select and ZeroPrologue onto sm_100a.
+# register-budget subset, Select and ZeroPrologue onto sm_100a, and handlers/wgmma.py the
+# warpgroup tensor-core statements (Wgmma*) onto tcgen05.
 
 
 @dataclass(frozen=True)
@@ -566,10 +567,48 @@ class SetMaxNReg(Stmt):
 
 
 @dataclass(frozen=True)
+class WgmmaDescriptor(Stmt):
+    name: str
+    smem: str = ""
+    smem_index: tuple = ()
+    swizzle: Any = None
+    lbo_bytes: Any = 0
+    sbo_bytes: Any = 0
+
+
+@dataclass(frozen=True)
+class WgmmaMma(Stmt):
+    c_frags: tuple
+    b_desc: str = ""
+    shape: tuple = ()
+    ab_dtype: str = "f16"
+    a_desc: Any = None
+    a_frag: Any = None
+    scale_d: Any = 1
+    trans_a: bool = False
+    trans_b: bool = False
+
+
+@dataclass(frozen=True)
+class WgmmaFence(Stmt):
+    pass
+
+
+@dataclass(frozen=True)
+class WgmmaCommit(Stmt):
+    pass
+
+
+@dataclass(frozen=True)
+class WgmmaWait(Stmt):
+    group: Any = 0
+
+
+@dataclass(frozen=True)
 class Opaque(Stmt):
     """A constructor this reader does not model; kept so the walker can name
-    it when it fails (Wgmma*, Fragment*, ... appear in the IR reference but in
-    no shipped kernel)."""
+    it when it fails (Fragment*, BlockScaleLoad ... appear in the IR reference
+    but in no shipped kernel)."""
     kind: str
     fields: tuple = field(default=())
 
@@ -587,7 +626,8 @@ _CONSTRUCTORS: dict[str, type] = {
         Assign, Let, Accum, Init, Write, WarpShuffle, TreeHalve, Smem, Sync, CpAsyncCopy,
         CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
         Branch, Select, Pre, Carry, ZeroPrologue, TmaDescriptor, TmaLoad, MbarrierInit,
-        MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg)
+        MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg, WgmmaDescriptor, WgmmaMma,
+        WgmmaFence, WgmmaCommit, WgmmaWait)
 }
 
 

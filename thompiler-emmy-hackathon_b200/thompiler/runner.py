@@ -270,7 +270,8 @@ def prepare(module: Module, plan: LaunchPlan, arg_order: list[str], ptrs: dict[s
 
 
 def read_error_word(module: Module, plan: LaunchPlan) -> int:
-    """The kernel's wait-time-out record (0: no wait gave up), or 0 if it has none."""
+    """The kernel's error word (0: no bounded wait gave up and no guarded copy or MMA was skipped),
+    or 0 if it has none."""
     if not plan.error_word:
         return 0
     dst, _ = module.global_ptr(plan.error_word)
@@ -333,7 +334,7 @@ def run(function: Function, plan: LaunchPlan, args: list[dict], warmup: int = 0,
             a["array"][...] = x
     err = read_error_word(function.module, plan)
     if err:
-        return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
+        return {"ok": False, "stage": "run", "stderr": f"kernel error word {err:#x} (a bounded wait gave up or a guarded copy was skipped)"}
     return {"ok": True, "median_us": float(med.value)}
 
 
@@ -390,7 +391,7 @@ class PreparedBatch:
         for module, plan in self._checks:
             err = read_error_word(module, plan)
             if err:
-                return {"ok": False, "stage": "run", "stderr": f"kernel wait gave up (error word {err:#x})"}
+                return {"ok": False, "stage": "run", "stderr": f"kernel error word {err:#x} (a bounded wait gave up or a guarded copy was skipped)"}
         return {"ok": True}
 
 

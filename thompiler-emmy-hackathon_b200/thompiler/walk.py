@@ -28,6 +28,8 @@ from thompiler.handlers.compute import emit_assign, emit_let, emit_load, emit_se
 from thompiler.handlers.cp_async import emit_cp_async_commit, emit_cp_async_copy, emit_cp_async_wait
 from thompiler.handlers.memory import emit_smem, emit_sync
 from thompiler.handlers.mma import emit_ldmatrix_load, emit_mma_sync, emit_reg_fragment, emit_reg_store
+from thompiler.handlers.wgmma import (emit_wgmma_commit, emit_wgmma_descriptor, emit_wgmma_fence,
+                                      emit_wgmma_mma, emit_wgmma_wait)
 from thompiler.handlers.reduce import emit_accum, emit_init, emit_tree_halve, emit_warp_shuffle
 from thompiler.load import KernelInfo
 
@@ -39,6 +41,7 @@ class Walker:
         self.smem: dict = {}
         self.fragments: dict = {}
         self.consts: dict[str, int] = {}
+        self.wgmma = None                      # tensor-memory plan of Wgmma* accumulators
         self.load_hook: Callable[[Any, ir.Load], bool] | None = None
         self.write_hook: Callable[[Any, ir.Write], bool] | None = None
         self._writes = Counter(s.output for s in ir.walk_stmts(kernel.body) if isinstance(s, ir.Write))
@@ -90,6 +93,11 @@ HANDLERS: dict[type, Callable[[Walker, Any], None]] = {
     ir.MbarrierArrive: emit_mbarrier_arrive,
     ir.MbarrierWait: emit_mbarrier_wait,
     ir.SetMaxNReg: emit_set_max_nreg,
+    ir.WgmmaDescriptor: emit_wgmma_descriptor,
+    ir.WgmmaFence: emit_wgmma_fence,
+    ir.WgmmaMma: emit_wgmma_mma,
+    ir.WgmmaCommit: emit_wgmma_commit,
+    ir.WgmmaWait: emit_wgmma_wait,
     ir.Carry: emit_carry,
     ir.Pre: emit_pre,
     StepBegin: emit_step_begin,
