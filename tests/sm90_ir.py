@@ -8,7 +8,7 @@ from __future__ import annotations
 from pathlib import Path
 
 from thompiler import ir
-from thompiler.synth import B, F16T, F32T, L, V, _graph, _write, assign, axis
+from thompiler.synth import B, E, F16T, F32T, L, V, _graph, _write, assign, axis
 
 N, TILE, T = 256, 64, 256            # x[N, N] f32, one CTA per TILE x TILE tile, T threads
 
@@ -212,3 +212,142 @@ def wgmma_gemm_package(outdir: Path, M: int, N: int, K: int, BN: int = 128, n_wg
     kmeta = {"node": "y", "arg_order": ["x0", "x1", "y"], "grid": [(M // rows) * (N // BN), 1, 1],
              "block": [128 * n_wg, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_wgmma_gemm", "x0 @ x1", entry, g, kmeta, 1e-3, 1e-3)
+
+
+def _copy_tile(smem: str, src: str, row0, tid):
+    """Four 16-byte cp.async copies per thread of 128: a 64 x 64 f16 tile of ``src`` (rows row0..)
+    into ``smem`` with the 128-byte swizzle."""
+    out = []
+    for i in range(4):
+        chunk = B("+", tid, L(128 * i))
+        row, c8 = B("/", chunk, L(8)), B("*", B("%", chunk, L(8)), L(8))
+        out.append(ir.CpAsyncCopy(smem, (L(0), L(0)), src, (B("+", row0, row), c8), 16, "B128", (row, c8), None))
+    return out
+
+
+def _ldm(frag, smem, idx, role, b_trans=False, pair=None):
+    return ir.LdmatrixLoad(frag, smem, idx, role, 64, "B128", True, None, None, b_trans, pair, False, None, (), 0,
+                           "m16n8k16", None)
+
+
+def _unrolled(var, n, body):
+    return ir.Loop(axis(var, n), tuple(body), True, False)
+
+
+def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64) -> Path:
+    """o = softmax(q k^T / sqrt(D)) v for one head (q, k, v f16 [S, D], o f32), written with the
+    register-fragment statements on mma.sync m16n8k16: per warp a 16-query strip, keys in blocks
+    of 64 staged by cp.async; FragmentApply scales the scores (a scalar argument, in place),
+    subtracts the running row maximum (a row argument) with an exp ``post``, rescales the
+    output strip and divides it by the row sums at the end; FragmentRowReduce gives the block's
+    row maxima and sums; FragmentRepack turns the probabilities into the A fragments of P V."""
+    if S % 64 or D != 64:
+        raise ValueError("fragment_attention_package: S a multiple of 64, D = 64")
+    F16 = F16T
+    tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
+    sfr = tuple(f"s[{n}]" for n in range(8))
+    frags = [ir.RegFragment("qa", "a", (16, 8, 16), F16, 4, None), ir.RegFragment("kb", "b", (16, 8, 16), F16, 8, None),
+             ir.RegFragment("s", "c", (16, 8, 16), F32T, 8, None), ir.RegFragment("pa", "a", (16, 8, 16), F16, 4, None),
+             ir.RegFragment("vb", "b", (16, 8, 16), F16, 8, None), ir.RegFragment("o", "c", (16, 8, 16), F32T, 8, None)]
+    smem = [ir.Smem(n, (64, 64), "__half", 1024) for n in ("q_s", "k_s", "v_s")]
+    load_q = [*_copy_tile("q_s", "q", B("*", V("qb"), L(64)), tid), ir.CpAsyncCommit(), ir.CpAsyncWait(0),
+              ir.Sync(0, None, False),
+              _unrolled("_kq", 4, [_ldm("qa[_kq]", "q_s", (B("*", V("_w"), L(16)), B("*", V("_kq"), L(16))), "a")])]
+    init = [ir.Let(n, L(v, "float"), F32T) for n, v in (("m_t", -1e30), ("m_b", -1e30), ("l_t", 0.0), ("l_b", 0.0))]
+    row = ("frag", "row")
+    block = [
+        *_copy_tile("k_s", "k", V("_kv"), tid), *_copy_tile("v_s", "v", V("_kv"), tid),
+        ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False),
+        _unrolled("_z", 8, [ir.FragmentApply("s[_z]", E("copy"), (L(0.0, "float"),), ("scalar",), False, None, None,
+                                             None, None)]),
+        _unrolled("_kk", 4, [
+            _unrolled("_j", 4, [_ldm("kb[_j * 2]", "k_s", (B("*", V("_j"), L(16)), B("*", V("_kk"), L(16))), "b",
+                                     True, "kb[_j * 2 + 1]")]),
+            _unrolled("_n", 8, [ir.MmaSyncPtx("s[_n]", "qa[_kk]", "kb[_n]", (16, 8, 16), "f16", "f32", False, None,
+                                              None)])]),
+        _unrolled("_c", 8, [ir.FragmentApply("s[_c]", E("multiply"), (L(1.0 / D ** 0.5, "float"),), ("scalar",), True,
+                                             None, None, None, None)]),
+        ir.FragmentRowReduce("mx_t", "mx_b", sfr, E("maximum"), None, F32T),
+        assign("mn_t", "maximum", "m_t", "mx_t"), assign("mn_b", "maximum", "m_b", "mx_b"),
+        assign("d_t", "subtract", "m_t", "mn_t"), assign("d_b", "subtract", "m_b", "mn_b"),
+        assign("al_t", "exp", "d_t"), assign("al_b", "exp", "d_b"),
+        _unrolled("_e", 8, [ir.FragmentApply("s[_e]", E("subtract"), ("s[_e]", ("mn_t", "mn_b")), row, False,
+                                             ir.FragLayout(4, (0, 0, 1, 1), (1, 2), None, (), None, None), E("exp"),
+                                             None, None)]),
+        ir.FragmentRowReduce("ls_t", "ls_b", sfr, E("add"), ir.FragLayout(4, (0, 0, 1, 1), (1, 2), None, (), None,
+                                                                           None), F32T),
+        assign("lt1", "multiply", "l_t", "al_t"), assign("lb1", "multiply", "l_b", "al_b"),
+        assign("l_t", "add", "lt1", "ls_t"), assign("l_b", "add", "lb1", "ls_b"),
+        assign("m_t", "copy", "mn_t"), assign("m_b", "copy", "mn_b"),
+        _unrolled("_r", 8, [ir.FragmentApply("o[_r]", E("multiply"), ("o[_r]", ("al_t", "al_b")), row, False, None,
+                                             None, None, None)]),
+        _unrolled("_p", 4, [ir.FragmentRepack("pa[_p]", sfr, "f16", "m16n8k16", V("_p"))]),
+        _unrolled("_kk", 4, [
+            _unrolled("_j", 4, [_ldm("vb[_j * 2]", "v_s", (B("*", V("_kk"), L(16)), B("*", V("_j"), L(16))), "b",
+                                     False, "vb[_j * 2 + 1]")]),
+            _unrolled("_n", 8, [ir.MmaSyncPtx("o[_n]", "pa[_kk]", "vb[_n]", (16, 8, 16), "f16", "f32", False, None,
+                                              None)])]),
+        ir.Sync(0, None, False),
+    ]
+    finish = [_unrolled("_f", 8, [
+        ir.FragmentApply("o[_f]", E("divide"), ("o[_f]", ("l_t", "l_b")), row, False, None, None, None, None),
+        ir.RegStore("o", (B("+", B("*", V("qb"), L(64)), B("*", V("_w"), L(16))), B("*", V("_f"), L(8))), "o[_f]",
+                    (16, 8, 16), 0, None, (), None, None, False, "m16n8k16", False, None, "NONE", None, None)])]
+    body = (*frags, *smem, *load_q, *init, ir.StridedLoop(axis("_kv", S), L(0), L(64), tuple(block), False, None, False),
+            *finish)
+    tile = ir.Tile((axis("qb", S // 64), axis("_w", 4), axis("_lane", 32)), body, 128, 0, None, None, "m")
+    entry = "k_fragment_attention"
+    g = _graph({"q": ((S, D), "f16"), "k": ((S, D), "f16"), "v": ((S, D), "f16")}, {}, "o", (S, D), entry, tile)
+    args = [{"name": n, "dtype": "f16", "shape": [S, D], "seed": i} for i, n in enumerate(("q", "k", "v"))]
+    args.append({"name": "o", "dtype": "f32", "shape": [S, D], "output": True})
+    kmeta = {"node": "o", "arg_order": ["q", "k", "v", "o"], "grid": [S // 64, 1, 1], "block": [128, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_fragment_attention", "softmax(q @ k.T / 8) @ v", entry, g, kmeta, 2e-2, 2e-3)
+
+
+def promote_matmul_package(outdir: Path, M: int = 128, N: int = 128, K: int = 512) -> Path:
+    """y = x0 @ x1^T (x1 [N, K]) accumulated in f16 fragments (mma.sync with f16 C) for each K block
+    of 64 and promoted into f32 shadows after the block (FragmentPromote, which also zeroes the
+    f16 ones).  Inputs are integers in -2..2, so every f16 partial (at most 256 in magnitude) and
+    every f32 sum is exact: the result equals the integer product bit for bit."""
+    if M % 64 or N % 64 or K % 64:
+        raise ValueError("promote_matmul_package: M, N, K multiples of 64")
+    F16 = F16T
+    tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
+    body = [ir.RegFragment("a", "a", (16, 8, 16), F16, 1, None), ir.RegFragment("b", "b", (16, 8, 16), F16, 8, None),
+            ir.RegFragment("c16", "c", (16, 8, 16), F16, 8, None), ir.RegFragment("c", "c", (16, 8, 16), F32T, 8, None),
+            ir.Smem("a_s", (64, 64), "__half", 1024), ir.Smem("b_s", (64, 64), "__half", 1024)]
+    ks = [*_copy_tile("a_s", "x0", B("*", V("bm"), L(64)), tid)]
+    for i in range(4):                     # B rows bn*64.., columns kb..kb+63
+        chunk = B("+", tid, L(128 * i))
+        r, c8 = B("/", chunk, L(8)), B("*", B("%", chunk, L(8)), L(8))
+        ks.append(ir.CpAsyncCopy("b_s", (L(0), L(0)), "x1", (B("+", B("*", V("bn"), L(64)), r), B("+", V("kb"), c8)),
+                                 16, "B128", (r, c8), None))
+    # the A copies read columns kb.. too
+    ks[:4] = [ir.CpAsyncCopy(c.smem, c.smem_index, c.src, (c.src_index[0], B("+", V("kb"), c.src_index[1])), 16,
+                             "B128", c.lane_index, None) for c in ks[:4]]
+    ks += [ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False),
+           _unrolled("_kk", 4, [
+               _ldm("a", "a_s", (B("*", V("_w"), L(16)), B("*", V("_kk"), L(16))), "a"),
+               _unrolled("_j", 4, [_ldm("b[_j * 2]", "b_s", (B("*", V("_j"), L(16)), B("*", V("_kk"), L(16))), "b",
+                                        True, "b[_j * 2 + 1]")]),
+               _unrolled("_n", 8, [ir.MmaSyncPtx("c16[_n]", "a", "b[_n]", (16, 8, 16), "f16", "f16", False, None,
+                                                 None)])]),
+           _unrolled("_q", 8, [ir.FragmentPromote("c[_q]", "c16[_q]")]),
+           ir.Sync(0, None, False)]
+    body.append(ir.StridedLoop(axis("kb", K), L(0), L(64), tuple(ks), False, None, False))
+    body.append(_unrolled("_s", 8, [ir.RegStore("y", (B("+", B("*", V("bm"), L(64)), B("*", V("_w"), L(16))),
+                                                      B("+", B("*", V("bn"), L(64)), B("*", V("_s"), L(8)))), "c[_s]",
+                                                (16, 8, 16), 0, None, (), None, None, False, "m16n8k16", False, None,
+                                                "NONE", None, None)]))
+    tile = ir.Tile((axis("bm", M // 64), axis("bn", N // 64), axis("_w", 4), axis("_lane", 32)), tuple(body), 128, 0,
+                   None, None, "m")
+    entry = "k_promote_matmul"
+    g = _graph({"x0": ((M, K), "f16"), "x1": ((N, K), "f16")}, {}, "y", (M, N), entry, tile)
+    ints = {"dist": "integers", "low": -2, "high": 2}
+    args = [{"name": "x0", "dtype": "f16", "shape": [M, K], "seed": 0, "init": dict(ints, seed=0)},
+            {"name": "x1", "dtype": "f16", "shape": [N, K], "seed": 1, "init": dict(ints, seed=1)},
+            {"name": "y", "dtype": "f32", "shape": [M, N], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x0", "x1", "y"], "grid": [(M // 64) * (N // 64), 1, 1], "block": [128, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_promote_matmul", "x0 @ x1.T", entry, g, kmeta, 0, 0)

@@ -7,8 +7,8 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import (COLS, M, N, ROWS, scan_package, select_package, stuck_wait_package, tma_transpose_package,
-                     wgmma_gemm_package)
+from sm90_ir import (COLS, M, N, ROWS, fragment_attention_package, promote_matmul_package, scan_package,
+                     select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -113,3 +113,28 @@ def test_wgmma_gemm(tmp_path, kw):
     if kw.get("tail_overwrite"):
         a, bk = a[:, K_ - 16:], bk[K_ - 16:, :]
     np.testing.assert_allclose(res["outputs"]["y"], a @ bk, rtol=1e-3, atol=2e-3)
+
+
+def test_fragment_attention(tmp_path):
+    """Flash attention in register fragments (FragmentApply / FragmentRowReduce / FragmentRepack on
+    mma.sync): one head, S = 256 keys in four blocks of 64, against float64 numpy softmax attention
+    on the same f16 inputs.  The probabilities are rounded to f16 before P V, as any f16 flash
+    attention does; the tolerance is the attention one (rtol 2e-2, atol 2e-3)."""
+    pkg = problems.load_package(fragment_attention_package(tmp_path / "a", 256, 64))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    q, k, v = (x[n].astype(np.float64) for n in ("q", "k", "v"))
+    sc = q @ k.T / 8.0
+    p = np.exp(sc - sc.max(axis=1, keepdims=True))
+    want = (p / p.sum(axis=1, keepdims=True)) @ v
+    np.testing.assert_allclose(res["outputs"]["o"], want, rtol=2e-2, atol=2e-3)
+
+
+def test_promote_matmul_exact(tmp_path):
+    """f16 accumulation per K block of 64, promoted into f32 (FragmentPromote): with integer inputs
+    in -2..2 every partial is exact, so the result is the integer product bit for bit."""
+    pkg = problems.load_package(promote_matmul_package(tmp_path / "p", 128, 128, 512))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    want = (x["x0"].astype(np.int64) @ x["x1"].astype(np.int64).T).astype(np.float32)
+    np.testing.assert_array_equal(res["outputs"]["y"], want)

@@ -33,10 +33,9 @@ def test_kernel_info_follows_arg_order():
 
 
 def test_unknown_constructor_is_kept_opaque():
-    s = ir.parse_stmt("FragmentApply(out='c0', op=ElementwiseImpl('exp'), args=('c0',), kinds=('frag',), "
-                      "row_base=Var(name='i'))")
-    assert isinstance(s, ir.Opaque) and s.kind == "FragmentApply"
-    assert dict(s.fields)["out"] == "c0"
+    s = ir.parse_stmt("BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='i'),), role='a', ldm=64)")
+    assert isinstance(s, ir.Opaque) and s.kind == "BlockScaleLoad"
+    assert dict(s.fields)["src_buffer"] == "x"
 
 
 def test_rejects_non_constructor_syntax():

@@ -94,14 +94,15 @@ def test_set_max_nreg_and_checks(tmp_path):
 
 
 def test_unbuilt_vocabulary_fails_loudly(tmp_path):
-    """Fragment* statements still fail at lowering, naming the statement, as the reference does
-    for every statement it lacks; a Wgmma statement in a kernel with no WgmmaMma is refused."""
+    """BlockScaleLoad (the block-scaled fp4 mma.sync path) still fails at lowering, naming the
+    statement, as the reference does for every statement it lacks; a Wgmma statement in a
+    kernel with no WgmmaMma is refused."""
     d = select_package(tmp_path / "s")
     f = next(d.glob("*.ir.json"))
     text = f.read_text()
     zp = "ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))"
-    f.write_text(text.replace(zp, "FragmentPromote(dst='c', src='c16')"))
-    with pytest.raises(NotImplementedError, match="FragmentPromote"):
+    f.write_text(text.replace(zp, "BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='a0'),), role='a')"))
+    with pytest.raises(NotImplementedError, match="BlockScaleLoad"):
         _ptx(d)
     f.write_text(text.replace(zp, "WgmmaFence()"))
     with pytest.raises(ValueError, match="WgmmaFence in a kernel without a WgmmaMma"):

@@ -474,8 +474,9 @@ class RegStore(Stmt):
 # Statements of the IR reference that the reference compiler does not lower (the entries marked
 # * in its TASK.md:95-180) and no shipped kernel uses.  Field names follow that table; the
 # handlers in thompiler/handlers/async_copy.py and compute.py lower the TMA / mbarrier /
-# register-budget subset, Select and ZeroPrologue onto sm_100a, and handlers/wgmma.py the
-# warpgroup tensor-core statements (Wgmma*) onto tcgen05.
+# register-budget subset, Select and ZeroPrologue onto sm_100a, handlers/wgmma.py the
+# warpgroup tensor-core statements (Wgmma*) onto tcgen05, handlers/fragments.py the register
+# fragment operations (Fragment*).
 
 
 @dataclass(frozen=True)
@@ -567,6 +568,57 @@ class SetMaxNReg(Stmt):
 
 
 @dataclass(frozen=True)
+class FragLayout:
+    """Per-atom geometry of a C fragment: element count, the row (0 top, 1 bottom) of each
+    element, the lane xors that combine a row's lanes, and text the IR's renderer uses."""
+    n_elems: int = 4
+    elem_row: tuple = ()
+    reduce_xors: tuple = ()
+    lane_decl: Any = None
+    lane_names: tuple = ()
+    row_off: Any = None
+    col_off: Any = None
+
+
+@dataclass(frozen=True)
+class FragmentPromote(Stmt):
+    dst: str
+    src: str = ""
+
+
+@dataclass(frozen=True)
+class FragmentApply(Stmt):
+    out: str
+    op: Any = None
+    args: tuple = ()
+    kinds: tuple = ()
+    in_place: bool = False
+    layout: Any = None
+    post: Any = None
+    row_base: Any = None
+    col_base: Any = None
+
+
+@dataclass(frozen=True)
+class FragmentRowReduce(Stmt):
+    top: str
+    bot: str = ""
+    frags: tuple = ()
+    op: Any = None
+    layout: Any = None
+    dtype: Any = None
+
+
+@dataclass(frozen=True)
+class FragmentRepack(Stmt):
+    frag: str
+    srcs: tuple = ()
+    ab_dtype: str = "f16"
+    fragment_layout: str = "m16n8k16"
+    part: Any = None
+
+
+@dataclass(frozen=True)
 class WgmmaDescriptor(Stmt):
     name: str
     smem: str = ""
@@ -607,8 +659,8 @@ class WgmmaWait(Stmt):
 @dataclass(frozen=True)
 class Opaque(Stmt):
     """A constructor this reader does not model; kept so the walker can name
-    it when it fails (Fragment*, BlockScaleLoad ... appear in the IR reference
-    but in no shipped kernel)."""
+    it when it fails (BlockScaleLoad, Lambda ... appear in the IR reference but
+    in no shipped kernel)."""
     kind: str
     fields: tuple = field(default=())
 
@@ -627,7 +679,8 @@ _CONSTRUCTORS: dict[str, type] = {
         CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
         Branch, Select, Pre, Carry, ZeroPrologue, TmaDescriptor, TmaLoad, MbarrierInit,
         MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg, WgmmaDescriptor, WgmmaMma,
-        WgmmaFence, WgmmaCommit, WgmmaWait)
+        WgmmaFence, WgmmaCommit, WgmmaWait, FragLayout, FragmentPromote, FragmentApply, FragmentRowReduce,
+        FragmentRepack)
 }
 
 

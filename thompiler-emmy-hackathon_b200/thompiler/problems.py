@@ -57,13 +57,15 @@ def load_package(pdir: str | Path) -> Package:
 def seeded_input(shape, seed: int, dtype: str, init: dict | None = None) -> np.ndarray:
     """The runner's seeded input (standard normal), or the distribution an
     ``init`` record names (synthetic packages: ``uniform`` low/high,
-    ``normal`` mean/std)."""
+    ``normal`` mean/std, ``integers`` low..high inclusive)."""
     shape = list(shape) or [1]
     if init is None:
         return np.random.default_rng(seed).standard_normal(shape).astype(NP_DTYPES[dtype])
     rng = np.random.default_rng(init.get("seed", seed))
     if init["dist"] == "uniform":
         return rng.uniform(init.get("low", 0.0), init.get("high", 1.0), shape).astype(NP_DTYPES[dtype])
+    if init["dist"] == "integers":
+        return rng.integers(init.get("low", -2), init.get("high", 2) + 1, shape).astype(NP_DTYPES[dtype])
     if init["dist"] == "normal":
         return (rng.standard_normal(shape) * init.get("std", 1.0) + init.get("mean", 0.0)).astype(NP_DTYPES[dtype])
     raise ValueError(f"input distribution {init['dist']!r}")

@@ -26,6 +26,8 @@ from thompiler.handlers.async_copy import (emit_mbarrier_arrive, emit_mbarrier_a
                                            emit_mbarrier_wait, emit_set_max_nreg, emit_tma_descriptor, emit_tma_load)
 from thompiler.handlers.compute import emit_assign, emit_let, emit_load, emit_select, emit_write, emit_zero_prologue
 from thompiler.handlers.cp_async import emit_cp_async_commit, emit_cp_async_copy, emit_cp_async_wait
+from thompiler.handlers.fragments import (emit_fragment_apply, emit_fragment_promote, emit_fragment_repack,
+                                         emit_fragment_row_reduce)
 from thompiler.handlers.memory import emit_smem, emit_sync
 from thompiler.handlers.mma import emit_ldmatrix_load, emit_mma_sync, emit_reg_fragment, emit_reg_store
 from thompiler.handlers.wgmma import (emit_wgmma_commit, emit_wgmma_descriptor, emit_wgmma_fence,
@@ -98,6 +100,10 @@ HANDLERS: dict[type, Callable[[Walker, Any], None]] = {
     ir.WgmmaMma: emit_wgmma_mma,
     ir.WgmmaCommit: emit_wgmma_commit,
     ir.WgmmaWait: emit_wgmma_wait,
+    ir.FragmentPromote: emit_fragment_promote,
+    ir.FragmentRowReduce: emit_fragment_row_reduce,
+    ir.FragmentApply: emit_fragment_apply,
+    ir.FragmentRepack: emit_fragment_repack,
     ir.Carry: emit_carry,
     ir.Pre: emit_pre,
     StepBegin: emit_step_begin,
