@@ -139,7 +139,7 @@ def scan_package(outdir: Path) -> Path:
 
 
 def wgmma_gemm_package(outdir: Path, M: int, N: int, K: int, BN: int = 128, n_wg: int = 1,
-                       trans_b: bool = False, tail_overwrite: bool = False) -> Path:
+                       trans_b: bool = False, tail_overwrite: bool = False, out_scale: float | None = None) -> Path:
     """y[M, N] = x0[M, K] @ B (f16 in, f32 out) in the warpgroup vocabulary of sm_90 kernels:
     WgmmaDescriptor / WgmmaFence / WgmmaMma / WgmmaCommit / WgmmaWait with an m64 accumulator
     RegFragment and a RegStore of it, the operands staged by TMA with the 128-byte swizzle.
@@ -149,7 +149,8 @@ def wgmma_gemm_package(outdir: Path, M: int, N: int, K: int, BN: int = 128, n_wg
     64g..64g+63; K runs in blocks of 64, four k16 MMAs per block, the first of them
     overwriting the accumulator (``scale_d`` false at kb = kk = 0).  With ``tail_overwrite``
     one more MMA after the loop, with ``scale_d`` 0, replaces the result by the product of
-    the last 16 columns of K alone: y = x0[:, K-16:] @ B[K-16:, :]."""
+    the last 16 columns of K alone: y = x0[:, K-16:] @ B[K-16:, :].  With ``out_scale`` y is f16,
+    out_scale * (x0 @ B) through a RegStore epilogue Lambda."""
     if M % (64 * n_wg) or N % BN or K % 64 or BN % 64:
         raise ValueError("wgmma_gemm_package: M, N, K and BN must be whole tiles")
     F16 = F16T
@@ -199,16 +200,21 @@ def wgmma_gemm_package(outdir: Path, M: int, N: int, K: int, BN: int = 128, n_wg
     ]
     if tail_overwrite:
         body += [*descs(L(3 * 16)), ir.WgmmaFence(), mma(L(0)), ir.WgmmaCommit(), ir.WgmmaWait(L(0))]
+    epilogue = None
+    if out_scale is not None:
+        epilogue = ir.Lambda(("v",), (ir.Let("sc", L(float(out_scale), "float"), F32T),
+                                      assign("o", "multiply", "v", "sc")), ("o",))
     body.append(ir.RegStore("y", (B("+", B("*", V("tm"), L(rows)), B("*", wg, L(64))), B("*", V("tn"), L(BN))),
-                            "acc", (64, BN, 16), 0, None, (), None, None, False, "m64nNk16", False, None, "NONE",
+                            "acc", (64, BN, 16), 0, epilogue, (), None, None, False, "m64nNk16", False, None, "NONE",
                             None, None))
+    out_dtype = "f32" if out_scale is None else "f16"
     tile = ir.Tile((axis("tm", M // rows), axis("tn", N // BN), axis("t", 128 * n_wg)), tuple(body), 128 * n_wg, 0,
                    None, None, "m")
     entry = "k_wgmma_gemm"
-    g = _graph({"x0": ((M, K), "f16"), "x1": (bshape, "f16")}, {}, "y", (M, N), entry, tile)
+    g = _graph({"x0": ((M, K), "f16"), "x1": (bshape, "f16")}, {}, "y", (M, N), entry, tile, out_dtype)
     args = [{"name": "x0", "dtype": "f16", "shape": [M, K], "seed": 0},
             {"name": "x1", "dtype": "f16", "shape": list(bshape), "seed": 1},
-            {"name": "y", "dtype": "f32", "shape": [M, N], "output": True}]
+            {"name": "y", "dtype": out_dtype, "shape": [M, N], "output": True}]
     kmeta = {"node": "y", "arg_order": ["x0", "x1", "y"], "grid": [(M // rows) * (N // BN), 1, 1],
              "block": [128 * n_wg, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_wgmma_gemm", "x0 @ x1", entry, g, kmeta, 1e-3, 1e-3)
@@ -351,3 +357,99 @@ def promote_matmul_package(outdir: Path, M: int = 128, N: int = 128, K: int = 51
     kmeta = {"node": "y", "arg_order": ["x0", "x1", "y"], "grid": [(M // 64) * (N // 64), 1, 1], "block": [128, 1, 1],
              "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_promote_matmul", "x0 @ x1.T", entry, g, kmeta, 0, 0)
+
+
+EPILOGUE_FORMS = ("bias_relu_mask", "guarded", "atomic", "extra")
+
+
+def epilogue_matmul_package(outdir: Path, form: str, M: int = 128, N: int = 128, K: int = 256) -> Path:
+    """An mma.sync GEMM (f32 accumulators, cp.async-staged 64 x 64 tiles, a 16 x 64 strip per warp)
+    whose result leaves through the fused RegStore forms: ``x0 @ x1^T`` with x0 [M, K], x1 [N, K]
+    integers in -2..2, so every accumulator is an exact integer.
+
+    * ``bias_relu_mask``: y f16 [M, N] = (col <= row) ? relu(0.5 acc + bias[col]) : 0, an epilogue
+      Lambda with the element's row and column bound (Let, Assign, a Load of the bias, Select);
+    * ``guarded``: y f32 [M - 28, N - 38], the tiles past its edges dropped by ``m_guard`` /
+      ``n_guard``;
+    * ``atomic``: K split over four CTAs per tile, each adding its partial product into y f32 [M, N]
+      (zeroed before the launch) with ``red.global.add``;
+    * ``extra``: a second accumulator d = x0 @ x2^T passed through ``extra_frags``; y = acc * d."""
+    if form not in EPILOGUE_FORMS or M % 64 or N % 64 or K % 64:
+        raise ValueError("epilogue_matmul_package: a known form and M, N, K multiples of 64")
+    F16 = F16T
+    ks_n = 4 if form == "atomic" else 1
+    if K % (64 * ks_n):
+        raise ValueError("epilogue_matmul_package: K must split into whole blocks")
+    tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
+    srcs = ["x1"] + (["x2"] if form == "extra" else [])
+    accs = ["c"] + (["d"] if form == "extra" else [])
+    body = [ir.RegFragment("a", "a", (16, 8, 16), F16, 1, None)]
+    body += [ir.RegFragment(f"b{i}", "b", (16, 8, 16), F16, 8, None) for i in range(len(srcs))]
+    body += [ir.RegFragment(n, "c", (16, 8, 16), F32T, 8, None) for n in accs]
+    body += [ir.Smem("a_s", (64, 64), "__half", 1024)]
+    body += [ir.Smem(f"b{i}_s", (64, 64), "__half", 1024) for i in range(len(srcs))]
+    ks = []
+    for i in range(4):
+        chunk = B("+", tid, L(128 * i))
+        r, c8 = B("/", chunk, L(8)), B("*", B("%", chunk, L(8)), L(8))
+        ks.append(ir.CpAsyncCopy("a_s", (L(0), L(0)), "x0", (B("+", B("*", V("bm"), L(64)), r), B("+", V("kb"), c8)),
+                                 16, "B128", (r, c8), None))
+        for j, src in enumerate(srcs):
+            ks.append(ir.CpAsyncCopy(f"b{j}_s", (L(0), L(0)), src,
+                                     (B("+", B("*", V("bn"), L(64)), r), B("+", V("kb"), c8)), 16, "B128", (r, c8),
+                                     None))
+    mmas = [_ldm("a", "a_s", (B("*", V("_w"), L(16)), B("*", V("_kk"), L(16))), "a")]
+    for j, acc in enumerate(accs):
+        mmas += [_unrolled("_j", 4, [_ldm(f"b{j}[_j * 2]", f"b{j}_s", (B("*", V("_j"), L(16)), B("*", V("_kk"), L(16))),
+                                          "b", True, f"b{j}[_j * 2 + 1]")]),
+                 _unrolled("_n", 8, [ir.MmaSyncPtx(f"{acc}[_n]", "a", f"b{j}[_n]", (16, 8, 16), "f16", "f32", False,
+                                                   None, None)])]
+    ks += [ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False), _unrolled("_kk", 4, mmas),
+           ir.Sync(0, None, False)]
+    if ks_n == 1:
+        body.append(ir.StridedLoop(axis("kb", K), L(0), L(64), tuple(ks), False, None, False))
+    else:               # CTA ks of the tile covers K columns ks * K / 4 .. (ks + 1) * K / 4
+        k0 = B("*", V("ks"), L(K // ks_n))
+        body.append(ir.StridedLoop(axis("kb", K), k0, L(64), tuple(ks), False, B("+", k0, L(K // ks_n)), False))
+    epilogue, extra, m_guard, n_guard, atomic = None, (), None, None, False
+    out_shape, out_dtype = (M, N), "f32"
+    if form == "bias_relu_mask":
+        out_dtype = "f16"
+        epilogue = ir.Lambda(("v", "row", "col"), (
+            ir.Let("half", L(0.5, "float"), F32T),
+            assign("sv", "multiply", "v", "half"),
+            ir.Load(("bv",), "bias", (V("col"),), F32T),
+            assign("tv", "add", "sv", "bv"),
+            assign("uv", "relu", "tv"),
+            ir.Select("ov", (ir.Branch("uv", B("<=", V("col"), V("row"))), ir.Branch(L(0.0, "float"), None)))),
+            ("ov",))
+    elif form == "guarded":
+        out_shape = (M - 28, N - 38)
+        m_guard, n_guard = L(M - 28), L(N - 38)
+    elif form == "atomic":
+        atomic = True
+    else:
+        epilogue = ir.Lambda(("v", "w"), (assign("pv", "multiply", "v", "w"),), ("pv",))
+        extra = ("d[_s]",)
+    body.append(_unrolled("_s", 8, [ir.RegStore("y", (B("+", B("*", V("bm"), L(64)), B("*", V("_w"), L(16))),
+                                                      B("+", B("*", V("bn"), L(64)), B("*", V("_s"), L(8)))), "c[_s]",
+                                                (16, 8, 16), 0, epilogue, extra, m_guard, n_guard, atomic, "m16n8k16",
+                                                False, None, "NONE", None, None)]))
+    axes = (axis("bm", M // 64), axis("bn", N // 64)) + ((axis("ks", ks_n),) if ks_n > 1 else ())
+    tile = ir.Tile(axes + (axis("_w", 4), axis("_lane", 32)), tuple(body), 128, 0, None, None, "m")
+    entry = f"k_epilogue_{form}"
+    inputs = {"x0": ((M, K), "f16"), **{s: ((N, K), "f16") for s in srcs}}
+    ints = {"dist": "integers", "low": -2, "high": 2}
+    args = [{"name": n, "dtype": "f16", "shape": list(shape), "seed": i, "init": dict(ints, seed=i)}
+            for i, (n, (shape, _)) in enumerate(inputs.items())]
+    order = list(inputs)
+    if form == "bias_relu_mask":
+        inputs["bias"] = ((N,), "f32")
+        args.append({"name": "bias", "dtype": "f32", "shape": [N], "seed": 7})
+        order.append("bias")
+    args.append({"name": "y", "dtype": out_dtype, "shape": list(out_shape), "output": True})
+    g = _graph(inputs, {}, "y", out_shape, entry, tile, out_dtype)
+    kmeta = {"node": "y", "arg_order": order + ["y"], "grid": [(M // 64) * (N // 64) * ks_n, 1, 1],
+             "block": [128, 1, 1], "smem_bytes": 0, "zero_outputs": ["y"] if atomic else [], "args": args}
+    return _write(outdir, f"sm90_epilogue_{form}", "x0 @ x1.T", entry, g, kmeta, 1e-3, 1e-3)
+

@@ -7,8 +7,9 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import (COLS, M, N, ROWS, fragment_attention_package, promote_matmul_package, scan_package,
-                     select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
+from sm90_ir import (COLS, EPILOGUE_FORMS, M, N, ROWS, epilogue_matmul_package, fragment_attention_package,
+                     promote_matmul_package, scan_package, select_package, stuck_wait_package, tma_transpose_package,
+                     wgmma_gemm_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -93,7 +94,8 @@ def test_carried_state_scan(tmp_path):
     assert np.all(res["outputs"]["f"] == fib[1]) and fib[1] == 75025
 
 
-WGMMA_CASES = [{}, {"n_wg": 2}, {"trans_b": True}, {"tail_overwrite": True}, {"BN": 64}, {"BN": 256}]
+WGMMA_CASES = [{}, {"n_wg": 2}, {"trans_b": True}, {"tail_overwrite": True}, {"BN": 64}, {"BN": 256},
+               {"out_scale": 0.25}]
 
 
 @pytest.mark.parametrize("kw", WGMMA_CASES, ids=[",".join(f"{k}={v}" for k, v in c.items()) or "base"
@@ -102,7 +104,9 @@ def test_wgmma_gemm(tmp_path, kw):
     """The sm_90-style GEMM (Wgmma* statements, m64 accumulator fragments) on tcgen05: y = x0 @ B
     against float64 numpy on the same f16 inputs, through the host-buffer run (TMA maps encoded
     per request; a non-zero error word -- a wait that gave up, a skipped copy or MMA -- fails the
-    run).  The tolerance covers f32 accumulation over K = 512 products of N(0, 1) halves (|y| ~ 23)."""
+    run).  The tolerance covers f32 accumulation over K = 512 products of N(0, 1) halves (|y| ~ 23);
+    with ``out_scale`` the result leaves through a RegStore epilogue as f16, whose rounding (half
+    an f16 ulp, 2.4e-4 relative) the same tolerance covers."""
     M_, N_, K_ = 256, 512, 512
     pkg = problems.load_package(wgmma_gemm_package(tmp_path / "g", M_, N_, K_, **kw))
     res = problems.run_package(pkg, problems.compile_package(pkg))
@@ -112,7 +116,10 @@ def test_wgmma_gemm(tmp_path, kw):
     bk = b if kw.get("trans_b") else b.T                      # [K, N]
     if kw.get("tail_overwrite"):
         a, bk = a[:, K_ - 16:], bk[K_ - 16:, :]
-    np.testing.assert_allclose(res["outputs"]["y"], a @ bk, rtol=1e-3, atol=2e-3)
+    want = a @ bk * kw.get("out_scale", 1.0)
+    got = res["outputs"]["y"]
+    assert got.dtype == (np.float16 if "out_scale" in kw else np.float32)
+    np.testing.assert_allclose(got.astype(np.float64), want, rtol=1e-3, atol=2e-3)
 
 
 def test_fragment_attention(tmp_path):
@@ -138,3 +145,32 @@ def test_promote_matmul_exact(tmp_path):
     x = problems.make_inputs(pkg)
     want = (x["x0"].astype(np.int64) @ x["x1"].astype(np.int64).T).astype(np.float32)
     np.testing.assert_array_equal(res["outputs"]["y"], want)
+
+
+@pytest.mark.parametrize("form", EPILOGUE_FORMS)
+def test_regstore_fused_forms(tmp_path, form):
+    """The fused RegStore forms on an mma.sync GEMM of integer inputs in -2..2 (every accumulator an
+    exact integer): an epilogue with the bias load, relu and a coordinate mask into f16; edge
+    guards into a buffer smaller than the tile grid (a store past them would land outside it);
+    four K slices added atomically into a zeroed buffer; an extra accumulator multiplied in.
+    The integer forms are exact; the f16 one is within one f16 rounding of the float32 numpy
+    expression."""
+    pkg = problems.load_package(epilogue_matmul_package(tmp_path / form, form))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    acc = x["x0"].astype(np.int64) @ x["x1"].astype(np.int64).T
+    got = res["outputs"]["y"]
+    if form == "bias_relu_mask":
+        t = np.float32(0.5) * acc.astype(np.float32) + x["bias"].astype(np.float32)
+        rows, cols = np.indices(t.shape)
+        want = np.where(cols <= rows, np.maximum(t, np.float32(0)), np.float32(0)).astype(np.float16)
+        assert got.dtype == np.float16
+        np.testing.assert_allclose(got.astype(np.float32), want.astype(np.float32), rtol=1e-3, atol=1e-3)
+    elif form == "guarded":
+        np.testing.assert_array_equal(got.reshape(acc.shape[0] - 28, acc.shape[1] - 38),
+                                      acc[:-28, :-38].astype(np.float32))
+    elif form == "atomic":
+        np.testing.assert_array_equal(got, acc.astype(np.float32))
+    else:
+        d = x["x0"].astype(np.int64) @ x["x2"].astype(np.int64).T
+        np.testing.assert_array_equal(got, (acc * d).astype(np.float32))

@@ -154,7 +154,13 @@ class TcMatmul(TunedKernel):
                     trans.add(bool(s.b_trans))
         if set(roles) != {"a", "b"} or len(trans) != 1:
             return None
-        outs = {s.dst_buffer for s in stmts if isinstance(s, ir.RegStore)}
+        stores = [s for s in stmts if isinstance(s, ir.RegStore)]
+        # a fused store (epilogue, extra fragments, edge guards, atomic accumulation) is not the plain
+        # product this schedule writes: those kernels take the generic lowering
+        if any(s.epilogue is not None or s.extra_frags or s.m_guard is not None or s.n_guard is not None
+               or s.atomic or s.volta_interleaved or s.swizzle not in ("NONE", None) for s in stores):
+            return None
+        outs = {s.dst_buffer for s in stores}
         if len(outs) != 1:
             return None
         a, b, c = kernel.param(roles["a"]), kernel.param(roles["b"]), kernel.param(outs.pop())
@@ -180,7 +186,11 @@ class TcMatmul(TunedKernel):
         # the K loop of the schedule must cover the whole (split) K range
         loops = [s for s in stmts if isinstance(s, (ir.Loop, ir.StridedLoop))
                  and any(isinstance(x, ir.MmaSyncPtx) for x in ir.walk_stmts(s.body))]
-        if not any(lp.axis.extent.is_static and lp.axis.size == K // S for lp in loops):
+        def whole(lp):
+            start = getattr(lp, "start", ir.Literal(0, "int"))
+            return (lp.axis.extent.is_static and lp.axis.size == K // S and getattr(lp, "end", None) is None
+                    and isinstance(start, ir.Literal) and start.value == 0)
+        if not any(whole(lp) for lp in loops):
             return None
         static = sum(int(__import__("math").prod(s.extents)) * (2 if s.dtype in ("__half", "half") else 4)
                      for s in stmts if isinstance(s, ir.Smem)) if kernel.dynamic_smem_bytes == 0 else 0

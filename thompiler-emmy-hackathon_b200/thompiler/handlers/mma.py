@@ -201,13 +201,90 @@ def emit_mma_sync(w: "Walker", mma: ir.MmaSyncPtx) -> None:
     em.ins(f"mma.sync.aligned.m16n8k16.row.col.{mma.c_dtype}.{ab}.{ab}.{mma.c_dtype} {c}, {a}, {b}, {c}")
 
 
+EPILOGUE_STMTS = (ir.Load, ir.Assign, ir.Let, ir.Select)
+
+
+def _param_name(p) -> str:
+    name = p.name if isinstance(p, ir.Var) else p
+    if not isinstance(name, str):
+        raise ValueError(f"Lambda parameter {p!r}")
+    return name
+
+
+def _epilogue_value(w: "Walker", lam: ir.Lambda, elems: list[str], row: str, col: str) -> tuple[str, Ty]:
+    """One fragment element through a RegStore epilogue: the Lambda's leading parameters are bound
+    to ``elems`` (the element of the stored fragment, then the same element of each extra
+    fragment); two further parameters, when declared, to the element's destination row and
+    column (s32).  The body (Load / Assign / Let / Select) is lowered for this element, and the
+    register of its one result is returned with the result's type."""
+    em = w.em
+    params = [_param_name(p) for p in lam.params]
+    if len(params) not in (len(elems), len(elems) + 2):
+        raise ValueError(f"RegStore epilogue takes {len(params)} parameters for {len(elems)} fragments "
+                         f"(one per fragment, optionally then row and column)")
+    for name, reg in zip(params, elems):
+        em.ins(f"mov.f32 {em.value(name, 'f32')}, {reg}")
+    if len(params) == len(elems) + 2:
+        em.ins(f"mov.s32 {em.value(params[-2], 'b32')}, {row}")
+        em.ins(f"mov.s32 {em.value(params[-1], 'b32')}, {col}")
+    for s in lam.body:
+        if not isinstance(s, EPILOGUE_STMTS):
+            kind = s.kind if isinstance(s, ir.Opaque) else type(s).__name__
+            raise NotImplementedError(f"RegStore epilogue statement {kind} (only Load, Assign, Let, Select)")
+        w.stmt(s)
+    results = [_param_name(r) for r in lam.results]
+    if len(results) != 1:
+        raise NotImplementedError(f"RegStore epilogue with {len(results)} results")
+    reg = em.get(results[0])
+    cls = em.named[reg]
+    if cls not in ("f32", "b16"):
+        raise TypeError(f"RegStore epilogue result {results[0]} is a .{cls} value, not a float")
+    out = em.tmp(cls)            # the result's name is rebound by the next element's evaluation
+    em.ins(f"mov.{'f32' if cls == 'f32' else 'b16'} {out}, {reg}")
+    return out, (F32 if cls == "f32" else F16)
+
+
+def _to(w: "Walker", reg: str, have: Ty, want: Ty) -> str:
+    if have is want:
+        return reg
+    out = w.em.tmp(want.reg)
+    w.em.ins(f"{'cvt.rn.f16.f32' if want is F16 else 'cvt.f32.f16'} {out}, {reg}")
+    return out
+
+
+def _plus(addr: str, nbytes: int) -> str:
+    base, _, off = addr.partition("+")
+    return f"{base}+{int(off or 0) + nbytes}"
+
+
 def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
+    """A C fragment (an m16n8 ``mma.sync`` accumulator or an m64nN warpgroup one) to global
+    memory, each lane storing its registers at the rows and columns of the accumulator layout.
+
+    Plain form: a two-element store per register pair (``st.global.v2.f32``, or one f16x2 word
+    for an f16 buffer).  Fused form, when any of these is given:
+
+    * ``epilogue``: an ``ir.Lambda`` evaluated per element (``_epilogue_value``), its result
+      rounded to the buffer's type: the fused pointwise tail of TASK.md:159 of the IR
+      reference;
+    * ``extra_frags``: further accumulators of the same geometry whose same element is passed
+      to the epilogue;
+    * ``m_guard`` / ``n_guard``: the element is stored only where its destination row is below
+      ``m_guard`` and its column below ``n_guard`` (exclusive bounds on the destination
+      coordinates; ragged edges of M and N);
+    * ``atomic``: ``red.global.add`` of each element instead of a store (split-K partial sums).
+
+    Guarded and atomic stores, and rows of an odd length, go element by element; an epilogue
+    alone keeps the pair stores."""
     em = w.em
     em.note(f"RegStore {st.dst_buffer} <- {st.frag}")
-    if (st.fragment_layout not in ("m16n8k16", "m64nNk16") or st.volta_interleaved or st.epilogue is not None
-            or st.extra_frags or st.m_guard is not None or st.n_guard is not None or st.atomic
+    if (st.fragment_layout not in ("m16n8k16", "m64nNk16") or st.volta_interleaved
             or st.swizzle not in ("NONE", None)):
-        raise NotImplementedError("RegStore form: epilogue, guards, atomics, swizzle or Volta layout")
+        raise NotImplementedError("RegStore form: swizzled or Volta layout")
+    if st.epilogue is not None and not isinstance(st.epilogue, ir.Lambda):
+        raise NotImplementedError(f"RegStore epilogue {type(st.epilogue).__name__} (a Lambda expected)")
+    if st.extra_frags and st.epilogue is None:
+        raise ValueError("RegStore extra_frags without an epilogue to read them")
     shape = tuple(int(x) for x in st.shape)
     wide = len(shape) == 3 and shape[0] == 64 and shape[2] == 16 and shape[1] % 8 == 0
     if shape != (16, 8, 16) and not wide:
@@ -221,6 +298,12 @@ def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
     want = shape[1] // 2 if wide else 4
     if frag.role != "c" or frag.ty is not F32 or len(regs) != want:
         raise ValueError(f"RegStore of {st.frag}: not an f32 accumulator of {want} registers")
+    extra = []
+    for ref in st.extra_frags:
+        f2, r2 = fragment_regs(w, ref)
+        if f2.role != "c" or f2.ty is not F32 or len(r2) != want:
+            raise ValueError(f"RegStore extra fragment {ref}: not an f32 accumulator of {want} registers")
+        extra.append(r2)
     index = list(st.dst_index)
     if len(index) < 2:
         raise ValueError(f"RegStore to {st.dst_buffer}: {len(index)}-d index")
@@ -233,20 +316,68 @@ def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
         row_stride *= e
     if st.ldm and int(st.ldm) != row_stride:
         raise NotImplementedError(f"RegStore ldm={st.ldm}, but the row stride is {row_stride}")
+    guarded = st.m_guard is not None or st.n_guard is not None
+    wants_coords = st.epilogue is not None and len(st.epilogue.params) == 1 + len(extra) + 2
+    # a pair store needs the pair's first element at an even offset: an odd row stride goes element by element
+    by_element = guarded or st.atomic or row_stride % 2 == 1
     lane = ir.Var("lane")
     g = _lane_expr("/", lane, 4)
     if wide:                     # a warpgroup accumulator: warp q of the group holds rows 16q..16q+15
         g = ir.BinaryExpr("+", g, _lane_expr("*", _lane_expr("%", ir.Var("warp"), 4), 16))
     col = _lane_expr("*", _lane_expr("%", lane, 4), 2)
-    for dr, dc, (lo, hi) in ((dr, 8 * i, regs[4 * i + (2 if dr else 0):4 * i + (4 if dr else 2)])
-                             for i in range(len(regs) // 4) for dr in (0, 8)):
-        idx = list(index)
-        idx[rdim] = ir.BinaryExpr("+", st.dst_index[rdim], g if dr == 0 else _lane_expr("+", g, dr))
-        idx[cdim] = ir.BinaryExpr("+", st.dst_index[cdim], col if dc == 0 else _lane_expr("+", col, dc))
-        addr = address.global_address(w, p, tuple(idx))
-        if p.ty is F32:
-            em.ins(f"st.global.v2.f32 [{addr}], {{{lo}, {hi}}}")
-        else:
-            packed = em.tmp("b32")
-            em.ins(f"cvt.rn.f16x2.f32 {packed}, {hi}, {lo}")
-            em.ins(f"st.global.b32 [{addr}], {packed}")
+    for i in range(len(regs) // 4):
+        for dr in (0, 8):
+            k = 4 * i + (2 if dr else 0)
+            row_e = ir.BinaryExpr("+", st.dst_index[rdim], g if dr == 0 else _lane_expr("+", g, dr))
+            col_e = ir.BinaryExpr("+", st.dst_index[cdim], col if i == 0 else _lane_expr("+", col, 8 * i))
+            idx = list(index)
+            idx[rdim], idx[cdim] = row_e, col_e
+            addr = address.global_address(w, p, tuple(idx))
+            row_r = col_r = None
+            if wants_coords:
+                row_r, col_r = expr.int_operand(w, row_e), expr.int_operand(w, col_e)
+            vals = []
+            for j in (0, 1):
+                v, ty = regs[k + j], F32
+                if st.epilogue is not None:
+                    c_j = col_r
+                    if j and wants_coords:
+                        c_j = em.tmp("b32")
+                        em.ins(f"add.s32 {c_j}, {col_r}, 1")
+                    v, ty = _epilogue_value(w, st.epilogue, [v] + [r[k + j] for r in extra], row_r, c_j)
+                vals.append((v, ty))
+            if not by_element:
+                if p.ty is F32:
+                    lo, hi = (_to(w, v, ty, F32) for v, ty in vals)
+                    em.ins(f"st.global.v2.f32 [{addr}], {{{lo}, {hi}}}")
+                    continue
+                packed = em.tmp("b32")
+                if vals[0][1] is F32 and vals[1][1] is F32:
+                    em.ins(f"cvt.rn.f16x2.f32 {packed}, {vals[1][0]}, {vals[0][0]}")
+                else:
+                    lo, hi = (_to(w, v, ty, F16) for v, ty in vals)
+                    em.ins(f"mov.b32 {packed}, {{{lo}, {hi}}}")
+                em.ins(f"st.global.b32 [{addr}], {packed}")
+                continue
+            vals = [_to(w, v, ty, p.ty) for v, ty in vals]
+            row_ok = None
+            if st.m_guard is not None:
+                row_ok = expr.pred_operand(w, ir.BinaryExpr("<", row_e, st.m_guard))
+            for j in (0, 1):
+                pred = row_ok
+                if st.n_guard is not None:
+                    col_j = col_e if j == 0 else ir.BinaryExpr("+", col_e, ir.Literal(1, "int"))
+                    col_ok = expr.pred_operand(w, ir.BinaryExpr("<", col_j, st.n_guard))
+                    if pred is None:
+                        pred = col_ok
+                    else:
+                        both = em.tmp("pred")
+                        em.ins(f"and.pred {both}, {row_ok}, {col_ok}")
+                        pred = both
+                at = addr if j == 0 else _plus(addr, p.ty.nbytes)
+                guard = f"@{pred} " if pred is not None else ""
+                if st.atomic:
+                    op = "red.global.add.f32" if p.ty is F32 else "red.global.add.noftz.f16"
+                else:
+                    op = "st.global.f32" if p.ty is F32 else "st.global.b16"
+                em.ins(f"{guard}{op} [{at}], {vals[j]}")

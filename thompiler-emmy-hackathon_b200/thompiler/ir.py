@@ -581,6 +581,16 @@ class FragLayout:
 
 
 @dataclass(frozen=True)
+class Lambda:
+    """A pure per-element function (a RegStore epilogue): ``params`` are bound on entry,
+    ``body`` (Load / Assign / Let / Select statements) is evaluated, ``results`` name the
+    values it returns."""
+    params: tuple = ()
+    body: tuple = ()
+    results: tuple = ()
+
+
+@dataclass(frozen=True)
 class FragmentPromote(Stmt):
     dst: str
     src: str = ""
@@ -659,8 +669,8 @@ class WgmmaWait(Stmt):
 @dataclass(frozen=True)
 class Opaque(Stmt):
     """A constructor this reader does not model; kept so the walker can name
-    it when it fails (BlockScaleLoad, Lambda ... appear in the IR reference but
-    in no shipped kernel)."""
+    it when it fails (BlockScaleLoad appears in the IR reference but in no
+    shipped kernel)."""
     kind: str
     fields: tuple = field(default=())
 
@@ -679,7 +689,7 @@ _CONSTRUCTORS: dict[str, type] = {
         CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
         Branch, Select, Pre, Carry, ZeroPrologue, TmaDescriptor, TmaLoad, MbarrierInit,
         MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg, WgmmaDescriptor, WgmmaMma,
-        WgmmaFence, WgmmaCommit, WgmmaWait, FragLayout, FragmentPromote, FragmentApply, FragmentRowReduce,
+        WgmmaFence, WgmmaCommit, WgmmaWait, FragLayout, Lambda, FragmentPromote, FragmentApply, FragmentRowReduce,
         FragmentRepack)
 }
 
