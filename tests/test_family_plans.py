@@ -122,3 +122,44 @@ def test_attention_pair_needs_opt_in_and_shape(tmp_path, monkeypatch):
     for shape in ((1, 2, 384, 128), (2, 2, 512, 64)):         # S not a multiple of 256, or d = 64
         fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / f"b{shape[2]}{shape[3]}", *shape))))
         assert not isinstance(fam, TcAttentionPair)
+
+
+@pytest.mark.parametrize("M,N,K,lay,bn,tiles,stages", [(4096, 4096, 4096, "col", 0, 256, 6),
+                                                      (8192, 3072, 1024, "col", 0, 384, 6),
+                                                      (256, 128, 256, "row", 0, 1, 8),
+                                                      (512, 256, 256, "col", 128, 4, 8)])
+def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages):
+    """The CTA-pair matmul (opt-in): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
+    of B; one pair per two SMs; a cluster launch of an even grid; shared memory (with the
+    generic path's static arrays) inside one SM's 227 KB."""
+    from thompiler.families.matmul_pair import TcMatmulPair
+    d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay)
+    assert not isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)          # off by default
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "1")
+    if bn:
+        monkeypatch.setenv("THOMPILER_MATMUL_BN", str(bn))
+    fam = recognise(_kernel(_ir(d)))
+    assert isinstance(fam, TcMatmulPair)
+    assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, bn or (256 if N % 256 == 0 else 128))
+    assert fam.b_bytes == fam.BN // 2 * 64 * 2 and fam.a_bytes == 128 * 64 * 2
+    assert fam.ctas == 2 * min(tiles, 74)
+    side = fam.sidecar()
+    assert side["cluster"] == [2, 1, 1] and side["grid"] == [fam.ctas, 1, 1]
+    assert fam.smem + fam.static_smem <= 227 * 1024
+    if lay == "col":
+        assert side["tmaps"][1]["box"] == [64, fam.BN // 2]
+
+
+def test_matmul_pair_declines_odd_generic_grid(tmp_path, monkeypatch):
+    """A cluster launch needs an even grid under meta.json's launch too: a package whose generic
+    grid is odd keeps the single-CTA kernel."""
+    import json
+    from thompiler.families.matmul_pair import TcMatmulPair
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "1")
+    d = synth.matmul_package(tmp_path / "mm", 256, 256, 256)        # generic grid 4 x 4 = 16: even
+    assert isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)
+    meta = json.loads((d / "meta.json").read_text())
+    meta["kernels"][0]["grid"] = [11, 1, 1]
+    (d / "meta.json").write_text(json.dumps(meta))
+    fam = recognise(_kernel(_ir(d)))
+    assert isinstance(fam, TcMatmul) and not isinstance(fam, TcMatmulPair)

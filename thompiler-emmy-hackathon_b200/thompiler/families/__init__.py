@@ -10,8 +10,8 @@ from thompiler.load import KernelInfo
 
 
 def recognise(kernel: KernelInfo):
-    from thompiler.families import attention, attention_pair, matmul, pointwise, strided
-    for fam in (strided, matmul, attention_pair, attention, pointwise):
+    from thompiler.families import attention, attention_pair, matmul, matmul_pair, pointwise, strided
+    for fam in (strided, matmul_pair, matmul, attention_pair, attention, pointwise):
         k = fam.recognise(kernel)
         if k is not None:
             return k

@@ -78,6 +78,7 @@ class TcMatmul(TunedKernel):
         self.M, self.N, self.K, self.S = M, N, K, S
         self.Ks = K // S
         self.b_kmajor = b_kmajor
+        self.static_smem = static_smem
         self.BN = self.pick_bn()
         self.a_bytes = BM * BK * 2
         self.b_bytes = self.BN * BK * 2

@@ -1,0 +1,414 @@
+"""Tuned family: the f16 tensor-core matmul of ``thompiler.families.matmul`` on CTA pairs
+(tcgen05 ``cta_group::2``).
+
+Same recognised IR and result (C[M, N] = A[M, K] @ B, B stored [N, K] or [K, N], f16 in, f32
+accumulate, f32 / f16 out, the split-K [S, M, N] form).  A pair of CTAs (a ``.reqnctapercluster
+2`` launch, one CTA per SM) computes a 256 x BN tile with one 2-SM MMA per K step of 16:
+
+  CTA r of the pair   holds A rows 128 r .. 128 r + 127 of the tile and B columns
+                      (BN / 2) r .. (BN / 2) r + BN / 2 - 1 (K-major: rows of B's [N, K]
+                      storage) in its own shared memory, 64-deep K stages;
+  leader (r = 0)      its MMA warp issues tcgen05.mma.cta_group::2 (M = 256, N = BN, K = 16)
+                      for the pair; the accumulator's rows 128 r .. live in CTA r's tensor memory.
+
+Per SM and K step this reads A 128 x 64 and half of B from shared memory -- a 256 x 256 pair tile
+moves a third less operand data per FLOP through L2 and shared memory than the single-CTA
+128 x 256 tile.
+
+Warp roles per CTA (192 threads): warp 0 TMA (this CTA's halves; each load completes on the
+leader's ``full`` barrier, which the leader posts both CTAs' bytes on), warp 1 the MMA issuer
+(leader only; allocates the pair's TMEM in both CTAs), warps 2-5 the epilogue of this CTA's 128
+rows (tcgen05.ld -> 64B-swizzled staging -> TMA store, as the single-CTA kernel).  Barriers at
+the same offsets in both CTAs: ``empty`` (per stage) and ``acc_full`` (per accumulator) arrive in
+both CTAs from one multicast tcgen05.commit; the leader's ``acc_empty`` takes one arrival per
+epilogue warp of either CTA.  Every wait is bounded (error word + common exit); the CTAs meet
+at a cluster barrier before freeing TMEM, so neither leaves while the other can still signal it.
+No TMA load uses cluster multicast: each CTA loads its own halves.
+"""
+
+from __future__ import annotations
+
+import os
+
+from thompiler.families.kit import Kit, desc_hi, idesc_f16
+from thompiler.families.matmul import BK, BM, EPI_WARPS, SM_COUNT, STAGE_TILE, TcMatmul
+from thompiler.families.base import TunedKernel
+from thompiler.load import KernelInfo
+
+PM = 2 * BM                  # rows of a pair tile
+PAIR_SLOTS = SM_COUNT // 2   # pairs resident at once
+SMEM_LIMIT = 227 * 1024
+
+
+class TcMatmulPair(TcMatmul):
+    family = "tcgen05-matmul-pair"
+
+    @classmethod
+    def match(cls, kernel: KernelInfo):
+        if os.environ.get("THOMPILER_MATMUL_PAIR", "0") != "1":
+            return None
+        one = TcMatmul.match.__func__(TcMatmul, kernel)
+        if one is None or one.M % PM or kernel.grid[0] % 2:
+            return None                    # the cluster launch needs an even generic grid too
+        bn = cls.pair_bn(one.M, one.N, one.S)
+        if bn is None:
+            return None
+        return cls(kernel, one.a, one.b, one.c, one.M, one.N, one.K, one.S, one.b_kmajor, bn, one.static_smem)
+
+    @staticmethod
+    def pair_bn(M: int, N: int, S: int) -> int | None:
+        forced = int(os.environ.get("THOMPILER_MATMUL_BN", "0"))     # tuning knob
+        if forced in (128, 256) and N % forced == 0:
+            return forced
+        for bn in (256, 128):
+            if N % bn == 0:
+                return bn
+        return None
+
+    def __init__(self, kernel, a, b, c, M, N, K, S, b_kmajor, bn, static_smem):  # noqa: D107
+        TunedKernel.__init__(self, kernel)
+        self.a, self.b, self.c = a, b, c
+        self.M, self.N, self.K, self.S = M, N, K, S
+        self.Ks = K // S
+        self.b_kmajor = b_kmajor
+        self.static_smem = static_smem
+        self.BN = bn
+        self.HN = bn // 2                                    # B columns held by each CTA
+        self.a_bytes = BM * BK * 2
+        self.b_bytes = self.HN * BK * 2
+        stage = self.a_bytes + self.b_bytes
+        self.staging = EPI_WARPS * 2 * STAGE_TILE
+        room = SMEM_LIMIT - static_smem - 2048 - self.staging
+        self.stages = max(2, min(8, room // stage))
+        forced = int(os.environ.get("THOMPILER_MATMUL_STAGES", "0"))
+        if 2 <= forced <= room // stage:
+            self.stages = forced
+        self.smem = self.stages * stage + self.staging + 1024 + 256
+        self.tiles = (M // PM) * (N // bn) * S
+        self.pairs = min(self.tiles, PAIR_SLOTS)
+        self.ctas = 2 * self.pairs
+        self.rem, self.parts, self.full_tiles, self.units = 0, 1, self.tiles, self.tiles
+
+    def sidecar(self) -> dict:
+        side = super().sidecar()
+        a, b = self.a, self.b
+        side["tmaps"][0]["box"] = [BK, BM]
+        if self.b_kmajor:
+            side["tmaps"][1]["box"] = [BK, self.HN]
+        side["grid"] = [self.ctas, 1, 1]
+        side["cluster"] = [2, 1, 1]
+        side["tile"] = [PM, self.BN, BK]
+        assert side["tmap_ptrs"]["params"] == [a.name, b.name, self.c.name]
+        return side
+
+    def guard(self, generic: str) -> None:
+        super().guard(generic)
+        self.em.entry_attrs.append(".reqnctapercluster 2, 1, 1")
+
+    # ---- the tuned body -------------------------------------------------------------
+
+    def emit_tuned(self) -> None:  # noqa: C901 - one kernel, written out in order
+        em = self.em
+        t, ins, place, lab = em.tmp, em.ins, em.place, em.label
+        BN, HN, ST = self.BN, self.HN, self.stages
+        a_bytes, b_bytes = self.a_bytes, self.b_bytes
+        tiles_m, tiles_n = self.M // PM, self.N // BN
+        kblocks = self.Ks // BK
+        tiles = self.tiles
+        mcommit = "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        tma_ld = "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+
+        tid, warp, lane = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {tid}, %tid.x")
+        ins(f"shr.u32 {warp}, {tid}, 5")
+        ins(f"and.b32 {lane}, {tid}, 31")
+        rank = self.special("%cluster_ctarank")
+        base = t("b32")
+        ins(f"mov.u32 {base}, smem_pool")
+        ins(f"add.u32 {base}, {base}, 1023")
+        ins(f"and.b32 {base}, {base}, -1024")
+        # shared (same offsets in both CTAs): A stages | B stages | epilogue staging | barriers
+        a_st, b_st, bars = base, t("b32"), t("b32")
+        ins(f"add.u32 {b_st}, {base}, {ST * a_bytes}")
+        ins(f"add.u32 {bars}, {base}, {ST * (a_bytes + b_bytes) + self.staging}")
+        empty_off, accf_off, acce_off, slot_off = 8 * ST, 16 * ST, 16 * ST + 16, 16 * ST + 32
+        p = t("pred")
+        skip = lab("mp_noinit")
+        ins(f"setp.ne.u32 {p}, {tid}, 0")
+        ins(f"@{p} bra {skip}")
+        for s in range(ST):
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{8 * s}], 1")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{empty_off + 8 * s}], 1")
+        for b in range(2):
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{accf_off + 8 * b}], 1")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{acce_off + 8 * b}], {2 * EPI_WARPS}")
+        ins("fence.mbarrier_init.release.cluster")
+        ins("fence.proxy.async.shared::cta")
+        place(skip)
+        # TMEM: warp 1 of both CTAs allocates the pair's 2 x BN accumulator columns
+        tmem_cols = 512 if 2 * BN > 256 else 256
+        noalloc = lab("mp_noalloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {noalloc}")
+        slot = t("b32")
+        ins(f"add.u32 {slot}, {bars}, {slot_off}")
+        ins(f"tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [{slot}], {tmem_cols}")
+        ins("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned")
+        place(noalloc)
+        ins("tcgen05.fence::before_thread_sync")
+        ins("bar.sync 0")
+        # both CTAs' barriers are initialised before either signals the other's
+        ins("barrier.cluster.arrive.release")
+        ins("barrier.cluster.wait.acquire")
+        ins("tcgen05.fence::after_thread_sync")
+        tmem = t("b32")
+        ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
+        lbars = t("b32")                                   # the leader's barriers, cluster address
+        ins(f"mapa.shared::cluster.u32 {lbars}, {bars}, 0")
+        mask = t("b16")
+        ins(f"mov.b16 {mask}, 3")
+        lead_cta = t("pred")
+        ins(f"setp.eq.u32 {lead_cta}, {rank}, 0")
+        pid, npair = self.special("%clusterid.x"), self.special("%nclusterid.x")
+
+        tma, tmb, tmc = t("b64"), t("b64"), t("b64")
+        for r, n in ((tma, "a"), (tmb, "b"), (tmc, "c")):
+            ins(f"mov.u64 {r}, thc_tmap_{n}")
+            ins(f"cvta.global.u64 {r}, {r}")
+        errp = t("b64")
+        ins(f"mov.u64 {errp}, thc_error")
+        end = lab("mp_end")
+        kit = Kit(em, errp, end)
+
+        def decode(tile: str):
+            tm_, tn_, ts_, r = t("b32"), t("b32"), t("b32"), t("b32")
+            ins(f"rem.u32 {tm_}, {tile}, {tiles_m}")
+            ins(f"div.u32 {r}, {tile}, {tiles_m}")
+            ins(f"rem.u32 {tn_}, {r}, {tiles_n}")
+            ins(f"div.u32 {ts_}, {r}, {tiles_n}")
+            return tm_, tn_, ts_
+
+        role_mma, role_epi = lab("mp_mma"), lab("mp_epi")
+        ins(f"setp.eq.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_mma}")
+        ins(f"setp.gt.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {role_epi}")
+
+        # ---------------- producer (warp 0 of each CTA: this CTA's A rows and B half) ----------------
+        is0, post = t("pred"), t("pred")
+        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        ins(f"and.pred {post}, {is0}, {lead_cta}")       # the leader posts both CTAs' bytes
+        it, pu = t("b32"), t("b32")
+        ins(f"mov.u32 {it}, 0")
+        ins(f"mov.u32 {pu}, {pid}")
+        ptop = lab("mp_prod_tile")
+        ins(f"setp.ge.u32 {p}, {pu}, {tiles}")
+        ins(f"@{p} bra {end}")
+        place(ptop)
+        tm_, tn_, ts_ = decode(pu)
+        m0, n0, k0, kb = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"mul.lo.u32 {m0}, {tm_}, {PM}")
+        ins(f"mad.lo.u32 {m0}, {rank}, {BM}, {m0}")
+        ins(f"mul.lo.u32 {n0}, {tn_}, {BN}")
+        ins(f"mad.lo.u32 {n0}, {rank}, {HN}, {n0}")
+        ins(f"mul.lo.u32 {k0}, {ts_}, {self.Ks}")
+        ins(f"mov.u32 {kb}, 0")
+        ktop = lab("mp_prod_k")
+        place(ktop)
+        stage, eb, fb = t("b32"), t("b32"), t("b32")
+        ins(f"rem.u32 {stage}, {it}, {ST}")
+        ins(f"mad.lo.u32 {eb}, {stage}, 8, {bars}")
+        kit.wait(f"{eb}+{empty_off}", kit.parity(it, ST, flip=True), 0)
+        ins(f"mad.lo.u32 {fb}, {stage}, 8, {lbars}")
+        sa, sb, kc = t("b32"), t("b32"), t("b32")
+        ins(f"mad.lo.u32 {sa}, {stage}, {a_bytes}, {a_st}")
+        ins(f"mad.lo.u32 {sb}, {stage}, {b_bytes}, {b_st}")
+        ins(f"mad.lo.u32 {kc}, {kb}, {BK}, {k0}")
+        ins(f"@{post} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{eb}], {2 * (a_bytes + b_bytes)}")
+        ins(f"@{is0} {tma_ld} [{sa}], [{tma}, {{{kc}, {m0}}}], [{fb}]")
+        if self.b_kmajor:
+            ins(f"@{is0} {tma_ld} [{sb}], [{tmb}, {{{kc}, {n0}}}], [{fb}]")
+        else:
+            for nb in range(HN // 64):
+                nn = t("b32")
+                ins(f"add.u32 {nn}, {n0}, {nb * 64}")
+                ins(f"@{is0} {tma_ld} [{sb}+{nb * 64 * BK * 2}], [{tmb}, {{{nn}, {kc}}}], [{fb}]")
+        ins(f"add.u32 {it}, {it}, 1")
+        ins(f"add.u32 {kb}, {kb}, 1")
+        ins(f"setp.lt.u32 {p}, {kb}, {kblocks}")
+        ins(f"@{p} bra {ktop}")
+        ins(f"add.u32 {pu}, {pu}, {npair}")
+        ins(f"setp.lt.u32 {p}, {pu}, {tiles}")
+        ins(f"@{p} bra {ptop}")
+        # every load of this CTA is consumed by an MMA whose completion the epilogues wait for
+        # before the common exit's cluster barrier, so none is in flight when the CTAs leave
+        ins(f"bra {end}")
+
+        # ---------------- MMA issuer (the leader's warp 1, for the pair) ----------------
+        place(role_mma)
+        ins(f"@!{lead_cta} bra {end}")
+        ism = t("pred")
+        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        hi = t("b32")
+        ins(f"mov.u32 {hi}, {desc_hi(1024)}")
+        idesc = idesc_f16(PM, BN, b_mn_major=not self.b_kmajor)
+        zero = t("b32")
+        ins(f"mov.u32 {zero}, 0")
+        always, never = t("pred"), t("pred")
+        ins(f"setp.eq.u32 {always}, {zero}, 0")
+        ins(f"setp.ne.u32 {never}, {zero}, 0")
+        it2, mu, lt = t("b32"), t("b32"), t("b32")
+        ins(f"mov.u32 {it2}, 0")
+        ins(f"mov.u32 {lt}, 0")
+        ins(f"mov.u32 {mu}, {pid}")
+        mtop = lab("mp_mma_tile")
+        ins(f"setp.ge.u32 {p}, {mu}, {tiles}")
+        ins(f"@{p} bra {end}")
+        place(mtop)
+        buf, ab = t("b32"), t("b32")
+        ins(f"and.b32 {buf}, {lt}, 1")
+        ins(f"mad.lo.u32 {ab}, {buf}, 8, {bars}")
+        use = t("b32")
+        ins(f"shr.u32 {use}, {lt}, 1")
+        kit.wait(f"{ab}+{acce_off}", kit.parity(use, 1, flip=True), 1, cluster=True)
+        ins("tcgen05.fence::after_thread_sync")
+        dt = t("b32")
+        ins(f"mad.lo.u32 {dt}, {buf}, {BN}, {tmem}")
+        kb2 = t("b32")
+        ins(f"mov.u32 {kb2}, 0")
+        mk = lab("mp_mma_k")
+        place(mk)
+        st2, fb2 = t("b32"), t("b32")
+        ins(f"rem.u32 {st2}, {it2}, {ST}")
+        ins(f"mad.lo.u32 {fb2}, {st2}, 8, {bars}")
+        kit.wait(fb2, kit.parity(it2, ST), 1)
+        ins("tcgen05.fence::after_thread_sync")
+        sa2, sb2 = t("b32"), t("b32")
+        ins(f"mad.lo.u32 {sa2}, {st2}, {a_bytes}, {a_st}")
+        ins(f"mad.lo.u32 {sb2}, {st2}, {b_bytes}, {b_st}")
+        ad0 = kit.desc(sa2, 16, hi)
+        bd0 = kit.desc(sb2, 16 if self.b_kmajor else 64 * BK * 2, hi)
+        first = t("pred")
+        ins(f"setp.ne.u32 {first}, {kb2}, 0")        # the tile's first MMA overwrites the accumulator
+        for k in range(BK // 16):
+            ad = kit.desc_add(ad0, k * 32)
+            bd = kit.desc_add(bd0, k * 32 if self.b_kmajor else k * 16 * 128)
+            ins(f"@{ism} tcgen05.mma.cta_group::2.kind::f16 [{dt}], {ad}, {bd}, {idesc}, "
+                f"{first if k == 0 else always}")
+        ins(f"@{ism} {mcommit} [{fb2}+{empty_off}], {mask}")
+        ins(f"add.u32 {it2}, {it2}, 1")
+        ins(f"add.u32 {kb2}, {kb2}, 1")
+        ins(f"setp.lt.u32 {p}, {kb2}, {kblocks}")
+        ins(f"@{p} bra {mk}")
+        ins(f"@{ism} {mcommit} [{ab}+{accf_off}], {mask}")
+        ins(f"add.u32 {lt}, {lt}, 1")
+        ins(f"add.u32 {mu}, {mu}, {npair}")
+        ins(f"setp.lt.u32 {p}, {mu}, {tiles}")
+        ins(f"@{p} bra {mtop}")
+        ins(f"bra {end}")
+
+        # ---------------- epilogue (warps 2..5 of each CTA: its 128 rows) ----------------
+        place(role_epi)
+        quarter = t("b32")
+        ins(f"and.b32 {quarter}, {warp}, 3")
+        lane_off = t("b32")
+        ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
+        lane0 = t("pred")
+        ins(f"setp.eq.u32 {lane0}, {lane}, 0")
+        ebase = t("b32")
+        ins(f"sub.u32 {ebase}, {warp}, 2")
+        ins(f"mad.lo.u32 {ebase}, {ebase}, {2 * STAGE_TILE}, {b_st}")
+        ins(f"add.u32 {ebase}, {ebase}, {ST * b_bytes}")
+        stage_buf = [ebase, t("b32")]
+        ins(f"add.u32 {stage_buf[1]}, {ebase}, {STAGE_TILE}")
+        sw = t("b32")
+        ins(f"shr.u32 {sw}, {lane}, 1")
+        ins(f"and.b32 {sw}, {sw}, 3")
+        soff = []
+        for i in range(4):
+            o = t("b32")
+            ins(f"xor.b32 {o}, {sw}, {i}")
+            ins(f"shl.b32 {o}, {o}, 4")
+            ins(f"mad.lo.u32 {o}, {lane}, 64, {o}")
+            soff.append(o)
+        eu, lt3 = t("b32"), t("b32")
+        ins(f"mov.u32 {lt3}, 0")
+        ins(f"mov.u32 {eu}, {pid}")
+        etop, edone = lab("mp_epi_tile"), lab("mp_epi_done")
+        ins(f"setp.ge.u32 {p}, {eu}, {tiles}")
+        ins(f"@{p} bra {edone}")
+        place(etop)
+        tm3, tn3, ts3 = decode(eu)
+        buf3, ab3, lab3 = t("b32"), t("b32"), t("b32")
+        ins(f"and.b32 {buf3}, {lt3}, 1")
+        ins(f"mad.lo.u32 {ab3}, {buf3}, 8, {bars}")
+        ins(f"mad.lo.u32 {lab3}, {buf3}, 8, {lbars}")
+        use3 = t("b32")
+        ins(f"shr.u32 {use3}, {lt3}, 1")
+        kit.wait(f"{ab3}+{accf_off}", kit.parity(use3, 1), 2)
+        ins("tcgen05.fence::after_thread_sync")
+        taddr = t("b32")
+        ins(f"mad.lo.u32 {taddr}, {buf3}, {BN}, {tmem}")
+        ins(f"add.u32 {taddr}, {taddr}, {lane_off}")
+        esz = self.c.ty.nbytes
+        cw = 64 // esz
+        row0, col0 = t("b32"), t("b32")
+        ins(f"mul.lo.u32 {row0}, {ts3}, {self.M}")
+        ins(f"mad.lo.u32 {row0}, {tm3}, {PM}, {row0}")
+        ins(f"mad.lo.u32 {row0}, {rank}, {BM}, {row0}")
+        ins(f"mad.lo.u32 {row0}, {quarter}, 32, {row0}")
+        ins(f"mul.lo.u32 {col0}, {tn3}, {BN}")
+        for j, c0 in enumerate(range(0, BN, cw)):
+            sbuf = stage_buf[j % 2]
+            ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
+            ins("bar.warp.sync -1")
+            nv = 16 if esz == 4 else 32
+            v = [t("b32") for _ in range(nv)]
+            tc = t("b32")
+            ins(f"add.u32 {tc}, {taddr}, {c0}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x{nv}.b32 {{{', '.join(v)}}}, [{tc}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            if esz == 2:
+                h = [t("b32") for _ in range(16)]
+                for i in range(16):
+                    ins(f"cvt.rn.f16x2.f32 {h[i]}, {v[2 * i + 1]}, {v[2 * i]}")
+                v = h
+            if c0 + cw == BN:
+                # the accumulator is read out: one arrival per warp on the leader's barrier
+                ins("tcgen05.fence::before_thread_sync")
+                ins("bar.warp.sync -1")
+                ins(f"@{lane0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{lab3}+{acce_off}]")
+            for i in range(4):
+                a_ = t("b32")
+                ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
+                ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+            ins("fence.proxy.async.shared::cta")
+            ins("bar.warp.sync -1")
+            cc = t("b32")
+            ins(f"add.u32 {cc}, {col0}, {c0}")
+            ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], "
+                f"[{sbuf}]")
+            ins(f"@{lane0} cp.async.bulk.commit_group")
+        ins(f"add.u32 {lt3}, {lt3}, 1")
+        ins(f"add.u32 {eu}, {eu}, {npair}")
+        ins(f"setp.lt.u32 {p}, {eu}, {tiles}")
+        ins(f"@{p} bra {etop}")
+        place(edone)
+        ins(f"@{lane0} cp.async.bulk.wait_group 0")       # stores done before the CTA leaves
+
+        # ---------------- common exit: both CTAs, then free the pair's TMEM ----------------
+        place(end)
+        ins("tcgen05.fence::before_thread_sync")
+        ins("barrier.sync 0")
+        ins("barrier.cluster.arrive.release")
+        ins("barrier.cluster.wait.acquire")
+        nod = lab("mp_nodealloc")
+        ins(f"setp.ne.u32 {p}, {warp}, 1")
+        ins(f"@{p} bra {nod}")
+        ins("tcgen05.fence::after_thread_sync")
+        ins(f"tcgen05.dealloc.cta_group::2.sync.aligned.b32 {tmem}, {tmem_cols}")
+        place(nod)
+
+
+def recognise(kernel: KernelInfo):
+    return TcMatmulPair.match(kernel)
