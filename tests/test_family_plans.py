@@ -24,7 +24,8 @@ def _ir(d):
 
 @pytest.mark.parametrize("M,N,K,rem,parts", [(4096, 4096, 4096, 68, 2), (8192, 3072, 1024, 0, 1),
                                             (2048, 2560, 2048, 12, 2), (256, 256, 512, 0, 1)])
-def test_matmul_split_tail_plan(tmp_path, M, N, K, rem, parts):
+def test_matmul_split_tail_plan(tmp_path, monkeypatch, M, N, K, rem, parts):
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")
     fam = recognise(_kernel(_ir(synth.matmul_package(tmp_path / "mm", M, N, K))))
     assert isinstance(fam, TcMatmul)
     assert (fam.rem, fam.parts) == (rem, parts)
@@ -129,13 +130,14 @@ def test_attention_pair_needs_opt_in_and_shape(tmp_path, monkeypatch):
                                                       (256, 128, 256, "row", 0, 1, 8),
                                                       (512, 256, 256, "col", 128, 4, 8)])
 def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages):
-    """The CTA-pair matmul (opt-in): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
+    """The CTA-pair matmul (the default where it applies): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
     of B; one pair per two SMs; a cluster launch of an even grid; shared memory (with the
     generic path's static arrays) inside one SM's 227 KB."""
     from thompiler.families.matmul_pair import TcMatmulPair
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay)
-    assert not isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)          # off by default
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "1")
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")
+    assert not isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)
+    monkeypatch.delenv("THOMPILER_MATMUL_PAIR")                                # on by default
     if bn:
         monkeypatch.setenv("THOMPILER_MATMUL_BN", str(bn))
     fam = recognise(_kernel(_ir(d)))

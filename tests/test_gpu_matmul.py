@@ -83,12 +83,13 @@ def test_matmul_benchmark_shapes(tmp_path, M, N, K):
 
 
 @pytest.mark.parametrize("grid", [0, 5])
-def test_matmul_split_tail(tmp_path, grid):
+def test_matmul_split_tail(tmp_path, monkeypatch, grid):
     """More tiles than SMs with a partial last wave (2048 x 2560 x 2048: 160 tiles of 128 x 256,
     12 left over): those are cut along K into parts whose partials meet in the module's
     workspace, the last part to arrive adding them in part order.  grid 5 puts several whole
     tiles and several parts on each CTA (the arrival barriers' phases carry over)."""
     import torch
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")     # the split tail belongs to the single-CTA kernel
     M, N, K = 2048, 2560, 2048
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
     k = DeviceKernel(d / "k_matmul_f16.ir.json")

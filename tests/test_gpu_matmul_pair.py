@@ -26,7 +26,7 @@ FAMILY = "family: tcgen05-matmul-pair"
 
 @pytest.fixture(autouse=True)
 def _pair(monkeypatch):
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "1")
+    monkeypatch.delenv("THOMPILER_MATMUL_PAIR", raising=False)          # on by default
 
 
 @pytest.mark.parametrize("M,N,K,lay,out,bn", [(256, 256, 512, "col", "f32", 0), (256, 128, 256, "row", "f32", 0),

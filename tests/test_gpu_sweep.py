@@ -17,11 +17,16 @@ pytestmark = pytest.mark.gpu
     (1024, 1536, 512, "col", "f32"), (768, 640, 1024, "row", "f16"), (2048, 1536, 256, "col", "f16"),
     (4096, 384, 2048, "row", "f32"), (640, 320, 192, "col", "f32"), (8192, 256, 512, "col", "f32"),
     (3072, 4096, 1024, "col", "f32")])
-def test_matmul_shape_sweep(tmp_path, M, N, K, lay, out):
+@pytest.mark.parametrize("pair", ["0", "1"], ids=["single", "pair"])
+def test_matmul_shape_sweep(tmp_path, monkeypatch, M, N, K, lay, out, pair):
+    """Both matmul kernels: the single-CTA one (pair off) and, where M is a multiple of 256 and
+    N of 128, the CTA-pair one (the default there)."""
     import torch
+    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", pair)
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay, out_dtype=out)
     k = DeviceKernel(d / "k_matmul_f16.ir.json")
-    assert k.family == "tcgen05-matmul"
+    paired = pair == "1" and M % 256 == 0 and N % 128 == 0
+    assert k.family == ("tcgen05-matmul-pair" if paired else "tcgen05-matmul")
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
     b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half() if lay == "col" else \

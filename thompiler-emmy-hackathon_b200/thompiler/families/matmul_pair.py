@@ -45,7 +45,7 @@ class TcMatmulPair(TcMatmul):
 
     @classmethod
     def match(cls, kernel: KernelInfo):
-        if os.environ.get("THOMPILER_MATMUL_PAIR", "0") != "1":
+        if os.environ.get("THOMPILER_MATMUL_PAIR", "1") == "0":     # the single-CTA kernel instead
             return None
         one = TcMatmul.match.__func__(TcMatmul, kernel)
         if one is None or one.M % PM or kernel.grid[0] % 2:
