@@ -76,11 +76,14 @@ def test_package_writes_stay_in_bounds(name):
 @pytest.mark.parametrize("builder,args", [(synth.attention_package, (1, 2, 256, 128)),
                                           (synth.attention_package, (1, 3, 384, 64)),
                                           (synth.matmul_package, (384, 320, 512)),
+                                          (synth.matmul_package, (512, 384, 256)),
                                           (synth.pointwise_package, (1 << 20, "relu_mul")),
                                           (synth.sum_package, (1 << 20,))])
 def test_tuned_family_writes_stay_in_bounds(tmp_path, builder, args):
     """The tuned families at sizes whose last tile is partial or whose tile count is not a
-    multiple of the SM count, against the oracle interpreter (exact expression for attention)."""
+    multiple of the SM count, against the oracle interpreter (exact expression for attention).
+    The matmul cases take the single-CTA kernel (M = 384) and the CTA-pair one (M = 512,
+    N = 384: three 256 x 128 pair tiles per row band)."""
     pkg = problems.load_package(builder(tmp_path / "p", *args))
     inputs = problems.make_inputs(pkg)
     out = _run_guarded(pkg, inputs)
