@@ -183,10 +183,29 @@ RegStore = _stmt("RegStore", [(n, None) for n in (
     "dst_buffer", "dst_index", "frag", "shape", "ldm", "epilogue", "extra_frags", "m_guard", "n_guard",
     "atomic", "fragment_layout", "volta_interleaved", "fragment_index", "swizzle", "row_dim", "col_dim")])
 
+# The sm_90 vocabulary's Select (TASK.md:120-135 of the reference) and the RegStore epilogue
+# Lambda (TASK.md:159): plain records, interpreted by oracle/interp.py.
+Select = _stmt("Select", [("name", REQ), ("branches", ())])
+
+
+@dataclass
+class Branch:
+    value: Any = None
+    select: Any = None
+
+
+@dataclass
+class Lambda:
+    params: tuple = ()
+    body: tuple = ()
+    results: tuple = ()
+
+
 _CTORS = {c.__name__: c for c in (
     DataType, Dim, Window, Axis, ElementwiseImpl, Var, Literal, BinaryExpr, TernaryExpr, FlatIndex,
     Tile, Loop, StridedLoop, Cond, Load, Assign, Let, Accum, Init, Write, WarpShuffle, TreeHalve, Smem,
-    Sync, CpAsyncCopy, CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore)}
+    Sync, CpAsyncCopy, CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
+    Select, Branch, Lambda)}
 
 
 def _build(node):

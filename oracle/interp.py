@@ -566,7 +566,18 @@ class Interp:
             raise OracleError("f16 accumulator fragments")
 
     def s_RegStore(self, s, m):
+        """C registers 0, 1 at row g, columns 2q, 2q + 1 and 2, 3 at row g + 8 (g = lane / 4,
+        q = lane % 4), stored from the fragment's origin ``dst_index``.  The fused forms of the
+        IR reference (TASK.md:157-160): an ``epilogue`` Lambda applied per element, its leading
+        parameters bound to the element of ``frag`` and of each of ``extra_frags``, two more
+        (when declared) to the element's destination row and column, its one result stored in
+        the buffer's type; ``m_guard`` / ``n_guard`` exclusive bounds on that row and column;
+        ``atomic`` adds instead of storing."""
+        if (s.fragment_layout not in (None, "m16n8k16") or s.volta_interleaved
+                or s.swizzle not in (None, "NONE")):
+            raise OracleError("RegStore layout")
         f, mem = self._frag(s.frag)
+        extra = [self._frag(r) for r in (s.extra_frags or ())]
         dst = self.buf[s.dst_buffer]
         index = list(s.dst_index)
         rd = len(index) - 2 if s.row_dim is None else int(s.row_dim)
@@ -574,16 +585,54 @@ class Interp:
         lane = self.tid & 31
         g, q = lane // 4, lane % 4
         regs = f["regs"][mem]
-        for dr, (lo, hi) in ((0, (0, 1)), (8, (2, 3))):
-            idx = [self.ival(e) for e in index]
-            idx[rd] = idx[rd] + g + dr
-            idx[cd] = idx[cd] + 2 * q
-            flat = np.zeros(self.T, np.int64)
-            for size, i in zip(dst.shape, idx):
-                flat = flat * size + i
-            d = dst.reshape(-1)
-            d[flat[m]] = regs[m, lo].astype(dst.dtype)
-            d[flat[m] + 1] = regs[m, hi].astype(dst.dtype)
+        d = dst.reshape(-1)
+        for dr, pair in ((0, (0, 1)), (8, (2, 3))):
+            for j, reg in enumerate(pair):
+                idx = [self.ival(e) for e in index]
+                row, col = idx[rd] + g + dr, idx[cd] + 2 * q + j
+                idx[rd], idx[cd] = row, col
+                v = regs[:, reg]
+                if s.epilogue is not None:
+                    v = self._epilogue(s.epilogue, [v] + [ef["regs"][em][:, reg] for ef, em in extra], row, col, m)
+                ok = m.copy()
+                if s.m_guard is not None:
+                    ok &= row < self.ival(s.m_guard)
+                if s.n_guard is not None:
+                    ok &= col < self.ival(s.n_guard)
+                flat = np.zeros(self.T, np.int64)
+                for size, i in zip(dst.shape, idx):
+                    if np.any(ok & ((i < 0) | (i >= size))):
+                        raise OracleError(f"RegStore to {s.dst_buffer}: index out of range for extent {size}")
+                    flat = flat * size + i
+                if s.atomic:
+                    np.add.at(d, flat[ok], v[ok].astype(dst.dtype))
+                else:
+                    d[flat[ok]] = v[ok].astype(dst.dtype)
+
+    def _epilogue(self, lam, elems, row, col, m):
+        params = [p.name if isinstance(p, M.Var) else p for p in lam.params]
+        if len(params) not in (len(elems), len(elems) + 2):
+            raise OracleError(f"epilogue of {len(params)} parameters for {len(elems)} fragments")
+        for name, v in zip(params, elems):
+            self.set(name, v.astype(np.float32), m)
+        if len(params) == len(elems) + 2:
+            self.set(params[-2], row, m)
+            self.set(params[-1], col, m)
+        self.body(lam.body, m)
+        (res,) = lam.results
+        return self.get(res).copy()
+
+    def s_Select(self, s, m):
+        """``name`` = the value of the first branch whose predicate holds, else the last's."""
+        def value(v):
+            if isinstance(v, str):
+                return self.get(v)
+            return self.fval(v)
+        arms = [(value(b.value), None if b.select is None else self.pval(b.select)) for b in s.branches]
+        out = arms[-1][0]
+        for v, p in reversed(arms[:-1]):
+            out = v if p is None else np.where(p, v, out)
+        self.set(s.name, out, m)
 
 
 def _indexes_fragment(var, node):
@@ -635,6 +684,8 @@ def run_package(pdir: Path, inputs: dict | None = None) -> dict:
                     rng = np.random.default_rng(ini.get("seed", a.get("seed", 0)))
                     if ini["dist"] == "uniform":
                         v = rng.uniform(ini.get("low", 0.0), ini.get("high", 1.0), list(shape) or [1])
+                    elif ini["dist"] == "integers":        # low..high inclusive
+                        v = rng.integers(ini.get("low", -2), ini.get("high", 2) + 1, list(shape) or [1])
                     else:
                         v = rng.standard_normal(list(shape) or [1]) * ini.get("std", 1.0) + ini.get("mean", 0.0)
                     params[a["name"]] = v.astype(dt).reshape(shape)

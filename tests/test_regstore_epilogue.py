@@ -122,3 +122,31 @@ def test_refusals(tmp_path):
     _edit(d, "epilogue=None", "epilogue=Opaque(kind='x')")
     with pytest.raises(NotImplementedError):
         _ptx(d)
+
+
+@pytest.mark.parametrize("form", EPILOGUE_FORMS)
+def test_oracle_interprets_fused_forms(tmp_path, form):
+    """The oracle interpreter's restatement of the fused forms (epilogue Lambda with a bias load,
+    relu and a coordinate Select; edge guards; atomic K slices; an extra fragment) gives the
+    numpy expression of each kernel on the same inputs -- the same expectation the GPU tests
+    check the compiled kernels against.  Integer inputs make every form but the f16 one exact."""
+    import numpy as np
+    from oracle.interp import run_package as oracle_run
+    from thompiler import problems
+    d = epilogue_matmul_package(tmp_path / form, form, 128, 128, 256)
+    x = problems.make_inputs(problems.load_package(d))
+    got = oracle_run(d)["y"]
+    acc = x["x0"].astype(np.int64) @ x["x1"].astype(np.int64).T
+    if form == "bias_relu_mask":
+        t = np.float32(0.5) * acc.astype(np.float32) + x["bias"].astype(np.float32)
+        rows, cols = np.indices(t.shape)
+        want = np.where(cols <= rows, np.maximum(t, np.float32(0)), np.float32(0)).astype(np.float16)
+        assert got.dtype == np.float16
+        np.testing.assert_array_equal(got, want)
+    elif form == "guarded":
+        np.testing.assert_array_equal(got, acc[:-28, :-38].astype(np.float32))
+    elif form == "atomic":
+        np.testing.assert_array_equal(got, acc.astype(np.float32))
+    else:
+        dd = x["x0"].astype(np.int64) @ x["x2"].astype(np.int64).T
+        np.testing.assert_array_equal(got, (acc * dd).astype(np.float32))
