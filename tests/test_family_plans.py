@@ -125,11 +125,11 @@ def test_attention_pair_needs_opt_in_and_shape(tmp_path, monkeypatch):
         assert not isinstance(fam, TcAttentionPair)
 
 
-@pytest.mark.parametrize("M,N,K,lay,bn,tiles,stages", [(4096, 4096, 4096, "col", 0, 256, 6),
-                                                      (8192, 3072, 1024, "col", 0, 384, 6),
-                                                      (256, 128, 256, "row", 0, 1, 8),
-                                                      (512, 256, 256, "col", 128, 4, 8)])
-def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages):
+@pytest.mark.parametrize("M,N,K,lay,bn,tiles,stages,rem,parts", [
+    (4096, 4096, 4096, "col", 0, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 384, 6, 0, 1),
+    (2048, 2560, 2048, "col", 0, 80, 6, 6, 2), (256, 128, 256, "row", 0, 1, 8, 0, 1),
+    (512, 256, 256, "col", 128, 4, 8, 0, 1)])
+def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages, rem, parts):
     """The CTA-pair matmul (the default where it applies): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
     of B; one pair per two SMs; a cluster launch of an even grid; shared memory (with the
     generic path's static arrays) inside one SM's 227 KB."""
@@ -144,7 +144,9 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages
     assert isinstance(fam, TcMatmulPair)
     assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, bn or (256 if N % 256 == 0 else 128))
     assert fam.b_bytes == fam.BN // 2 * 64 * 2 and fam.a_bytes == 128 * 64 * 2
-    assert fam.ctas == 2 * min(tiles, 74)
+    assert (fam.rem, fam.parts) == (rem, parts)                  # the last wave cut along K
+    assert fam.units == tiles - rem + rem * parts
+    assert fam.ctas == 2 * min(fam.units, 74)
     side = fam.sidecar()
     assert side["cluster"] == [2, 1, 1] and side["grid"] == [fam.ctas, 1, 1]
     assert fam.smem + fam.static_smem <= 227 * 1024

@@ -91,3 +91,25 @@ def test_pair_large(tmp_path, M, N, K, grid):
     assert torch.allclose(c1.double().sum(1), ones_ref, rtol=1e-4, atol=1e-3)
     tuned.close()
     generic.close()
+
+
+@pytest.mark.parametrize("grid", [0, 10])
+def test_pair_split_tail(tmp_path, grid):
+    """More pair tiles than pairs with a partial last wave (2048 x 2560 x 2048: 80 tiles of
+    256 x 256 on 74 pairs, 6 left over): those are cut along K into two parts whose partials
+    meet in the module's workspace per tile and CTA rank, the last part to arrive adding them in
+    part order.  grid 10 (5 pairs) puts several whole tiles and several parts on each pair."""
+    import torch
+    M, N, K = 2048, 2560, 2048
+    d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
+    k = DeviceKernel(d / "k_matmul_f16.ir.json")
+    assert k.family == "tcgen05-matmul-pair" and "thc_tail_ws" in k.ptx
+    if grid:
+        k.plan.grid = (grid, 1, 1)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    c = _run_twice(k, a, b, M, N, torch.cuda.current_stream().cuda_stream)   # the part order fixes the rounding
+    ref = a.double() @ b.double().t()
+    assert (c.double() - ref).abs().max().item() < 1e-4
+    k.close()

@@ -154,12 +154,16 @@ def test_regstore_fused_forms(tmp_path, form):
     guards into a buffer smaller than the tile grid (a store past them would land outside it);
     four K slices added atomically into a zeroed buffer; an extra accumulator multiplied in.
     The integer forms are exact; the f16 one is within one f16 rounding of the float32 numpy
-    expression."""
-    pkg = problems.load_package(epilogue_matmul_package(tmp_path / form, form))
+    expression.  The oracle interpreter's restatement of the forms agrees to the same bar."""
+    from oracle.interp import run_package as oracle_run
+    d = epilogue_matmul_package(tmp_path / form, form)
+    pkg = problems.load_package(d)
     res = problems.run_package(pkg, problems.compile_package(pkg))
     x = problems.make_inputs(pkg)
     acc = x["x0"].astype(np.int64) @ x["x1"].astype(np.int64).T
     got = res["outputs"]["y"]
+    np.testing.assert_allclose(got.astype(np.float64).reshape(-1), oracle_run(d)["y"].astype(np.float64).reshape(-1),
+                               rtol=1e-3, atol=1e-3)
     if form == "bias_relu_mask":
         t = np.float32(0.5) * acc.astype(np.float32) + x["bias"].astype(np.float32)
         rows, cols = np.indices(t.shape)

@@ -71,6 +71,7 @@ def idesc_f16(n: int, b_mn_major: bool) -> int:
 
 class TcMatmul(TunedKernel):
     family = "tcgen05-matmul"
+    tail_ranks = 1               # CTAs sharing one output tile (2 for the CTA-pair kernel)
 
     def __init__(self, kernel: KernelInfo, a, b, c, M, N, K, S, b_kmajor, static_smem):
         super().__init__(kernel)
@@ -225,9 +226,10 @@ class TcMatmul(TunedKernel):
         em.module(".global .align 64 .b8 thc_tmap_c[128]")
         em.module(".global .align 8 .u64 thc_tmap_ptr[3]")
         em.module(".global .align 4 .u32 thc_error")
-        if self.rem:
-            em.module(f".global .align 4 .u32 thc_tile_arrivals[{self.rem}]")
-            em.module(f".global .align 16 .b8 thc_tail_ws[{self.rem * self.parts * BM * self.BN * 4}]")
+        if self.rem:                 # one counter and one partial per (tail tile, CTA of the tile's pair)
+            ranks = self.tail_ranks
+            em.module(f".global .align 4 .u32 thc_tile_arrivals[{self.rem * ranks}]")
+            em.module(f".global .align 16 .b8 thc_tail_ws[{self.rem * ranks * self.parts * BM * self.BN * 4}]")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         p = em.tmp("pred")
         r = self.special("%ntid.x")

@@ -34,6 +34,7 @@ from thompiler.families.kit import Kit, desc_hi, idesc_f16
 from thompiler.families.matmul import BK, BM, EPI_WARPS, SM_COUNT, STAGE_TILE, TcMatmul
 from thompiler.families.base import TunedKernel
 from thompiler.load import KernelInfo
+from thompiler.lowering.types import F32
 
 PM = 2 * BM                  # rows of a pair tile
 PAIR_SLOTS = SM_COUNT // 2   # pairs resident at once
@@ -42,6 +43,7 @@ SMEM_LIMIT = 227 * 1024
 
 class TcMatmulPair(TcMatmul):
     family = "tcgen05-matmul-pair"
+    tail_ranks = 2
 
     @classmethod
     def match(cls, kernel: KernelInfo):
@@ -85,9 +87,18 @@ class TcMatmulPair(TcMatmul):
             self.stages = forced
         self.smem = self.stages * stage + self.staging + 1024 + 256
         self.tiles = (M // PM) * (N // bn) * S
-        self.pairs = min(self.tiles, PAIR_SLOTS)
+        # the last, partial wave of pair tiles: its `rem` tiles are cut along K into `parts` units,
+        # as in the single-CTA kernel (each CTA of a pair keeps its own partial and counter)
+        kblocks = self.Ks // BK
+        rem = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
+        parts = min(kblocks // 16, PAIR_SLOTS // rem) if rem else 1
+        if S != 1 or c.ty is not F32 or parts < 2 or os.environ.get("THOMPILER_MATMUL_SPLIT_TAIL") == "0":
+            rem, parts = 0, 1
+        self.rem, self.parts = rem, parts
+        self.full_tiles = self.tiles - rem
+        self.units = self.full_tiles + rem * parts
+        self.pairs = min(self.units, PAIR_SLOTS)
         self.ctas = 2 * self.pairs
-        self.rem, self.parts, self.full_tiles, self.units = 0, 1, self.tiles, self.tiles
 
     def sidecar(self) -> dict:
         side = super().sidecar()
@@ -114,7 +125,6 @@ class TcMatmulPair(TcMatmul):
         a_bytes, b_bytes = self.a_bytes, self.b_bytes
         tiles_m, tiles_n = self.M // PM, self.N // BN
         kblocks = self.Ks // BK
-        tiles = self.tiles
         mcommit = "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
         tma_ld = "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
 
@@ -132,6 +142,7 @@ class TcMatmulPair(TcMatmul):
         ins(f"add.u32 {b_st}, {base}, {ST * a_bytes}")
         ins(f"add.u32 {bars}, {base}, {ST * (a_bytes + b_bytes) + self.staging}")
         empty_off, accf_off, acce_off, slot_off = 8 * ST, 16 * ST, 16 * ST + 16, 16 * ST + 32
+        tail_done_off, tail_last_off, tail_flag_off = 16 * ST + 40, 16 * ST + 48, 16 * ST + 56
         p = t("pred")
         skip = lab("mp_noinit")
         ins(f"setp.ne.u32 {p}, {tid}, 0")
@@ -142,6 +153,9 @@ class TcMatmulPair(TcMatmul):
         for b in range(2):
             ins(f"mbarrier.init.shared::cta.b64 [{bars}+{accf_off + 8 * b}], 1")
             ins(f"mbarrier.init.shared::cta.b64 [{bars}+{acce_off + 8 * b}], {2 * EPI_WARPS}")
+        if self.rem:
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{tail_done_off}], {32 * EPI_WARPS}")
+            ins(f"mbarrier.init.shared::cta.b64 [{bars}+{tail_last_off}], 1")
         ins("fence.mbarrier_init.release.cluster")
         ins("fence.proxy.async.shared::cta")
         place(skip)
@@ -188,6 +202,28 @@ class TcMatmulPair(TcMatmul):
             ins(f"div.u32 {ts_}, {r}, {tiles_n}")
             return tm_, tn_, ts_
 
+        units, full_tiles, parts = self.units, self.full_tiles, self.parts
+
+        def unit(u: str):
+            """Work unit u -> (pair tile, first and end K block, is-whole-tile predicate, part):
+            units below full_tiles are whole tiles, the rest cut the last tiles along K."""
+            tile_, lo, hi_, part, v, whole = t("b32"), t("b32"), t("b32"), t("b32"), t("b32"), t("pred")
+            ins(f"setp.lt.u32 {whole}, {u}, {full_tiles}")
+            ins(f"mov.u32 {tile_}, {u}")
+            ins(f"mov.u32 {lo}, 0")
+            ins(f"mov.u32 {hi_}, {kblocks}")
+            ins(f"mov.u32 {part}, 0")
+            if self.rem:
+                ins(f"sub.u32 {v}, {u}, {full_tiles}")
+                ins(f"@!{whole} div.u32 {tile_}, {v}, {parts}")
+                ins(f"@!{whole} add.u32 {tile_}, {tile_}, {full_tiles}")
+                ins(f"@!{whole} rem.u32 {part}, {v}, {parts}")
+                ins(f"@!{whole} mul.lo.u32 {lo}, {part}, {kblocks}")
+                ins(f"@!{whole} div.u32 {lo}, {lo}, {parts}")
+                ins(f"@!{whole} mad.lo.u32 {hi_}, {part}, {kblocks}, {kblocks}")
+                ins(f"@!{whole} div.u32 {hi_}, {hi_}, {parts}")
+            return tile_, lo, hi_, whole, part
+
         role_mma, role_epi = lab("mp_mma"), lab("mp_epi")
         ins(f"setp.eq.u32 {p}, {warp}, 1")
         ins(f"@{p} bra {role_mma}")
@@ -202,17 +238,17 @@ class TcMatmulPair(TcMatmul):
         ins(f"mov.u32 {it}, 0")
         ins(f"mov.u32 {pu}, {pid}")
         ptop = lab("mp_prod_tile")
-        ins(f"setp.ge.u32 {p}, {pu}, {tiles}")
+        ins(f"setp.ge.u32 {p}, {pu}, {units}")
         ins(f"@{p} bra {end}")
         place(ptop)
-        tm_, tn_, ts_ = decode(pu)
-        m0, n0, k0, kb = t("b32"), t("b32"), t("b32"), t("b32")
+        ptile, kb, kend, _, _ = unit(pu)
+        tm_, tn_, ts_ = decode(ptile)
+        m0, n0, k0 = t("b32"), t("b32"), t("b32")
         ins(f"mul.lo.u32 {m0}, {tm_}, {PM}")
         ins(f"mad.lo.u32 {m0}, {rank}, {BM}, {m0}")
         ins(f"mul.lo.u32 {n0}, {tn_}, {BN}")
         ins(f"mad.lo.u32 {n0}, {rank}, {HN}, {n0}")
         ins(f"mul.lo.u32 {k0}, {ts_}, {self.Ks}")
-        ins(f"mov.u32 {kb}, 0")
         ktop = lab("mp_prod_k")
         place(ktop)
         stage, eb, fb = t("b32"), t("b32"), t("b32")
@@ -235,10 +271,10 @@ class TcMatmulPair(TcMatmul):
                 ins(f"@{is0} {tma_ld} [{sb}+{nb * 64 * BK * 2}], [{tmb}, {{{nn}, {kc}}}], [{fb}]")
         ins(f"add.u32 {it}, {it}, 1")
         ins(f"add.u32 {kb}, {kb}, 1")
-        ins(f"setp.lt.u32 {p}, {kb}, {kblocks}")
+        ins(f"setp.lt.u32 {p}, {kb}, {kend}")
         ins(f"@{p} bra {ktop}")
         ins(f"add.u32 {pu}, {pu}, {npair}")
-        ins(f"setp.lt.u32 {p}, {pu}, {tiles}")
+        ins(f"setp.lt.u32 {p}, {pu}, {units}")
         ins(f"@{p} bra {ptop}")
         # every load of this CTA is consumed by an MMA whose completion the epilogues wait for
         # before the common exit's cluster barrier, so none is in flight when the CTAs leave
@@ -262,9 +298,12 @@ class TcMatmulPair(TcMatmul):
         ins(f"mov.u32 {lt}, 0")
         ins(f"mov.u32 {mu}, {pid}")
         mtop = lab("mp_mma_tile")
-        ins(f"setp.ge.u32 {p}, {mu}, {tiles}")
+        ins(f"setp.ge.u32 {p}, {mu}, {units}")
         ins(f"@{p} bra {end}")
         place(mtop)
+        _, kb2, kend2, _, _ = unit(mu)
+        kfirst = t("b32")
+        ins(f"mov.u32 {kfirst}, {kb2}")
         buf, ab = t("b32"), t("b32")
         ins(f"and.b32 {buf}, {lt}, 1")
         ins(f"mad.lo.u32 {ab}, {buf}, 8, {bars}")
@@ -274,8 +313,6 @@ class TcMatmulPair(TcMatmul):
         ins("tcgen05.fence::after_thread_sync")
         dt = t("b32")
         ins(f"mad.lo.u32 {dt}, {buf}, {BN}, {tmem}")
-        kb2 = t("b32")
-        ins(f"mov.u32 {kb2}, 0")
         mk = lab("mp_mma_k")
         place(mk)
         st2, fb2 = t("b32"), t("b32")
@@ -289,7 +326,7 @@ class TcMatmulPair(TcMatmul):
         ad0 = kit.desc(sa2, 16, hi)
         bd0 = kit.desc(sb2, 16 if self.b_kmajor else 64 * BK * 2, hi)
         first = t("pred")
-        ins(f"setp.ne.u32 {first}, {kb2}, 0")        # the tile's first MMA overwrites the accumulator
+        ins(f"setp.ne.u32 {first}, {kb2}, {kfirst}")  # the unit's first MMA overwrites the accumulator
         for k in range(BK // 16):
             ad = kit.desc_add(ad0, k * 32)
             bd = kit.desc_add(bd0, k * 32 if self.b_kmajor else k * 16 * 128)
@@ -298,19 +335,20 @@ class TcMatmulPair(TcMatmul):
         ins(f"@{ism} {mcommit} [{fb2}+{empty_off}], {mask}")
         ins(f"add.u32 {it2}, {it2}, 1")
         ins(f"add.u32 {kb2}, {kb2}, 1")
-        ins(f"setp.lt.u32 {p}, {kb2}, {kblocks}")
+        ins(f"setp.lt.u32 {p}, {kb2}, {kend2}")
         ins(f"@{p} bra {mk}")
         ins(f"@{ism} {mcommit} [{ab}+{accf_off}], {mask}")
         ins(f"add.u32 {lt}, {lt}, 1")
         ins(f"add.u32 {mu}, {mu}, {npair}")
-        ins(f"setp.lt.u32 {p}, {mu}, {tiles}")
+        ins(f"setp.lt.u32 {p}, {mu}, {units}")
         ins(f"@{p} bra {mtop}")
         ins(f"bra {end}")
 
         # ---------------- epilogue (warps 2..5 of each CTA: its 128 rows) ----------------
         place(role_epi)
-        quarter = t("b32")
+        quarter, row = t("b32"), t("b32")
         ins(f"and.b32 {quarter}, {warp}, 3")
+        ins(f"mad.lo.u32 {row}, {quarter}, 32, {lane}")   # this thread's row of the CTA's 128
         lane_off = t("b32")
         ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
         lane0 = t("pred")
@@ -331,14 +369,16 @@ class TcMatmulPair(TcMatmul):
             ins(f"shl.b32 {o}, {o}, 4")
             ins(f"mad.lo.u32 {o}, {lane}, 64, {o}")
             soff.append(o)
-        eu, lt3 = t("b32"), t("b32")
+        eu, lt3, ls = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {lt3}, 0")
+        ins(f"mov.u32 {ls}, 0")
         ins(f"mov.u32 {eu}, {pid}")
-        etop, edone = lab("mp_epi_tile"), lab("mp_epi_done")
-        ins(f"setp.ge.u32 {p}, {eu}, {tiles}")
+        etop, edone, enext = lab("mp_epi_tile"), lab("mp_epi_done"), lab("mp_epi_next")
+        ins(f"setp.ge.u32 {p}, {eu}, {units}")
         ins(f"@{p} bra {edone}")
         place(etop)
-        tm3, tn3, ts3 = decode(eu)
+        tile3, _, _, whole3, part3 = unit(eu)
+        tm3, tn3, ts3 = decode(tile3)
         buf3, ab3, lab3 = t("b32"), t("b32"), t("b32")
         ins(f"and.b32 {buf3}, {lt3}, 1")
         ins(f"mad.lo.u32 {ab3}, {buf3}, 8, {bars}")
@@ -358,10 +398,37 @@ class TcMatmulPair(TcMatmul):
         ins(f"mad.lo.u32 {row0}, {rank}, {BM}, {row0}")
         ins(f"mad.lo.u32 {row0}, {quarter}, 32, {row0}")
         ins(f"mul.lo.u32 {col0}, {tn3}, {BN}")
-        for j, c0 in enumerate(range(0, BN, cw)):
-            sbuf = stage_buf[j % 2]
-            ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
+
+        def free_accumulator() -> None:
+            """This warp has read the accumulator out: one arrival on the leader's barrier."""
+            ins("tcgen05.fence::before_thread_sync")
             ins("bar.warp.sync -1")
+            ins(f"@{lane0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{lab3}+{acce_off}]")
+
+        def store_boxes(values, free_after_last: bool) -> None:
+            """Columns c0 .. c0 + cw of this warp's 32 rows, for each c0: ``values(c0)`` gives the
+            row's cw values as b32 registers (f32, or f16 pairs), staged (64-byte swizzle) and
+            stored with TMA."""
+            for j, c0 in enumerate(range(0, BN, cw)):
+                sbuf = stage_buf[j % 2]
+                ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
+                ins("bar.warp.sync -1")
+                v = values(c0)
+                if free_after_last and c0 + cw == BN:
+                    free_accumulator()
+                for i in range(4):
+                    a_ = t("b32")
+                    ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
+                    ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+                ins("fence.proxy.async.shared::cta")
+                ins("bar.warp.sync -1")
+                cc = t("b32")
+                ins(f"add.u32 {cc}, {col0}, {c0}")
+                ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], "
+                    f"[{sbuf}]")
+                ins(f"@{lane0} cp.async.bulk.commit_group")
+
+        def from_tmem(c0):
             nv = 16 if esz == 4 else 32
             v = [t("b32") for _ in range(nv)]
             tc = t("b32")
@@ -373,25 +440,20 @@ class TcMatmulPair(TcMatmul):
                 for i in range(16):
                     ins(f"cvt.rn.f16x2.f32 {h[i]}, {v[2 * i + 1]}, {v[2 * i]}")
                 v = h
-            if c0 + cw == BN:
-                # the accumulator is read out: one arrival per warp on the leader's barrier
-                ins("tcgen05.fence::before_thread_sync")
-                ins("bar.warp.sync -1")
-                ins(f"@{lane0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{lab3}+{acce_off}]")
-            for i in range(4):
-                a_ = t("b32")
-                ins(f"add.u32 {a_}, {sbuf}, {soff[i]}")
-                ins(f"st.shared.v4.b32 [{a_}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
-            ins("fence.proxy.async.shared::cta")
-            ins("bar.warp.sync -1")
-            cc = t("b32")
-            ins(f"add.u32 {cc}, {col0}, {c0}")
-            ins(f"@{lane0} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmc}, {{{cc}, {row0}}}], "
-                f"[{sbuf}]")
-            ins(f"@{lane0} cp.async.bulk.commit_group")
+            return v
+
+        tail = lab("mp_epi_tail")
+        if self.rem:
+            ins(f"@!{whole3} bra {tail}")
+        store_boxes(from_tmem, True)
+        if self.rem:
+            ins(f"bra {enext}")
+            self._pair_tail(tail, enext, tile3, part3, rank, taddr, row, bars, ls, store_boxes, free_accumulator,
+                            tail_done_off, tail_last_off, tail_flag_off, kit, p)
+        place(enext)
         ins(f"add.u32 {lt3}, {lt3}, 1")
         ins(f"add.u32 {eu}, {eu}, {npair}")
-        ins(f"setp.lt.u32 {p}, {eu}, {tiles}")
+        ins(f"setp.lt.u32 {p}, {eu}, {units}")
         ins(f"@{p} bra {etop}")
         place(edone)
         ins(f"@{lane0} cp.async.bulk.wait_group 0")       # stores done before the CTA leaves
@@ -409,6 +471,84 @@ class TcMatmulPair(TcMatmul):
         ins(f"tcgen05.dealloc.cta_group::2.sync.aligned.b32 {tmem}, {tmem_cols}")
         place(nod)
 
+
+    def _pair_tail(self, tail, enext, tile3, part3, rank, taddr, row, bars, ls, store_boxes, free_accumulator,
+                   done_off, last_off, flag_off, kit, p) -> None:
+        """A K part of one of the last pair tiles, for this CTA's 128 rows: its partial goes to the
+        module workspace, and the part that arrives last (per tile and CTA rank) adds all parts in
+        part order -- deterministic -- and stores C.
+
+        Workspace slot (tail tile, rank, part): [BN / 4 chunks][128 rows] of 16-byte chunks, so a
+        warp's store or load of one chunk index touches 512 contiguous bytes.  Arrival: every
+        epilogue thread fences its stores and arrives on a CTA mbarrier; thread 0 then bumps the
+        (tile, rank) counter (``atom.acq_rel.gpu.inc`` wrapping at parts - 1: self-resetting) and
+        publishes through shared memory whether it was the last.  No CTA waits for another."""
+        em, ins, t, place = self.em, self.em.ins, self.em.tmp, self.em.place
+        BN, parts = self.BN, self.parts
+        slot_bytes = BN // 4 * 128 * 16
+        place(tail)
+        slot, ws, cnt = t("b32"), t("b64"), t("b64")
+        ins(f"sub.u32 {slot}, {tile3}, {self.full_tiles}")
+        ins(f"mad.lo.u32 {slot}, {slot}, 2, {rank}")           # (tail tile, rank)
+        ins(f"mov.u64 {cnt}, thc_tile_arrivals")
+        ins(f"mad.wide.u32 {cnt}, {slot}, 4, {cnt}")
+        ins(f"mul.lo.u32 {slot}, {slot}, {parts}")             # its part 0
+        ins("mov.u64 " + ws + ", thc_tail_ws")
+        rowb = t("b64")                                        # this row's first chunk, 16 bytes apart per row
+        ins(f"mul.wide.u32 {rowb}, {row}, 16")
+        ins(f"add.u64 {rowb}, {rowb}, {ws}")
+        first, mine = t("b64"), t("b64")
+        ins(f"mul.wide.u32 {first}, {slot}, {slot_bytes}")
+        ins(f"add.u64 {first}, {first}, {rowb}")
+        ins(f"mul.wide.u32 {mine}, {part3}, {slot_bytes}")
+        ins(f"add.u64 {mine}, {mine}, {first}")
+        for c0 in range(0, BN, 16):
+            v = [t("b32") for _ in range(16)]
+            tc = t("b32")
+            ins(f"add.u32 {tc}, {taddr}, {c0}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x16.b32 {{{', '.join(v)}}}, [{tc}]")
+            ins("tcgen05.wait::ld.sync.aligned")
+            for i in range(4):
+                ins(f"st.global.v4.b32 [{mine}+{(c0 // 4 + i) * 128 * 16}], {{{', '.join(v[4 * i:4 * i + 4])}}}")
+        free_accumulator()
+        ins("fence.acq_rel.gpu")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{done_off}]")
+        par, lead, flag = t("b32"), t("pred"), t("b32")
+        ins(f"and.b32 {par}, {ls}, 1")
+        ins(f"add.u32 {ls}, {ls}, 1")
+        ins(f"setp.eq.u32 {lead}, {row}, 0")
+        notlead = em.label("mp_tail_notlead")
+        ins(f"@!{lead} bra {notlead}")
+        kit.wait(f"{bars}+{done_off}", par, 3)                 # all 128 rows of the partial are stored
+        old = t("b32")
+        ins(f"atom.acq_rel.gpu.global.inc.u32 {old}, [{cnt}], {parts - 1}")
+        ins(f"setp.eq.u32 {p}, {old}, {parts - 1}")
+        ins(f"selp.u32 {flag}, 1, 0, {p}")
+        ins(f"st.shared.u32 [{bars}+{flag_off}], {flag}")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{bars}+{last_off}]")
+        place(notlead)
+        kit.wait(f"{bars}+{last_off}", par, 3)
+        ins(f"ld.shared.u32 {flag}, [{bars}+{flag_off}]")
+        ins(f"setp.eq.u32 {p}, {flag}, 0")
+        ins(f"@{p} bra {enext}")
+        ins("fence.acq_rel.gpu")
+
+        def summed(c0):
+            acc = [t("f32") for _ in range(16)]
+            for pp in range(parts):
+                for i in range(4):
+                    off = pp * slot_bytes + (c0 // 4 + i) * 128 * 16
+                    v = acc[4 * i:4 * i + 4] if pp == 0 else [t("f32") for _ in range(4)]
+                    ins(f"ld.global.cg.v4.f32 {{{', '.join(v)}}}, [{first}+{off}]")
+                    if pp:
+                        for a_, b_ in zip(acc[4 * i:4 * i + 4], v):
+                            ins(f"add.rn.f32 {a_}, {a_}, {b_}")
+            out = [t("b32") for _ in range(16)]
+            for o_, a_ in zip(out, acc):
+                ins(f"mov.b32 {o_}, {a_}")
+            return out
+
+        store_boxes(summed, False)
 
 def recognise(kernel: KernelInfo):
     return TcMatmulPair.match(kernel)
