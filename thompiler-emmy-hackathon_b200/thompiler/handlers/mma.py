@@ -31,7 +31,6 @@ thompiler/handlers/mma.py:129-199, since both follow from the ISA):
 from __future__ import annotations
 
 import ast
-import dataclasses
 import re
 from dataclasses import dataclass
 from typing import TYPE_CHECKING
@@ -125,8 +124,8 @@ def indexes_fragment(var: str, node: object) -> bool:
         return bool(m and m["index"] and re.search(rf"\b{re.escape(var)}\b", m["index"]))
     if isinstance(node, tuple):
         return any(indexes_fragment(var, x) for x in node)
-    if dataclasses.is_dataclass(node) and not isinstance(node, type):
-        return any(indexes_fragment(var, getattr(node, f.name)) for f in dataclasses.fields(node))
+    if ir.is_record(node):
+        return any(indexes_fragment(var, getattr(node, f)) for f in node._fields)
     return False
 
 

@@ -4,7 +4,7 @@ A Kernel IR file stores each KernelOp body as the Python ``repr`` of emmy's
 statement dataclasses, e.g. ``Tile(axes=(Axis(name='a0', extent=Dim(64),
 window=None),), body=(...), block_threads=128, ...)``.  emmy-ml is not a
 dependency of this compiler, so this module gives every constructor of that
-vocabulary a frozen dataclass of its own and rebuilds the tree from the
+vocabulary a frozen record class of its own and rebuilds the tree from the
 string with ``ast`` -- never ``eval``: only whitelisted constructor names,
 literals, tuples and lists are accepted.
 
@@ -21,15 +21,111 @@ from __future__ import annotations
 
 import ast
 import dataclasses
-from dataclasses import dataclass, field
+from dataclasses import field
 from typing import Any
+
+
+# ---------------------------------------------------------------------------
+# frozen records
+#
+# The IR's node classes are frozen records with the behaviour of frozen dataclasses (keyword or
+# positional construction with defaults, field-wise equality and hash, the dataclass repr), but
+# their methods are shared functions installed on each class rather than source generated and
+# compiled per class: a frozen dataclass costs about a millisecond to create, and this module
+# defines some sixty, which every ``compile.py`` process would pay on start-up.
+
+
+def _rec_init(self, *args, **kwargs) -> None:
+    cls = type(self)
+    names = cls._fields
+    if len(args) > len(names):
+        raise TypeError(f"{cls.__name__}.__init__() takes {len(names)} positional arguments but "
+                        f"{len(args)} were given")
+    d = self.__dict__
+    for k, v in zip(names, args):
+        d[k] = v
+    for k, v in kwargs.items():
+        if k not in cls._defaults and k not in names:
+            raise TypeError(f"{cls.__name__}.__init__() got an unexpected keyword argument '{k}'")
+        if k in d:
+            raise TypeError(f"{cls.__name__}.__init__() got multiple values for argument '{k}'")
+        d[k] = v
+    if len(d) < len(names):
+        for k in names:
+            if k not in d:
+                if k not in cls._defaults:
+                    raise TypeError(f"{cls.__name__}.__init__() missing 1 required positional argument: '{k}'")
+                d[k] = cls._defaults[k]
+
+
+def _rec_values(self) -> tuple:
+    return tuple(getattr(self, k) for k in self._fields)
+
+
+def _rec_eq(self, other) -> bool:
+    if other.__class__ is not self.__class__:
+        return NotImplemented
+    return _rec_values(self) == _rec_values(other)
+
+
+def _rec_hash(self) -> int:
+    return hash(_rec_values(self))
+
+
+def _rec_repr(self) -> str:
+    return f"{type(self).__qualname__}(" + ", ".join(f"{k}={getattr(self, k)!r}" for k in self._fields) + ")"
+
+
+def _rec_setattr(self, name, value) -> None:
+    raise dataclasses.FrozenInstanceError(f"cannot assign to field '{name}'")
+
+
+def _rec_delattr(self, name) -> None:
+    raise dataclasses.FrozenInstanceError(f"cannot delete field '{name}'")
+
+
+def record(cls):
+    """Make ``cls`` a frozen record: its fields are its annotations after its bases' fields, their
+    defaults the class attributes of those names (a ``dataclasses.field(default=...)`` too)."""
+    names: list[str] = []
+    defaults: dict[str, Any] = {}
+    for base in reversed(cls.__mro__[1:]):
+        for k in getattr(base, "_fields", ()):
+            if k not in names:
+                names.append(k)
+        defaults.update(getattr(base, "_defaults", {}))
+    for k in cls.__dict__.get("__annotations__", {}):
+        if k not in names:
+            names.append(k)
+        if k in cls.__dict__:
+            v = cls.__dict__[k]
+            defaults[k] = v.default if isinstance(v, dataclasses.Field) else v
+            delattr(cls, k)
+    cls._fields, cls._defaults = tuple(names), defaults
+    cls.__init__, cls.__eq__, cls.__hash__ = _rec_init, _rec_eq, _rec_hash
+    cls.__setattr__, cls.__delattr__ = _rec_setattr, _rec_delattr
+    if "__repr__" not in cls.__dict__:
+        cls.__repr__ = _rec_repr
+    return cls
+
+
+def is_record(o) -> bool:
+    """An IR node (an instance of a record class)?"""
+    return hasattr(o, "_fields") and not isinstance(o, type)
+
+
+def field_names(o) -> tuple:
+    """The field names of a record (or of a dataclass instance)."""
+    if is_record(o):
+        return o._fields
+    return tuple(f.name for f in dataclasses.fields(o))
 
 
 # ---------------------------------------------------------------------------
 # leaf values
 
 
-@dataclass(frozen=True)
+@record
 class DataType:
     """An element type: ``name`` is the IR dtype ("f32", "f16", "f64", ...)."""
     name: str
@@ -37,7 +133,7 @@ class DataType:
     nbytes: int = 0
 
 
-@dataclass(frozen=True)
+@record
 class Dim:
     value: Any
 
@@ -51,7 +147,7 @@ class Dim:
         return int(self.value)
 
 
-@dataclass(frozen=True)
+@record
 class Window:
     parent: Any = None
     base: Any = None
@@ -59,7 +155,7 @@ class Window:
     partition: bool = False
 
 
-@dataclass(frozen=True)
+@record
 class Axis:
     name: str
     extent: Dim
@@ -85,7 +181,7 @@ ELEMENTWISE: dict[str, tuple[int, float | None]] = {
 }
 
 
-@dataclass(frozen=True)
+@record
 class ElementwiseImpl:
     name: str
 
@@ -109,7 +205,7 @@ class Expr:
         return repr(self)
 
 
-@dataclass(frozen=True)
+@record
 class Var(Expr):
     name: str
 
@@ -117,7 +213,7 @@ class Var(Expr):
         return self.name
 
 
-@dataclass(frozen=True)
+@record
 class Literal(Expr):
     value: Any
     dtype: str = "int"
@@ -126,7 +222,7 @@ class Literal(Expr):
         return repr(self.value)
 
 
-@dataclass(frozen=True)
+@record
 class BinaryExpr(Expr):
     op: str
     left: Any
@@ -136,7 +232,7 @@ class BinaryExpr(Expr):
         return f"({pretty(self.left)} {self.op} {pretty(self.right)})"
 
 
-@dataclass(frozen=True)
+@record
 class TernaryExpr(Expr):
     cond: Any
     if_true: Any
@@ -146,24 +242,24 @@ class TernaryExpr(Expr):
         return f"({pretty(self.cond)} ? {pretty(self.if_true)} : {pretty(self.if_false)})"
 
 
-@dataclass(frozen=True)
+@record
 class Builtin(Expr):
     name: str
 
 
-@dataclass(frozen=True)
+@record
 class FuncCallExpr(Expr):
     name: str
     args: tuple = ()
 
 
-@dataclass(frozen=True)
+@record
 class CastExpr(Expr):
     dtype: Any
     expr: Any
 
 
-@dataclass(frozen=True)
+@record
 class FlatIndex(Expr):
     buffer: str
     index: tuple = ()
@@ -186,7 +282,7 @@ class Stmt:
     """Base of every statement; ``pretty`` is a one-line summary for comments."""
 
     def pretty(self) -> str:
-        names = [f.name for f in dataclasses.fields(self)][:3]  # type: ignore[arg-type]
+        names = list(field_names(self))[:3]
         return f"{type(self).__name__}(" + ", ".join(
             f"{n}={_short(getattr(self, n))}" for n in names) + ")"
 
@@ -196,7 +292,7 @@ def _short(v: Any) -> str:
     return text if len(text) < 60 else text[:57] + "..."
 
 
-@dataclass(frozen=True)
+@record
 class Tile(Stmt):
     axes: tuple
     body: tuple
@@ -221,7 +317,7 @@ class Tile(Stmt):
         return f"Tile[{', '.join(a.name for a in self.axes)}] (N={self.n_elements})"
 
 
-@dataclass(frozen=True)
+@record
 class Loop(Stmt):
     axis: Axis
     body: tuple
@@ -233,7 +329,7 @@ class Loop(Stmt):
         return f"for {self.axis.name} in 0..{pretty(self.axis.extent.value)}"
 
 
-@dataclass(frozen=True)
+@record
 class StridedLoop(Stmt):
     axis: Axis
     start: Any
@@ -248,7 +344,7 @@ class StridedLoop(Stmt):
         return f"for {self.axis.name} in {pretty(self.start)}..{end}:{pretty(self.step)}"
 
 
-@dataclass(frozen=True)
+@record
 class Cond(Stmt):
     cond: Any
     body: tuple
@@ -258,7 +354,7 @@ class Cond(Stmt):
         return f"if {pretty(self.cond)}"
 
 
-@dataclass(frozen=True)
+@record
 class Load(Stmt):
     names: tuple
     input: str
@@ -269,7 +365,7 @@ class Load(Stmt):
         return f"{', '.join(self.names)} = load {self.input}[{pretty(self.index)}]"
 
 
-@dataclass(frozen=True)
+@record
 class Assign(Stmt):
     name: str
     op: ElementwiseImpl
@@ -280,7 +376,7 @@ class Assign(Stmt):
         return f"{self.name} = {self.op.name}({', '.join(self.args)})"
 
 
-@dataclass(frozen=True)
+@record
 class Let(Stmt):
     name: str
     value: Any
@@ -290,7 +386,7 @@ class Let(Stmt):
         return f"{self.name} = {pretty(self.value)}"
 
 
-@dataclass(frozen=True)
+@record
 class Accum(Stmt):
     name: str
     value: str
@@ -303,7 +399,7 @@ class Accum(Stmt):
         return f"{self.name} <- {self.op.name}({self.base or self.name}, {self.value})"
 
 
-@dataclass(frozen=True)
+@record
 class Init(Stmt):
     name: str
     identity: Any
@@ -313,7 +409,7 @@ class Init(Stmt):
         return f"Init({self.name} = {self.identity})"
 
 
-@dataclass(frozen=True)
+@record
 class Write(Stmt):
     output: str
     index: tuple
@@ -327,7 +423,7 @@ class Write(Stmt):
         return f"{self.output}[{pretty(self.index)}] {op} ({', '.join(self.values)})"
 
 
-@dataclass(frozen=True)
+@record
 class WarpShuffle(Stmt):
     state: tuple
     state_b: tuple
@@ -339,7 +435,7 @@ class WarpShuffle(Stmt):
         return f"WarpShuffle({', '.join(self.state)}, length={self.length})"
 
 
-@dataclass(frozen=True)
+@record
 class TreeHalve(Stmt):
     bufs: tuple
     state: tuple
@@ -356,7 +452,7 @@ class TreeHalve(Stmt):
         return f"TreeHalve({', '.join(self.state)}, length={self.length}, tid={self.tid_var})"
 
 
-@dataclass(frozen=True)
+@record
 class Smem(Stmt):
     name: str
     extents: tuple
@@ -368,7 +464,7 @@ class Smem(Stmt):
         return f"Smem {self.dtype} {self.name}{dims} align={self.align}"
 
 
-@dataclass(frozen=True)
+@record
 class Sync(Stmt):
     barrier_id: int = 0
     count: Any = None
@@ -378,7 +474,7 @@ class Sync(Stmt):
         return "SyncWarp" if self.warp else f"Sync(id={self.barrier_id}, count={self.count})"
 
 
-@dataclass(frozen=True)
+@record
 class CpAsyncCopy(Stmt):
     smem: str
     smem_index: tuple
@@ -393,17 +489,17 @@ class CpAsyncCopy(Stmt):
         return f"cp.async[{self.nbytes}B] {self.smem}[{pretty(self.smem_index)}] <- {self.src}[...]"
 
 
-@dataclass(frozen=True)
+@record
 class CpAsyncCommit(Stmt):
     pass
 
 
-@dataclass(frozen=True)
+@record
 class CpAsyncWait(Stmt):
     group: int = 0
 
 
-@dataclass(frozen=True)
+@record
 class RegFragment(Stmt):
     name: str
     role: str
@@ -413,7 +509,7 @@ class RegFragment(Stmt):
     nregs: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class LdmatrixLoad(Stmt):
     frag: str
     src_buffer: str
@@ -434,7 +530,7 @@ class LdmatrixLoad(Stmt):
     fragment_index: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class MmaSyncPtx(Stmt):
     c_frag: str
     a_frag: str
@@ -451,7 +547,7 @@ class MmaSyncPtx(Stmt):
         return self.sfa_frag is not None
 
 
-@dataclass(frozen=True)
+@record
 class RegStore(Stmt):
     dst_buffer: str
     dst_index: tuple
@@ -479,27 +575,27 @@ class RegStore(Stmt):
 # fragment operations (Fragment*).
 
 
-@dataclass(frozen=True)
+@record
 class Branch:
     """One arm of a Select: ``value`` when ``select`` (a coordinate predicate; None = otherwise)."""
     value: Any
     select: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class Select(Stmt):
     name: str
     branches: tuple = ()
 
 
-@dataclass(frozen=True)
+@record
 class Pre(Stmt):
     name: str
     carrier: str = ""
     index: tuple = ()
 
 
-@dataclass(frozen=True)
+@record
 class Carry(Stmt):
     name: str
     value: Any = None
@@ -508,13 +604,13 @@ class Carry(Stmt):
     dtype: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class ZeroPrologue(Stmt):
     dst: str
     words: Any = 0
 
 
-@dataclass(frozen=True)
+@record
 class TmaDescriptor(Stmt):
     name: str
     src_buf: str = ""
@@ -524,7 +620,7 @@ class TmaDescriptor(Stmt):
     dtype: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class TmaLoad(Stmt):
     smem: str
     smem_index: tuple = ()
@@ -534,40 +630,40 @@ class TmaLoad(Stmt):
     mbar_slot: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class MbarrierInit(Stmt):
     mbar: str
     count: Any = 1
     slot: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class MbarrierArriveExpectTx(Stmt):
     mbar: str
     bytes_: Any = 0
     slot: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class MbarrierArrive(Stmt):
     mbar: str
     slot: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class MbarrierWait(Stmt):
     mbar: str
     phase: Any = 0
     slot: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class SetMaxNReg(Stmt):
     count: int
     direction: Any = "inc"
 
 
-@dataclass(frozen=True)
+@record
 class FragLayout:
     """Per-atom geometry of a C fragment: element count, the row (0 top, 1 bottom) of each
     element, the lane xors that combine a row's lanes, and text the IR's renderer uses."""
@@ -580,7 +676,7 @@ class FragLayout:
     col_off: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class Lambda:
     """A pure per-element function (a RegStore epilogue): ``params`` are bound on entry,
     ``body`` (Load / Assign / Let / Select statements) is evaluated, ``results`` name the
@@ -590,13 +686,13 @@ class Lambda:
     results: tuple = ()
 
 
-@dataclass(frozen=True)
+@record
 class FragmentPromote(Stmt):
     dst: str
     src: str = ""
 
 
-@dataclass(frozen=True)
+@record
 class FragmentApply(Stmt):
     out: str
     op: Any = None
@@ -609,7 +705,7 @@ class FragmentApply(Stmt):
     col_base: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class FragmentRowReduce(Stmt):
     top: str
     bot: str = ""
@@ -619,7 +715,7 @@ class FragmentRowReduce(Stmt):
     dtype: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class FragmentRepack(Stmt):
     frag: str
     srcs: tuple = ()
@@ -628,7 +724,7 @@ class FragmentRepack(Stmt):
     part: Any = None
 
 
-@dataclass(frozen=True)
+@record
 class WgmmaDescriptor(Stmt):
     name: str
     smem: str = ""
@@ -638,7 +734,7 @@ class WgmmaDescriptor(Stmt):
     sbo_bytes: Any = 0
 
 
-@dataclass(frozen=True)
+@record
 class WgmmaMma(Stmt):
     c_frags: tuple
     b_desc: str = ""
@@ -651,22 +747,22 @@ class WgmmaMma(Stmt):
     trans_b: bool = False
 
 
-@dataclass(frozen=True)
+@record
 class WgmmaFence(Stmt):
     pass
 
 
-@dataclass(frozen=True)
+@record
 class WgmmaCommit(Stmt):
     pass
 
 
-@dataclass(frozen=True)
+@record
 class WgmmaWait(Stmt):
     group: Any = 0
 
 
-@dataclass(frozen=True)
+@record
 class Opaque(Stmt):
     """A constructor this reader does not model; kept so the walker can name
     it when it fails (BlockScaleLoad appears in the IR reference but in no
@@ -745,14 +841,14 @@ def parse_body(body: list[str] | tuple[str, ...] | str) -> tuple:
 # graph level
 
 
-@dataclass(frozen=True)
+@record
 class TensorInfo:
     name: str
     shape: tuple
     dtype: str
 
 
-@dataclass(frozen=True)
+@record
 class KernelNode:
     """The one KernelOp node of an IR file."""
     node: str
@@ -763,7 +859,7 @@ class KernelNode:
     inputs: tuple
 
 
-@dataclass(frozen=True)
+@record
 class Graph:
     inputs: tuple
     outputs: tuple

@@ -47,9 +47,9 @@ def to_repr(o) -> str:
     if isinstance(o, tuple):
         inner = ", ".join(to_repr(x) for x in o)
         return f"({inner},)" if len(o) == 1 else f"({inner})"
-    if dataclasses.is_dataclass(o):
+    if ir.is_record(o) or dataclasses.is_dataclass(o):
         name = type(o).__name__
-        names = EMMY_FIELDS.get(name) or [f.name for f in dataclasses.fields(o)]
+        names = EMMY_FIELDS.get(name) or list(ir.field_names(o))
         return f"{name}(" + ", ".join(f"{n}={to_repr(getattr(o, n))}" for n in names) + ")"
     return repr(o)
 
