@@ -50,3 +50,32 @@ def test_elementwise_identities():
     assert ir.ElementwiseImpl("multiply").identity == 1.0
     assert ir.ElementwiseImpl("maximum").identity == -1e30
     assert ir.ElementwiseImpl("exp").arity == 1
+
+
+def test_records_behave_as_frozen_dataclasses():
+    """The IR's node classes are frozen records: positional or keyword construction with the
+    declared defaults, field-wise equality and hash, the dataclass repr, no assignment, and
+    construction errors that name the class (the reader turns them into IRSyntaxError)."""
+    import dataclasses
+
+    from thompiler.synth import F32T, L, V
+    a = ir.Load(("v",), "x", (V("i"),), F32T)
+    b = ir.Load(names=("v",), input="x", index=(V("i"),), dtype=F32T)
+    assert a == b and hash(a) == hash(b) and a != ir.Load(("w",), "x", (V("i"),), F32T)
+    assert ir.field_names(a) == ("names", "input", "index", "dtype") and ir.is_record(a)
+    assert not ir.is_record(ir.Load)
+    assert repr(L(3)) == "Literal(value=3, dtype='int')"
+    st = ir.RegStore("y", (L(0), L(0)), "c", (16, 8, 16))
+    assert (st.ldm, st.epilogue, st.extra_frags, st.atomic, st.swizzle) == (0, None, (), False, "NONE")
+    assert ir.Opaque("K").fields == ()
+    assert ir.Tile.extents.fget is not None                     # properties survive
+    with pytest.raises(dataclasses.FrozenInstanceError):
+        a.input = "y"
+    with pytest.raises(TypeError, match="Load.__init__\\(\\) got an unexpected keyword argument 'bogus'"):
+        ir.Load(("v",), "x", (), F32T, bogus=1)
+    with pytest.raises(TypeError, match="missing 1 required positional argument: 'input'"):
+        ir.Load(("v",))
+    with pytest.raises(TypeError, match="multiple values for argument 'names'"):
+        ir.Load(("v",), names=("w",), input="x", index=())
+    with pytest.raises(ir.IRSyntaxError, match="Write: "):
+        ir.parse_stmt("Write(output='y', index=(), values=(), dtype=None)")
