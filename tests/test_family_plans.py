@@ -152,6 +152,11 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages
     assert fam.smem + fam.static_smem <= 227 * 1024
     if lay == "col":
         assert side["tmaps"][1]["box"] == [64, fam.BN // 2]
+    ptx = fam.emit()
+    assert ".reqnctapercluster 2, 1, 1" in ptx and "tcgen05.mma.cta_group::2.kind::f16" in ptx
+    assert "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global" in ptx   # each CTA's own loads
+    assert not re.search(r"cp\.async\.bulk[^\n]*multicast", ptx)     # no load is multicast
+    assert ("thc_tail_ws" in ptx) == bool(rem)
 
 
 def test_matmul_pair_declines_odd_generic_grid(tmp_path, monkeypatch):
