@@ -56,13 +56,15 @@ def peaks() -> dict:
             "source": "fallback"}
 
 
-def profile_traffic(name: str):
-    """dram bytes per launch from the committed ncu summary of this kernel, if any."""
+def profile_traffic(name: str, tag: str = ""):
+    """dram bytes per launch from the committed ncu summary of this kernel, if any: the line
+    ``dram_bytes_per_launch: B`` (or ``dram_bytes_per_launch[tag]: B`` for one of several shapes)."""
     f = ROOT / "profiles" / f"{name}.md"
     if not f.exists():
         return None
+    key = f"dram_bytes_per_launch[{tag}]:" if tag else "dram_bytes_per_launch:"
     for line in f.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
+        if line.strip().startswith(key):
             return int(line.split(":")[1].strip().replace(",", ""))
     return None
 
@@ -385,7 +387,7 @@ class RowOps:
                 "sample": f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {self.cols}] (1/8 of a step), "
                           "best of 3"}
 
-    def config(self, world: int) -> dict:
+    def details(self, world: int) -> dict:
         return {"workload": f"fused row ops f32[{self.rows}, {self.cols}] x3 (softmax, rmsnorm eps=1e-6, l2norm), "
                             "one row per CTA", "rows_per_gpu": self.rows, "cols": self.cols,
                 "kernels": {k: self.k[k].family for k in self.kinds},
@@ -482,7 +484,7 @@ class Pointwise:
         gk.close()
         return {"ms": ms, "gbs": 12 * self.n / ms / 1e6}
 
-    def config(self, world: int) -> dict:
+    def details(self, world: int) -> dict:
         return {"workload": f"pointwise relu(x0) * x1, f32[{self.n}] N(0,1), p03 schedule (4 per thread)",
                 "kernel": self.k.family, "l2": "operands (3 GiB per step) far exceed L2; no flush",
                 "parallelism": f"replicas over {world} GPU(s)"}
@@ -580,7 +582,7 @@ class FullSum:
         return {"value": n * 4 / r["seconds"] / 1e9, "unit": "GB/s", "cores": r["cores"], "kind": "port",
                 "sample": f"torch CPU sum of f32[{n}], best of 3"}
 
-    def config(self, world: int) -> dict:
+    def details(self, world: int) -> dict:
         how = {"peer": "in-kernel combine over NVLink peer memory (no NCCL in the step)",
                "nccl": "NCCL all-reduce of the per-GPU results", None: "no exchange (one GPU)"}
         c = {"workload": (f"sharded sum f32[2^{self.n_total.bit_length() - 1}] -> per-GPU two-pass reduction "
@@ -601,14 +603,19 @@ class Matmul:
     dtype = "f16"
     bound = "tensor"
 
-    def __init__(self, rank: int, world: int, dev: int, scale: int = 0):
+    SHAPES = {"square": (4096, 4096, 4096), "rect": (8192, 3072, 1024)}
+
+    def __init__(self, rank: int, world: int, dev: int, scale: int = 0, which: tuple = ("square", "rect")):
         import torch
         from thompiler import synth
         from thompiler.device import DeviceKernel
         self.torch = torch
-        self.shapes = {"square": (4096, 4096, 4096), "rect": (8192, 3072, 1024)}
+        self.shapes = {k: self.SHAPES[k] for k in which}
         if scale:
             self.shapes = {"square": (scale, scale, scale)}
+        if len(self.shapes) == 1:
+            self.metric = (f"achieved tensor TFLOP/s (f16 matmul, f32 accumulate: "
+                           f"{'x'.join(map(str, next(iter(self.shapes.values()))))})")
         tmp = Path(tempfile.mkdtemp(prefix=f"bench_mm_{rank}_"))
         self.k, self.gen, self.t = {}, {}, {}
         g = torch.Generator(device=f"cuda:{dev}").manual_seed(2000 + rank)
@@ -626,7 +633,7 @@ class Matmul:
         self.flops_per_step = sum(self.flops.values())
         self.bytes_per_step = self.flops_per_step        # value is flops-based for this workload
         self.launches_per_step = len(self.kinds)
-        self.dominant = "square"
+        self.dominant = "square" if "square" in self.shapes else next(iter(self.shapes))
 
     def ptrs(self, name):
         a, b, c = self.t[name]
@@ -649,8 +656,8 @@ class Matmul:
             self.k[name](self.ptrs(name), s)
             torch.cuda.synchronize()
             assert runner.read_error_word(self.k[name].module, self.k[name].plan) == 0, "kernel wait gave up"
-            ref = a.double() @ b.double().sum(0)
-            assert torch.allclose(c.double().sum(1), ref, rtol=1e-4, atol=1e-3), f"{name} checksum mismatch"
+            ref = a.double() @ b.double().t()
+            assert torch.allclose(c.double(), ref, rtol=2e-2, atol=2e-3), f"{name} mismatch against float64"
 
     def reference_lowering(self) -> dict:
         """The same IR through the statement-by-statement lowering (mma.sync, the
@@ -708,7 +715,7 @@ class Matmul:
         return {"value": 2 * 1024 ** 3 / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": r["cores"],
                 "kind": "port", "sample": "torch CPU f16 matmul 1024^3 (f32 result), one run"}
 
-    def config(self, world: int) -> dict:
+    def details(self, world: int) -> dict:
         return {"workload": "f16 matmul, f32 accumulate/out, A row-major, B column-major: "
                             + ", ".join(f"{m}x{n}x{k}" for m, n, k in self.shapes.values()),
                 "kernels": {k: self.k[k].family for k in self.kinds},
@@ -805,7 +812,7 @@ class Attention:
         return {"value": fl / r["seconds"] / 1e12, "unit": "TFLOP/s", "cores": r["cores"], "kind": "port",
                 "sample": f"torch CPU f16 attention on 2 of the 128 heads ([2, {self.S}, {self.D}]), one run"}
 
-    def config(self, world: int) -> dict:
+    def details(self, world: int) -> dict:
         return {"workload": f"attention f16 [{self.B}, {self.H}, {self.S}, {self.D}] non-causal, "
                             "scale 1/sqrt(d), f32 accumulate",
                 "kernels": {"attention": self.k["attention"].family},
@@ -814,83 +821,144 @@ class Attention:
                 "parallelism": f"(batch, head) sharding over {world} GPU(s), no collective"}
 
 
-# about one second of timed work per workload at one GPU (the clock sampler needs a region that long)
-DEFAULT_STEPS = {"rowops": 6000, "sum": 20000, "bigsum": 1500, "matmul": 5000, "attention": 2500,
-                 "pointwise": 2000}
+# ---- the suite ------------------------------------------------------------------------
+
+# about one second of timed work per workload at one GPU (used with an explicit --config
+# when --steps is not given)
+DEFAULT_STEPS = {"rowops": 6000, "sum": 20000, "bigsum": 1500, "bigsum_nccl": 1500, "matmul": 5000,
+                 "matmul_square": 5000, "matmul_rect": 10000, "attention": 2500, "pointwise": 2000}
 
 CONFIGS = {"rowops": lambda r, w, d, n: RowOps(r, w, d, rows=n or 8192),
            "pointwise": lambda r, w, d, n: Pointwise(r, w, d, n),
            "attention": lambda r, w, d, n: Attention(r, w, d, n),
            "matmul": lambda r, w, d, n: Matmul(r, w, d, n),
+           "matmul_square": lambda r, w, d, n: Matmul(r, w, d, n, which=("square",)),
+           "matmul_rect": lambda r, w, d, n: Matmul(r, w, d, n, which=("rect",)),
            "sum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 20),
-           "bigsum": lambda r, w, d, n, coll="peer": FullSum(r, w, d, n or 1 << 30, sharded=True,
-                                                             collective=coll)}
+           "bigsum": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True, collective="peer"),
+           "bigsum_nccl": lambda r, w, d, n: FullSum(r, w, d, n or 1 << 30, sharded=True, collective="nccl")}
+
+# the default run: the row ops are the headline line, every workload is one record of `configs`
+SUITE = ("rowops", "sum", "bigsum", "matmul_square", "matmul_rect", "attention", "pointwise")
+SUITE_MULTI = ("rowops", "sum", "bigsum", "bigsum_nccl", "matmul_square", "matmul_rect", "attention",
+               "pointwise")
+
+SHARDED = {"bigsum", "bigsum_nccl", "attention"}
+
+METRICS = {"rowops": RowOps.metric, "pointwise": Pointwise.metric, "attention": Attention.metric,
+           "matmul": Matmul.metric,
+           "matmul_square": "achieved tensor TFLOP/s (f16 matmul, f32 accumulate: 4096x4096x4096)",
+           "matmul_rect": "achieved tensor TFLOP/s (f16 matmul, f32 accumulate: 8192x3072x1024)",
+           "sum": "achieved HBM GB/s (single-kernel array sum)", "bigsum": BIGSUM_METRIC,
+           "bigsum_nccl": BIGSUM_METRIC}
 
 
-REFERENCE_BUDGET_S = 90.0      # wall-time cap on the reference arm's timed samples
-
-
-def reference_arm(args, out=None) -> None:
-    """The reference's CPU path (the torch expression each problem was generated from, evaluated on
-    this host's cores) on a bounded sample of the same workload, same metric and config."""
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
-    from oracle import cpu_baseline
-    cfg = args.config
-    if cfg == "rowops":
-        rows, cols = 1024, 4096
-        run = lambda: cpu_baseline.rowops_sample(rows, cols)             # noqa: E731
-        work, unit, scale, dtype = 3 * 2 * rows * cols * 4 + cols * 4, "GB/s", 1e9, "f32"
-        sample = f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {cols}] (1/8 of a [8192, 4096] step)"
-        metric, scaling = RowOps.metric, "weak"
-        config = {"workload": "fused row ops f32[8192, 4096] x3 (softmax, rmsnorm eps=1e-6, l2norm)",
-                  "sample_rows": rows}
-    elif cfg == "pointwise":
-        m_ = 1 << 24
-        run = lambda: cpu_baseline.pointwise_sample(m_)                  # noqa: E731
-        work, unit, scale, dtype = 12 * m_, "GB/s", 1e9, "f32"
-        sample = f"torch CPU relu(x0) * x1 on f32[{m_}] (1/16 of a step)"
-        metric, scaling = Pointwise.metric, "weak"
-        config = {"workload": "pointwise relu(x0) * x1, f32[268435456] N(0,1), p03 schedule (4 per thread)",
-                  "sample_elements": m_}
-    elif cfg == "matmul":
-        m = n = k = 1024
-        run = lambda: cpu_baseline.matmul_sample(m, n, k)                # noqa: E731
-        work, unit, scale, dtype = 2 * m * n * k, "TFLOP/s", 1e12, "f16"
-        sample = f"torch CPU f16 matmul {m}x{n}x{k} (B column-major, f32 result)"
-        metric, scaling = Matmul.metric, "weak"
-        config = {"workload": "f16 matmul, f32 accumulate/out, A row-major, B column-major: "
-                              "4096x4096x4096, 8192x3072x1024", "sample": f"{m}x{n}x{k}"}
-    elif cfg == "attention":
-        bh, sq, d = 2, 2048, 128
-        run = lambda: cpu_baseline.attention_sample(bh, sq, d)           # noqa: E731
-        work, unit, scale, dtype = 4 * bh * sq * sq * d, "TFLOP/s", 1e12, "f16"
-        sample = f"torch CPU f16 attention on {bh} of the 128 heads ([{bh}, {sq}, {d}])"
-        metric, scaling = Attention.metric, "strong"
-        config = {"workload": "attention f16 [8, 16, 2048, 128] non-causal, scale 1/sqrt(d), f32 accumulate",
-                  "sample_heads": bh}
+def workload_config(name: str, world: int) -> dict:
+    """The workload a line measures, identical in both arms (ours and the reference's CPU path)."""
+    mm = {"matmul": "4096x4096x4096, 8192x3072x1024", "matmul_square": "4096x4096x4096",
+          "matmul_rect": "8192x3072x1024"}
+    if name == "rowops":
+        c = {"workload": "fused row ops f32[8192, 4096] x3 (softmax, rmsnorm eps=1e-6, l2norm)",
+             "l2": "inputs larger than L2 (3 x 128 MiB distinct input matrices per GPU)",
+             "parallelism": f"weak: {world} GPU(s), one matrix set each, no collective"}
+    elif name == "pointwise":
+        c = {"workload": "pointwise relu(x0) * x1, f32[268435456] N(0,1), p03 schedule (4 per thread)",
+             "l2": "operands (3 GiB per step) far exceed L2; no flush",
+             "parallelism": f"replicas over {world} GPU(s)"}
+    elif name in mm:
+        c = {"workload": f"f16 matmul, f32 accumulate/out, A row-major, B column-major, N(0,0.02): {mm[name]}",
+             "l2": "operands (56-96 MiB per GEMM incl. output) exceed half of L2; no flush",
+             "parallelism": f"replicas over {world} GPU(s)"}
+    elif name == "attention":
+        c = {"workload": "attention f16 [8, 16, 2048, 128] N(0,1) non-causal, scale 1/sqrt(d), f32 accumulate",
+             "l2": "K/V of a head (1 MiB) shared in L2 by its 16 query tiles; no flush",
+             "parallelism": f"strong: (batch, head) units split over {world} GPU(s), no collective"}
+    elif name == "sum":
+        c = {"workload": "array sum f32[1048576] U[-1,1), one kernel",
+             "l2": "input (4 MiB) fits in L2: every step after the first reads it from L2",
+             "parallelism": f"replicas over {world} GPU(s)"}
     else:
-        n = 1 << 26
-        run = lambda: cpu_baseline.sum_sample(n)                         # noqa: E731
-        work, unit, scale, dtype = n * 4, "GB/s", 1e9, "f32"
-        sample = f"torch CPU sum of f32[{n}]"
-        metric = "achieved HBM GB/s (single-kernel array sum)" if cfg == "sum" else BIGSUM_METRIC
-        scaling = "weak" if cfg == "sum" else "strong"
-        config = {"workload": f"{cfg} (CPU sample of {n} elements)"}
-    for _ in range(min(args.warmup, 3)):
-        run()
+        how = ("NCCL all-reduce of the per-GPU results" if name == "bigsum_nccl" else
+               "in-kernel combine over NVLink peer memory (no NCCL in the step)")
+        c = {"workload": f"sharded sum f32[2^30] U[-1,1): per-GPU two-pass reduction + "
+                         f"{how if world > 1 else 'no exchange (one GPU)'}",
+             "l2": "inputs larger than L2",
+             "parallelism": f"strong: contiguous slices over {world} GPU(s)"}
+    return c
+
+
+def cpu_sample(name: str) -> dict:
+    """The reference's CPU path (the torch expression each problem was generated from, on this
+    host's cores) over a bounded sample of one step of workload ``name``: the callable, the
+    sample's algorithmic work in the metric's unit and what the sample is."""
+    from oracle import cpu_baseline as cb
+    if name == "rowops":
+        rows, cols = 1024, 4096
+        return {"run": lambda: cb.rowops_sample(rows, cols), "work": 3 * 2 * rows * cols * 4 + cols * 4,
+                "unit": "GB/s", "scale": 1e9, "dtype": "f32",
+                "sample": f"torch CPU softmax + RMSNorm + L2-norm on f32[{rows}, {cols}] (1/8 of a step)"}
+    if name == "pointwise":
+        m = 1 << 24
+        return {"run": lambda: cb.pointwise_sample(m), "work": 12 * m, "unit": "GB/s", "scale": 1e9,
+                "dtype": "f32", "sample": f"torch CPU relu(x0) * x1 on f32[{m}] (1/16 of a step)"}
+    if name in ("matmul", "matmul_square", "matmul_rect"):
+        m, n, k = (512, 4096, 4096) if name == "matmul_square" else (1024, 3072, 1024)
+        part = "1/8 of the 4096^3 rows" if name == "matmul_square" else "1/8 of the 8192x3072x1024 rows"
+        return {"run": lambda: cb.matmul_sample(m, n, k), "work": 2 * m * n * k, "unit": "TFLOP/s",
+                "scale": 1e12, "dtype": "f16",
+                "sample": f"torch CPU f16 matmul {m}x{n}x{k} (B column-major, f32 result; {part})"}
+    if name == "attention":
+        bh, sq, d = 2, 2048, 128
+        return {"run": lambda: cb.attention_sample(bh, sq, d), "work": 4 * bh * sq * sq * d, "unit": "TFLOP/s",
+                "scale": 1e12, "dtype": "f16",
+                "sample": f"torch CPU f16 attention on {bh} of the 128 heads ([{bh}, {sq}, {d}])"}
+    n = 1 << 20 if name == "sum" else 1 << 26
+    return {"run": lambda: cb.sum_sample(n), "work": n * 4, "unit": "GB/s", "scale": 1e9, "dtype": "f32",
+            "sample": f"torch CPU sum of f32[{n}]" + ("" if name == "sum" else " (1/16 of the 2^30 array)")}
+
+
+def time_cpu_sample(name: str, steps: int, warmup: int, budget_s: float) -> dict:
+    from oracle import cpu_baseline as cb
+    smp = cpu_sample(name)
+    for _ in range(min(warmup, 3)):
+        smp["run"]()
     samples, t0 = [], time.perf_counter()
-    while len(samples) < args.steps and (not samples or time.perf_counter() - t0 < REFERENCE_BUDGET_S):
-        samples.append(run()["seconds"])
+    while len(samples) < steps and (not samples or time.perf_counter() - t0 < budget_s):
+        samples.append(smp["run"]()["seconds"])
     sec = statistics.median(samples)
-    value, cores = work / sec / scale, cpu_baseline.threads()
-    config["samples_timed"] = len(samples)
-    line = {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-            "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic", "config": config,
-            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+    return {"value": smp["work"] / sec / smp["scale"], "unit": smp["unit"], "cores": cb.threads(), "kind": "port",
+            "sample": smp["sample"], "seconds": sec, "samples_timed": len(samples), "dtype": smp["dtype"]}
+
+
+REFERENCE_BUDGET_S = 90.0      # wall-time cap on the reference arm's timed samples (one workload)
+SUITE_REFERENCE_BUDGET_S = 15.0    # the same, per workload of the default suite
+
+
+def reference_record(name: str, args, world: int, budget_s: float) -> dict:
+    r = time_cpu_sample(name, args.steps, args.warmup, budget_s)
+    value, unit = r["value"], r["unit"]
+    return {"impl": "reference", "metric": METRICS[name], "value": value, "unit": unit,
+            "ms_per_step": r["seconds"] * 1e3, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong" if name in SHARDED else "weak",
+            "dtype": r["dtype"], "config": workload_config(name, world),
+            "cpu_baseline": {"value": value, "unit": unit, "cores": r["cores"], "kind": "port",
+                             "sample": r["sample"], "samples_timed": r["samples_timed"]},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_arm(args, world: int, out=None) -> None:
+    """The reference's CPU path (the torch expression each problem was generated from, evaluated on
+    this host's cores, all of its threads) on a bounded sample of the same workload, same metric and
+    config as our arm.  Under torchrun rank 0 alone runs and prints; the other ranks exit."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    if args.config != "all":
+        line = reference_record(args.config, args, world, REFERENCE_BUDGET_S)
+    else:
+        suite = SUITE_MULTI if world > 1 else SUITE
+        line = reference_record("rowops", args, world, SUITE_REFERENCE_BUDGET_S)
+        line["configs"] = {n: reference_record(n, args, world, SUITE_REFERENCE_BUDGET_S) for n in suite}
+    line.update(n_gpus=world, vs_baseline=None, data="synthetic")
     print(json.dumps(line), file=out or sys.stdout, flush=True)
 
 
@@ -904,52 +972,23 @@ def _result_stream():
     return out
 
 
-def main() -> None:
-    out = _result_stream()
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=0,
-                    help="timed steps (default: about one second of work for the chosen workload)")
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="rowops", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-graph", action="store_true",
-                    help="launch the timed steps one by one instead of replaying CUDA graphs")
-    ap.add_argument("--collective", default="peer", choices=["peer", "nccl"],
-                    help="bigsum's exchange step: in-kernel peer combine (default) or an NCCL all-reduce")
-    ap.add_argument("--size", type=int, default=0,
-                    help="override the workload size (rows for rowops, elements for sums); profiling only")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    if args.steps <= 0:
-        args.steps = DEFAULT_STEPS[args.config]
-    if args.impl == "reference":
-        reference_arm(args, out)
-        return
+PROFILE = {"rowops": ("k_softmax_rows_rowops", ""), "sum": ("k_sum_1_reduce_sum", ""),
+           "bigsum": ("k_sum_1_reduce_bigsum", ""), "bigsum_nccl": ("k_sum_1_reduce_bigsum", ""),
+           "matmul": ("k_matmul_f16_matmul", "square"), "matmul_square": ("k_matmul_f16_matmul", "square"),
+           "matmul_rect": ("k_matmul_f16_matmul", "rect"), "attention": ("k_attention_attention", ""),
+           "pointwise": ("k_mul_pointwise_pointwise", "")}
 
+
+def measure(name: str, w, args, steps: int, world: int, rank: int, local: int) -> dict | None:
+    """Check, warm up and time ``steps`` steps of workload ``w``; rank 0 gets its record."""
     import torch
     import torch.distributed as dist
-    from thompiler import runner
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
-    runner.init(local)
-    if args.config == "bigsum":
-        w = CONFIGS[args.config](rank, world, local, args.size, args.collective)
-    else:
-        w = CONFIGS[args.config](rank, world, local, args.size)
     stream = torch.cuda.current_stream().cuda_stream
     w.check()
     for _ in range(args.warmup):
         w.step(stream)
     # per-kernel durations: CUDA events around every launch of an untimed pass on the launch stream
-    n_ev = min(args.steps, 200)
+    n_ev = min(steps, 200)
     events = {k: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(n_ev)] for k in w.kinds}
     for i in range(n_ev):
@@ -961,7 +1000,7 @@ def main() -> None:
     use_graph = not args.no_graph and getattr(w, "collective", None) != "nccl"
     graph, G = None, 1
     if use_graph:
-        G = next(g for g in range(min(args.steps, 500), 0, -1) if args.steps % g == 0)
+        G = next(g for g in range(min(steps, 500), 0, -1) if steps % g == 0)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             cap = torch.cuda.current_stream().cuda_stream
@@ -976,17 +1015,17 @@ def main() -> None:
     clocks = ClockSampler(local)
     start.record()
     if graph is not None:
-        for _ in range(args.steps // G):
+        for _ in range(steps // G):
             graph.replay()
     else:
-        for _ in range(args.steps):
+        for _ in range(steps):
             w.step(stream)
     end.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
     if world > 1:
         dist.barrier()
-    ms = start.elapsed_time(end) / args.steps
+    ms = start.elapsed_time(end) / steps
     if graph is not None:
         # kernels run back to back inside the graphs: share the timed step among them in the
         # proportions of their event-timed durations (one kernel per step: the step itself)
@@ -999,52 +1038,121 @@ def main() -> None:
     ms_max = float(t.item())
     e2e = None
     if not args.no_e2e:
-        e2e = w.e2e(max(1, min(args.steps, 5)))
+        e2e = w.e2e(max(1, min(steps, 5)))
         if world > 1:
             v = torch.tensor([e2e["ms_per_step"]], device=f"cuda:{local}")
             dist.all_reduce(v, op=dist.ReduceOp.MAX)
             unit_scale = 1e12 if getattr(w, "bound", "hbm") == "tensor" else 1e9
             work = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
             e2e["value"] = work / (float(v.item()) / 1e3) / unit_scale
-    if rank == 0:
-        pk = peaks()
-        dom = w.dominant
-        kms = per_kernel[dom]
-        kernel_name = f"{w.k[dom].info.name if isinstance(w.k, dict) else w.k.info.name}"
-        traffic = profile_traffic(f"{kernel_name}_{args.config}")
-        total = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
-        if getattr(w, "bound", "hbm") == "tensor":
-            long_run = ms_max * args.steps > 1000.0
-            peak = pk.get("bf16_tflops_sustained" if long_run else "bf16_tflops", pk["bf16_tflops"])
-            achieved = w.flops[dom] / (kms / 1e3) / 1e12
-            value, unit = total / (ms_max / 1e3) / 1e12, "TFLOP/s"
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": traffic,
-                    "peak_kind": "sustained" if long_run else "burst"}
-        else:
-            achieved = w.kbytes[dom] / (kms / 1e3) / 1e9
-            value, unit = total / (ms_max / 1e3) / 1e9, "GB/s"
-            roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "frac": achieved / pk["hbm_gbs"], "traffic": traffic}
-        roof.update(kernel=kernel_name, peak_source=pk["source"], kernel_ms=kms, per_kernel_ms=per_kernel)
-        cfg = w.config(world)
-        how = f"{args.steps // G} replays of a CUDA graph of {G} steps" if use_graph else "steps launched one by one"
-        cfg["timing"] = how + ("; per-kernel times: the timed step shared in the proportions of per-launch "
+    if rank != 0:
+        return None
+    pk = peaks()
+    dom = w.dominant
+    kms = per_kernel[dom]
+    kernel_name = f"{w.k[dom].info.name if isinstance(w.k, dict) else w.k.info.name}"
+    prof, tag = PROFILE.get(name, (f"{kernel_name}_{name}", ""))
+    traffic = profile_traffic(prof, tag)
+    total = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
+    if getattr(w, "bound", "hbm") == "tensor":
+        long_run = ms_max * steps > 1000.0
+        peak = pk.get("bf16_tflops_sustained" if long_run else "bf16_tflops", pk["bf16_tflops"])
+        achieved = w.flops[dom] / (kms / 1e3) / 1e12
+        value, unit = total / (ms_max / 1e3) / 1e12, "TFLOP/s"
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": traffic,
+                "peak_kind": "sustained" if long_run else "burst"}
+    else:
+        achieved = w.kbytes[dom] / (kms / 1e3) / 1e9
+        value, unit = total / (ms_max / 1e3) / 1e9, "GB/s"
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": traffic}
+    roof.update(kernel=kernel_name, peak_source=pk["source"], kernel_ms=kms, per_kernel_ms=per_kernel)
+    details = w.details(world)
+    how = f"{steps // G} replays of a CUDA graph of {G} steps" if use_graph else "steps launched one by one"
+    details["timing"] = how + ("; per-kernel times: the timed step shared in the proportions of per-launch "
                                "CUDA events" if use_graph else "; per-kernel times from per-launch CUDA events")
-        if hasattr(w, "reference_lowering"):
-            cfg["reference_lowering"] = w.reference_lowering()
-        line = {
-            "metric": w.metric, "value": value, "unit": unit, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "weak" if not getattr(w, "sharded", False) else "strong",
-            "vs_baseline": None, "dtype": w.dtype, "data": "synthetic", "config": cfg,
-            "roofline": roof,
-            "cpu_baseline": w.cpu_baseline() if world == 1 else None,
-            "e2e": e2e, "gpu_launches": w.launches_per_step * args.steps, "clocks": clk,
-        }
+    if hasattr(w, "reference_lowering"):
+        details["reference_lowering"] = w.reference_lowering()
+    cpu = None
+    if world == 1:
+        r = time_cpu_sample(name, 3, 1, 10.0)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return {"metric": w.metric, "value": value, "unit": unit, "ms_per_step": ms_max, "steps": steps,
+            "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong" if getattr(w, "sharded", False) else "weak", "dtype": w.dtype,
+            "config": workload_config(name, world), "details": details, "roofline": roof,
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": w.launches_per_step * steps, "clocks": clk}
+
+
+def run_workload(name: str, args, steps: int, world: int, rank: int, local: int) -> dict | None:
+    import gc
+
+    import torch
+    w = CONFIGS[name](rank, world, local, args.size)
+    try:
+        return measure(name, w, args, steps, world, rank, local)
+    finally:
+        if hasattr(w, "close"):
+            w.close()
+        ks = w.k.values() if isinstance(w.k, dict) else [w.k]
+        for k in ks:
+            k.close()
+        for g in getattr(w, "gen", {}).values():
+            g.close()
+        del w
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
+
+def main() -> None:
+    out = _result_stream()
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=0,
+                    help="timed steps (default: 20 for the suite; about one second of work for one --config)")
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="all", choices=["all", *sorted(CONFIGS)],
+                    help="all (default): the row ops as the headline line and every workload as a record "
+                         "of its `configs` object; otherwise one workload")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="launch the timed steps one by one instead of replaying CUDA graphs")
+    ap.add_argument("--size", type=int, default=0,
+                    help="override the workload size (rows for rowops, elements for sums); profiling only")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.steps <= 0:
+        args.steps = 20 if args.config == "all" else DEFAULT_STEPS[args.config]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        reference_arm(args, world, out)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from thompiler import runner
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    runner.init(local)
+    if args.config == "all":
+        suite = SUITE_MULTI if world > 1 else SUITE
+        records = {n: run_workload(n, args, args.steps, world, rank, local) for n in suite}
+        line = dict(records["rowops"]) if rank == 0 else None
+        if line is not None:
+            line["configs"] = records
+    else:
+        line = run_workload(args.config, args, args.steps, world, rank, local)
+    if rank == 0:
+        line.update(n_gpus=world, vs_baseline=None, data="synthetic")
         print(json.dumps(line), file=out, flush=True)
-    if hasattr(w, "close"):
-        w.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

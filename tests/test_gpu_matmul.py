@@ -73,6 +73,12 @@ def test_matmul_benchmark_shapes(tmp_path, M, N, K):
     # checksum: every row of C sums to the row of A times the column sums of B^T
     ones_ref = a.double() @ b.double().sum(0)
     assert torch.allclose(c1.double().sum(1), ones_ref, rtol=1e-4, atol=1e-3)
+    # every element against an independent float64 product, at the f16-input tolerance
+    ref = a.double() @ b.double().t()
+    assert torch.allclose(c1.double(), ref, rtol=RTOL, atol=ATOL)
+    err64 = (c1.double() - ref).abs().max().item()
+    print(f"{M}x{N}x{K}: max |C - C_f64| = {err64:.3e}")
+    assert err64 < 1e-4, err64                           # exact f16 products summed in f32
     # a second launch (tensor maps already in place) gives the same bits
     c1b = torch.empty_like(c1)
     tuned({"x0": a.data_ptr(), "x1": b.data_ptr(), "matmul": c1b.data_ptr()}, s)

@@ -89,6 +89,12 @@ def test_pair_large(tmp_path, M, N, K, grid):
     assert err < 1e-4, err
     ones_ref = a.double() @ b.double().sum(0)
     assert torch.allclose(c1.double().sum(1), ones_ref, rtol=1e-4, atol=1e-3)
+    # every element against an independent float64 product, at the f16-input tolerance
+    ref = a.double() @ b.double().t()
+    assert torch.allclose(c1.double(), ref, rtol=2e-2, atol=2e-3)
+    err64 = (c1.double() - ref).abs().max().item()
+    print(f"{M}x{N}x{K}: max |C - C_f64| = {err64:.3e}")
+    assert err64 < 1e-4, err64                           # exact f16 products summed in f32
     tuned.close()
     generic.close()
 

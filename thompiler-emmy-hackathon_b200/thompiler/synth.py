@@ -145,9 +145,9 @@ def sum_package(outdir, n: int, kind: str = "sum", T: int = 128, init: dict | No
         ir.Load(("in0",), "x", (V(a0),), F32T),
         ir.Accum("acc0", "in0", E("add"), F32T, (a0,), None)), False, None, True)
     if kind == "mean":
-        tail_body = (ir.Load(("in1",), "mean_count", (L(0),), F32T), assign("v0", "divide", "acc0", "in1"),
-                     ir.Write("mean", (), ("v0",), F32T, False, "NONE"))
-        out, consts = "mean", {"mean_count": (float(n), "f32")}
+        tail_body = (ir.Load(("in1",), "mean_keepdim_count", (L(0),), F32T),
+                     assign("v0", "divide", "acc0", "in1"), ir.Write("mean", (), ("v0",), F32T, False, "NONE"))
+        out, consts = "mean", {"mean_keepdim_count": (float(n), "f32")}
     else:
         tail_body = (ir.Write("sum_1", (), ("acc0",), F32T, False, "NONE"),)
         out, consts = "sum_1", {}
@@ -330,7 +330,10 @@ def attention_package(outdir, B: int, H: int, S: int, D: int, dtype: str = "f16"
 def row_package(outdir, kind: str, rows: int, cols: int, T: int = 128, eps: float = 1e-6,
                 init: dict | None = None, w_init: dict | None = None) -> Path:
     """Row softmax / RMSNorm / L2-normalise / row sum of x[rows, cols], one row per CTA (f01/f02/f03/r04)."""
-    a0, co, a1, a2 = "a0", "a1_co", "a1", "a2"
+    # axis and value names as emmy writes them for f01 / f02 / f03 / r04 (the softmax's second
+    # pass walks its own axis a3; the L2-norm's first pass loads in0, the RMSNorm's in2)
+    a0, co, a1 = "a0", "a1_co", "a1"
+    a2 = "a3" if kind == "softmax" else "a2"
     x_at = lambda v: ir.Load(("in0",), "x", (V(a0), V(v)), F32T)  # noqa: E731
     consts: dict = {}
     inputs = {"x": ((rows, cols), "f32")}
@@ -352,17 +355,19 @@ def row_package(outdir, kind: str, rows: int, cols: int, T: int = 128, eps: floa
         out, code = "softmax", f"torch.softmax(torch.randn({rows}, {cols}), dim=-1)"
     elif kind in ("rmsnorm", "l2norm", "rowsum"):
         sq = kind != "rowsum"
+        sq_in = 2 if kind == "rmsnorm" else 0
         l1 = ir.StridedLoop(axis(a1, cols), V(co), L(T), (
-            (ir.Load(("in2",), "x", (V(a0), V(a1)), F32T), assign("v1", "multiply", "in2", "in2"),
-             ir.Accum("acc0", "v1", E("add"), F32T, (a1,), None)) if sq else
+            (ir.Load((f"in{sq_in}",), "x", (V(a0), V(a1)), F32T),
+             assign(f"v{sq_in // 2}", "multiply", f"in{sq_in}", f"in{sq_in}"),
+             ir.Accum("acc0", f"v{sq_in // 2}", E("add"), F32T, (a1,), None)) if sq else
             (x_at(a1), ir.Accum("acc0", "in0", E("add"), F32T, (a1,), None))), False, None, True)
         states, partners, comb = ["acc0"], ["acc0__o"], add_combine("acc0")
         if kind == "rmsnorm":
             consts = {"mean_count": (float(cols), "f32"), "add_c1": (float(eps), "f32")}
             inputs["w"] = ((cols,), "f32")
             mid = [ir.Load(("in1",), "mean_count", (L(0),), F32T), assign("v0", "reciprocal", "in1"),
-                   assign("v2", "multiply", "acc0", "v0"), ir.Load(("inE",), "add_c1", (L(0),), F32T),
-                   assign("v3", "add", "inE", "v2"), assign("v4", "sqrt", "v3"), assign("v5", "reciprocal", "v4")]
+                   assign("v2", "multiply", "acc0", "v0"), ir.Load(("in0",), "add_c1", (L(0),), F32T),
+                   assign("v3", "add", "in0", "v2"), assign("v4", "sqrt", "v3"), assign("v5", "reciprocal", "v4")]
             tail = ir.StridedLoop(axis(a2, cols), V(co), L(T), (
                 ir.Load(("in3",), "x", (V(a0), V(a2)), F32T), assign("v6", "multiply", "in3", "v5"),
                 ir.Load(("in4",), "w", (V(a2),), F32T), assign("v7", "multiply", "in4", "v6"),
