@@ -18,17 +18,15 @@ IRS = sorted(p for d in PACKAGES for p in (GOLDEN / d).glob("*.ir.json"))
 PTXAS = shutil.which("ptxas")
 
 
-def run_compile(path, env=None):
-    return subprocess.run([sys.executable, str(ROOT / "compile.py"), str(path)], capture_output=True, text=True,
-                          env=env)
+def run_compile(path, *flags):
+    return subprocess.run([sys.executable, str(ROOT / "compile.py"), *flags, str(path)], capture_output=True,
+                          text=True)
 
 
 @pytest.mark.parametrize("mode", ["tuned", "generic"])
 @pytest.mark.parametrize("path", IRS, ids=lambda p: f"{p.parent.name}/{p.stem}")
 def test_compile_contract(path, mode, tmp_path):
-    import os
-    env = dict(os.environ, THOMPILER_GENERIC="1" if mode == "generic" else "0")
-    r = run_compile(path, env)
+    r = run_compile(path, *(["--generic"] if mode == "generic" else []))
     assert r.returncode == 0, r.stderr
     ptx = r.stdout
     assert ptx.startswith(".version") and ptx.isascii()

@@ -12,6 +12,7 @@ from thompiler.families.attention import TcAttention
 from thompiler.families.matmul import TcMatmul
 from thompiler.families.pointwise import Pointwise
 from thompiler.families.strided import StridedReduce
+from thompiler.families.tuning import TUNING
 
 
 def _kernel(path):
@@ -25,7 +26,7 @@ def _ir(d):
 @pytest.mark.parametrize("M,N,K,rem,parts", [(4096, 4096, 4096, 68, 2), (8192, 3072, 1024, 0, 1),
                                             (2048, 2560, 2048, 12, 2), (256, 256, 512, 0, 1)])
 def test_matmul_split_tail_plan(tmp_path, monkeypatch, M, N, K, rem, parts):
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")
+    monkeypatch.setattr(TUNING, "matmul_pair", False)
     fam = recognise(_kernel(_ir(synth.matmul_package(tmp_path / "mm", M, N, K))))
     assert isinstance(fam, TcMatmul)
     assert (fam.rem, fam.parts) == (rem, parts)
@@ -35,36 +36,21 @@ def test_matmul_split_tail_plan(tmp_path, monkeypatch, M, N, K, rem, parts):
     assert fam.stages * (fam.a_bytes + fam.b_bytes) + fam.staging + 1024 + 256 == fam.smem <= 227 * 1024
 
 
-def test_attention_plan_two_threads_per_row(tmp_path, monkeypatch):
-    monkeypatch.setenv("THOMPILER_ATTN_SPLIT", "2")         # 16 softmax warps, 640 threads
-    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
-    assert isinstance(fam, TcAttention)
-    assert (fam.qt, fam.h, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 2, 640, 2, 2, 1024)
-    assert (fam.maxnreg, fam.reg_split) == (96, (104, 56))
-    # per sub-partition (5 warps): 4 softmax warps at 104 + 1 producer warp at 56 registers fit its
-    # 16384, and the split never asks for more than the launch holds (96 per thread)
-    assert 32 * (4 * 104 + 56) <= 16384 and 512 * 104 + 128 * 56 <= 640 * 96
-    assert fam.stage_bytes == 16 * 32 * 32 and fam.xchg_bytes == 2 * 2 * 2 * 128 * 4
-    assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + fam.xchg_bytes + 1024 + 256 <= 227 * 1024
-    ptx = fam.emit()
-    assert ".maxnreg 96" in ptx and "setmaxnreg.inc.sync.aligned.u32 104" in ptx
-    assert '"grid":[148,1,1]' in ptx                            # persistent: one CTA per SM
-    assert '"box":[16,32]' in ptx.replace(" ", "")              # the output's 32 x 32 B staging boxes
-
-
 def test_attention_plan_benchmark_shape(tmp_path, monkeypatch):
-    monkeypatch.delenv("THOMPILER_ATTN_SPLIT", raising=False)    # default: one thread per query row
     fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
     assert isinstance(fam, TcAttention)
-    assert (fam.qt, fam.h, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 1, 384, 2, 2, 1024)
+    assert (fam.qt, fam.threads, fam.ks, fam.vs, fam.tiles) == (2, 384, 2, 2, 1024)
     assert (fam.maxnreg, fam.reg_split) == (168, (224, 56))
     # per sub-partition: 2 softmax warps at 224 + 1 producer warp at 56 registers <= 512 per thread,
     # and the split hands over exactly what the launch holds (168 per thread)
     assert 2 * 224 + 56 <= 512 and 256 * 224 + 128 * 56 == 384 * 168
-    assert fam.xchg_bytes == 0
     assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + 1024 + 256 <= 227 * 1024
     ptx = fam.emit()
     assert ".maxnreg 168" in ptx and "setmaxnreg.inc.sync.aligned.u32 224" in ptx
+    # P reaches the MMA warp in two parts per group: four barriers of 128 arrivals (the softmax
+    # threads of one group), besides the two of O's release
+    inits = re.findall(r"mbarrier\.init\.shared::cta\.b64 \[[^\]]+\], (\d+);", ptx)
+    assert fam.p_parts == 2 and inits.count("128") == 2 * 2 + 2
 
 
 @pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 192), ((2, 2, 384, 64), 1, 192),
@@ -96,35 +82,6 @@ def test_strided_sum_plans():
     assert "peer" not in (r03.sidecar() or {})                 # a mean is not combined across GPUs
 
 
-@pytest.mark.parametrize("split,threads,box", [("1", 192, 64), ("2", 320, 64), ("4", 576, 32)])
-def test_attention_pair_plan(tmp_path, monkeypatch, split, threads, box):
-    """The opt-in 2-SM attention: CTA pairs (.reqnctapercluster 2), an even grid of at most 74
-    pairs, the leader-signalled TMA of each CTA's halves, tcgen05 cta_group::2 throughout."""
-    from thompiler.families.attention_pair import TcAttentionPair
-    monkeypatch.setenv("THOMPILER_ATTN_PAIR", "1")
-    monkeypatch.setenv("THOMPILER_ATTN_PAIR_SPLIT", split)
-    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 8, 16, 2048, 128))))
-    assert isinstance(fam, TcAttentionPair)
-    assert (fam.threads, fam.box_cols, fam.pair_tiles, fam.pairs) == (threads, box, 1024, 74)
-    assert fam.smem <= 227 * 1024 and fam.ks >= 4
-    ptx = fam.emit()
-    assert ".reqnctapercluster 2, 1, 1" in ptx and '"grid":[148,1,1]' in ptx
-    assert "tcgen05.mma.cta_group::1" not in ptx and "tcgen05.cp.cta_group::2.128x256b" in ptx
-    assert "cp.async.bulk.tensor.2d.cta_group::2" in ptx and "mapa.shared::cluster" in ptx
-    assert not re.search(r"cp\.async\.bulk[^\n]*multicast", ptx)     # no load is multicast
-
-
-def test_attention_pair_needs_opt_in_and_shape(tmp_path, monkeypatch):
-    from thompiler.families.attention_pair import TcAttentionPair
-    monkeypatch.delenv("THOMPILER_ATTN_PAIR", raising=False)
-    fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", 1, 2, 256, 128))))
-    assert isinstance(fam, TcAttention) and not isinstance(fam, TcAttentionPair)
-    monkeypatch.setenv("THOMPILER_ATTN_PAIR", "1")
-    for shape in ((1, 2, 384, 128), (2, 2, 512, 64)):         # S not a multiple of 256, or d = 64
-        fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / f"b{shape[2]}{shape[3]}", *shape))))
-        assert not isinstance(fam, TcAttentionPair)
-
-
 @pytest.mark.parametrize("M,N,K,lay,bn,tiles,stages,rem,parts", [
     (4096, 4096, 4096, "col", 0, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 384, 6, 0, 1),
     (2048, 2560, 2048, "col", 0, 80, 6, 6, 2), (256, 128, 256, "row", 0, 1, 8, 0, 1),
@@ -135,11 +92,11 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages
     generic path's static arrays) inside one SM's 227 KB."""
     from thompiler.families.matmul_pair import TcMatmulPair
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay)
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")
+    monkeypatch.setattr(TUNING, "matmul_pair", False)
     assert not isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)
-    monkeypatch.delenv("THOMPILER_MATMUL_PAIR")                                # on by default
+    monkeypatch.setattr(TUNING, "matmul_pair", True)                           # on by default
     if bn:
-        monkeypatch.setenv("THOMPILER_MATMUL_BN", str(bn))
+        monkeypatch.setattr(TUNING, "matmul_bn", bn)
     fam = recognise(_kernel(_ir(d)))
     assert isinstance(fam, TcMatmulPair)
     assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, bn or (256 if N % 256 == 0 else 128))
@@ -164,7 +121,7 @@ def test_matmul_pair_declines_odd_generic_grid(tmp_path, monkeypatch):
     grid is odd keeps the single-CTA kernel."""
     import json
     from thompiler.families.matmul_pair import TcMatmulPair
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "1")
+    monkeypatch.setattr(TUNING, "matmul_pair", True)
     d = synth.matmul_package(tmp_path / "mm", 256, 256, 256)        # generic grid 4 x 4 = 16: even
     assert isinstance(recognise(_kernel(_ir(d))), TcMatmulPair)
     meta = json.loads((d / "meta.json").read_text())

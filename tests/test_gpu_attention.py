@@ -102,56 +102,3 @@ def test_attention_benchmark_shape(tmp_path):
     ref64 = _sdpa64(q[0, :2].cpu().numpy(), kk[0, :2].cpu().numpy(), v[0, :2].cpu().numpy())
     np.testing.assert_allclose(o[0, :2].float().cpu().numpy(), ref64, rtol=RTOL, atol=ATOL)
     k.close()
-
-
-@pytest.mark.parametrize("shape,grid", [((2, 3, 512, 128), 5), ((2, 2, 512, 64), 148)])
-def test_attention_two_threads_per_row(tmp_path, monkeypatch, shape, grid):
-    """THOMPILER_ATTN_SPLIT=2: two softmax threads per query row exchanging the row max and row
-    sum through shared memory, carried over several tiles per CTA."""
-    import torch
-    monkeypatch.setenv("THOMPILER_ATTN_SPLIT", "2")
-    d = synth.attention_package(tmp_path / "att", *shape)
-    k = DeviceKernel(d / "k_attention.ir.json")
-    assert k.plan.block[0] == 640
-    k.plan.grid = (grid, 1, 1)
-    g = torch.Generator(device="cuda").manual_seed(13)
-    q, kk, v = (torch.randn(*shape, device="cuda", generator=g).half() for _ in range(3))
-    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
-    o = torch.full(shape, float("nan"), device="cuda", dtype=torch.float16)
-    for _ in range(2):
-        k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(),
-           "attn": o.data_ptr()}, torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    assert runner.read_error_word(k.module, k.plan) == 0
-    ref = _sdpa64(q.cpu().numpy(), kk.cpu().numpy(), v.cpu().numpy())
-    np.testing.assert_allclose(o.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
-    k.close()
-
-
-@pytest.mark.parametrize("split", ["4", "1"])
-@pytest.mark.parametrize("shape,grid", [((1, 2, 256, 128), None), ((2, 3, 512, 128), 2), ((2, 3, 512, 128), 6),
-                                        ((1, 2, 1024, 128), None)])
-def test_attention_cta_pair(tmp_path, monkeypatch, shape, grid, split):
-    """The opt-in 2-SM kernel (THOMPILER_ATTN_PAIR=1): pairs of CTAs share each K / V block, Q copied
-    into tensor memory, S and O on tcgen05 cta_group::2; persistent over pair-tiles (grid 2 = one
-    pair walks all of them)."""
-    import torch
-    monkeypatch.setenv("THOMPILER_ATTN_PAIR", "1")
-    monkeypatch.setenv("THOMPILER_ATTN_PAIR_SPLIT", split)
-    d = synth.attention_package(tmp_path / "att", *shape)
-    k = DeviceKernel(d / "k_attention.ir.json")
-    assert k.family == "tcgen05-attention-pair"
-    if grid:
-        k.plan.grid = (grid, 1, 1)
-    g = torch.Generator(device="cuda").manual_seed(17)
-    q, kk, v = (torch.randn(*shape, device="cuda", generator=g).half() for _ in range(3))
-    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
-    o = torch.full(shape, float("nan"), device="cuda", dtype=torch.float16)
-    for _ in range(2):
-        k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(),
-           "attn": o.data_ptr()}, torch.cuda.current_stream().cuda_stream)
-    torch.cuda.synchronize()
-    assert runner.read_error_word(k.module, k.plan) == 0
-    ref = _sdpa64(q.cpu().numpy(), kk.cpu().numpy(), v.cpu().numpy())
-    np.testing.assert_allclose(o.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
-    k.close()

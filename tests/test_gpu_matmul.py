@@ -19,6 +19,7 @@ import pytest
 from oracle.interp import run_package as oracle_run
 from thompiler import problems, runner, synth
 from thompiler.device import DeviceKernel
+from thompiler.families.tuning import TUNING
 
 pytestmark = pytest.mark.gpu
 
@@ -95,7 +96,7 @@ def test_matmul_split_tail(tmp_path, monkeypatch, grid):
     workspace, the last part to arrive adding them in part order.  grid 5 puts several whole
     tiles and several parts on each CTA (the arrival barriers' phases carry over)."""
     import torch
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", "0")     # the split tail belongs to the single-CTA kernel
+    monkeypatch.setattr(TUNING, "matmul_pair", False)     # this split tail belongs to the single-CTA kernel
     M, N, K = 2048, 2560, 2048
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
     k = DeviceKernel(d / "k_matmul_f16.ir.json")

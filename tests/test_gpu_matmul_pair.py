@@ -17,6 +17,7 @@ import pytest
 from oracle.interp import run_package as oracle_run
 from thompiler import problems, runner, synth
 from thompiler.device import DeviceKernel
+from thompiler.families.tuning import TUNING
 
 pytestmark = pytest.mark.gpu
 
@@ -26,7 +27,7 @@ FAMILY = "family: tcgen05-matmul-pair"
 
 @pytest.fixture(autouse=True)
 def _pair(monkeypatch):
-    monkeypatch.delenv("THOMPILER_MATMUL_PAIR", raising=False)          # on by default
+    monkeypatch.setattr(TUNING, "matmul_pair", True)                    # on by default
 
 
 @pytest.mark.parametrize("M,N,K,lay,out,bn", [(256, 256, 512, "col", "f32", 0), (256, 128, 256, "row", "f32", 0),
@@ -34,7 +35,7 @@ def _pair(monkeypatch):
                                               (512, 256, 256, "col", "f32", 128)])
 def test_pair_small_vs_oracle(tmp_path, monkeypatch, M, N, K, lay, out, bn):
     if bn:
-        monkeypatch.setenv("THOMPILER_MATMUL_BN", str(bn))
+        monkeypatch.setattr(TUNING, "matmul_bn", bn)
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay, out_dtype=out)
     pkg = problems.load_package(d)
     ptx = problems.compile_package(pkg)

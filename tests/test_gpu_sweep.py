@@ -22,7 +22,8 @@ def test_matmul_shape_sweep(tmp_path, monkeypatch, M, N, K, lay, out, pair):
     """Both matmul kernels: the single-CTA one (pair off) and, where M is a multiple of 256 and
     N of 128, the CTA-pair one (the default there)."""
     import torch
-    monkeypatch.setenv("THOMPILER_MATMUL_PAIR", pair)
+    from thompiler.families.tuning import TUNING
+    monkeypatch.setattr(TUNING, "matmul_pair", pair == "1")
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay, out_dtype=out)
     k = DeviceKernel(d / "k_matmul_f16.ir.json")
     paired = pair == "1" and M % 256 == 0 and N % 128 == 0

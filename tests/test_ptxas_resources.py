@@ -23,8 +23,10 @@ CASES = [
     ("attention", synth.attention_package, (1, 2, 384, 128), {}),
     ("attention", synth.attention_package, (2, 2, 512, 64), {}),
     ("attention", synth.attention_package, (1, 1, 128, 64), {}),
-    ("attention h=2", synth.attention_package, (8, 16, 2048, 128), {"THOMPILER_ATTN_SPLIT": "2"}),
-    ("attention pair", synth.attention_package, (8, 16, 2048, 128), {"THOMPILER_ATTN_PAIR": "1"}),
+    ("attention p_parts=1", synth.attention_package, (8, 16, 2048, 128), {"attention_p_parts": 1}),
+    ("attention p_parts=4", synth.attention_package, (8, 16, 2048, 128), {"attention_p_parts": 4}),
+    ("attention poly", synth.attention_package, (8, 16, 2048, 128), {"attention_poly_pairs": 2}),
+    ("matmul single CTA", synth.matmul_package, (4096, 4096, 4096), {"matmul_pair": False}),
     ("matmul", synth.matmul_package, (4096, 4096, 4096), {}),
     ("matmul", synth.matmul_package, (8192, 3072, 1024), {}),
     ("matmul", synth.matmul_package, (384, 320, 512), {}),
@@ -51,10 +53,12 @@ def _ptxas_info(ptx: str, tmp_path) -> dict:
             "spill_ld": int(re.search(r"(\d+) bytes spill loads", out).group(1))}
 
 
-@pytest.mark.parametrize("what,builder,args,env", CASES, ids=[f"{c[0]}-{'x'.join(map(str, c[2][:4]))}" for c in CASES])
-def test_tuned_module_has_no_spills(tmp_path, monkeypatch, what, builder, args, env):
-    for k, v in env.items():
-        monkeypatch.setenv(k, v)
+@pytest.mark.parametrize("what,builder,args,tuning", CASES,
+                         ids=[f"{c[0]}-{'x'.join(map(str, c[2][:4]))}" for c in CASES])
+def test_tuned_module_has_no_spills(tmp_path, monkeypatch, what, builder, args, tuning):
+    from thompiler.families.tuning import TUNING
+    for k, v in tuning.items():
+        monkeypatch.setattr(TUNING, k, v)
     d = builder(tmp_path / "p", *args)
     ir = next(d.glob("*.ir.json"))
     ptx = compile_kernel(load.load(str(ir)))

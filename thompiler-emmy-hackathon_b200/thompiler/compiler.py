@@ -10,12 +10,11 @@ named after the IR kernel and taking meta.json's ``arg_order`` pointers, and
 both are correct under meta.json's launch.  A family may add a tuned launch
 record (``// @thompiler-launch {...}``) that this backend's runner honours.
 
-``THOMPILER_GENERIC=1`` in the environment forces the generic lowering.
+``compile_kernel(kernel, tuned=False)`` (``compile.py --generic``) forces the
+generic lowering.  Nothing here reads the environment.
 """
 
 from __future__ import annotations
-
-import os
 
 from thompiler import prologue
 from thompiler.emitter import Emitter
@@ -38,9 +37,7 @@ def compile_generic(kernel: KernelInfo) -> str:
     return em.render(prologue.header(), kernel.name, prologue.params(kernel))
 
 
-def compile_kernel(kernel: KernelInfo, tuned: bool | None = None) -> str:
-    if tuned is None:
-        tuned = os.environ.get("THOMPILER_GENERIC", "") in ("", "0")
+def compile_kernel(kernel: KernelInfo, tuned: bool = True) -> str:
     if tuned:
         from thompiler import families
         family = families.recognise(kernel)

@@ -27,12 +27,12 @@ written over the first 64 columns of S_g.  Softmax per row and key block: the
 128 scores in registers (four loads, one wait), a three-input max tree, O and
 the running sum rescaled only when the max grew by more than 2^8 (P <= 256
 stays exact in f16, the rescale is rare), P = 2^(s c' - m) with packed f32x2
-FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  Epilogue:
-O / l as f16 through each warp's own 32-row staging box (128B-swizzled), one
-TMA store per box.  THOMPILER_ATTN_SPLIT=2 (two query tiles only) runs two
-threads per query row instead: 640 threads, each with half of the row's keys
-and half of O's columns, the row max and row sum exchanged through shared
-memory under their own mbarriers, 32-byte unswizzled staging boxes.
+FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  P goes to
+the MMA warp in P_PARTS parts along the keys, each under its own mbarrier:
+O_g += P_g V for the first keys starts while the exponentials of the last
+ones still run, so the softmax chain of a group (S ready -> P stored) hides
+behind the other group's MMAs.  Epilogue: O / l as f16 through each warp's
+own 32-row staging box (128B-swizzled), one TMA store per box.
 Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
 exactly as the IR's exp lowering.  All mbarrier waits are bounded
 (thompiler.families.kit).
@@ -41,11 +41,11 @@ exactly as the IR's exp lowering.  All mbarrier waits are bounded
 from __future__ import annotations
 
 import math
-import os
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
 from thompiler.families.kit import Kit, desc_hi, idesc_f16
+from thompiler.families.tuning import TUNING
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
@@ -53,7 +53,6 @@ BM = BN = 128
 SM_COUNT = 148
 STAGES = 3                  # K and V rings each
 LOG2E = math.log2(math.e)
-POLY_PAIRS = int(os.environ.get("THOMPILER_ATTN_POLY", "0"))    # of every 8 score pairs (0 .. 8)
 
 
 def _var_tail(index: tuple, names: tuple) -> bool:
@@ -67,21 +66,17 @@ class TcAttention(TunedKernel):
         super().__init__(kernel)
         self.pq, self.pk, self.pv, self.pout, self.pscale = q, k, v, out, scale
         self.heads, self.Sq, self.Sk, self.D = heads, Sq, Sk, D
+        # P handed to the MMA warp in this many parts along the keys (1, 2 or 4); of every 8
+        # score pairs, poly_pairs take 2^x from a polynomial on the FMA pipe (0 .. 8)
+        self.p_parts, self.poly_pairs = TUNING.attention_p_parts, TUNING.attention_poly_pairs
         self.q_bytes = BM * D * 2
         self.kv_bytes = BN * D * 2
         # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
         self.qt = 2 if Sq % (2 * BM) == 0 else 1
-        # h threads per query row: one by default; with two query tiles THOMPILER_ATTN_SPLIT=2 gives
-        # two (each takes half of the row's keys and half of O's columns, the row max and the row
-        # sum exchanged through shared memory), two softmax warps per tile on each SM
-        # sub-partition.  Measured on B200 at [8, 16, 2048 | 4096, 128] it is about 1% slower
-        # than one thread per row (the exponentials' latency is hidden already)
-        self.h = int(os.environ.get("THOMPILER_ATTN_SPLIT", "1")) if self.qt == 2 else 1
-        self.h = self.h if self.h in (1, 2) else 1
-        # warps 0 .. 4 qt h - 1 softmax (warp w reads TMEM lanes 32 (w % 4) ..), then the TMA warp and
-        # the MMA warp; with two query tiles they fill one more warpgroup (two warps idle) whose
-        # registers go to the softmax warpgroups through setmaxnreg
-        sm_warps = 4 * self.qt * self.h
+        # warps 0 .. 4 qt - 1 softmax, one thread per query row (warp w reads TMEM lanes 32 (w % 4) ..),
+        # then the TMA warp and the MMA warp; with two query tiles they fill one more warpgroup (two
+        # warps idle) whose registers go to the softmax warpgroups through setmaxnreg
+        sm_warps = 4 * self.qt
         self.sm_threads = 32 * sm_warps
         self.w_tma, self.w_mma = sm_warps, sm_warps + 1
         self.threads = 32 * sm_warps + 128 if self.qt == 2 else 192
@@ -92,19 +87,17 @@ class TcAttention(TunedKernel):
         if self.qt == 2:
             dec = 56
             inc = min(248, self.maxnreg + ((self.maxnreg - dec) * 128 // self.sm_threads) // 8 * 8)
-            assert self.qt * self.h * inc + dec <= 512, "setmaxnreg split over one sub-partition's file"
+            assert self.qt * inc + dec <= 512, "setmaxnreg split over one sub-partition's file"
             self.reg_split = (inc, dec)
         else:
             self.reg_split = None
         self.ks, self.vs = ((2, 2) if self.qt == 2 else (3, 2)) if D == 128 else (STAGES, STAGES)
         # per softmax warp: a 32-row staging box for the output's TMA stores, 128 bytes wide
-        # (128B swizzle) with one thread per row, 32 bytes wide (no swizzle) with two
-        self.box_bytes = 128 if self.h == 1 else 32
+        # (128B swizzle), one thread per row
+        self.box_bytes = 128
         self.stage_bytes = sm_warps * 32 * self.box_bytes
-        # with two threads per row: the partial row maxima and row sums they exchange
-        self.xchg_bytes = 2 * self.qt * self.h * BM * 4 if self.h == 2 else 0
         self.smem = (self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + self.stage_bytes
-                     + self.xchg_bytes + 1024 + 256)
+                     + 1024 + 256)
         self.tiles = heads * (Sq // (BM * self.qt))
 
     # ---- recognition -------------------------------------------------------------
@@ -187,7 +180,7 @@ class TcAttention(TunedKernel):
         o_box = (self.box_bytes // 2, 32)                 # one warp's staging box of the output
         maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
                 tm("thc_tmap_v", self.pv, self.heads * self.Sk),
-                tm("thc_tmap_o", self.pout, self.heads * self.Sq, o_box, 3 if self.h == 1 else 0)]
+                tm("thc_tmap_o", self.pout, self.heads * self.Sq, o_box, 3)]
         return {"grid": [min(self.tiles, SM_COUNT), 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
                 "tmaps": maps, "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
                 "error_word": "thc_error", "tile": [BM * self.qt, BN, D], "stages": [self.ks, self.vs]}
@@ -233,15 +226,15 @@ class TcAttention(TunedKernel):
         ins(f"add.u32 {base}, {base}, 1023")
         ins(f"and.b32 {base}, {base}, -1024")
         # shared: Q tiles (QT of them) | K ring | V ring | output staging (one 32-row box per
-        # softmax warp) | exchanged row maxima and sums (two threads per row) | barriers
-        H = self.h
+        # softmax warp) | barriers
+        PP = self.p_parts
+        assert PP in (1, 2, 4)
         q_s = base
-        k0, v0, stage0, xchg, bars = t("b32"), t("b32"), t("b32"), t("b32"), t("b32")
+        k0, v0, stage0, bars = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"add.u32 {k0}, {base}, {QT * qb}")
         ins(f"add.u32 {v0}, {base}, {QT * qb + KS * kvb}")
         ins(f"add.u32 {stage0}, {base}, {QT * qb + (KS + VS) * kvb}")
-        ins(f"add.u32 {xchg}, {stage0}, {self.stage_bytes}")
-        ins(f"add.u32 {bars}, {xchg}, {self.xchg_bytes}")
+        ins(f"add.u32 {bars}, {stage0}, {self.stage_bytes}")
         nb = 0
 
         def bar() -> int:
@@ -252,14 +245,13 @@ class TcAttention(TunedKernel):
         k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
         v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
         s_full = [bar() for _ in range(QT)]
-        p_full = [bar() for _ in range(QT)]
+        # p_full[h][g]: part h of P_g (keys 128 h / PP ..) stored by group g's 128 softmax threads
+        p_full = [[bar() for _ in range(QT)] for _ in range(PP)]
         o_done = [bar() for _ in range(QT)]
         o_free = [bar() for _ in range(QT)]
-        mx_full = [bar() for _ in range(QT)] if H == 2 else []     # both halves' row maxima written
-        l_full = [bar() for _ in range(QT)] if H == 2 else []      # both halves' row sums written
         counts = {o: 1 for o in range(0, nb * 8, 8)}
-        for o in p_full + o_free + mx_full + l_full:
-            counts[o] = 128 * H
+        for o in [x for part in p_full for x in part] + o_free:
+            counts[o] = 128
         slot_off = nb * 8
         assert slot_off + 8 <= 256, "barriers outgrow their shared-memory slot"
         p = t("pred")
@@ -422,8 +414,9 @@ class TcAttention(TunedKernel):
             ins("tcgen05.fence::after_thread_sync")
             return ks_, kb_
 
-        def issue_pv(g: int, jj: str, acc0: str, release_v: bool) -> None:
-            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile."""
+        def issue_pv(g: int, jj: str, acc0: str, release_v: bool, pwait) -> None:
+            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile.  The
+            MMAs of each part of the keys go out once ``pwait(h)`` saw that part of P stored."""
             st_, vs_, vb_ = t("b32"), t("b32"), t("b32")
             ins(f"rem.u32 {st_}, {jj}, {VS}")
             ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
@@ -431,12 +424,15 @@ class TcAttention(TunedKernel):
                 vf = t("b32")
                 ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
                 kit.wait(vf, kit.parity(jj, VS), 1)
-            ins("tcgen05.fence::after_thread_sync")
             ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
             vd = kit.desc(vs_, BN * 128, hi)
             dcol = t("b32")
             ins(f"add.u32 {dcol}, {tmem}, {O_COL + 128 * g}")
+            per = BN // 16 // PP
             for kk in range(BN // 16):
+                if kk % per == 0:
+                    pwait(kk // per)
+                    ins("tcgen05.fence::after_thread_sync")
                 a = t("b32")
                 ins(f"add.u32 {a}, {tmem}, {S_COL + 128 * g + 8 * kk}")
                 bb = kit.desc_add(vd, kk * 16 * 128)
@@ -478,8 +474,9 @@ class TcAttention(TunedKernel):
         ins(f"setp.lt.u32 {more}, {nxt}, {total}")
         ins(f"setp.ne.u32 {acc0}, {mblk}, 0")
         ins(f"setp.eq.u32 {newtile}, {mblk}, {n_blk - 1}")           # S(j + 1) opens the next tile
+        mpar = t("b32")
         for g in range(QT):
-            kit.wait(f"{bars}+{p_full[g]}", kit.parity(mj, 1), 1)
+            ins(f"and.b32 {mpar}, {mj}, 1")
             nowait = lab("at_o_ready")
             ins(f"@{acc0} bra {nowait}")
             ins(f"setp.eq.u32 {p}, {mti}, 0")
@@ -488,7 +485,8 @@ class TcAttention(TunedKernel):
             ins(f"sub.u32 {pt}, {mti}, 1")
             kit.wait(f"{bars}+{o_free[g]}", kit.parity(pt, 1), 1)     # the previous tile's O_g was read
             place(nowait)
-            issue_pv(g, mj, acc0, g == QT - 1)
+            issue_pv(g, mj, acc0, g == QT - 1,
+                     lambda h, g=g: kit.wait(f"{bars}+{p_full[h][g]}", mpar, 1))
             if g == 0:
                 nk = lab("at_nok")
                 ins(f"@!{more} bra {nk}")
@@ -518,29 +516,21 @@ class TcAttention(TunedKernel):
         ins(f"@{more} bra {mtop}")
         ins(f"bra {end}")
 
-        # ---------------- softmax + epilogue (warps 0 .. 4 QT H - 1) ----------------
-        # warp w: query tile g = w / 4H, half h = (w / 4) % H of the row's keys and of O's columns,
-        # TMEM lanes 32 (w % 4) .. (= the tile's rows of this thread)
-        KH, DH = BN // H, D // H                       # keys and O columns per thread
+        # ---------------- softmax + epilogue (warps 0 .. 4 QT - 1) ----------------
+        # warp w: query tile g = w / 4, TMEM lanes 32 (w % 4) .. (= the tile's rows of this thread)
         place(role_sm)
         if self.reg_split:
             ins(f"setmaxnreg.inc.sync.aligned.u32 {self.reg_split[0]}")
-        grp, half, quarter, r = t("b32"), t("b32"), t("b32"), t("b32")
-        ins(f"shr.u32 {grp}, {warp}, {2 + (H - 1)}")
-        ins(f"shr.u32 {half}, {warp}, 2")
-        ins(f"and.b32 {half}, {half}, {H - 1}")
+        grp, quarter, r = t("b32"), t("b32"), t("b32")
+        ins(f"shr.u32 {grp}, {warp}, 2")
         ins(f"and.b32 {quarter}, {warp}, 3")
         ins(f"mad.lo.u32 {r}, {quarter}, 32, {lane}")
         trow = t("b32")
         ins(f"shl.b32 {trow}, {quarter}, 21")
         ins(f"add.u32 {trow}, {trow}, {tmem}")
-        ocol, scol, pcol, gb8 = t("b32"), t("b32"), t("b32"), t("b32")
+        ocol, scol, gb8 = t("b32"), t("b32"), t("b32")
         ins(f"mad.lo.u32 {ocol}, {grp}, 128, {trow}")
-        ins(f"mad.lo.u32 {scol}, {half}, {KH}, {ocol}")           # this half's keys' scores
-        ins(f"add.u32 {scol}, {scol}, {S_COL}")
-        ins(f"mad.lo.u32 {pcol}, {half}, {KH // 2}, {ocol}")      # their P (key k in column k / 2)
-        ins(f"add.u32 {pcol}, {pcol}, {S_COL}")
-        ins(f"mad.lo.u32 {ocol}, {half}, {DH}, {ocol}")           # this half's O columns
+        ins(f"add.u32 {scol}, {ocol}, {S_COL}")                  # the row's scores; P (key k in column k / 2)
         ins(f"add.u32 {ocol}, {ocol}, {O_COL}")
         ins(f"mad.lo.u32 {gb8}, {grp}, 8, {bars}")
         rowoff = t("b32")                                  # this thread's query row within the tile pair
@@ -549,17 +539,6 @@ class TcAttention(TunedKernel):
         ins(f"mad.lo.u32 {wstage}, {warp}, {32 * self.box_bytes}, {stage0}")
         ins(f"mad.lo.u32 {srowa}, {lane}, {self.box_bytes}, {wstage}")
         ins(f"and.b32 {r7}, {lane}, 7")
-        if H == 2:
-            # exchange slots: [max | sum][group][half][row] f32
-            xmine, xpart, xi = t("b32"), t("b32"), t("b32")
-            ins(f"mad.lo.u32 {xi}, {grp}, 2, {half}")
-            ins(f"mad.lo.u32 {xi}, {xi}, {BM}, {r}")
-            ins(f"mad.lo.u32 {xmine}, {xi}, 4, {xchg}")
-            ins(f"xor.b32 {xi}, {half}, 1")
-            ins(f"mad.lo.u32 {xpart}, {grp}, 2, {xi}")
-            ins(f"mad.lo.u32 {xpart}, {xpart}, {BM}, {r}")
-            ins(f"mad.lo.u32 {xpart}, {xpart}, 4, {xchg}")
-            sum_off = QT * 2 * BM * 4
         lead = t("pred")
         ins(f"setp.eq.u32 {lead}, {lane}, 0")
         tmap_o = t("b64")
@@ -584,25 +563,14 @@ class TcAttention(TunedKernel):
         place(stop)
         kit.wait(f"{gb8}+{s_full[0]}", kit.parity(sj, 1), 2)
         ins("tcgen05.fence::after_thread_sync")
-        # this thread's 128 / H scores of the row into registers: all loads in flight, one wait
-        srow = [t("f32") for _ in range(KH)]
-        for c in range(KH // 32):
+        # the row's 128 scores into registers: all loads in flight, one wait
+        srow = [t("f32") for _ in range(BN)]
+        for c in range(BN // 32):
             a = t("b32")
             ins(f"add.u32 {a}, {scol}, {32 * c}")
             ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(srow[32 * c:32 * c + 32])}}}, [{a}]")
         ins("tcgen05.wait::ld.sync.aligned")
         mx = _tree(em, "max.f32", srow, arity=3)
-        if H == 2:
-            # the two halves' maxima through shared memory; the barrier also orders both halves'
-            # score loads before either half's P stores (half 1's P columns are half 0's scores)
-            ins(f"st.shared.f32 [{xmine}], {mx}")
-            ins("tcgen05.fence::before_thread_sync")
-            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{mx_full[0]}]")
-            kit.wait(f"{gb8}+{mx_full[0]}", kit.parity(sj, 1), 4)
-            ins("tcgen05.fence::after_thread_sync")
-            other = t("f32")
-            ins(f"ld.shared.f32 {other}, [{xpart}]")
-            ins(f"max.f32 {mx}, {mx}, {other}")
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
         norescale, noowait = lab("at_norescale"), lab("at_first")
@@ -618,8 +586,8 @@ class TcAttention(TunedKernel):
         ins(f"sub.u32 {prevb}, {sj}, 1")
         kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
         ins("tcgen05.fence::after_thread_sync")
-        rw = 16 if H == 1 else 8            # columns at a time: the scores hold the registers
-        for c in range(DH // rw):
+        rw = 16                             # columns at a time: the scores hold the registers
+        for c in range(D // rw):
             ov = [t("f32") for _ in range(rw)]
             a = t("b32")
             ins(f"add.u32 {a}, {ocol}, {rw * c}")
@@ -636,14 +604,16 @@ class TcAttention(TunedKernel):
         negm = t("f32")
         ins(f"neg.f32 {negm}, {mref}")
         # P = 2^(s c' - m), 16 scores at a time, written back as f16 pairs over S's first 64 columns
-        # (every score of the row is already in registers, so the stores cannot overtake a load).  Pairs of
-        # scores go through the packed f32x2 FMA pipe; POLY_PAIRS of every 8 pairs take 2^x from
-        # a polynomial on that pipe instead of the MUFU unit.
+        # (every score of the row is already in registers, so the stores cannot overtake a load).
+        # Pairs of scores go through the packed f32x2 FMA pipe; poly_pairs of every 8 pairs take
+        # 2^x from a polynomial on that pipe instead of the MUFU unit.  Each part of P is handed to
+        # the MMA warp as soon as it is stored.
         pair = t("b64"), t("b64")
         ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
         ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
-        ex2 = _Exp2(em) if POLY_PAIRS else None
-        for c in range(KH // 16):
+        ex2 = _Exp2(em) if self.poly_pairs else None
+        chunks = BN // 16
+        for c in range(chunks):
             sv = srow[16 * c:16 * c + 16]
             packs = []
             for k in range(8):
@@ -651,7 +621,7 @@ class TcAttention(TunedKernel):
                 d = t("b64")
                 ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
                 ins(f"fma.rn.ftz.f32x2 {d}, {d}, {pair[0]}, {pair[1]}")
-                if k < POLY_PAIRS:
+                if k < self.poly_pairs:
                     d = ex2.pair(d, x0, x1)
                 else:
                     ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
@@ -669,11 +639,12 @@ class TcAttention(TunedKernel):
             for k in range(8):
                 ins(f"cvt.rn.f16x2.f32 {hp[k]}, {sv[2 * k + 1]}, {sv[2 * k]}")
             a2 = t("b32")
-            ins(f"add.u32 {a2}, {pcol}, {8 * c}")
+            ins(f"add.u32 {a2}, {scol}, {8 * c}")
             ins(f"tcgen05.st.sync.aligned.32x32b.x8.b32 [{a2}], {{{', '.join(hp)}}}")
-        ins("tcgen05.wait::st.sync.aligned")
-        ins("tcgen05.fence::before_thread_sync")
-        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[0]}]")
+            if (c + 1) % (chunks // PP) == 0:
+                ins("tcgen05.wait::st.sync.aligned")
+                ins("tcgen05.fence::before_thread_sync")
+                ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[(c + 1) // (chunks // PP) - 1][0]}]")
         ins(f"add.u32 {sj}, {sj}, 1")
         ins(f"add.u32 {blk2}, {blk2}, 1")
         ins(f"setp.lt.u32 {p}, {blk2}, {n_blk}")
@@ -687,83 +658,39 @@ class TcAttention(TunedKernel):
         ins(f"sub.u32 {orow}, {orow}, {lane}")                    # the warp's first row
         lastb = t("b32")
         ins(f"sub.u32 {lastb}, {sj}, 1")
-        if H == 2:
-            # the row sum is the two halves' partial sums (f32 addition commutes: both halves get
-            # the same bits); then O 32 columns at a time, 16 per box (32 x 32 B, unswizzled), lane
-            # 0 storing the box at columns D/2 h + 16 b
-            ins(f"st.shared.f32 [{xmine}+{sum_off}], {l}")
-            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{l_full[0]}]")
-            kit.wait(f"{gb8}+{l_full[0]}", kit.parity(sti, 1), 5)
-            other = t("f32")
-            ins(f"ld.shared.f32 {other}, [{xpart}+{sum_off}]")
-            ins(f"add.rn.f32 {l}, {l}, {other}")
-            inv = t("f32")
-            ins(f"rcp.rn.f32 {inv}, {l}")
-            ocol0 = t("b32")
-            ins(f"mul.lo.u32 {ocol0}, {half}, {DH}")
-            kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
-            ins("tcgen05.fence::after_thread_sync")
-            for c in range(DH // 32):
-                ov = [t("f32") for _ in range(32)]
-                a = t("b32")
-                ins(f"add.u32 {a}, {ocol}, {32 * c}")
-                ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{a}]")
-                ins("tcgen05.wait::ld.sync.aligned")
-                if c == DH // 32 - 1:
-                    ins("tcgen05.fence::before_thread_sync")
-                    ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
-                for b in range(2):
-                    ins(f"@{lead} cp.async.bulk.wait_group.read 0")
-                    ins("bar.warp.sync -1")
-                    oh = [t("b32") for _ in range(8)]
-                    for k in range(8):
-                        x0, x1 = ov[16 * b + 2 * k], ov[16 * b + 2 * k + 1]
-                        ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
-                        ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
-                        ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
-                    ins(f"st.shared.v4.b32 [{srowa}], {{{', '.join(oh[:4])}}}")
-                    ins(f"st.shared.v4.b32 [{srowa}+16], {{{', '.join(oh[4:])}}}")
-                    ins("fence.proxy.async.shared::cta")
-                    ins("bar.warp.sync -1")
-                    oc = t("b32")
-                    ins(f"add.u32 {oc}, {ocol0}, {32 * c + 16 * b}")
-                    ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
-                        f"{{{oc}, {orow}}}], [{wstage}]")
-                    ins(f"@{lead} cp.async.bulk.commit_group")
-        else:
-            kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
-            ins("tcgen05.fence::after_thread_sync")
-            ov = [t("f32") for _ in range(D)]
-            for c in range(D // 32):
-                a = t("b32")
-                ins(f"add.u32 {a}, {ocol}, {32 * c}")
-                ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
-            ins("tcgen05.wait::ld.sync.aligned")
-            ins("tcgen05.fence::before_thread_sync")
-            ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
-            inv = t("f32")
-            ins(f"rcp.rn.f32 {inv}, {l}")
-            # 64 columns at a time: this row's 128 bytes into the warp's 32 x 128 B box (16-byte chunk
-            # c of row r at chunk c ^ (r % 8): the 128-byte swizzle, conflict-free)
-            for hb in range(D // 64):
-                ins(f"@{lead} cp.async.bulk.wait_group.read 0")
-                ins("bar.warp.sync -1")
-                for c in range(8):
-                    oh = [t("b32") for _ in range(4)]
-                    for k in range(4):
-                        x0, x1 = ov[64 * hb + 8 * c + 2 * k], ov[64 * hb + 8 * c + 2 * k + 1]
-                        ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
-                        ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
-                        ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
-                    ch = t("b32")
-                    ins(f"xor.b32 {ch}, {r7}, {c}")
-                    ins(f"mad.lo.u32 {ch}, {ch}, 16, {srowa}")
-                    ins(f"st.shared.v4.b32 [{ch}], {{{', '.join(oh)}}}")
-                ins("fence.proxy.async.shared::cta")
-                ins("bar.warp.sync -1")
-                ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
-                    f"{{{64 * hb}, {orow}}}], [{wstage}]")
-                ins(f"@{lead} cp.async.bulk.commit_group")
+        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
+        ins("tcgen05.fence::after_thread_sync")
+        ov = [t("f32") for _ in range(D)]
+        for c in range(D // 32):
+            a = t("b32")
+            ins(f"add.u32 {a}, {ocol}, {32 * c}")
+            ins(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov[32 * c:32 * c + 32])}}}, [{a}]")
+        ins("tcgen05.wait::ld.sync.aligned")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{o_free[0]}]")
+        inv = t("f32")
+        ins(f"rcp.rn.f32 {inv}, {l}")
+        # 64 columns at a time: this row's 128 bytes into the warp's 32 x 128 B box (16-byte chunk
+        # c of row r at chunk c ^ (r % 8): the 128-byte swizzle, conflict-free)
+        for hb in range(D // 64):
+            ins(f"@{lead} cp.async.bulk.wait_group.read 0")
+            ins("bar.warp.sync -1")
+            for c in range(8):
+                oh = [t("b32") for _ in range(4)]
+                for k in range(4):
+                    x0, x1 = ov[64 * hb + 8 * c + 2 * k], ov[64 * hb + 8 * c + 2 * k + 1]
+                    ins(f"mul.rn.f32 {x0}, {x0}, {inv}")
+                    ins(f"mul.rn.f32 {x1}, {x1}, {inv}")
+                    ins(f"cvt.rn.f16x2.f32 {oh[k]}, {x1}, {x0}")
+                ch = t("b32")
+                ins(f"xor.b32 {ch}, {r7}, {c}")
+                ins(f"mad.lo.u32 {ch}, {ch}, 16, {srowa}")
+                ins(f"st.shared.v4.b32 [{ch}], {{{', '.join(oh)}}}")
+            ins("fence.proxy.async.shared::cta")
+            ins("bar.warp.sync -1")
+            ins(f"@{lead} cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [{tmap_o}, "
+                f"{{{64 * hb}, {orow}}}], [{wstage}]")
+            ins(f"@{lead} cp.async.bulk.commit_group")
         ins(f"add.u32 {sti}, {sti}, 1")
         ins(f"add.u32 {stile}, {stile}, {ncta}")
         ins(f"setp.lt.u32 {p}, {sti}, {nt}")

@@ -43,10 +43,9 @@ meta.json's launch.
 
 from __future__ import annotations
 
-import os
-
 from thompiler import ir
 from thompiler.families.base import TunedKernel
+from thompiler.families.tuning import TUNING
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
@@ -87,7 +86,7 @@ class TcMatmul(TunedKernel):
         self.staging = EPI_WARPS * 2 * STAGE_TILE        # per-warp double-buffered store staging
         room = SMEM_LIMIT - static_smem - 2048 - self.staging
         self.stages = max(2, min(6, room // stage))
-        forced = int(os.environ.get("THOMPILER_MATMUL_STAGES", "0"))   # tuning knob
+        forced = TUNING.matmul_stages
         if 2 <= forced <= room // stage:
             self.stages = forced
         self.smem = self.stages * stage + self.staging + 1024 + 256
@@ -100,14 +99,14 @@ class TcMatmul(TunedKernel):
         # a part must be long enough to pay for its partial's round trip through L2: the last part
         # to arrive reads all `parts` partials (128 KB each at N = 256), so at least 16 K blocks
         parts = min(kblocks // 16, SM_COUNT // rem) if rem else 1
-        if S != 1 or c.ty is not F32 or parts < 2 or os.environ.get("THOMPILER_MATMUL_SPLIT_TAIL") == "0":
+        if S != 1 or c.ty is not F32 or parts < 2 or not TUNING.matmul_split_tail:
             rem, parts = 0, 1
         self.rem, self.parts = rem, parts
         self.full_tiles = self.tiles - rem
         self.units = self.full_tiles + rem * parts
 
     def pick_bn(self) -> int:
-        forced = int(os.environ.get("THOMPILER_MATMUL_BN", "0"))     # tuning knob: force the tile width
+        forced = TUNING.matmul_bn                                   # force the tile width
         if forced and self.N % forced == 0 and forced % 16 == 0 and 16 <= forced <= 256:
             return forced
         best, best_score = None, -1.0

@@ -28,11 +28,10 @@ No TMA load uses cluster multicast: each CTA loads its own halves.
 
 from __future__ import annotations
 
-import os
-
 from thompiler.families.kit import Kit, desc_hi, idesc_f16
 from thompiler.families.matmul import BK, BM, EPI_WARPS, SM_COUNT, STAGE_TILE, TcMatmul
 from thompiler.families.base import TunedKernel
+from thompiler.families.tuning import TUNING
 from thompiler.load import KernelInfo
 from thompiler.lowering.types import F32
 
@@ -47,7 +46,7 @@ class TcMatmulPair(TcMatmul):
 
     @classmethod
     def match(cls, kernel: KernelInfo):
-        if os.environ.get("THOMPILER_MATMUL_PAIR", "1") == "0":     # the single-CTA kernel instead
+        if not TUNING.matmul_pair:                                  # the single-CTA kernel instead
             return None
         one = TcMatmul.match.__func__(TcMatmul, kernel)
         if one is None or one.M % PM or kernel.grid[0] % 2:
@@ -59,7 +58,7 @@ class TcMatmulPair(TcMatmul):
 
     @staticmethod
     def pair_bn(M: int, N: int, S: int) -> int | None:
-        forced = int(os.environ.get("THOMPILER_MATMUL_BN", "0"))     # tuning knob
+        forced = TUNING.matmul_bn
         if forced in (128, 256) and N % forced == 0:
             return forced
         for bn in (256, 128):
@@ -82,7 +81,7 @@ class TcMatmulPair(TcMatmul):
         self.staging = EPI_WARPS * 2 * STAGE_TILE
         room = SMEM_LIMIT - static_smem - 2048 - self.staging
         self.stages = max(2, min(8, room // stage))
-        forced = int(os.environ.get("THOMPILER_MATMUL_STAGES", "0"))
+        forced = TUNING.matmul_stages
         if 2 <= forced <= room // stage:
             self.stages = forced
         self.smem = self.stages * stage + self.staging + 1024 + 256
@@ -92,7 +91,7 @@ class TcMatmulPair(TcMatmul):
         kblocks = self.Ks // BK
         rem = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
         parts = min(kblocks // 16, PAIR_SLOTS // rem) if rem else 1
-        if S != 1 or c.ty is not F32 or parts < 2 or os.environ.get("THOMPILER_MATMUL_SPLIT_TAIL") == "0":
+        if S != 1 or c.ty is not F32 or parts < 2 or not TUNING.matmul_split_tail:
             rem, parts = 0, 1
         self.rem, self.parts = rem, parts
         self.full_tiles = self.tiles - rem
