@@ -47,10 +47,9 @@ def test_attention_plan_benchmark_shape(tmp_path, monkeypatch):
     assert fam.smem == 2 * 32768 + 4 * 32768 + fam.stage_bytes + 1024 + 256 <= 227 * 1024
     ptx = fam.emit()
     assert ".maxnreg 168" in ptx and "setmaxnreg.inc.sync.aligned.u32 224" in ptx
-    # P reaches the MMA warp in two parts per group: four barriers of 128 arrivals (the softmax
-    # threads of one group), besides the two of O's release
+    # P handed over and O released by the 128 softmax threads of a group: four barriers of 128
     inits = re.findall(r"mbarrier\.init\.shared::cta\.b64 \[[^\]]+\], (\d+);", ptx)
-    assert fam.p_parts == 2 and inits.count("128") == 2 * 2 + 2
+    assert inits.count("128") == 2 + 2
 
 
 @pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 192), ((2, 2, 384, 64), 1, 192),

@@ -23,9 +23,6 @@ CASES = [
     ("attention", synth.attention_package, (1, 2, 384, 128), {}),
     ("attention", synth.attention_package, (2, 2, 512, 64), {}),
     ("attention", synth.attention_package, (1, 1, 128, 64), {}),
-    ("attention p_parts=1", synth.attention_package, (8, 16, 2048, 128), {"attention_p_parts": 1}),
-    ("attention p_parts=4", synth.attention_package, (8, 16, 2048, 128), {"attention_p_parts": 4}),
-    ("attention poly", synth.attention_package, (8, 16, 2048, 128), {"attention_poly_pairs": 2}),
     ("matmul single CTA", synth.matmul_package, (4096, 4096, 4096), {"matmul_pair": False}),
     ("matmul", synth.matmul_package, (4096, 4096, 4096), {}),
     ("matmul", synth.matmul_package, (8192, 3072, 1024), {}),

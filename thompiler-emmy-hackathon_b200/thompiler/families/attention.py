@@ -27,11 +27,7 @@ written over the first 64 columns of S_g.  Softmax per row and key block: the
 128 scores in registers (four loads, one wait), a three-input max tree, O and
 the running sum rescaled only when the max grew by more than 2^8 (P <= 256
 stays exact in f16, the rescale is rare), P = 2^(s c' - m) with packed f32x2
-FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  P goes to
-the MMA warp in P_PARTS parts along the keys, each under its own mbarrier:
-O_g += P_g V for the first keys starts while the exponentials of the last
-ones still run, so the softmax chain of a group (S ready -> P stored) hides
-behind the other group's MMAs.  Epilogue: O / l as f16 through each warp's
+FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  Epilogue: O / l as f16 through each warp's
 own 32-row staging box (128B-swizzled), one TMA store per box.
 Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
 exactly as the IR's exp lowering.  All mbarrier waits are bounded
@@ -45,7 +41,6 @@ import math
 from thompiler import ir
 from thompiler.families.base import TunedKernel
 from thompiler.families.kit import Kit, desc_hi, idesc_f16
-from thompiler.families.tuning import TUNING
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
@@ -66,9 +61,6 @@ class TcAttention(TunedKernel):
         super().__init__(kernel)
         self.pq, self.pk, self.pv, self.pout, self.pscale = q, k, v, out, scale
         self.heads, self.Sq, self.Sk, self.D = heads, Sq, Sk, D
-        # P handed to the MMA warp in this many parts along the keys (1, 2 or 4); of every 8
-        # score pairs, poly_pairs take 2^x from a polynomial on the FMA pipe (0 .. 8)
-        self.p_parts, self.poly_pairs = TUNING.attention_p_parts, TUNING.attention_poly_pairs
         self.q_bytes = BM * D * 2
         self.kv_bytes = BN * D * 2
         # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
@@ -227,8 +219,6 @@ class TcAttention(TunedKernel):
         ins(f"and.b32 {base}, {base}, -1024")
         # shared: Q tiles (QT of them) | K ring | V ring | output staging (one 32-row box per
         # softmax warp) | barriers
-        PP = self.p_parts
-        assert PP in (1, 2, 4)
         q_s = base
         k0, v0, stage0, bars = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"add.u32 {k0}, {base}, {QT * qb}")
@@ -245,12 +235,11 @@ class TcAttention(TunedKernel):
         k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
         v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
         s_full = [bar() for _ in range(QT)]
-        # p_full[h][g]: part h of P_g (keys 128 h / PP ..) stored by group g's 128 softmax threads
-        p_full = [[bar() for _ in range(QT)] for _ in range(PP)]
+        p_full = [bar() for _ in range(QT)]              # P_g stored by group g's 128 softmax threads
         o_done = [bar() for _ in range(QT)]
         o_free = [bar() for _ in range(QT)]
         counts = {o: 1 for o in range(0, nb * 8, 8)}
-        for o in [x for part in p_full for x in part] + o_free:
+        for o in p_full + o_free:
             counts[o] = 128
         slot_off = nb * 8
         assert slot_off + 8 <= 256, "barriers outgrow their shared-memory slot"
@@ -414,9 +403,8 @@ class TcAttention(TunedKernel):
             ins("tcgen05.fence::after_thread_sync")
             return ks_, kb_
 
-        def issue_pv(g: int, jj: str, acc0: str, release_v: bool, pwait) -> None:
-            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile.  The
-            MMAs of each part of the keys go out once ``pwait(h)`` saw that part of P stored."""
+        def issue_pv(g: int, jj: str, acc0: str, release_v: bool) -> None:
+            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile."""
             st_, vs_, vb_ = t("b32"), t("b32"), t("b32")
             ins(f"rem.u32 {st_}, {jj}, {VS}")
             ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
@@ -424,15 +412,12 @@ class TcAttention(TunedKernel):
                 vf = t("b32")
                 ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
                 kit.wait(vf, kit.parity(jj, VS), 1)
+            ins("tcgen05.fence::after_thread_sync")
             ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
             vd = kit.desc(vs_, BN * 128, hi)
             dcol = t("b32")
             ins(f"add.u32 {dcol}, {tmem}, {O_COL + 128 * g}")
-            per = BN // 16 // PP
             for kk in range(BN // 16):
-                if kk % per == 0:
-                    pwait(kk // per)
-                    ins("tcgen05.fence::after_thread_sync")
                 a = t("b32")
                 ins(f"add.u32 {a}, {tmem}, {S_COL + 128 * g + 8 * kk}")
                 bb = kit.desc_add(vd, kk * 16 * 128)
@@ -474,9 +459,8 @@ class TcAttention(TunedKernel):
         ins(f"setp.lt.u32 {more}, {nxt}, {total}")
         ins(f"setp.ne.u32 {acc0}, {mblk}, 0")
         ins(f"setp.eq.u32 {newtile}, {mblk}, {n_blk - 1}")           # S(j + 1) opens the next tile
-        mpar = t("b32")
         for g in range(QT):
-            ins(f"and.b32 {mpar}, {mj}, 1")
+            kit.wait(f"{bars}+{p_full[g]}", kit.parity(mj, 1), 1)
             nowait = lab("at_o_ready")
             ins(f"@{acc0} bra {nowait}")
             ins(f"setp.eq.u32 {p}, {mti}, 0")
@@ -485,8 +469,7 @@ class TcAttention(TunedKernel):
             ins(f"sub.u32 {pt}, {mti}, 1")
             kit.wait(f"{bars}+{o_free[g]}", kit.parity(pt, 1), 1)     # the previous tile's O_g was read
             place(nowait)
-            issue_pv(g, mj, acc0, g == QT - 1,
-                     lambda h, g=g: kit.wait(f"{bars}+{p_full[h][g]}", mpar, 1))
+            issue_pv(g, mj, acc0, g == QT - 1)
             if g == 0:
                 nk = lab("at_nok")
                 ins(f"@!{more} bra {nk}")
@@ -605,15 +588,11 @@ class TcAttention(TunedKernel):
         ins(f"neg.f32 {negm}, {mref}")
         # P = 2^(s c' - m), 16 scores at a time, written back as f16 pairs over S's first 64 columns
         # (every score of the row is already in registers, so the stores cannot overtake a load).
-        # Pairs of scores go through the packed f32x2 FMA pipe; poly_pairs of every 8 pairs take
-        # 2^x from a polynomial on that pipe instead of the MUFU unit.  Each part of P is handed to
-        # the MMA warp as soon as it is stored.
+        # Pairs of scores go through the packed f32x2 FMA pipe.
         pair = t("b64"), t("b64")
         ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
         ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
-        ex2 = _Exp2(em) if self.poly_pairs else None
-        chunks = BN // 16
-        for c in range(chunks):
+        for c in range(BN // 16):
             sv = srow[16 * c:16 * c + 16]
             packs = []
             for k in range(8):
@@ -621,14 +600,11 @@ class TcAttention(TunedKernel):
                 d = t("b64")
                 ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
                 ins(f"fma.rn.ftz.f32x2 {d}, {d}, {pair[0]}, {pair[1]}")
-                if k < self.poly_pairs:
-                    d = ex2.pair(d, x0, x1)
-                else:
-                    ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
-                    ins(f"ex2.approx.ftz.f32 {x0}, {x0}")
-                    ins(f"ex2.approx.ftz.f32 {x1}, {x1}")
-                    d = t("b64")
-                    ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
+                ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
+                ins(f"ex2.approx.ftz.f32 {x0}, {x0}")
+                ins(f"ex2.approx.ftz.f32 {x1}, {x1}")
+                d = t("b64")
+                ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
                 packs.append(d)
             sp = _tree(em, "add.rn.f32x2", packs, kind="b64")
             lo, hi2 = t("f32"), t("f32")
@@ -641,10 +617,9 @@ class TcAttention(TunedKernel):
             a2 = t("b32")
             ins(f"add.u32 {a2}, {scol}, {8 * c}")
             ins(f"tcgen05.st.sync.aligned.32x32b.x8.b32 [{a2}], {{{', '.join(hp)}}}")
-            if (c + 1) % (chunks // PP) == 0:
-                ins("tcgen05.wait::st.sync.aligned")
-                ins("tcgen05.fence::before_thread_sync")
-                ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[(c + 1) // (chunks // PP) - 1][0]}]")
+        ins("tcgen05.wait::st.sync.aligned")
+        ins("tcgen05.fence::before_thread_sync")
+        ins(f"mbarrier.arrive.shared::cta.b64 _, [{gb8}+{p_full[0]}]")
         ins(f"add.u32 {sj}, {sj}, 1")
         ins(f"add.u32 {blk2}, {blk2}, 1")
         ins(f"setp.lt.u32 {p}, {blk2}, {n_blk}")
@@ -711,53 +686,6 @@ class TcAttention(TunedKernel):
 def _f32bits(x: float) -> str:
     import struct
     return "%08X" % struct.unpack("<I", struct.pack("<f", x))[0]
-
-
-class _Exp2:
-    """2^x for a pair of f32 lanes on the FMA pipe (packed f32x2), in place of ex2.approx.
-
-    x is clamped to >= -125 (below that the result is ~2^-125, which rounds to 0 in the
-    f16 P tile), split as x = j + f with j = round(x) (adding and subtracting 1.5 * 2^23)
-    and |f| <= 1/2; 2^f comes from a degree-3 polynomial fitted here for least maximum
-    relative error on [-1/2, 1/2] (7.5e-5 evaluated in f32, below f16's 2^-11 rounding),
-    and j is added into the exponent field as an integer (j << 23).
-    """
-
-    COEF = (0.9999280727914258, 0.6932609870112008, 0.24261113509452387, 0.055171666814684134)
-
-    def __init__(self, em):
-        self.em = em
-        self.k = []
-        for v in (12582912.0,) + self.COEF:
-            r = em.tmp("b64")
-            h = _f32bits(v)
-            em.ins(f"mov.b64 {r}, 0x{h}{h}")
-            self.k.append(r)
-
-    def pair(self, d: str, x0: str, x1: str) -> str:
-        em, ins = self.em, self.em.ins
-        mag, c0, c1, c2, c3 = self.k
-        ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
-        ins(f"max.f32 {x0}, {x0}, 0fC2FA0000")
-        ins(f"max.f32 {x1}, {x1}, 0fC2FA0000")
-        x, tj, f, p = em.tmp("b64"), em.tmp("b64"), em.tmp("b64"), em.tmp("b64")
-        ins(f"mov.b64 {x}, {{{x0}, {x1}}}")
-        ins(f"add.rn.f32x2 {tj}, {x}, {mag}")
-        ins(f"sub.rn.f32x2 {f}, {tj}, {mag}")
-        ins(f"sub.rn.f32x2 {f}, {x}, {f}")
-        ins(f"fma.rn.f32x2 {p}, {f}, {c3}, {c2}")
-        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c1}")
-        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c0}")
-        j0, j1, p0, p1 = (em.tmp("b32") for _ in range(4))
-        ins(f"mov.b64 {{{j0}, {j1}}}, {tj}")
-        ins(f"mov.b64 {{{p0}, {p1}}}, {p}")
-        for j, q, x_ in ((j0, p0, x0), (j1, p1, x1)):
-            ins(f"shl.b32 {j}, {j}, 23")
-            ins(f"add.s32 {q}, {q}, {j}")
-            ins(f"mov.b32 {x_}, {q}")
-        r = em.tmp("b64")
-        ins(f"mov.b64 {r}, {{{x0}, {x1}}}")
-        return r
 
 
 def _tree(em, op: str, regs: list[str], arity: int = 2, kind: str = "f32") -> str:

@@ -22,10 +22,6 @@ class Tuning:
     matmul_stages: int = 0
     # cut a partial last wave of matmul tiles along K
     matmul_split_tail: bool = True
-    # attention: P handed to the MMA warp in this many parts along the keys (1, 2 or 4)
-    attention_p_parts: int = 2
-    # attention: of every 8 score pairs, this many take 2^x from a polynomial on the FMA pipe
-    attention_poly_pairs: int = 0
 
 
 TUNING = Tuning()
