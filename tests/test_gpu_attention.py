@@ -102,3 +102,32 @@ def test_attention_benchmark_shape(tmp_path):
     ref64 = _sdpa64(q[0, :2].cpu().numpy(), kk[0, :2].cpu().numpy(), v[0, :2].cpu().numpy())
     np.testing.assert_allclose(o[0, :2].float().cpu().numpy(), ref64, rtol=RTOL, atol=ATOL)
     k.close()
+
+
+@pytest.mark.parametrize("grid", [None, 3])
+def test_attention_rescale_in_part_of_a_warp(tmp_path, grid):
+    """Rows whose running maximum jumps in a later key block rescale O and the running sum; here
+    the lanes of a warp disagree: keys 400-403 of each head are set to 1.2 q_r for query rows r =
+    0, 5, 17 and 31 (scores about 13.6 there against about N(0, 1) elsewhere), so in key block 3
+    only those rows of warp 0 grow by more than 2^8.  The warp takes the rescale path together
+    (the other lanes with a factor of 1) and every row matches the float64 expression."""
+    import torch
+    shape = (1, 2, 1024, 128)
+    d = synth.attention_package(tmp_path / "att", *shape)
+    k = DeviceKernel(d / "k_attention.ir.json")
+    if grid:
+        k.plan.grid = (grid, 1, 1)
+    g = torch.Generator(device="cuda").manual_seed(19)
+    q, kk, v = (torch.randn(*shape, device="cuda", generator=g) for _ in range(3))
+    for i, r in enumerate((0, 5, 17, 31)):
+        kk[0, :, 400 + i] = 1.2 * q[0, :, r]
+    q, kk, v = q.half(), kk.half(), v.half()
+    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
+    o = torch.full(shape, float("nan"), device="cuda", dtype=torch.float16)
+    k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(), "attn": o.data_ptr()},
+      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert k.error_word() == 0
+    ref = _sdpa64(q.cpu().numpy(), kk.cpu().numpy(), v.cpu().numpy())
+    np.testing.assert_allclose(o.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
+    k.close()

@@ -117,3 +117,43 @@ def test_matmul_split_tail(tmp_path, monkeypatch, grid):
     assert (outs[0].double() - ref).abs().max().item() < 1e-4
     assert torch.equal(outs[0], outs[1])                 # the part order fixes the rounding
     k.close()
+
+
+def test_split_tail_counters_cleared_after_a_give_up(tmp_path, monkeypatch):
+    """A bounded wait that gives up can leave a split-tail (tile, rank) counter part-way through
+    its count.  The failure is made on the host: the counter of tail tile 0 is set to 1 (one of
+    its two parts arrived) and the error word to the wait's code, as a give-up would leave them.
+    A launch on new data then takes the wrong part as the last and adds a stale partial; after
+    ``clear_error`` (error word and counters zeroed) the next launch is right again."""
+    import ctypes
+
+    import torch
+    monkeypatch.setattr(TUNING, "matmul_pair", False)
+    M, N, K = 2048, 2560, 2048
+    d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
+    k = DeviceKernel(d / "k_matmul_f16.ir.json")
+    assert k.plan.counters == ["thc_tile_arrivals"]
+    g = torch.Generator(device="cuda").manual_seed(6)
+    a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
+    b1, b2 = ((torch.randn(N, K, device="cuda", generator=g) * 0.02).half() for _ in range(2))
+    c = torch.empty(M, N, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run(b):
+        c.fill_(float("nan"))
+        k({"x0": a.data_ptr(), "x1": b.data_ptr(), "matmul": c.data_ptr()}, s)
+        torch.cuda.synchronize()
+        return (c.double() - a.double() @ b.double().t()).abs().max().item()
+
+    assert run(b1) < 1e-4 and k.error_word() == 0
+    lib = runner.library()
+    for name, val in (("thc_tile_arrivals", 1), ("thc_error", 1 << 2)):
+        dst, _ = k.module.global_ptr(name)
+        v = ctypes.c_uint32(val)
+        runner.check(lib.thr_memcpy_htod(dst, ctypes.byref(v), 4, 0), name)
+    runner.check(lib.thr_synchronize(), "sync")
+    assert run(b2) > 1e-3                                  # the stale partial of tail tile 0
+    k.clear_error()
+    assert k.error_word() == 0
+    assert run(b2) < 1e-4 and run(b1) < 1e-4
+    k.close()

@@ -58,6 +58,38 @@ def test_noalloc_sum_matches_the_compiled_kernel(tmp_path, n):
     k.close()
 
 
+@pytest.mark.parametrize("n,ctas", [(1 << 24, 4096), (3, 1), (1, 1), (4097, 4096)])
+def test_noalloc_explicit_cta_counts(n, ctas):
+    """Explicit CTA counts, twice each: 4096 fills the whole partials array (the last CTA folds 16
+    partials per thread); one CTA with fewer than 4 elements is all tail; 4096 CTAs over 4097
+    elements leave most CTAs without a chunk.  Against the float64 sum of the same f32 data."""
+    import torch
+    runner.init(0)
+    g = torch.Generator(device="cuda").manual_seed(n + ctas)
+    x = torch.rand(n, device="cuda", generator=g) * 2 - 1
+    out = torch.full((2,), float("nan"), device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    f = entry()
+    for i in range(2):
+        st = f(x.data_ptr(), n, out.data_ptr() + 4 * i, ctas, stream)
+        assert st == 0, runner.last_error()
+    torch.cuda.synchronize()
+    exact = float(np.sum(x.cpu().numpy(), dtype=np.float64))
+    l2 = float(np.linalg.norm(x.cpu().numpy().astype(np.float64)))
+    for v in out.cpu().numpy():
+        assert abs(float(v) - exact) <= RTOL * max(1.0, l2), (v, exact)
+
+
+def test_noalloc_rejects_unaligned_pointers():
+    import torch
+    runner.init(0)
+    x = torch.zeros(1024, device="cuda")
+    out = torch.zeros(2, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert entry()(x.data_ptr() + 4, 1000, out.data_ptr(), 0, s) == 4 and "16-byte" in runner.last_error()
+    assert entry()(x.data_ptr(), 1024, out.data_ptr() + 2, 0, s) == 4 and "4-byte" in runner.last_error()
+
+
 def test_noalloc_rejects_more_ctas_than_its_scratch():
     import torch
     runner.init(0)

@@ -13,9 +13,12 @@
 //
 // Set-up: the first call on each device (with that device current) asks the
 // runtime for the device address of the array with cudaGetSymbolAddress and
-// caches it; in host code the array's name is only a host-side stand-in, so
-// the kernel always receives the looked-up address.  Make that first call
-// before any stream capture.
+// caches it with the current context's ID; in host code the array's name is
+// only a host-side stand-in, so the kernel always receives the looked-up
+// address.  A call that finds another context current (the first call after
+// a cudaDeviceReset, which destroys the context and the module that held the
+// array) looks the address up again.  Make the first call on a device, and
+// the first after a reset, before any stream capture.
 //
 // Sharing: every call uses the same array and leaves its contents behind.
 // The arrival counter, which must start at zero, is cleared on the stream
@@ -23,6 +26,7 @@
 // Calls whose kernels overlap on the GPU (other streams, other threads)
 // race on the array and give wrong sums: issue them in order on one stream.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -48,8 +52,39 @@ struct SumScratch {
 
 static __device__ __align__(256) SumScratch g_sum_scratch;
 
-SumScratch *g_scratch_ptr[kMaxDevices] = {};
+struct ScratchAddr {
+    SumScratch *ptr = nullptr;
+    unsigned long long ctx_id = 0;    // the context the address belongs to
+};
+ScratchAddr g_scratch[kMaxDevices];
 std::mutex g_setup_mu;
+
+typedef CUresult (*PFN_CtxGetCurrent)(CUcontext *);
+typedef CUresult (*PFN_CtxGetId)(CUcontext, unsigned long long *);
+
+// The current context's unique ID (0 when there is none or the driver lacks cuCtxGetId).
+unsigned long long current_ctx_id() {
+    static PFN_CtxGetCurrent get_current = nullptr;
+    static PFN_CtxGetId get_id = nullptr;
+    static bool looked = false;
+    if (!looked) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_CtxGetCurrent>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_CtxGetId>(f);
+        looked = true;
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 
 __device__ __forceinline__ float block_sum(float v, float *slots) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -115,8 +150,9 @@ extern "C" int thr_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_
         thr_noalloc_set_error(msg);
         return THR_ERR_REQUEST;
     }
-    if (!x || !out || (x & 15)) {
-        thr_noalloc_set_error("thr_sum_f32_noalloc: x and out must be device pointers, x 16-byte aligned");
+    if (!x || !out || (x & 15) || (out & 3)) {
+        thr_noalloc_set_error(
+            "thr_sum_f32_noalloc: x and out must be device pointers, x 16-byte and out 4-byte aligned");
         return THR_ERR_REQUEST;
     }
     int dev = 0;
@@ -128,7 +164,9 @@ extern "C" int thr_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_
     SumScratch *s = nullptr;
     {
         std::lock_guard<std::mutex> lk(g_setup_mu);
-        if (!g_scratch_ptr[dev]) {
+        ScratchAddr &a = g_scratch[dev];
+        unsigned long long ctx = current_ctx_id();
+        if (!a.ptr || !ctx || ctx != a.ctx_id) {
             void *p = nullptr;
             e = cudaGetSymbolAddress(&p, g_sum_scratch);
             if (e != cudaSuccess || !p) {
@@ -136,9 +174,10 @@ extern "C" int thr_sum_f32_noalloc(uint64_t x, uint64_t n, uint64_t out, uint32_
                 thr_noalloc_set_error(m.c_str());
                 return THR_ERR_CUDA;
             }
-            g_scratch_ptr[dev] = static_cast<SumScratch *>(p);
+            a.ptr = static_cast<SumScratch *>(p);
+            a.ctx_id = current_ctx_id();      // the lookup made the device's context current
         }
-        s = g_scratch_ptr[dev];
+        s = a.ptr;
     }
     if (ctas == 0) {
         int sms = 0;

@@ -49,5 +49,13 @@ class DeviceKernel:
             self._tmap_ptrs = dict(ptrs)
         self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, [ptrs[n] for n in self.arg_order], stream)
 
+    def error_word(self) -> int:
+        """The module's error word (0: no bounded wait gave up, no guarded access was skipped)."""
+        return runner.read_error_word(self.module, self.plan)
+
+    def clear_error(self) -> None:
+        """Zero the error word and the family's self-resetting counters (``runner.clear_error_word``)."""
+        runner.clear_error_word(self.module, self.plan)
+
     def close(self) -> None:
         self.module.unload()

@@ -556,12 +556,17 @@ class TcAttention(TunedKernel):
         mx = _tree(em, "max.f32", srow, arity=3)
         mnew = t("f32")
         ins(f"mul.rn.f32 {mnew}, {mx}, {sc}")
+        # a row rescales when its maximum grew by more than 2^8; the warp decides together (the
+        # O rescale is warp-wide tcgen05 work): a lane whose row need not rescale takes alpha = 1
         norescale, noowait = lab("at_norescale"), lab("at_first")
-        ins(f"setp.gt.f32 {p}, {mnew}, {mref8}")
-        ins(f"@!{p} bra {norescale}")
+        grew, anyg = t("pred"), t("pred")
+        ins(f"setp.gt.f32 {grew}, {mnew}, {mref8}")
+        ins(f"vote.sync.any.pred {anyg}, {grew}, -1")
+        ins(f"@!{anyg} bra {norescale}")
         alpha, dm = t("f32"), t("f32")
         ins(f"sub.rn.f32 {dm}, {mref}, {mnew}")
         ins(f"ex2.approx.ftz.f32 {alpha}, {dm}")
+        ins(f"selp.f32 {alpha}, {alpha}, 0f3F800000, {grew}")
         ins(f"mul.rn.f32 {l}, {l}, {alpha}")
         ins(f"setp.eq.u32 {p}, {blk2}, 0")
         ins(f"@{p} bra {noowait}")
@@ -581,8 +586,10 @@ class TcAttention(TunedKernel):
             ins(f"tcgen05.st.sync.aligned.32x32b.x{rw}.b32 [{a}], {{{', '.join(ov)}}}")
         ins("tcgen05.wait::st.sync.aligned")
         place(noowait)
-        ins(f"mov.f32 {mref}, {mnew}")
-        ins(f"add.rn.f32 {mref8}, {mnew}, 0f41000000")
+        m8 = t("f32")
+        ins(f"add.rn.f32 {m8}, {mnew}, 0f41000000")
+        ins(f"selp.f32 {mref}, {mnew}, {mref}, {grew}")
+        ins(f"selp.f32 {mref8}, {m8}, {mref8}, {grew}")
         place(norescale)
         negm = t("f32")
         ins(f"neg.f32 {negm}, {mref}")

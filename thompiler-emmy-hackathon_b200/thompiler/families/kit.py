@@ -9,7 +9,8 @@
   MN-major), N >> 3 at bit 17, M >> 4 at bit 24;
 * bounded mbarrier waits: every wait gives up after ``WAIT_LIMIT`` rounds of
   ``mbarrier.try_wait``, records a code in the module's error word and jumps
-  to the kernel's common exit -- no kernel here can hang its GPU.
+  to the kernel's common exit -- no kernel here can hang its GPU; a wait run
+  by a whole warp makes that decision for all its lanes at once.
 """
 
 from __future__ import annotations
@@ -36,9 +37,15 @@ class Kit:
         self.em, self.errp, self.end = em, errp, end
         self.q = em.tmp("pred")
 
-    def wait(self, bar: str, parity: str, code: int, cluster: bool = False) -> None:
+    def wait(self, bar: str, parity: str, code: int, cluster: bool = False, warp: bool = True) -> None:
         """Bounded wait for the phase of parity ``parity`` of the barrier at ``bar``; ``cluster``
-        acquires at cluster scope (the barrier's arrivals come from the other CTA of a pair)."""
+        acquires at cluster scope (the barrier's arrivals come from the other CTA of a pair).
+
+        ``warp`` (the default): all 32 lanes of the warp run this wait, and they decide together
+        -- the warp leaves the loop once every lane has seen the phase complete (``vote.sync.all``
+        each round), and gives up with all lanes at once, so the warp-wide ``.sync.aligned``
+        instructions after a wait never meet a warp split between the exit and the work.  A wait
+        that a single lane runs passes ``warp=False``."""
         em = self.em
         sem = ".acquire.cluster" if cluster else ""
         top, ok = em.label("wait"), em.label("waited")
@@ -46,6 +53,8 @@ class Kit:
         em.ins(f"mov.u32 {n}, 0")
         em.place(top)
         em.ins(f"mbarrier.try_wait.parity{sem}.shared::cta.b64 {self.q}, [{bar}], {parity}")
+        if warp:
+            em.ins(f"vote.sync.all.pred {self.q}, {self.q}, -1")
         em.ins(f"@{self.q} bra {ok}")
         em.ins(f"add.u32 {n}, {n}, 1")
         em.ins(f"setp.lt.u32 {self.q}, {n}, {WAIT_LIMIT}")

@@ -213,10 +213,13 @@ class TcMatmul(TunedKernel):
         tm_c = {"global": "thc_tmap_c", "param": self.c.name, "dtype": "f32" if esz == 4 else "f16",
                 "dims": [self.N, self.S * self.M], "strides": [self.N * esz], "box": [64 // esz, 32],
                 "swizzle": 2}
-        return {"grid": [self.ctas, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem,
+        side = {"grid": [self.ctas, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem,
                 "tmaps": [tm_a, tm_b, tm_c],
                 "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [a.name, b.name, self.c.name]},
                 "error_word": "thc_error", "tile": [BM, self.BN, BK], "stages": self.stages}
+        if self.rem:
+            side["counters"] = ["thc_tile_arrivals"]           # the split tail's (tile, rank) counters
+        return side
 
     def guard(self, generic: str) -> None:
         em = self.em
@@ -318,13 +321,16 @@ class TcMatmul(TunedKernel):
 
         end = lab("mm_end")
 
-        def wait(bar_addr: str, parity: str, code: int) -> None:
-            """Bounded mbarrier wait; on expiry record ``code`` and leave."""
+        def wait(bar_addr: str, parity: str, code: int, warp: bool = True) -> None:
+            """Bounded mbarrier wait; on expiry record ``code`` and leave.  ``warp``: the whole warp
+            runs it and its lanes leave, or give up, together (as ``Kit.wait``)."""
             top, ok = lab("wait"), lab("waited")
             n = t("b32")
             ins(f"mov.u32 {n}, 0")
             place(top)
             ins(f"mbarrier.try_wait.parity.shared::cta.b64 {q}, [{bar_addr}], {parity}")
+            if warp:
+                ins(f"vote.sync.all.pred {q}, {q}, -1")
             ins(f"@{q} bra {ok}")
             ins(f"add.u32 {n}, {n}, 1")
             ins(f"setp.lt.u32 {q}, {n}, {WAIT_LIMIT}")
@@ -678,7 +684,7 @@ class TcMatmul(TunedKernel):
         ins(f"setp.eq.u32 {lead}, {row}, 0")
         notlead = em.label("tail_notlead")
         ins(f"@!{lead} bra {notlead}")
-        wait(f"{bars}+{done_off}", par, 3)                 # all 128 rows of the partial are stored
+        wait(f"{bars}+{done_off}", par, 3, warp=False)     # all 128 rows of the partial are stored
         old = t("b32")
         ins(f"atom.acq_rel.gpu.global.inc.u32 {old}, [{cnt}], {parts - 1}")
         ins(f"setp.eq.u32 {p}, {old}, {parts - 1}")

@@ -518,7 +518,7 @@ class TcMatmulPair(TcMatmul):
         ins(f"setp.eq.u32 {lead}, {row}, 0")
         notlead = em.label("mp_tail_notlead")
         ins(f"@!{lead} bra {notlead}")
-        kit.wait(f"{bars}+{done_off}", par, 3)                 # all 128 rows of the partial are stored
+        kit.wait(f"{bars}+{done_off}", par, 3, warp=False)     # all 128 rows of the partial are stored
         old = t("b32")
         ins(f"atom.acq_rel.gpu.global.inc.u32 {old}, [{cnt}], {parts - 1}")
         ins(f"setp.eq.u32 {p}, {old}, {parts - 1}")

@@ -225,6 +225,7 @@ class LaunchPlan:
     tmaps: list = field(default_factory=list)       # tensor-map specs the tuned launch reads
     tmap_ptrs: dict | None = None                   # {"global": name, "params": [...]}
     error_word: str | None = None                   # module global a kernel records wait time-outs in
+    counters: list = field(default_factory=list)    # self-resetting arrival counters (module globals)
 
 
 def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> LaunchPlan:
@@ -232,12 +233,14 @@ def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> Launc
     declares (TmaDescriptor statements: the sidecar's ``ir_tmaps``) belong to every launch."""
     side = module.sidecar or {}
     ir_maps = list(side.get("ir_tmaps", []))
+    counters = list(side.get("counters", []))
     if "grid" not in side or honour_meta:
         err = side.get("error_word") if "grid" not in side else None
         return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False,
-                          ir_maps, None, err)
+                          ir_maps, None, err, counters)
     return LaunchPlan(tuple(side["grid"]), tuple(side["block"]), int(side.get("smem_bytes", 0)), True,
-                      list(side.get("tmaps", [])) + ir_maps, side.get("tmap_ptrs"), side.get("error_word"))
+                      list(side.get("tmaps", [])) + ir_maps, side.get("tmap_ptrs"), side.get("error_word"),
+                      counters)
 
 
 def encode_tensor_map(spec: dict, base: int) -> bytes:
@@ -278,6 +281,21 @@ def read_error_word(module: Module, plan: LaunchPlan) -> int:
     v = ctypes.c_uint32()
     check(library().thr_memcpy_dtoh(ctypes.byref(v), dst, 4), "error word")
     return v.value
+
+
+def clear_error_word(module: Module, plan: LaunchPlan) -> None:
+    """Zero the kernel's error word and the self-resetting arrival counters its family declares
+    (``counters`` in the launch record).  A bounded wait that gave up can leave such a counter
+    part-way through its count, and the next launch would then take the wrong K part of a tile
+    as the last to arrive and add partials that were never written.  Call this after a launch
+    whose error word was non-zero, before the module is launched again."""
+    lib = library()
+    names = ([plan.error_word] if plan.error_word else []) + list(plan.counters)
+    for name in names:
+        dst, size = module.global_ptr(name)
+        zeros = ctypes.create_string_buffer(size)
+        check(lib.thr_memcpy_htod(dst, zeros, size, 0), f"clear {name}")
+    check(lib.thr_synchronize(), "clear error word")
 
 
 def _tmap_specs(plan: LaunchPlan, arg_order: list[str]):
