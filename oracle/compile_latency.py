@@ -3,7 +3,7 @@
 Run in a container that has the reference checkout (its compile.py runs unmodified, with the
 clean-room emmy stand-in oracle/emmy_shim on the path, as tests/golden/make_golden.py runs it):
 
-    python oracle/compile_latency.py [--reference /root/reference] [--repeat 3]
+    python oracle/compile_latency.py --reference <reference checkout> [--repeat 3]
 
 For every kernel of the 19 golden packages it reports the median wall time of one
 ``python3 compile.py <kernel>.ir.json`` process for each compiler (interpreter start-up
@@ -40,7 +40,7 @@ def _proc_ms(cmd: list[str], env: dict, repeat: int) -> float:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="a checkout of the reference repository")
     ap.add_argument("--repeat", type=int, default=3)
     args = ap.parse_args()
     sys.path.insert(0, str(REPO / "thompiler-emmy-hackathon_b200"))

@@ -3,7 +3,7 @@
 Run where the reference checkout is present (the fixtures it writes are
 all the tests need; nothing reads the checkout at test time):
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 For every problem package of the reference (problems/ and tests/problems/)
 it writes, into tests/golden/packages/<id>/:
@@ -46,7 +46,7 @@ def sha(p: Path) -> str:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="a checkout of the reference repository")
     args = ap.parse_args()
     ref = Path(args.reference)
     out_root = HERE / "packages"

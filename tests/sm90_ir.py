@@ -240,15 +240,28 @@ def _unrolled(var, n, body):
     return ir.Loop(axis(var, n), tuple(body), True, False)
 
 
-def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64) -> Path:
+FRAGMENT_ATTENTION_EXTRAS = ("causal", "causal_pred", "bias", "bias_cols", "bias_index")
+
+
+def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64, extra: str | None = None) -> Path:
     """o = softmax(q k^T / sqrt(D)) v for one head (q, k, v f16 [S, D], o f32), written with the
     register-fragment statements on mma.sync m16n8k16: per warp a 16-query strip, keys in blocks
     of 64 staged by cp.async; FragmentApply scales the scores (a scalar argument, in place),
     subtracts the running row maximum (a row argument) with an exp ``post``, rescales the
     output strip and divides it by the row sums at the end; FragmentRowReduce gives the block's
-    row maxima and sums; FragmentRepack turns the probabilities into the A fragments of P V."""
+    row maxima and sums; FragmentRepack turns the probabilities into the A fragments of P V.
+
+    ``extra`` adds one FragmentApply whose argument is a function of each score's (query, key)
+    coordinates (row_base = the warp's first query, col_base = the fragment's first key):
+      causal       -- a ``mask`` Lambda: add 0 where key <= query, -1e30 elsewhere (scores);
+      causal_pred  -- a ``mask`` predicate key <= query (1 / 0) multiplying the probabilities;
+      bias         -- a ``bias`` from the f32 [S, S] buffer ``bias`` at (query, key), added;
+      bias_cols    -- a ``bias`` from the f32 [S] buffer ``kbias`` at (key), added;
+      bias_index   -- the same [S, S] bias through an explicit (buffer, (row, col)) index."""
     if S % 64 or D != 64:
         raise ValueError("fragment_attention_package: S a multiple of 64, D = 64")
+    if extra not in (None, *FRAGMENT_ATTENTION_EXTRAS):
+        raise ValueError(f"fragment_attention_package: extra {extra!r}")
     F16 = F16T
     tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
     sfr = tuple(f"s[{n}]" for n in range(8))
@@ -273,6 +286,7 @@ def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64) -> Path:
                                               None)])]),
         _unrolled("_c", 8, [ir.FragmentApply("s[_c]", E("multiply"), (L(1.0 / D ** 0.5, "float"),), ("scalar",), True,
                                              None, None, None, None)]),
+        *_coordinate_apply(extra, "scores"),
         ir.FragmentRowReduce("mx_t", "mx_b", sfr, E("maximum"), None, F32T),
         assign("mn_t", "maximum", "m_t", "mx_t"), assign("mn_b", "maximum", "m_b", "mx_b"),
         assign("d_t", "subtract", "m_t", "mn_t"), assign("d_b", "subtract", "m_b", "mn_b"),
@@ -280,6 +294,7 @@ def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64) -> Path:
         _unrolled("_e", 8, [ir.FragmentApply("s[_e]", E("subtract"), ("s[_e]", ("mn_t", "mn_b")), row, False,
                                              ir.FragLayout(4, (0, 0, 1, 1), (1, 2), None, (), None, None), E("exp"),
                                              None, None)]),
+        *_coordinate_apply(extra, "probabilities"),
         ir.FragmentRowReduce("ls_t", "ls_b", sfr, E("add"), ir.FragLayout(4, (0, 0, 1, 1), (1, 2), None, (), None,
                                                                            None), F32T),
         assign("lt1", "multiply", "l_t", "al_t"), assign("lb1", "multiply", "l_b", "al_b"),
@@ -303,12 +318,42 @@ def fragment_attention_package(outdir: Path, S: int = 256, D: int = 64) -> Path:
             *finish)
     tile = ir.Tile((axis("qb", S // 64), axis("_w", 4), axis("_lane", 32)), body, 128, 0, None, None, "m")
     entry = "k_fragment_attention"
-    g = _graph({"q": ((S, D), "f16"), "k": ((S, D), "f16"), "v": ((S, D), "f16")}, {}, "o", (S, D), entry, tile)
+    inputs = {"q": ((S, D), "f16"), "k": ((S, D), "f16"), "v": ((S, D), "f16")}
     args = [{"name": n, "dtype": "f16", "shape": [S, D], "seed": i} for i, n in enumerate(("q", "k", "v"))]
+    if extra in ("bias", "bias_index"):
+        inputs["bias"] = ((S, S), "f32")
+        args.append({"name": "bias", "dtype": "f32", "shape": [S, S], "seed": 3})
+    elif extra == "bias_cols":
+        inputs["kbias"] = ((S,), "f32")
+        args.append({"name": "kbias", "dtype": "f32", "shape": [S], "seed": 3})
+    g = _graph(inputs, {}, "o", (S, D), entry, tile)
     args.append({"name": "o", "dtype": "f32", "shape": [S, D], "output": True})
-    kmeta = {"node": "o", "arg_order": ["q", "k", "v", "o"], "grid": [S // 64, 1, 1], "block": [128, 1, 1],
+    kmeta = {"node": "o", "arg_order": [a["name"] for a in args], "grid": [S // 64, 1, 1], "block": [128, 1, 1],
              "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_fragment_attention", "softmax(q @ k.T / 8) @ v", entry, g, kmeta, 2e-2, 2e-3)
+
+
+def _coordinate_apply(extra: str | None, stage: str) -> list:
+    """The FragmentApply of ``extra`` at its stage (on the scaled scores, or on the
+    probabilities), over the 8 score fragments of the warp's 16 x 64 block."""
+    row_base = B("+", B("*", V("qb"), L(64)), B("*", V("_w"), L(16)))
+    col_base = B("+", V("_kv"), B("*", V("_x"), L(8)))
+    if extra is None or (stage == "probabilities") != (extra == "causal_pred"):
+        return []
+    if extra == "causal":
+        arg, kind, op = ir.Lambda(("qr", "kc"), (ir.Select("mv", (ir.Branch(L(0.0, "float"), B("<=", V("kc"), V("qr"))),
+                                                                ir.Branch(L(-1e30, "float"), None))),), ("mv",)), \
+            "mask", "add"
+    elif extra == "causal_pred":
+        arg, kind, op = B("<=", V("col"), V("row")), "mask", "multiply"
+    elif extra == "bias":
+        arg, kind, op = "bias", "bias", "add"
+    elif extra == "bias_cols":
+        arg, kind, op = "kbias", "bias", "add"
+    else:
+        arg, kind, op = ("bias", (V("row"), V("col"))), "bias", "add"
+    return [_unrolled("_x", 8, [ir.FragmentApply("s[_x]", E(op), (arg,), (kind,), True, None, None, row_base,
+                                                 col_base)])]
 
 
 def promote_matmul_package(outdir: Path, M: int = 128, N: int = 128, K: int = 512) -> Path:

@@ -128,3 +128,32 @@ def test_matmul_pair_declines_odd_generic_grid(tmp_path, monkeypatch):
     (d / "meta.json").write_text(json.dumps(meta))
     fam = recognise(_kernel(_ir(d)))
     assert isinstance(fam, TcMatmul) and not isinstance(fam, TcMatmulPair)
+
+
+@pytest.mark.parametrize("name,tile,grid", [("m01_matmul_512", [32, 32, 16], 256), ("m02_matmul_rect", [32, 32, 16], 8)])
+def test_matmul_f32_plan(name, tile, grid):
+    """The reference's f32 matmul schedules (m01: 512^3 in 32 x 32 cp.async tiles; m02: 128 x 64 x
+    256 as 32 split-K slices added atomically into a zeroed C) compile to the FMA-pipe family:
+    one thread per 2 x 2 outputs with the full K sum in registers, no atomics."""
+    from thompiler.families.matmul_f32 import MatmulF32
+    fam = recognise(_kernel(_ir(GOLDEN / name)))
+    assert isinstance(fam, MatmulF32)
+    side = fam.sidecar()
+    assert side["tile"] == tile and side["grid"] == [grid, 1, 1] and side["block"] == [256, 1, 1]
+    ptx = fam.emit()
+    tuned = ptx[:ptx.index("generic lowering")]
+    assert "fma.rn.f32" in tuned and "red.global" not in tuned and "atom." not in tuned
+    assert (fam.a.name, fam.b.name, fam.c.name) == ("x0", "x1", "matmul")
+
+
+def test_matmul_f32_declines_an_accumulating_output(tmp_path):
+    """Atomic Writes into an output meta.json does not zero mean C += A B: the full-sum body would
+    drop C's old value, so the family declines and the generic lowering runs."""
+    import json
+    import shutil
+    d = tmp_path / "m02"
+    shutil.copytree(GOLDEN / "m02_matmul_rect", d)
+    meta = json.loads((d / "meta.json").read_text())
+    meta["kernels"][0]["zero_outputs"] = []
+    (d / "meta.json").write_text(json.dumps(meta))
+    assert recognise(_kernel(_ir(d))) is None

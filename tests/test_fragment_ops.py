@@ -10,7 +10,7 @@ import subprocess
 
 import pytest
 
-from sm90_ir import fragment_attention_package, promote_matmul_package
+from sm90_ir import FRAGMENT_ATTENTION_EXTRAS, fragment_attention_package, promote_matmul_package
 from thompiler import ir, load, synth
 from thompiler.compiler import compile_kernel
 
@@ -94,7 +94,12 @@ def _edit(d, old, new):
 def test_refusals(tmp_path):
     d = fragment_attention_package(tmp_path / "a")
     _edit(d, "kinds=('frag', 'row'), in_place=False, layout=None", "kinds=('frag', 'mask'), in_place=False, layout=None")
-    with pytest.raises(NotImplementedError, match="kind 'mask'"):
+    with pytest.raises(ValueError, match="needs row_base and col_base"):
+        _ptx(d)
+
+    d = fragment_attention_package(tmp_path / "a2")
+    _edit(d, "kinds=('frag', 'row'), in_place=False, layout=None", "kinds=('frag', 'halo'), in_place=False, layout=None")
+    with pytest.raises(NotImplementedError, match="kind 'halo'"):
         _ptx(d)
 
     d = fragment_attention_package(tmp_path / "b")
@@ -118,3 +123,21 @@ def test_refusals(tmp_path):
     _edit(d, "FragmentPromote(dst='c[_q]', src='c16[_q]')", "FragmentPromote(dst='c[_q]', src='c[_q]')")
     with pytest.raises(ValueError, match="not the packed f16 shadow"):
         _ptx(d)
+
+
+@pytest.mark.parametrize("extra", FRAGMENT_ATTENTION_EXTRAS)
+def test_fragment_apply_coordinate_arguments(tmp_path, extra):
+    """FragmentApply mask and bias arguments: each score's coordinates are row_base + the element's
+    row (lane / 4, + 8 for the bottom registers) and col_base + its column (8 i + 2 (lane % 4) +
+    j), and the argument is evaluated per element at them -- a Lambda (a Select of 0 / -1e30), a
+    predicate (selp 1 / 0), a global load at (row, col) or at (col) of a 1-d buffer."""
+    ptx = _ptx(fragment_attention_package(tmp_path / "a", 256, 64, extra))
+    body = ptx.splitlines()
+    if extra == "causal":
+        assert sum("selp.f32" in ln and "0fF149F2CA" in ln for ln in body) == 8 * 4   # -1e30 where masked
+    elif extra == "causal_pred":
+        assert sum(ln.strip().startswith("selp.f32") and "0f3F800000, 0f00000000" in ln for ln in body) == 8 * 4
+    else:
+        loads = [ln for ln in body if "ld.global.nc.f32" in ln]
+        assert len(loads) == 8 * 4                          # one per score element
+    _ptxas(ptx, tmp_path)

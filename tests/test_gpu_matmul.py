@@ -123,8 +123,9 @@ def test_split_tail_counters_cleared_after_a_give_up(tmp_path, monkeypatch):
     """A bounded wait that gives up can leave a split-tail (tile, rank) counter part-way through
     its count.  The failure is made on the host: the counter of tail tile 0 is set to 1 (one of
     its two parts arrived) and the error word to the wait's code, as a give-up would leave them.
-    A launch on new data then takes the wrong part as the last and adds a stale partial; after
-    ``clear_error`` (error word and counters zeroed) the next launch is right again."""
+    The counter then stays off by one launch after launch (each launch's first part to arrive
+    takes itself for the last and may add a partial the other part has not written yet), until
+    ``clear_error`` zeroes the error word and the counters; then every launch leaves them at 0."""
     import ctypes
 
     import torch
@@ -135,25 +136,33 @@ def test_split_tail_counters_cleared_after_a_give_up(tmp_path, monkeypatch):
     assert k.plan.counters == ["thc_tile_arrivals"]
     g = torch.Generator(device="cuda").manual_seed(6)
     a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
-    b1, b2 = ((torch.randn(N, K, device="cuda", generator=g) * 0.02).half() for _ in range(2))
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
     c = torch.empty(M, N, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
+    lib = runner.library()
+    cnt_ptr, cnt_bytes = k.module.global_ptr("thc_tile_arrivals")
 
-    def run(b):
+    def run():
         c.fill_(float("nan"))
         k({"x0": a.data_ptr(), "x1": b.data_ptr(), "matmul": c.data_ptr()}, s)
         torch.cuda.synchronize()
         return (c.double() - a.double() @ b.double().t()).abs().max().item()
 
-    assert run(b1) < 1e-4 and k.error_word() == 0
-    lib = runner.library()
+    def counters():
+        buf = (ctypes.c_uint32 * (cnt_bytes // 4))()
+        runner.check(lib.thr_memcpy_dtoh(buf, cnt_ptr, cnt_bytes), "read counters")
+        return list(buf)
+
+    assert cnt_bytes // 4 == 12                            # 12 tail tiles, one counter each
+    assert run() < 1e-4 and k.error_word() == 0 and set(counters()) == {0}
     for name, val in (("thc_tile_arrivals", 1), ("thc_error", 1 << 2)):
         dst, _ = k.module.global_ptr(name)
         v = ctypes.c_uint32(val)
         runner.check(lib.thr_memcpy_htod(dst, ctypes.byref(v), 4, 0), name)
     runner.check(lib.thr_synchronize(), "sync")
-    assert run(b2) > 1e-3                                  # the stale partial of tail tile 0
+    run()
+    assert counters()[0] == 1 and set(counters()[1:]) == {0}    # still part-way: the hazard persists
     k.clear_error()
-    assert k.error_word() == 0
-    assert run(b2) < 1e-4 and run(b1) < 1e-4
+    assert k.error_word() == 0 and set(counters()) == {0}
+    assert run() < 1e-4 and set(counters()) == {0}
     k.close()

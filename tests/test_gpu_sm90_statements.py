@@ -7,9 +7,9 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import (COLS, EPILOGUE_FORMS, M, N, ROWS, epilogue_matmul_package, fragment_attention_package,
-                     promote_matmul_package, scan_package, select_package, stuck_wait_package, tma_transpose_package,
-                     wgmma_gemm_package)
+from sm90_ir import (COLS, EPILOGUE_FORMS, FRAGMENT_ATTENTION_EXTRAS, M, N, ROWS, epilogue_matmul_package,
+                     fragment_attention_package, promote_matmul_package, scan_package, select_package,
+                     stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -132,6 +132,28 @@ def test_fragment_attention(tmp_path):
     x = problems.make_inputs(pkg)
     q, k, v = (x[n].astype(np.float64) for n in ("q", "k", "v"))
     sc = q @ k.T / 8.0
+    p = np.exp(sc - sc.max(axis=1, keepdims=True))
+    want = (p / p.sum(axis=1, keepdims=True)) @ v
+    np.testing.assert_allclose(res["outputs"]["o"], want, rtol=2e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("extra", FRAGMENT_ATTENTION_EXTRAS)
+def test_fragment_attention_mask_and_bias(tmp_path, extra):
+    """FragmentApply mask and bias arguments on the register-fragment flash attention (one head,
+    S = 256): a causal mask as a Lambda added to the scores, the same mask as a predicate
+    multiplying the probabilities, an [S, S] f32 bias at (query, key) by buffer name and by an
+    explicit index, and a per-key [S] bias -- each against the float64 numpy expression."""
+    pkg = problems.load_package(fragment_attention_package(tmp_path / "a", 256, 64, extra))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    q, k, v = (x[n].astype(np.float64) for n in ("q", "k", "v"))
+    sc = q @ k.T / 8.0
+    if extra in ("causal", "causal_pred"):
+        sc = np.where(np.arange(256)[None, :] <= np.arange(256)[:, None], sc, -np.inf)
+    elif extra in ("bias", "bias_index"):
+        sc = sc + x["bias"].astype(np.float64)
+    else:
+        sc = sc + x["kbias"].astype(np.float64)[None, :]
     p = np.exp(sc - sc.max(axis=1, keepdims=True))
     want = (p / p.sum(axis=1, keepdims=True)) @ v
     np.testing.assert_allclose(res["outputs"]["o"], want, rtol=2e-2, atol=2e-3)

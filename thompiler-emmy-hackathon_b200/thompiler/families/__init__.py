@@ -23,8 +23,9 @@ def recognise(kernel: KernelInfo):
     top_loop = tile is not None and any(isinstance(s, ir.Loop) for s in tile.body)   # attention
     flat = tile is not None and all(isinstance(s, (ir.Load, ir.Assign, ir.Let, ir.Write))
                                     for s in tile.body)                  # pointwise
-    for name, maybe in (("strided", True), ("matmul_pair", mma), ("matmul", mma), ("attention", top_loop),
-                        ("pointwise", flat)):
+    simt_mm = ir.CpAsyncCopy in kinds and ir.MmaSyncPtx not in kinds    # f32 matmul on the FMA pipes
+    for name, maybe in (("strided", True), ("matmul_pair", mma), ("matmul", mma), ("matmul_f32", simt_mm),
+                        ("attention", top_loop), ("pointwise", flat)):
         if maybe:
             k = importlib.import_module(f"thompiler.families.{name}").recognise(kernel)
             if k is not None:

@@ -33,7 +33,7 @@ MAX_UNROLL = 16
 def emit_tile(w: "Walker", tile: ir.Tile) -> None:
     em = w.em
     if tile.aux_threads:
-        raise NotImplementedError(f"Tile with aux_threads={tile.aux_threads}")
+        raise NotImplementedError(f"no lowering for a tile that adds {tile.aux_threads} helper threads")
     extents = tile.extents
     n = tile.n_elements
     em.note(tile.pretty())

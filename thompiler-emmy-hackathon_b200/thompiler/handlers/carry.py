@@ -50,7 +50,7 @@ def _const(w: "Walker", e: Any) -> int:
         return w.consts[e.name]
     if isinstance(e, ir.BinaryExpr) and e.op in ("+", "-", "*", "/", "%"):
         return expr.fold(e.op, _const(w, e.left), _const(w, e.right))
-    raise NotImplementedError(f"carried-state cell index {ir.pretty(e)} is not a compile-time constant")
+    raise NotImplementedError(f"carried-state cell {ir.pretty(e)}: only indices that fold to a constant are lowered")
 
 
 def cell_key(w: "Walker", carrier: str, index) -> tuple:

@@ -20,12 +20,22 @@ Hence:
   fragment, ``bot`` the same for the bottom rows, each then combined across the quad by
   ``shfl.sync.bfly`` over the layout's ``reduce_xors`` (default 1, 2), so that every lane of
   the quad holds its rows' reduction over all the fragments' columns.  op: maximum, minimum, add;
-* ``FragmentApply(out, op, args, kinds, in_place, post)``: for every element e of ``out``,
-  out[e] = post(op(out[e] if in_place, arg_1[e], ...)), where an argument of kind ``frag`` is
-  the same element of another fragment, ``row`` a (top, bottom) pair of per-row values
-  (FragmentRowReduce's results) taken by the element's row, and ``scalar`` one value (a name or
-  a literal).  ``mask`` and ``bias`` arguments (coordinate predicates and global loads) are
-  refused: their coordinate expressions are not specified;
+* ``FragmentApply(out, op, args, kinds, in_place, post, row_base, col_base)``: for every
+  element e of ``out``, out[e] = post(op(out[e] if in_place, arg_1[e], ...)), where an argument
+  of kind ``frag`` is the same element of another fragment, ``row`` a (top, bottom) pair of
+  per-row values (FragmentRowReduce's results) taken by the element's row, and ``scalar`` one
+  value (a name or a literal).  ``mask`` and ``bias`` arguments are functions of the element's
+  coordinates in the output: row = row_base + the element's row (g or g + 8, plus 16 (warp % 4)
+  in a warpgroup accumulator), col = col_base + its column (8i + 2t + j):
+
+  - ``mask``: a predicate (an index expression in which ``Var('row')`` and ``Var('col')`` are
+    those coordinates), giving 1.0 where it holds and 0.0 where it does not; or an ``ir.Lambda``
+    with parameters (row, col) and one result, whose body (Load / Assign / Let / Select) gives
+    the operand -- e.g. a Select of 0 or -1e30 for an additive causal mask;
+  - ``bias``: a global load at the coordinates -- a buffer name (a 2-D buffer read at (row,
+    col); a 1-D one at (col), one value per column broadcast over the rows, as a linear layer's
+    bias), a (buffer, index) pair whose index is written in ``Var('row')`` / ``Var('col')``, or
+    an ``ir.Lambda`` as for a mask.  The loaded value is widened to f32.
 * ``FragmentRepack(frag, srcs, ab_dtype, part)``: the 16 x 16 A fragment of an m16n8k16 MMA
   from two f32 C fragments (columns 0-7 and 8-15 of its K): a0 = (c0[0], c0[1]), a1 =
   (c0[2], c0[3]), a2 = (c1[0], c1[1]), a3 = (c1[2], c1[3]), each pair rounded to f16x2 (or
@@ -173,6 +183,10 @@ def emit_fragment_apply(w: "Walker", s: ir.FragmentApply) -> None:
         elif kind == "scalar":
             r = _scalar(w, arg, "FragmentApply")
             operands.append(lambda e, r=r: r)
+        elif kind in ("mask", "bias"):
+            if s.row_base is None or s.col_base is None:
+                raise ValueError(f"FragmentApply: a {kind} argument needs row_base and col_base")
+            operands.append(lambda e, arg=arg, kind=kind: _coordinate_operand(w, s, len(out), e, arg, kind))
         else:
             raise NotImplementedError(f"FragmentApply argument of kind {kind!r}")
     arity = ir.ElementwiseImpl(op).arity
@@ -190,6 +204,98 @@ def emit_fragment_apply(w: "Walker", s: ir.FragmentApply) -> None:
     _written(w, s.out)
 
 
+def _element_coords(w: "Walker", s: ir.FragmentApply, nregs: int, e: int) -> tuple:
+    """Index expressions of element e's row and column in the output (see the module docstring)."""
+    from thompiler.handlers.mma import _lane_expr
+    lane = ir.Var("lane")
+    g = _lane_expr("/", lane, 4)
+    if nregs > 4:                            # a warpgroup accumulator: warp q holds rows 16q ..
+        g = ir.BinaryExpr("+", g, _lane_expr("*", _lane_expr("%", ir.Var("warp"), 4), 16))
+    t2 = _lane_expr("*", _lane_expr("%", lane, 4), 2)
+    i, r = divmod(e, 4)
+    row = ir.BinaryExpr("+", s.row_base, g if r < 2 else _lane_expr("+", g, 8))
+    col = ir.BinaryExpr("+", s.col_base, _lane_expr("+", t2, 8 * i + (r % 2)))
+    return row, col
+
+
+def _bind_coords(w: "Walker", names: tuple, row, col) -> None:
+    from thompiler.lowering import expr as ex
+    em = w.em
+    for name, e in zip(names, (row, col)):
+        em.ins(f"mov.s32 {em.value(name, 'b32')}, {ex.int_operand(w, e)}")
+
+
+def _coordinate_operand(w: "Walker", s: ir.FragmentApply, nregs: int, e: int, arg, kind: str) -> str:
+    """The f32 register holding a mask or bias argument's value at element e."""
+    from thompiler.handlers.mma import _param_name
+    from thompiler.lowering import address
+    from thompiler.lowering import expr as ex
+    em = w.em
+    row, col = _element_coords(w, s, nregs, e)
+    out = em.tmp("f32")
+    if isinstance(arg, ir.Lambda):
+        params = tuple(_param_name(p) for p in arg.params)
+        if len(params) != 2:
+            raise ValueError(f"FragmentApply {kind}: a Lambda takes (row, col), got {len(params)} parameters")
+        _bind_coords(w, params, row, col)
+        for st in arg.body:
+            if not isinstance(st, (ir.Load, ir.Assign, ir.Let, ir.Select)):
+                raise NotImplementedError(f"FragmentApply {kind}: statement {type(st).__name__} in a Lambda")
+            w.stmt(st)
+        results = [_param_name(r) for r in arg.results]
+        if len(results) != 1:
+            raise NotImplementedError(f"FragmentApply {kind}: a Lambda with {len(results)} results")
+        reg = em.get(results[0])
+        cls = em.named[reg]
+        if cls == "f32":
+            em.ins(f"mov.f32 {out}, {reg}")
+        elif cls == "b16":
+            em.ins(f"cvt.f32.f16 {out}, {reg}")
+        elif cls == "b32":
+            em.ins(f"cvt.rn.f32.s32 {out}, {reg}")
+        elif cls == "pred":
+            em.ins(f"selp.f32 {out}, 0f3F800000, 0f00000000, {reg}")
+        else:
+            raise TypeError(f"FragmentApply {kind}: a .{cls} result")
+        return out
+    if kind == "mask":
+        _bind_coords(w, ("row", "col"), row, col)
+        p = ex.pred_operand(w, arg)
+        em.ins(f"selp.f32 {out}, 0f3F800000, 0f00000000, {p}")
+        return out
+    # bias: a global load at the element's coordinates
+    if isinstance(arg, str):
+        prm = w.kernel.param(arg)
+        if prm is None:
+            raise ValueError(f"FragmentApply bias: {arg!r} is not a kernel parameter")
+        if len(prm.shape) == 2:
+            idx = (row, col)
+        elif len(prm.shape) == 1:
+            idx = (col,)
+        else:
+            raise NotImplementedError(f"FragmentApply bias from a {len(prm.shape)}-d buffer")
+        buf = arg
+    elif isinstance(arg, tuple) and len(arg) == 2 and isinstance(arg[0], str):
+        buf, idx = arg[0], tuple(arg[1])
+        _bind_coords(w, ("row", "col"), row, col)
+    else:
+        raise NotImplementedError(f"FragmentApply bias argument {arg!r}")
+    prm = w.kernel.param(buf)
+    if prm is None:
+        raise ValueError(f"FragmentApply bias: {buf!r} is not a kernel parameter")
+    addr = address.global_address(w, prm, idx)
+    ld = "ld.global" if prm.written else "ld.global.nc"      # a buffer the kernel writes: coherent loads
+    if prm.ty is F32:
+        em.ins(f"{ld}.f32 {out}, [{addr}]")
+    elif prm.ty is F16:
+        h = em.tmp("b16")
+        em.ins(f"{ld}.b16 {h}, [{addr}]")
+        em.ins(f"cvt.f32.f16 {out}, {h}")
+    else:
+        raise NotImplementedError(f"FragmentApply bias from a {prm.ty.name} buffer")
+    return out
+
+
 def emit_fragment_repack(w: "Walker", s: ir.FragmentRepack) -> None:
     em = w.em
     em.note(f"FragmentRepack {s.frag} <- {', '.join(s.srcs)}")
@@ -201,7 +307,7 @@ def emit_fragment_repack(w: "Walker", s: ir.FragmentRepack) -> None:
     if s.part is not None:
         part = expr.int_operand(w, s.part) if isinstance(s.part, ir.Expr) else str(int(s.part))
         if not expr.is_imm(part):
-            raise NotImplementedError(f"FragmentRepack: part {ir.pretty(s.part)} is not a compile-time constant")
+            raise NotImplementedError(f"FragmentRepack: part {ir.pretty(s.part)} must fold to a constant")
         srcs = srcs[2 * int(part):2 * int(part) + 2]
     if len(srcs) != 2:
         raise ValueError(f"FragmentRepack: an A fragment takes two C fragments, got {len(srcs)}")

@@ -100,7 +100,7 @@ def _const_index(w: "Walker", text: str, ref: str) -> int:
         if isinstance(node, ast.BinOp) and isinstance(node.op, (ast.Add, ast.Sub, ast.Mult)):
             a, b = ev(node.left), ev(node.right)
             return a + b if isinstance(node.op, ast.Add) else a - b if isinstance(node.op, ast.Sub) else a * b
-        raise NotImplementedError(f"{ref}: fragment index {text!r} is not a compile-time constant")
+        raise NotImplementedError(f"{ref}: member {text!r} must fold to a constant when the kernel is compiled")
     return ev(ast.parse(text, mode="eval").body)
 
 
@@ -149,7 +149,7 @@ def emit_ldmatrix_load(w: "Walker", ld: ir.LdmatrixLoad) -> None:
         raise ValueError(f"LdmatrixLoad role {ld.role} into a {frag.role} fragment")
     if ld.pair_frag is not None:
         if ld.role != "b":
-            raise ValueError("a paired ldmatrix loads two B fragments")
+            raise ValueError("an x4 ldmatrix of B fills exactly two fragments, not one")
         regs = regs + fragment_regs(w, ld.pair_frag)[1]
     ldm = int(ld.ldm) or arr.extents[-1]
     lane = ir.Var("lane")

@@ -56,7 +56,7 @@ def swizzle_params(mode: str) -> tuple[int, int] | None:
         return None
     base, sep, shift = mode.partition("@")
     if base not in SWIZZLES:
-        raise NotImplementedError(f"shared-memory swizzle {mode!r}")
+        raise NotImplementedError(f"no shared-memory layout {mode!r}")
     dshift, mask = SWIZZLES[base]
     return (int(shift) if sep else dshift, mask)
 
@@ -167,9 +167,9 @@ def access(w: "Walker", buffer: str, index: tuple, swizzle: str = "NONE") -> tup
     p = w.kernel.param(buffer)
     if p is not None:
         if swizzle not in ("NONE", None, ""):
-            raise ValueError(f"swizzle {swizzle} on global buffer {buffer}")
+            raise ValueError(f"{buffer} lives in global memory; swizzle {swizzle} applies to shared arrays only")
         return "global", global_address(w, p, index), p.ty, not p.written
     arr = w.smem.get(buffer)
     if arr is not None:
         return "shared", shared_address(w, arr, index, swizzle), arr.ty, False
-    raise ValueError(f"{buffer!r} is neither a kernel parameter nor a declared Smem array")
+    raise ValueError(f"{buffer!r}: no kernel parameter or Smem array has this name")

@@ -44,7 +44,7 @@ def fold(op: str, a: int, b: int) -> int:
         return c_div(a, b)
     if op == "%":
         return a - c_div(a, b) * b
-    raise NotImplementedError(f"integer operator {op!r}")
+    raise NotImplementedError(f"no integer lowering for {op!r}")
 
 
 def int_operand(w: "Walker", e: object) -> str:
@@ -64,7 +64,7 @@ def int_operand(w: "Walker", e: object) -> str:
         return str(e)
     if isinstance(e, ir.BinaryExpr):
         if e.op not in ops.INDEX_OPS:
-            raise NotImplementedError(f"integer operator {e.op!r}")
+            raise NotImplementedError(f"no integer lowering for {e.op!r}")
         a, b = int_operand(w, e.left), int_operand(w, e.right)
         if is_imm(a) and is_imm(b):
             return str(fold(e.op, int(a), int(b)))
@@ -136,7 +136,7 @@ def int_operand_wide(w: "Walker", e: object) -> str:
     em = w.em
     if isinstance(e, ir.BinaryExpr):
         if e.op not in WIDE_OPS:
-            raise NotImplementedError(f"integer operator {e.op!r}")
+            raise NotImplementedError(f"no integer lowering for {e.op!r}")
         a, b = int_operand_wide(w, e.left), int_operand_wide(w, e.right)
         if is_imm(a) and is_imm(b):
             return str(fold(e.op, int(a), int(b)))
@@ -178,12 +178,12 @@ def value_type(w: "Walker", e: object) -> Ty:
     if isinstance(e, ir.BinaryExpr) and e.op in ops.INDEX_OPS:
         a, b = value_type(w, e.left), value_type(w, e.right)
         if a != b:
-            raise TypeError(f"arithmetic on mixed types: {e.pretty()}")
+            raise TypeError(f"operands of different types in {e.pretty()}")
         return a
     if isinstance(e, ir.TernaryExpr):
         a, b = value_type(w, e.if_true), value_type(w, e.if_false)
         if a != b:
-            raise TypeError(f"conditional with mixed branch types: {e.pretty()}")
+            raise TypeError(f"the two arms of {e.pretty()} differ in type")
         return a
     if isinstance(e, (ir.Builtin, ir.FuncCallExpr)):
         return I32
