@@ -498,3 +498,73 @@ def epilogue_matmul_package(outdir: Path, form: str, M: int = 128, N: int = 128,
              "block": [128, 1, 1], "smem_bytes": 0, "zero_outputs": ["y"] if atomic else [], "args": args}
     return _write(outdir, f"sm90_epilogue_{form}", "x0 @ x1.T", entry, g, kmeta, 1e-3, 1e-3)
 
+
+
+def blockscaled_matmul_package(outdir: Path, M: int = 128, N: int = 128, K: int = 128) -> Path:
+    """y = dequant(xa) @ dequant(xb)^T with block-scaled fp4 operands: xa [M, K/2] and xb [N, K/2]
+    hold two e2m1 codes per byte (the lower k in the low nibble), sa [M, K/32] and sb [N, K/32]
+    one ue8m0 scale (2^(e - 127)) per 32 consecutive k.  Per warp a 16-row strip of a 64 x 64
+    tile: both operand tiles staged into byte Smem arrays by cp.async, then per 64-deep K step an
+    fp4 LdmatrixLoad of A, BlockScaleLoad of its scales, and for each of 8 column atoms an fp4
+    LdmatrixLoad of B, its BlockScaleLoad and one block-scaled m16n8k64 MmaSyncPtx into f32."""
+    if M % 64 or N % 64 or K % 64:
+        raise ValueError("blockscaled_matmul_package: M, N, K multiples of 64")
+    KB = K // 2
+    tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
+    body = [ir.RegFragment("fa", "a", (16, 8, 64), "e2m1", 1, None),
+            ir.RegFragment("fb", "b", (16, 8, 64), "e2m1", 8, None),
+            ir.RegFragment("sfa", "a", (16, 8, 64), "ue8m0", 1, None),
+            ir.RegFragment("sfb", "b", (16, 8, 64), "ue8m0", 8, None),
+            ir.RegFragment("c", "c", (16, 8, 64), F32T, 8, None),
+            ir.Smem("a_s", (64, KB), "uint8_t", 16), ir.Smem("b_s", (64, KB), "uint8_t", 16)]
+    per_row = KB // 16                                # 16-byte chunks per tile row
+    for smem, src, blk in (("a_s", "xa", "bm"), ("b_s", "xb", "bn")):
+        for i in range(64 * per_row // 128):
+            chunk = B("+", tid, L(128 * i))
+            r, c = B("/", chunk, L(per_row)), B("*", B("%", chunk, L(per_row)), L(16))
+            body.append(ir.CpAsyncCopy(smem, (r, c), src, (B("+", B("*", V(blk), L(64)), r), c), 16, "NONE", None, 0))
+    body += [ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False)]
+
+    def ldm(frag, smem, idx, role):
+        return ir.LdmatrixLoad(frag, smem, idx, role, KB, "NONE", True, None, None, False, None, False, None, (), 0,
+                               "m16n8k64", None)
+    row0 = B("*", V("_w"), L(16))
+    body.append(_unrolled("_ks", K // 64, [
+        ldm("fa", "a_s", (row0, B("*", V("_ks"), L(32))), "a"),
+        ir.BlockScaleLoad("sfa", "sa", (B("+", B("*", V("bm"), L(64)), row0), B("*", V("_ks"), L(2))), "a", 0),
+        _unrolled("_j", 8, [
+            ldm("fb[_j]", "b_s", (B("*", V("_j"), L(8)), B("*", V("_ks"), L(32))), "b"),
+            ir.BlockScaleLoad("sfb[_j]", "sb", (B("+", B("*", V("bn"), L(64)), B("*", V("_j"), L(8))),
+                                                B("*", V("_ks"), L(2))), "b", 0),
+            ir.MmaSyncPtx("c[_j]", "fa", "fb[_j]", (16, 8, 64), "e2m1", "f32", False, "sfa", "sfb[_j]")])]))
+    body.append(_unrolled("_s", 8, [ir.RegStore("y", (B("+", B("*", V("bm"), L(64)), row0),
+                                                      B("+", B("*", V("bn"), L(64)), B("*", V("_s"), L(8)))), "c[_s]",
+                                                (16, 8, 16), 0, None, (), None, None, False, "m16n8k16", False, None,
+                                                "NONE", None, None)]))
+    tile = ir.Tile((axis("bm", M // 64), axis("bn", N // 64), axis("_w", 4), axis("_lane", 32)), tuple(body), 128, 0,
+                   None, None, "m")
+    entry = "k_blockscaled_matmul"
+    g = _graph({"xa": ((M, KB), "u8"), "xb": ((N, KB), "u8"), "sa": ((M, K // 32), "u8"),
+                "sb": ((N, K // 32), "u8")}, {}, "y", (M, N), entry, tile)
+    codes = {"dist": "integers", "low": 0, "high": 255}
+    scales = {"dist": "integers", "low": 124, "high": 130}
+    args = [{"name": "xa", "dtype": "u8", "shape": [M, KB], "seed": 0, "init": dict(codes, seed=0)},
+            {"name": "xb", "dtype": "u8", "shape": [N, KB], "seed": 1, "init": dict(codes, seed=1)},
+            {"name": "sa", "dtype": "u8", "shape": [M, K // 32], "seed": 2, "init": dict(scales, seed=2)},
+            {"name": "sb", "dtype": "u8", "shape": [N, K // 32], "seed": 3, "init": dict(scales, seed=3)},
+            {"name": "y", "dtype": "f32", "shape": [M, N], "output": True}]
+    kmeta = {"node": "y", "arg_order": [a["name"] for a in args], "grid": [(M // 64) * (N // 64), 1, 1],
+             "block": [128, 1, 1], "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_blockscaled_matmul", "dequant(xa) @ dequant(xb).T", entry, g, kmeta, 1e-5, 1e-5)
+
+
+def dequant_fp4(codes: "np.ndarray", scales: "np.ndarray") -> "np.ndarray":
+    """The float64 values of packed fp4 rows (two e2m1 codes per byte, low nibble first) scaled by
+    ue8m0 bytes, one per 32 values -- the numpy statement of the block-scaled operands."""
+    import numpy as np
+    from thompiler.handlers.blockscale import e2m1_value
+    table = np.array([e2m1_value(n) for n in range(16)])
+    nib = np.stack([codes & 15, codes >> 4], axis=-1).reshape(codes.shape[0], -1)
+    vals = table[nib]
+    sc = np.exp2(scales.astype(np.float64) - 127.0)
+    return vals * np.repeat(sc, 32, axis=1)

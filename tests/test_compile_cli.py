@@ -51,13 +51,13 @@ def test_unsupported_statement_fails_loudly(tmp_path):
     g = json.loads((src / "k_add_pointwise.ir.json").read_text())
     node = next(n for n in g["nodes"].values() if n["op"] == "KernelOp")
     node["op_fields"]["body"] = ["Tile(axes=(Axis(name='a0', extent=Dim(64), window=None),), "
-                                 "body=(BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='a0'),), role='a', ldm=0),), block_threads=64, aux_threads=0, "
+                                 "body=(TensorMapPrefetch(desc='d', src_buffer='x'),), block_threads=64, aux_threads=0, "
                                  "raster_axes=None, raster_group=None, raster_orient='m')"]
     (tmp_path / "k_add_pointwise.ir.json").write_text(json.dumps(g))
     shutil.copy(src / "meta.json", tmp_path / "meta.json")
     r = run_compile(tmp_path / "k_add_pointwise.ir.json")
     assert r.returncode != 0 and r.stdout == ""
-    assert "BlockScaleLoad" in r.stderr and "NotImplementedError" in r.stderr
+    assert "TensorMapPrefetch" in r.stderr and "NotImplementedError" in r.stderr
 
 
 def test_missing_meta_entry_fails(tmp_path):

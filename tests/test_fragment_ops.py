@@ -10,7 +10,8 @@ import subprocess
 
 import pytest
 
-from sm90_ir import FRAGMENT_ATTENTION_EXTRAS, fragment_attention_package, promote_matmul_package
+from sm90_ir import (FRAGMENT_ATTENTION_EXTRAS, blockscaled_matmul_package, fragment_attention_package,
+                     promote_matmul_package)
 from thompiler import ir, load, synth
 from thompiler.compiler import compile_kernel
 
@@ -141,3 +142,25 @@ def test_fragment_apply_coordinate_arguments(tmp_path, extra):
         loads = [ln for ln in body if "ld.global.nc.f32" in ln]
         assert len(loads) == 8 * 4                          # one per score element
     _ptxas(ptx, tmp_path)
+
+
+def test_blockscaled_fp4_lowering(tmp_path):
+    """The block-scaled fp4 statements: fp4 LdmatrixLoad (x4 for A, x2 for B, from byte Smem
+    arrays), BlockScaleLoad (four scale bytes for A, two for B, from u8 buffers), and the
+    m16n8k64 e2m1 MmaSyncPtx emulated per warp on the FMA pipes (64 x 4 FMAs per lane through a
+    per-warp shared scratch, decoded through a 16-entry e2m1 table)."""
+    ptx = _ptx(blockscaled_matmul_package(tmp_path / "b", 128, 128, 128))
+    body = ptx.splitlines()
+    assert sum("ldmatrix.sync.aligned.m8n8.x4.shared.b16" in ln for ln in body) == 2
+    assert sum("ldmatrix.sync.aligned.m8n8.x2.shared.b16" in ln for ln in body) == 2 * 8
+    assert sum("ld.global.nc.u8" in ln for ln in body) == 2 * (4 + 8 * 2)
+    assert sum(ln.strip().startswith("fma.rn.f32") for ln in body) == 2 * 8 * 64 * 4
+    assert ".const .align 4 .b32 thc_e2m1[16] = {0x00000000, 0x3F000000" in ptx
+    assert "mma.sync" not in ptx                               # sm_100a has no block-scaled mma.sync
+    _ptxas(ptx, tmp_path)
+
+
+def test_fp4_decode_table():
+    from thompiler.handlers.blockscale import e2m1_value
+    assert [e2m1_value(n) for n in range(8)] == [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
+    assert [e2m1_value(n) for n in range(8, 16)] == [-0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]

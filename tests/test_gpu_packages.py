@@ -32,7 +32,10 @@ TOLERANCE = {
     "r": (1e-5, 1e-6),        # reductions
     "f": (1e-5, 1e-6),        # fused row ops
     "a": (1e-5, 1e-6),        # attention-like (ex2.approx vs exact exp2 in the oracle)
-    "m": (1e-5, 1e-5),        # f32 matmul (summation order)
+    # f32 matmul: the tuned FMA body adds K in ascending order, the oracle in the reference's
+    # (tiles of 64, or 32 split-K partials); reordering 512 f32 products of N(0, 1) values moves a
+    # sum of magnitude ~20 by a few 1e-5 (f32 epsilon x sqrt(K) x the sum)
+    "m": (1e-5, 1e-4),
     "t": (2e-2, 2e-3),        # f16 tensor-core matmul
 }
 

@@ -7,9 +7,9 @@ The reference has no lowering of these statements to compare with, so numpy is t
 import numpy as np
 import pytest
 
-from sm90_ir import (COLS, EPILOGUE_FORMS, FRAGMENT_ATTENTION_EXTRAS, M, N, ROWS, epilogue_matmul_package,
-                     fragment_attention_package, promote_matmul_package, scan_package, select_package,
-                     stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
+from sm90_ir import (COLS, EPILOGUE_FORMS, FRAGMENT_ATTENTION_EXTRAS, M, N, ROWS, blockscaled_matmul_package,
+                     dequant_fp4, epilogue_matmul_package, fragment_attention_package, promote_matmul_package,
+                     scan_package, select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -157,6 +157,20 @@ def test_fragment_attention_mask_and_bias(tmp_path, extra):
     p = np.exp(sc - sc.max(axis=1, keepdims=True))
     want = (p / p.sum(axis=1, keepdims=True)) @ v
     np.testing.assert_allclose(res["outputs"]["o"], want, rtol=2e-2, atol=2e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (64, 192, 256)])
+def test_blockscaled_fp4_matmul(tmp_path, M, N, K):
+    """Block-scaled fp4 (e2m1 codes, ue8m0 scales per 32 k) through fp4 LdmatrixLoad,
+    BlockScaleLoad and the m16n8k64 MmaSyncPtx, against the float64 numpy product of the
+    dequantised operands (every dequantised value and product is exact in f32; only the f32
+    sums round)."""
+    pkg = problems.load_package(blockscaled_matmul_package(tmp_path / "b", M, N, K))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    want = dequant_fp4(x["xa"], x["sa"]) @ dequant_fp4(x["xb"], x["sb"]).T
+    got = res["outputs"]["y"].astype(np.float64)
+    assert np.max(np.abs(got - want)) <= 1e-5 * np.max(np.abs(want)), np.max(np.abs(got - want))
 
 
 def test_promote_matmul_exact(tmp_path):

@@ -33,9 +33,16 @@ def test_kernel_info_follows_arg_order():
 
 
 def test_unknown_constructor_is_kept_opaque():
-    s = ir.parse_stmt("BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='i'),), role='a', ldm=64)")
-    assert isinstance(s, ir.Opaque) and s.kind == "BlockScaleLoad"
+    s = ir.parse_stmt("TensorMapPrefetch(desc='d', src_buffer='x', index=(Var(name='i'),))")
+    assert isinstance(s, ir.Opaque) and s.kind == "TensorMapPrefetch"
     assert dict(s.fields)["src_buffer"] == "x"
+
+
+def test_block_scale_load_is_read():
+    s = ir.parse_stmt("BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='i'), Literal(value=0, "
+                      "dtype='int')), role='a', ldm=64)")
+    assert isinstance(s, ir.BlockScaleLoad) and (s.frag, s.src_buffer, s.role, s.ldm) == ("sf", "x", "a", 64)
+    assert s.src_index == (ir.Var("i"), ir.Literal(0, "int"))
 
 
 def test_rejects_non_constructor_syntax():

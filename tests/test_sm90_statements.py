@@ -94,15 +94,19 @@ def test_set_max_nreg_and_checks(tmp_path):
 
 
 def test_unbuilt_vocabulary_fails_loudly(tmp_path):
-    """BlockScaleLoad (the block-scaled fp4 mma.sync path) still fails at lowering, naming the
-    statement, as the reference does for every statement it lacks; a Wgmma statement in a
-    kernel with no WgmmaMma is refused."""
+    """A statement this reader does not model fails at lowering, naming the statement, as the
+    reference does for every statement it lacks; a BlockScaleLoad into an undeclared fragment
+    and a Wgmma statement in a kernel with no WgmmaMma are refused."""
     d = select_package(tmp_path / "s")
     f = next(d.glob("*.ir.json"))
     text = f.read_text()
     zp = "ZeroPrologue(dst='z', words=Literal(value=64, dtype='int'))"
-    f.write_text(text.replace(zp, "BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='a0'),), role='a')"))
-    with pytest.raises(NotImplementedError, match="BlockScaleLoad"):
+    f.write_text(text.replace(zp, "TensorMapPrefetch(desc='d')"))
+    with pytest.raises(NotImplementedError, match="TensorMapPrefetch"):
+        _ptx(d)
+    f.write_text(text.replace(zp, "BlockScaleLoad(frag='sf', src_buffer='x', src_index=(Var(name='a0'), "
+                                  "Literal(value=0, dtype='int')), role='a')"))
+    with pytest.raises(KeyError, match="used before its RegFragment"):
         _ptx(d)
     f.write_text(text.replace(zp, "WgmmaFence()"))
     with pytest.raises(ValueError, match="WgmmaFence in a kernel without a WgmmaMma"):

@@ -37,7 +37,7 @@ from typing import TYPE_CHECKING
 
 from thompiler import ir
 from thompiler.lowering import address, expr
-from thompiler.lowering.types import F16, F32, Ty, dtype_of
+from thompiler.lowering.types import E2M1, F16, F32, FRAGMENT_TYPES, UE8M0, Ty, dtype_of
 
 if TYPE_CHECKING:
     from thompiler.walk import Walker
@@ -60,6 +60,10 @@ class Fragment:
 
 def operand_regs(role: str, shape: tuple, ty: Ty) -> int:
     m, n, k = shape
+    if ty is UE8M0:                               # block scales: four bytes in one register
+        return 1
+    if ty is E2M1 and role in ("a", "b"):         # fp4: eight values per register
+        return (m * k if role == "a" else k * n) // 256
     if role in ("a", "b"):
         if ty.nbytes != 2:
             raise NotImplementedError(f"mma operand {role} of {ty.name}")
@@ -75,7 +79,7 @@ def emit_reg_fragment(w: "Walker", f: ir.RegFragment) -> None:
     em.note(f"RegFragment {f.role}:{getattr(f.dtype, 'name', f.dtype)} {f.name}[{f.count}]")
     if f.name in w.fragments:
         raise ValueError(f"fragment {f.name} declared twice")
-    ty = dtype_of(f.dtype, f"RegFragment {f.name}")
+    ty = FRAGMENT_TYPES.get(str(getattr(f.dtype, "name", f.dtype))) or dtype_of(f.dtype, f"RegFragment {f.name}")
     shape = tuple(int(x) for x in f.shape)
     nregs = int(f.nregs) if f.nregs else operand_regs(f.role, shape, ty)
     cls = "f32" if (f.role == "c" and ty is F32) else "b32"
@@ -136,6 +140,10 @@ def _lane_expr(op: str, a, n: int):
 def emit_ldmatrix_load(w: "Walker", ld: ir.LdmatrixLoad) -> None:
     em = w.em
     em.note(f"LdmatrixLoad {ld.frag}{' + ' + ld.pair_frag if ld.pair_frag else ''} <- {ld.src_buffer}")
+    if fragment_regs(w, ld.frag)[0].ty is E2M1:
+        from thompiler.handlers.blockscale import emit_ldmatrix_fp4
+        emit_ldmatrix_fp4(w, ld)
+        return
     if (not ld.staged or ld.fragment_layout != "m16n8k16" or ld.byte_slab or ld.gmem_guard is not None
             or ld.k_zero is not None or ld.scale_buffer is not None):
         raise NotImplementedError("LdmatrixLoad form: unstaged, guarded, scaled or not m16n8k16")
@@ -184,10 +192,14 @@ def emit_mma_sync(w: "Walker", mma: ir.MmaSyncPtx) -> None:
     em = w.em
     shape = tuple(int(x) for x in mma.shape)
     em.note(f"MmaSyncPtx {mma.c_frag} += {mma.a_frag} @ {mma.b_frag}")
+    if mma.block_scaled:
+        from thompiler.handlers.blockscale import emit_block_scaled_mma
+        emit_block_scaled_mma(w, mma)
+        return
     if shape != (16, 8, 16) or mma.ab_dtype not in ("f16", "bf16") or mma.c_dtype not in ("f32", "f16"):
         raise NotImplementedError(f"MmaSyncPtx m{shape[0]}n{shape[1]}k{shape[2]} {mma.ab_dtype}->{mma.c_dtype}")
-    if mma.b_row_major or mma.block_scaled:
-        raise NotImplementedError("MmaSyncPtx with a row-major B (Volta) or block scales")
+    if mma.b_row_major:
+        raise NotImplementedError("MmaSyncPtx with a row-major B (Volta)")
     ops_ = []
     for role, ref in (("c", mma.c_frag), ("a", mma.a_frag), ("b", mma.b_frag)):
         frag, regs = fragment_regs(w, ref)

@@ -531,6 +531,15 @@ class LdmatrixLoad(Stmt):
 
 
 @record
+class BlockScaleLoad(Stmt):
+    frag: str
+    src_buffer: str
+    src_index: tuple = ()
+    role: str = "a"
+    ldm: int = 0
+
+
+@record
 class MmaSyncPtx(Stmt):
     c_frag: str
     a_frag: str
@@ -765,8 +774,7 @@ class WgmmaWait(Stmt):
 @record
 class Opaque(Stmt):
     """A constructor this reader does not model; kept so the walker can name
-    it when it fails (BlockScaleLoad appears in the IR reference but in no
-    shipped kernel)."""
+    it when it fails."""
     kind: str
     fields: tuple = field(default=())
 
@@ -782,7 +790,7 @@ _CONSTRUCTORS: dict[str, type] = {
         DataType, Dim, Window, Axis, ElementwiseImpl, Var, Literal, BinaryExpr, TernaryExpr,
         Builtin, FuncCallExpr, CastExpr, FlatIndex, Tile, Loop, StridedLoop, Cond, Load,
         Assign, Let, Accum, Init, Write, WarpShuffle, TreeHalve, Smem, Sync, CpAsyncCopy,
-        CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, MmaSyncPtx, RegStore,
+        CpAsyncCommit, CpAsyncWait, RegFragment, LdmatrixLoad, BlockScaleLoad, MmaSyncPtx, RegStore,
         Branch, Select, Pre, Carry, ZeroPrologue, TmaDescriptor, TmaLoad, MbarrierInit,
         MbarrierArriveExpectTx, MbarrierArrive, MbarrierWait, SetMaxNReg, WgmmaDescriptor, WgmmaMma,
         WgmmaFence, WgmmaCommit, WgmmaWait, FragLayout, Lambda, FragmentPromote, FragmentApply, FragmentRowReduce,

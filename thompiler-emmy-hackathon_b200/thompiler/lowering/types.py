@@ -54,16 +54,26 @@ F64 = Ty("f64", "float", "f64", "f64", "f64", 8)
 I32 = Ty("i32", "int", "s32", "s32", "b32", 4)
 I64 = Ty("i64", "int", "s64", "s64", "b64", 8)
 PRED = Ty("pred", "int", "pred", "pred", "pred", 0)
+# bytes: the packed fp4 operands and ue8m0 block scales of block-scaled MMAs (loaded into 32-bit
+# registers, zero-extended)
+U8 = Ty("u8", "int", "u8", "u8", "b32", 1)
+# register-fragment element types that no buffer holds: fp4 (e2m1, eight per 32-bit register) and
+# the ue8m0 block-scale bytes (four per register)
+E2M1 = Ty("e2m1", "float", "e2m1", "b32", "b32", 0)
+UE8M0 = Ty("ue8m0", "int", "ue8m0", "b32", "b32", 1)
+FRAGMENT_TYPES: dict[str, Ty] = {"e2m1": E2M1, "fp4": E2M1, "ue8m0": UE8M0}
 
-# Buffer / value dtypes by IR name.  Integer buffers are not part of the IR
-# vocabulary the problems use (no buffer holds integers), so only floats.
-BUFFER_TYPES: dict[str, Ty] = {"f16": F16, "f32": F32, "f64": F64}
+# Buffer / value dtypes by IR name: the float types of the problems, and bytes for the
+# block-scaled fp4 statements' packed operands and scales.
+BUFFER_TYPES: dict[str, Ty] = {"f16": F16, "f32": F32, "f64": F64, "u8": U8, "uint8": U8}
 
 # Smem.dtype is the C element type emmy renders, not an IR dtype.
 SMEM_TYPES: dict[str, Ty] = {"__half": F16, "half": F16, "float": F32, "double": F64,
                              # 8-byte words: the mbarrier arrays of the TMA statements
                              "uint64_t": I64, "int64_t": I64, "unsigned long long": I64, "long long": I64,
-                             "u64": I64, "i64": I64}
+                             "u64": I64, "i64": I64,
+                             # bytes: packed fp4 tiles and block scales
+                             "uint8_t": U8, "unsigned char": U8, "u8": U8}
 
 # Literal.dtype -> type of the literal.
 LITERAL_TYPES: dict[str, Ty] = {"int": I32, "float": F32}

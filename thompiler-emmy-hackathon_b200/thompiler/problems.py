@@ -30,7 +30,8 @@ from thompiler import runner
 from thompiler.compiler import compile_kernel
 from thompiler.load import load
 
-NP_DTYPES = {"f32": np.float32, "f16": np.float16, "f64": np.float64, "i32": np.int32, "i64": np.int64}
+NP_DTYPES = {"f32": np.float32, "f16": np.float16, "f64": np.float64, "i32": np.int32, "i64": np.int64,
+             "u8": np.uint8}
 
 
 @dataclass

@@ -21,6 +21,7 @@ from typing import Any, Callable
 from thompiler import ir
 from thompiler.emitter import Emitter
 from thompiler.handlers.blocks import emit_cond, emit_loop, emit_strided_loop, emit_tile
+from thompiler.handlers.blockscale import emit_block_scale_load
 from thompiler.handlers.carry import StepBegin, StepEnd, emit_carry, emit_pre, emit_step_begin, emit_step_end
 from thompiler.handlers.async_copy import (emit_mbarrier_arrive, emit_mbarrier_arrive_expect_tx, emit_mbarrier_init,
                                            emit_mbarrier_wait, emit_set_max_nreg, emit_tma_descriptor, emit_tma_load)
@@ -78,6 +79,7 @@ HANDLERS: dict[type, Callable[[Walker, Any], None]] = {
     ir.WarpShuffle: emit_warp_shuffle,
     ir.TreeHalve: emit_tree_halve,
     ir.Smem: emit_smem,
+    ir.BlockScaleLoad: emit_block_scale_load,
     ir.Sync: emit_sync,
     ir.CpAsyncCopy: emit_cp_async_copy,
     ir.CpAsyncCommit: emit_cp_async_commit,
