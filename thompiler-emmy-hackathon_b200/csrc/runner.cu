@@ -4,17 +4,20 @@
 // The library links the CUDA runtime statically and reaches the driver API
 // through cudaGetDriverEntryPointByVersion, so it loads on a machine
 // without a GPU driver (the build host) and only needs libcuda at thr_init.
-// It contains no kernels: every kernel it runs is PTX text from the
-// compiler.
+// The kernels it runs are PTX text from the compiler; the one kernel it
+// holds itself is the allocation-free sum (noalloc.cu).
 
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
+#include <deque>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -184,6 +187,226 @@ void release_batch_resources() {
     b.events.clear();
 }
 
+// ---- tensor-map sets ------------------------------------------------------------
+//
+// A tuned module reads its tensor maps from module globals.  Those laid out as a ring -- every map
+// spec naming one global of `sets` x `ntmaps` maps of 128 bytes, and a pointer table of `sets` x
+// `ntmaps` buffer addresses -- hold several sets at once: the kernel uses the set whose recorded
+// addresses equal its parameters, so launches of one module on different buffers can be in flight
+// together (on several streams, or one thr_run_batch).  Per module the runner keeps, for each set,
+// the addresses it is encoded for, an event after the last launch that read it and an event after
+// its last upload.  A launch binds the set already encoded for its buffers, else re-encodes the
+// least recently used one: the upload, from the set's own pinned staging, waits on the stream for
+// the set's last reader.  A set read by a launch captured into a CUDA graph is never re-encoded
+// (the graph may replay at any time), and a capture only binds sets uploaded before it: the
+// capturing stream makes no event queries or uploads (both would invalidate a global-mode
+// capture), so an upload's completion is also published to the host by a host function.  Maps
+// in separate globals (one per spec) form one set.
+
+struct TmapSet {
+    std::vector<uint64_t> ptrs;           // the buffers this set is encoded for; empty: unused
+    uint64_t stamp = 0;                   // last use (least recently used is re-encoded first)
+    cudaEvent_t read = nullptr;           // after the last launch that read the set
+    bool read_pending = false;
+    cudaEvent_t uploaded = nullptr;       // after the set's last upload
+    bool upload_pending = false;
+    unsigned char *staging = nullptr;     // pinned host copy of the maps, then the addresses
+    std::atomic<int> *upload_done = nullptr;  // set by a host function once the last upload ran
+    bool pinned = false;                  // read by a captured launch
+};
+
+std::deque<std::atomic<int>> g_upload_flags;  // never freed: a host function may still write one
+
+void CUDART_CB mark_uploaded(void *flag) { static_cast<std::atomic<int> *>(flag)->store(1); }
+
+struct TmapRing {
+    int sets = 0, nmaps = 0;
+    bool ring = false;                    // one global of sets x nmaps maps (else one global per map)
+    std::vector<uint64_t> globals;        // per map (ring: the ring global, repeated)
+    uint64_t table = 0;                   // the pointer table, 0 if none
+    uint64_t clock = 0;
+    std::vector<TmapSet> s;
+};
+
+std::map<uint64_t, TmapRing> g_rings;     // by module handle
+std::mutex g_ring_mu;
+
+bool stream_capturing(cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+}
+
+int ring_of(uint64_t module, const thr_tmap_spec *tmaps, int ntmaps, const char *ptr_table, TmapRing **out) {
+    auto it = g_rings.find(module);
+    if (it != g_rings.end()) {
+        if (it->second.nmaps != ntmaps) return fail(THR_ERR_REQUEST, "tensor maps: %d specs for a module of %d",
+                                                    ntmaps, it->second.nmaps);
+        *out = &it->second;
+        return THR_OK;
+    }
+    TmapRing r;
+    r.nmaps = ntmaps;
+    bool one = true;
+    for (int i = 1; i < ntmaps; ++i) one = one && !strcmp(tmaps[i].global, tmaps[0].global);
+    uint64_t g = 0, n = 0;
+    int s;
+    if (one && ntmaps > 0) {
+        if ((s = thr_module_global(module, tmaps[0].global, &g, &n))) return s;
+        r.ring = n >= 2 * 128 * (uint64_t)ntmaps;
+    }
+    if (r.ring) {
+        r.sets = (int)(n / (128 * (uint64_t)ntmaps));
+        r.globals.assign(ntmaps, g);
+    } else {
+        r.sets = 1;
+        for (int i = 0; i < ntmaps; ++i) {
+            if ((s = thr_module_global(module, tmaps[i].global, &g, &n))) return s;
+            if (n < 128) return fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", tmaps[i].global,
+                                     (unsigned long long)n);
+            r.globals.push_back(g);
+        }
+    }
+    if (ptr_table) {
+        if ((s = thr_module_global(module, ptr_table, &g, &n))) return s;
+        if (n < 8 * (uint64_t)ntmaps * r.sets)
+            return fail(THR_ERR_LOOKUP, "pointer table %s holds %llu bytes, %d sets of %d maps need %d", ptr_table,
+                        (unsigned long long)n, r.sets, ntmaps, 8 * ntmaps * r.sets);
+        r.table = g;
+    }
+    r.s.resize(r.sets);
+    *out = &g_rings.emplace(module, std::move(r)).first->second;
+    return THR_OK;
+}
+
+// Make the set encoded for the mapped buffers (args[tmaps[i].arg]) current for a launch on `st`.
+int tmap_bind(uint64_t module, const thr_tmap_spec *tmaps, int ntmaps, const char *ptr_table,
+              const uint64_t *args, int nargs, cudaStream_t st, int *set_out) {
+    std::lock_guard<std::mutex> lk(g_ring_mu);
+    TmapRing *r = nullptr;
+    int s = ring_of(module, tmaps, ntmaps, ptr_table, &r);
+    if (s) return s;
+    std::vector<uint64_t> want(ntmaps);
+    for (int i = 0; i < ntmaps; ++i) {
+        if (tmaps[i].arg < 0 || tmaps[i].arg >= nargs) return fail(THR_ERR_REQUEST, "tensor map %d: bad argument", i);
+        want[i] = args[tmaps[i].arg];
+    }
+    bool capturing = stream_capturing(st);
+    auto settle = [&](cudaEvent_t ev, bool &pending, const char *what) -> int {
+        // order `st` after ev (not capturing)
+        if (!pending) return THR_OK;
+        cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) {
+            pending = false;
+            return THR_OK;
+        }
+        if (q != cudaErrorNotReady) return cuda_fail(q, what);
+        cudaError_t e = cudaStreamWaitEvent(st, ev, 0);
+        return e == cudaSuccess ? THR_OK : cuda_fail(e, what);
+    };
+    for (int k = 0; k < r->sets; ++k) {
+        TmapSet &t = r->s[k];
+        if (t.ptrs == want) {
+            if (!capturing) {
+                if ((s = settle(t.uploaded, t.upload_pending, "the set's upload"))) return s;
+            } else if (t.upload_pending) {
+                if (!t.upload_done || !t.upload_done->load())
+                    return fail(THR_ERR_REQUEST, "tensor maps: the set for these buffers is still being uploaded "
+                                                 "while the stream is captured (synchronise before capturing)");
+                t.upload_pending = false;
+            }
+            t.stamp = ++r->clock;
+            *set_out = k;
+            return THR_OK;
+        }
+    }
+    if (capturing)
+        return fail(THR_ERR_REQUEST, "tensor maps: no set of the module is encoded for these buffers, and a "
+                                     "captured stream cannot upload one (launch on them once before capturing)");
+    int victim = -1;
+    for (int k = 0; k < r->sets; ++k)
+        if (!r->s[k].pinned && (victim < 0 || r->s[k].stamp < r->s[victim].stamp)) victim = k;
+    if (victim < 0)
+        return fail(THR_ERR_REQUEST, "tensor maps: all %d sets of the module are read by captured graphs", r->sets);
+    TmapSet &t = r->s[victim];
+    if ((s = settle(t.read, t.read_pending, "the set's last reader"))) return s;
+    cudaError_t e;
+    if (t.upload_pending) {                 // its staging is rewritten below
+        if ((e = cudaEventSynchronize(t.uploaded)) != cudaSuccess) return cuda_fail(e, "tensor-map staging");
+        t.upload_pending = false;
+    }
+    size_t mbytes = 128 * (size_t)ntmaps, pbytes = 8 * (size_t)ntmaps;
+    if (!t.staging && (e = cudaHostAlloc((void **)&t.staging, mbytes + pbytes, cudaHostAllocDefault)) != cudaSuccess)
+        return cuda_fail(e, "tensor-map staging");
+    for (int i = 0; i < ntmaps; ++i) {
+        const thr_tmap_spec &m = tmaps[i];
+        if ((s = thr_tensor_map(t.staging + 128 * i, m.dtype_code, m.rank, want[i], m.dims, m.strides, m.box,
+                                m.swizzle)))
+            return s;
+    }
+    memcpy(t.staging + mbytes, want.data(), pbytes);
+    if (!t.uploaded && (e = cudaEventCreateWithFlags(&t.uploaded, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "cudaEventCreate");
+    if (r->ring) {
+        e = cudaMemcpyAsync((void *)(uintptr_t)(r->globals[0] + victim * mbytes), t.staging, mbytes,
+                            cudaMemcpyHostToDevice, st);
+    } else {
+        e = cudaSuccess;
+        for (int i = 0; i < ntmaps && e == cudaSuccess; ++i)
+            e = cudaMemcpyAsync((void *)(uintptr_t)r->globals[i], t.staging + 128 * i, 128, cudaMemcpyHostToDevice, st);
+    }
+    if (e == cudaSuccess && r->table)
+        e = cudaMemcpyAsync((void *)(uintptr_t)(r->table + victim * pbytes), t.staging + mbytes, pbytes,
+                            cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaEventRecord(t.uploaded, st);
+    if (e == cudaSuccess) {
+        if (!t.upload_done) t.upload_done = &g_upload_flags.emplace_back(0);
+        t.upload_done->store(0);
+        e = cudaLaunchHostFunc(st, mark_uploaded, t.upload_done);
+    }
+    if (e != cudaSuccess) {
+        t.ptrs.clear();
+        return cuda_fail(e, "uploading tensor maps");
+    }
+    t.upload_pending = true;
+    t.ptrs = want;
+    t.stamp = ++r->clock;
+    *set_out = victim;
+    return THR_OK;
+}
+
+// A launch that reads set `k` was just issued on `st`.
+int tmap_launched(uint64_t module, int k, cudaStream_t st) {
+    std::lock_guard<std::mutex> lk(g_ring_mu);
+    auto it = g_rings.find(module);
+    if (it == g_rings.end() || k < 0 || k >= it->second.sets) return fail(THR_ERR_REQUEST, "tensor maps: set %d", k);
+    TmapSet &t = it->second.s[k];
+    if (stream_capturing(st)) {
+        t.pinned = true;
+        return THR_OK;
+    }
+    cudaError_t e;
+    if (!t.read && (e = cudaEventCreateWithFlags(&t.read, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "cudaEventCreate");
+    if ((e = cudaEventRecord(t.read, st)) != cudaSuccess) return cuda_fail(e, "recording a tensor-map reader");
+    t.read_pending = true;
+    return THR_OK;
+}
+
+void drop_ring(uint64_t module) {
+    std::lock_guard<std::mutex> lk(g_ring_mu);
+    auto it = g_rings.find(module);
+    if (it == g_rings.end()) return;
+    for (TmapSet &t : it->second.s) {
+        if (t.uploaded) {
+            cudaEventSynchronize(t.uploaded);
+            cudaEventDestroy(t.uploaded);
+        }
+        if (t.read) cudaEventDestroy(t.read);
+        if (t.staging) cudaFreeHost(t.staging);
+    }
+    g_rings.erase(it);
+}
+
 int wait_event(cudaEvent_t ev, double timeout_s) {
     auto t0 = std::chrono::steady_clock::now();
     for (;;) {
@@ -201,7 +424,7 @@ int wait_event(cudaEvent_t ev, double timeout_s) {
 
 extern "C" {
 
-int thr_version(void) { return 1; }
+int thr_version(void) { return 2; }
 
 int thr_init(int device) {
     int n = 0;
@@ -252,6 +475,7 @@ int thr_module_load(const char *ptx, uint64_t *module, char *log, size_t log_len
 int thr_module_unload(uint64_t module) {
     int s = ensure_driver();
     if (s) return s;
+    drop_ring(module);
     CUresult r = g_drv.unload((CUmodule)(uintptr_t)module);
     return r == CUDA_SUCCESS ? THR_OK : drv_fail(r, "cuModuleUnload");
 }
@@ -334,33 +558,8 @@ int thr_run_ex(uint64_t module, uint64_t function, const uint32_t grid[3], const
                             : cudaMemsetAsync(p, 0, args[i].nbytes, st);
         if (e != cudaSuccess) return cuda_fail(e, "staging a run argument");
     }
-    if (ntmaps) {
-        // encode the maps for the staged buffers and place them (and their pointers) in the module
-        std::vector<unsigned char> maps(128 * (size_t)ntmaps);
-        std::vector<uint64_t> ptrs(ntmaps);
-        for (int i = 0; i < ntmaps; ++i) {
-            const thr_tmap_spec &m = tmaps[i];
-            if (m.arg < 0 || m.arg >= nargs || !m.global) return fail(THR_ERR_REQUEST, "tensor map %d: bad argument", i);
-            ptrs[i] = dev[m.arg];
-            if ((s = thr_tensor_map(maps.data() + 128 * i, m.dtype_code, m.rank, dev[m.arg], m.dims, m.strides,
-                                    m.box, m.swizzle)))
-                return s;
-            uint64_t g = 0, n = 0;
-            if ((s = thr_module_global(module, m.global, &g, &n))) return s;
-            if (n < 128) return fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", m.global, (unsigned long long)n);
-            cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, maps.data() + 128 * i, 128, cudaMemcpyHostToDevice, st);
-            if (e != cudaSuccess) return cuda_fail(e, "uploading a tensor map");
-        }
-        if (ptr_table) {
-            uint64_t g = 0, n = 0;
-            if ((s = thr_module_global(module, ptr_table, &g, &n))) return s;
-            if (n < 8 * (uint64_t)ntmaps) return fail(THR_ERR_LOOKUP, "pointer table %s is too small", ptr_table);
-            cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, ptrs.data(), 8 * ntmaps, cudaMemcpyHostToDevice, st);
-            if (e != cudaSuccess) return cuda_fail(e, "uploading the tensor-map pointers");
-        }
-        cudaError_t e = cudaStreamSynchronize(st);   // the host copies above must not outlive this frame
-        if (e != cudaSuccess) return fail(THR_ERR_RUN, "staging tensor maps: %s", cudaGetErrorString(e));
-    }
+    int set = -1;
+    if (ntmaps && (s = tmap_bind(module, tmaps, ntmaps, ptr_table, dev.data(), nargs, st, &set))) return s;
     auto rezero = [&]() -> int {
         for (int i = 0; i < nargs; ++i)
             if (args[i].zero_each) {
@@ -378,6 +577,7 @@ int thr_run_ex(uint64_t module, uint64_t function, const uint32_t grid[3], const
         if ((rc = rezero())) break;
         cudaEventRecord(ev[2 * k], st);
         rc = thr_launch(function, grid, block, smem_bytes, dev.data(), nargs, stream);
+        if (rc == THR_OK && ntmaps) rc = tmap_launched(module, set, st);
         cudaEventRecord(ev[2 * k + 1], st);
     }
     if (rc == THR_OK) rc = wait_event(ev[2 * total - 1], timeout_s);
@@ -413,16 +613,11 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
         const thr_run_desc &d = runs[r];
         if (d.nargs < 0 || (d.nargs && !d.args) || d.ntmaps < 0 || (d.ntmaps && (!d.tmaps || !d.module)))
             return fail(THR_ERR_REQUEST, "thr_run_batch: request %d has bad arguments", r);
-        for (int q = 0; q < r; ++q)
-            if (d.ntmaps && runs[q].ntmaps && runs[q].module == d.module)
-                return fail(THR_ERR_REQUEST, "thr_run_batch: requests %d and %d need tensor maps in one module", q, r);
     }
     BatchRes *res = nullptr;
     int rc = batch_resources(&res);
     if (rc) return rc;
     cudaStream_t sin = res->s[0], scmp = res->s[1], sout = res->s[2];
-    std::vector<std::vector<unsigned char>> host_maps(nruns);   // alive until the batch is done
-    std::vector<std::vector<uint64_t>> host_ptrs(nruns);
     size_t nev = 0;
     auto event = [&](cudaEvent_t *e) -> bool { return batch_event(*res, nev++, e) == THR_OK; };
     // the batch's buffers sit after the slots thr_run uses for one request's arguments
@@ -440,43 +635,9 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
             if (e != cudaSuccess) rc = cuda_fail(e, "staging a batch argument");
         }
         if (rc) break;
-        if (d.ntmaps) {
-            host_maps[r].resize(128 * (size_t)d.ntmaps);
-            host_ptrs[r].resize(d.ntmaps);
-            for (int i = 0; i < d.ntmaps && rc == THR_OK; ++i) {
-                const thr_tmap_spec &m = d.tmaps[i];
-                if (m.arg < 0 || m.arg >= d.nargs || !m.global) {
-                    rc = fail(THR_ERR_REQUEST, "request %d tensor map %d: bad argument", r, i);
-                    break;
-                }
-                host_ptrs[r][i] = dev[m.arg];
-                if ((rc = thr_tensor_map(host_maps[r].data() + 128 * i, m.dtype_code, m.rank, dev[m.arg], m.dims,
-                                         m.strides, m.box, m.swizzle)))
-                    break;
-                uint64_t g = 0, n = 0;
-                if ((rc = thr_module_global(d.module, m.global, &g, &n))) break;
-                if (n < 128) {
-                    rc = fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", m.global, (unsigned long long)n);
-                    break;
-                }
-                cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, host_maps[r].data() + 128 * i, 128,
-                                                cudaMemcpyHostToDevice, sin);
-                if (e != cudaSuccess) rc = cuda_fail(e, "uploading a tensor map");
-            }
-            if (rc == THR_OK && d.ptr_table) {
-                uint64_t g = 0, n = 0;
-                if ((rc = thr_module_global(d.module, d.ptr_table, &g, &n)) == THR_OK) {
-                    if (n < 8 * (uint64_t)d.ntmaps) {
-                        rc = fail(THR_ERR_LOOKUP, "pointer table %s is too small", d.ptr_table);
-                    } else {
-                        cudaError_t e = cudaMemcpyAsync((void *)(uintptr_t)g, host_ptrs[r].data(), 8 * d.ntmaps,
-                                                        cudaMemcpyHostToDevice, sin);
-                        if (e != cudaSuccess) rc = cuda_fail(e, "uploading the tensor-map pointers");
-                    }
-                }
-            }
-            if (rc) break;
-        }
+        int set = -1;
+        if (d.ntmaps && (rc = tmap_bind(d.module, d.tmaps, d.ntmaps, d.ptr_table, dev.data(), d.nargs, sin, &set)))
+            break;
         cudaEvent_t staged, ran;
         if (!event(&staged) || !event(&ran)) {
             rc = fail(THR_ERR_CUDA, "cudaEventCreate");
@@ -487,6 +648,7 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
         if ((rc = thr_launch(d.function, d.grid, d.block, d.smem_bytes, dev.data(), d.nargs,
                              (uint64_t)(uintptr_t)scmp)))
             break;
+        if (d.ntmaps && (rc = tmap_launched(d.module, set, scmp))) break;
         cudaEventRecord(ran, scmp);
         cudaStreamWaitEvent(sout, ran, 0);
         for (int i = 0; i < d.nargs && rc == THR_OK; ++i)
@@ -514,6 +676,21 @@ int thr_run_batch(const thr_run_desc *runs, int nruns, double timeout_s) {
         cudaStreamSynchronize(sout);
     }
     return rc;
+}
+
+int thr_tmap_bind(uint64_t module, const thr_tmap_spec *tmaps, int ntmaps, const char *ptr_table,
+                  const uint64_t *args, int nargs, uint64_t stream, int *set) {
+    int s = ensure_driver();
+    if (s) return s;
+    if (!module || ntmaps <= 0 || !tmaps || !args || nargs <= 0 || !set)
+        return fail(THR_ERR_REQUEST, "thr_tmap_bind: bad arguments");
+    for (int i = 0; i < ntmaps; ++i)
+        if (!tmaps[i].global) return fail(THR_ERR_REQUEST, "thr_tmap_bind: tensor map %d names no global", i);
+    return tmap_bind(module, tmaps, ntmaps, ptr_table, args, nargs, (cudaStream_t)(uintptr_t)stream, set);
+}
+
+int thr_tmap_launched(uint64_t module, int set, uint64_t stream) {
+    return tmap_launched(module, set, (cudaStream_t)(uintptr_t)stream);
 }
 
 int thr_tensor_map(void *out128, int dtype_code, int rank, uint64_t base, const uint64_t *dims,

@@ -5,9 +5,10 @@ the module through the runner and plans its launch (the tuned launch a
 family recorded, else meta.json's).  Calling it launches the kernel on
 device pointers given by buffer name, in meta.json's ``arg_order``, on the
 given CUDA stream -- the path for callers that keep data in HBM (PyTorch
-tensors: pass ``t.data_ptr()``).  Tensor maps a tuned launch reads are
-encoded for the pointers of the first call and re-encoded whenever a
-pointer changes.
+tensors: pass ``t.data_ptr()``).  Tensor maps a tuned launch reads live in
+the module as a few sets, one per set of buffers (``runner.TensorMaps``):
+a call on buffers the module already has a set for uploads nothing, and
+calls on different buffers may be in flight together on any streams.
 """
 
 from __future__ import annotations
@@ -33,7 +34,7 @@ class DeviceKernel:
         self.fn = self.module.function(self.info.name)
         self.plan = runner.plan_launch(self.module, self.kmeta, honour_meta=honour_meta)
         self.arg_order = list(self.kmeta["arg_order"])
-        self._tmap_ptrs: dict | None = None
+        self.tmaps = runner.TensorMaps(self.module, self.plan, self.arg_order) if self.plan.tmaps else None
 
     @property
     def family(self) -> str:
@@ -44,10 +45,13 @@ class DeviceKernel:
         return m.group(1) if m else "generic"
 
     def __call__(self, ptrs: dict[str, int], stream: int = 0) -> None:
-        if self.plan.tmaps and ptrs != self._tmap_ptrs:
-            runner.prepare(self.module, self.plan, self.arg_order, ptrs, stream)
-            self._tmap_ptrs = dict(ptrs)
-        self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, [ptrs[n] for n in self.arg_order], stream)
+        args = [ptrs[n] for n in self.arg_order]
+        if self.tmaps is None:
+            self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream)
+            return
+        k = self.tmaps.bind(ptrs, stream)
+        self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream)
+        self.tmaps.launched(k, stream)
 
     def error_word(self) -> int:
         """The module's error word (0: no bounded wait gave up, no guarded access was skipped)."""

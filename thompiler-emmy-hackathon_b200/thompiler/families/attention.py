@@ -40,7 +40,8 @@ import math
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
-from thompiler.families.kit import Kit, desc_hi, idesc_f16
+from thompiler.families.kit import (TMAP_RING, TMAP_SETS, TMAP_TABLE, Kit, declare_tmap_ring, desc_hi, idesc_f16,
+                                   select_tmap_set, tmap_address)
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
@@ -166,22 +167,20 @@ class TcAttention(TunedKernel):
     def sidecar(self) -> dict:
         D = self.D
 
-        def tm(name, prm, rows, box=(64, 128), swizzle=3):
-            return {"global": name, "param": prm.name, "dtype": "f16", "dims": [D, rows],
+        def tm(prm, rows, box=(64, 128), swizzle=3):
+            return {"global": TMAP_RING, "param": prm.name, "dtype": "f16", "dims": [D, rows],
                     "strides": [D * 2], "box": list(box), "swizzle": swizzle}
         o_box = (self.box_bytes // 2, 32)                 # one warp's staging box of the output
-        maps = [tm("thc_tmap_q", self.pq, self.heads * self.Sq), tm("thc_tmap_k", self.pk, self.heads * self.Sk),
-                tm("thc_tmap_v", self.pv, self.heads * self.Sk),
-                tm("thc_tmap_o", self.pout, self.heads * self.Sq, o_box, 3)]
+        maps = [tm(self.pq, self.heads * self.Sq), tm(self.pk, self.heads * self.Sk),
+                tm(self.pv, self.heads * self.Sk), tm(self.pout, self.heads * self.Sq, o_box, 3)]
         return {"grid": [min(self.tiles, SM_COUNT), 1, 1], "block": [self.threads, 1, 1], "smem_bytes": self.smem,
-                "tmaps": maps, "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [m["param"] for m in maps]},
-                "error_word": "thc_error", "tile": [BM * self.qt, BN, D], "stages": [self.ks, self.vs]}
+                "tmaps": maps, "tmap_ptrs": {"global": TMAP_TABLE, "params": [m["param"] for m in maps]},
+                "tmap_sets": TMAP_SETS, "error_word": "thc_error", "tile": [BM * self.qt, BN, D],
+                "stages": [self.ks, self.vs]}
 
     def guard(self, generic: str) -> None:
         em = self.em
-        for n in ("q", "k", "v", "o"):
-            em.module(f".global .align 64 .b8 thc_tmap_{n}[128]")
-        em.module(".global .align 8 .u64 thc_tmap_ptr[4]")
+        declare_tmap_ring(em, 4)
         em.module(".global .align 4 .u32 thc_error")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         # the softmax rows live in registers: cap them so the tuned CTA (and meta.json's) can launch
@@ -190,12 +189,8 @@ class TcAttention(TunedKernel):
         r = self.special("%ntid.x")
         em.ins(f"setp.ne.u32 {p}, {r}, {self.threads}")
         em.ins(f"@{p} bra {generic}")
-        for i, prm in enumerate((self.pq, self.pk, self.pv, self.pout)):
-            raw, want = em.tmp("b64"), em.tmp("b64")
-            em.ins(f"ld.param.u64 {raw}, [p_{prm.name}]")
-            em.ins(f"ld.global.u64 {want}, [thc_tmap_ptr+{8 * i}]")
-            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
-            em.ins(f"@{p} bra {generic}")
+        # the tensor-map set encoded for these buffers (else the generic lowering)
+        self.tmap_set = select_tmap_set(em, [q.name for q in (self.pq, self.pk, self.pv, self.pout)], generic)
 
     # ---- the tuned body ----------------------------------------------------------------
 
@@ -271,12 +266,7 @@ class TcAttention(TunedKernel):
         ins(f"mov.u64 {errp}, thc_error")
         end = lab("at_end")
         kit = Kit(em, errp, end)
-        tmaps = {}
-        for n in ("q", "k", "v"):
-            r = t("b64")
-            ins(f"mov.u64 {r}, thc_tmap_{n}")
-            ins(f"cvta.global.u64 {r}, {r}")
-            tmaps[n] = r
+        tmaps = {n: tmap_address(em, self.tmap_set, 4, i) for i, n in enumerate(("q", "k", "v"))}
         # persistent: CTA c takes tiles c, c + nctaid, ...; nt of them, nt * n_blk key blocks in all
         cta, ncta = self.special("%ctaid.x"), self.special("%nctaid.x")
         nt, total = t("b32"), t("b32")
@@ -524,9 +514,7 @@ class TcAttention(TunedKernel):
         ins(f"and.b32 {r7}, {lane}, 7")
         lead = t("pred")
         ins(f"setp.eq.u32 {lead}, {lane}, 0")
-        tmap_o = t("b64")
-        ins("mov.u64 " + tmap_o + ", thc_tmap_o")
-        ins(f"cvta.global.u64 {tmap_o}, {tmap_o}")
+        tmap_o = tmap_address(em, self.tmap_set, 4, 3)
         sc = t("f32")
         ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")
         ins(f"rcp.rn.f32 {sc}, {sc}")

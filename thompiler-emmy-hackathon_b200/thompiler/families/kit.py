@@ -17,6 +17,56 @@ from __future__ import annotations
 
 WAIT_LIMIT = 1 << 18          # try_wait rounds (~4 us each while the phase is open): ~1 s
 SWIZZLE_128B = 2
+TMAP_SETS = 4                 # tensor-map sets a tuned module keeps (launches in flight on other buffers)
+TMAP_RING, TMAP_TABLE = "thc_tmap_ring", "thc_tmap_ptr"
+
+
+def declare_tmap_ring(em, nmaps: int) -> None:
+    """Module globals of TMAP_SETS sets of ``nmaps`` tensor maps and the buffer addresses each set
+    is encoded for (the runner fills them: thr_tmap_bind)."""
+    em.module(f".global .align 64 .b8 {TMAP_RING}[{TMAP_SETS * nmaps * 128}]")
+    em.module(f".global .align 8 .u64 {TMAP_TABLE}[{TMAP_SETS * nmaps}]")
+
+
+def select_tmap_set(em, params: list[str], generic: str) -> str:
+    """Guard code: a register with the index of the set whose recorded addresses equal the kernel
+    parameters ``params`` (in map order); no such set (or a null first parameter) branches to the
+    generic lowering."""
+    p = em.tmp("pred")
+    raws = []
+    for name in params:
+        r = em.tmp("b64")
+        em.ins(f"ld.param.u64 {r}, [p_{name}]")
+        raws.append(r)
+    em.ins(f"setp.eq.u64 {p}, {raws[0]}, 0")
+    em.ins(f"@{p} bra {generic}")
+    found, sel = em.label("tmap_set"), em.tmp("b32")
+    n = len(params)
+    for k in range(TMAP_SETS):
+        nxt = em.label("tmap_next")
+        for i, raw in enumerate(raws):
+            want = em.tmp("b64")
+            em.ins(f"ld.global.u64 {want}, [{TMAP_TABLE}+{8 * (k * n + i)}]")
+            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
+            em.ins(f"@{p} bra {nxt}")
+        em.ins(f"mov.u32 {sel}, {k}")
+        em.ins(f"bra {found}")
+        em.place(nxt)
+    em.ins(f"bra {generic}")
+    em.place(found)
+    return sel
+
+
+def tmap_address(em, sel: str, nmaps: int, i: int) -> str:
+    """Generic address of map ``i`` of the selected set."""
+    r, off = em.tmp("b64"), em.tmp("b64")
+    em.ins(f"mov.u64 {r}, {TMAP_RING}")
+    em.ins(f"cvta.global.u64 {r}, {r}")
+    em.ins(f"mul.wide.u32 {off}, {sel}, {nmaps * 128}")
+    em.ins(f"add.u64 {r}, {r}, {off}")
+    if i:
+        em.ins(f"add.u64 {r}, {r}, {128 * i}")
+    return r
 
 
 def desc_hi(sbo: int, layout: int = SWIZZLE_128B) -> int:

@@ -45,6 +45,7 @@ from __future__ import annotations
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
+from thompiler.families.kit import TMAP_RING, TMAP_SETS, TMAP_TABLE, declare_tmap_ring, select_tmap_set, tmap_address
 from thompiler.families.tuning import TUNING
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
@@ -201,48 +202,62 @@ class TcMatmul(TunedKernel):
 
     def sidecar(self) -> dict:
         a, b = self.a, self.b
-        tm_a = {"global": "thc_tmap_a", "param": a.name, "dtype": "f16", "dims": [self.K, self.M],
+        tm_a = {"global": TMAP_RING, "param": a.name, "dtype": "f16", "dims": [self.K, self.M],
                 "strides": [self.K * 2], "box": [BK, BM], "swizzle": 3}
         if self.b_kmajor:
-            tm_b = {"global": "thc_tmap_b", "param": b.name, "dtype": "f16", "dims": [self.K, self.N],
+            tm_b = {"global": TMAP_RING, "param": b.name, "dtype": "f16", "dims": [self.K, self.N],
                     "strides": [self.K * 2], "box": [BK, self.BN], "swizzle": 3}
         else:
-            tm_b = {"global": "thc_tmap_b", "param": b.name, "dtype": "f16", "dims": [self.N, self.K],
+            tm_b = {"global": TMAP_RING, "param": b.name, "dtype": "f16", "dims": [self.N, self.K],
                     "strides": [self.N * 2], "box": [64, BK], "swizzle": 3}
         esz = self.c.ty.nbytes
-        tm_c = {"global": "thc_tmap_c", "param": self.c.name, "dtype": "f32" if esz == 4 else "f16",
+        tm_c = {"global": TMAP_RING, "param": self.c.name, "dtype": "f32" if esz == 4 else "f16",
                 "dims": [self.N, self.S * self.M], "strides": [self.N * esz], "box": [64 // esz, 32],
                 "swizzle": 2}
         side = {"grid": [self.ctas, 1, 1], "block": [THREADS, 1, 1], "smem_bytes": self.smem,
                 "tmaps": [tm_a, tm_b, tm_c],
-                "tmap_ptrs": {"global": "thc_tmap_ptr", "params": [a.name, b.name, self.c.name]},
-                "error_word": "thc_error", "tile": [BM, self.BN, BK], "stages": self.stages}
+                "tmap_ptrs": {"global": TMAP_TABLE, "params": [a.name, b.name, self.c.name]},
+                "tmap_sets": TMAP_SETS, "error_word": "thc_error", "tile": [BM, self.BN, BK],
+                "stages": self.stages}
         if self.rem:
             side["counters"] = ["thc_tile_arrivals"]           # the split tail's (tile, rank) counters
         return side
 
+    @property
+    def tail_counters(self) -> int:
+        """Split-tail arrival counters per tensor-map set: one per (tail tile, CTA of the tile's pair)."""
+        return self.rem * self.tail_ranks
+
+    @property
+    def tail_ws_bytes(self) -> int:
+        """Split-tail partials per tensor-map set."""
+        return self.rem * self.tail_ranks * self.parts * BM * self.BN * 4
+
     def guard(self, generic: str) -> None:
         em = self.em
-        em.module(".global .align 64 .b8 thc_tmap_a[128]")
-        em.module(".global .align 64 .b8 thc_tmap_b[128]")
-        em.module(".global .align 64 .b8 thc_tmap_c[128]")
-        em.module(".global .align 8 .u64 thc_tmap_ptr[3]")
+        declare_tmap_ring(em, 3)
         em.module(".global .align 4 .u32 thc_error")
-        if self.rem:                 # one counter and one partial per (tail tile, CTA of the tile's pair)
-            ranks = self.tail_ranks
-            em.module(f".global .align 4 .u32 thc_tile_arrivals[{self.rem * ranks}]")
-            em.module(f".global .align 16 .b8 thc_tail_ws[{self.rem * ranks * self.parts * BM * self.BN * 4}]")
+        if self.rem:                 # per tensor-map set, so launches on other buffers run concurrently
+            em.module(f".global .align 4 .u32 thc_tile_arrivals[{TMAP_SETS * self.tail_counters}]")
+            em.module(f".global .align 16 .b8 thc_tail_ws[{TMAP_SETS * self.tail_ws_bytes}]")
         em.module(".extern .shared .align 1024 .b8 smem_pool[]")
         p = em.tmp("pred")
         r = self.special("%ntid.x")
         em.ins(f"setp.ne.u32 {p}, {r}, {THREADS}")
         em.ins(f"@{p} bra {generic}")
-        for i, prm in enumerate((self.a, self.b, self.c)):
-            raw, want = em.tmp("b64"), em.tmp("b64")
-            em.ins(f"ld.param.u64 {raw}, [p_{prm.name}]")
-            em.ins(f"ld.global.u64 {want}, [thc_tmap_ptr+{8 * i}]")
-            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
-            em.ins(f"@{p} bra {generic}")
+        # the tensor-map set encoded for these buffers (else the generic lowering)
+        self.tmap_set = select_tmap_set(em, [x.name for x in (self.a, self.b, self.c)], generic)
+
+    def tail_bases(self, cnt: str, ws: str) -> None:
+        """Point ``cnt`` / ``ws`` at the selected tensor-map set's split-tail counters / partials."""
+        em, t = self.em, self.em.tmp
+        off = t("b64")
+        em.ins(f"mov.u64 {cnt}, thc_tile_arrivals")
+        em.ins(f"mul.wide.u32 {off}, {self.tmap_set}, {4 * self.tail_counters}")
+        em.ins(f"add.u64 {cnt}, {cnt}, {off}")
+        em.ins(f"mov.u64 {ws}, thc_tail_ws")
+        em.ins(f"mul.wide.u32 {off}, {self.tmap_set}, {self.tail_ws_bytes}")
+        em.ins(f"add.u64 {ws}, {ws}, {off}")
 
     # ---- the tuned body -------------------------------------------------------------
 
@@ -307,15 +322,8 @@ class TcMatmul(TunedKernel):
         cta, ncta = self.special("%ctaid.x"), self.special("%nctaid.x")
         tiles = self.tiles
 
-        # generic addresses of the tensor maps
-        tma, tmb = t("b64"), t("b64")
-        ins(f"mov.u64 {tma}, thc_tmap_a")
-        ins(f"cvta.global.u64 {tma}, {tma}")
-        ins(f"mov.u64 {tmb}, thc_tmap_b")
-        ins(f"cvta.global.u64 {tmb}, {tmb}")
-        tmc = t("b64")
-        ins(f"mov.u64 {tmc}, thc_tmap_c")
-        ins(f"cvta.global.u64 {tmc}, {tmc}")
+        # generic addresses of the selected set's tensor maps
+        tma, tmb, tmc = (tmap_address(em, self.tmap_set, 3, i) for i in range(3))
         errp = t("b64")
         ins(f"mov.u64 {errp}, thc_error")
 
@@ -656,10 +664,9 @@ class TcMatmul(TunedKernel):
         place(tail)
         slot, ws, cnt = t("b32"), t("b64"), t("b64")
         ins(f"sub.u32 {slot}, {tile3}, {self.full_tiles}")
-        ins(f"mov.u64 {cnt}, thc_tile_arrivals")
+        self.tail_bases(cnt, ws)
         ins(f"mad.wide.u32 {cnt}, {slot}, 4, {cnt}")
         ins(f"mad.lo.u32 {slot}, {slot}, {parts}, {part3}")
-        ins("mov.u64 " + ws + ", thc_tail_ws")
         rowb = t("b64")                                   # this row's first chunk, 16 bytes apart per row
         ins(f"mul.wide.u32 {rowb}, {row}, 16")
         ins(f"add.u64 {rowb}, {rowb}, {ws}")

@@ -28,7 +28,7 @@ No TMA load uses cluster multicast: each CTA loads its own halves.
 
 from __future__ import annotations
 
-from thompiler.families.kit import Kit, desc_hi, idesc_f16
+from thompiler.families.kit import Kit, desc_hi, idesc_f16, tmap_address
 from thompiler.families.matmul import BK, BM, EPI_WARPS, SM_COUNT, STAGE_TILE, TcMatmul
 from thompiler.families.base import TunedKernel
 from thompiler.families.tuning import TUNING
@@ -184,10 +184,7 @@ class TcMatmulPair(TcMatmul):
         ins(f"setp.eq.u32 {lead_cta}, {rank}, 0")
         pid, npair = self.special("%clusterid.x"), self.special("%nclusterid.x")
 
-        tma, tmb, tmc = t("b64"), t("b64"), t("b64")
-        for r, n in ((tma, "a"), (tmb, "b"), (tmc, "c")):
-            ins(f"mov.u64 {r}, thc_tmap_{n}")
-            ins(f"cvta.global.u64 {r}, {r}")
+        tma, tmb, tmc = (tmap_address(em, self.tmap_set, 3, i) for i in range(3))
         errp = t("b64")
         ins(f"mov.u64 {errp}, thc_error")
         end = lab("mp_end")
@@ -489,10 +486,9 @@ class TcMatmulPair(TcMatmul):
         slot, ws, cnt = t("b32"), t("b64"), t("b64")
         ins(f"sub.u32 {slot}, {tile3}, {self.full_tiles}")
         ins(f"mad.lo.u32 {slot}, {slot}, 2, {rank}")           # (tail tile, rank)
-        ins(f"mov.u64 {cnt}, thc_tile_arrivals")
+        self.tail_bases(cnt, ws)
         ins(f"mad.wide.u32 {cnt}, {slot}, 4, {cnt}")
         ins(f"mul.lo.u32 {slot}, {slot}, {parts}")             # its part 0
-        ins("mov.u64 " + ws + ", thc_tail_ws")
         rowb = t("b64")                                        # this row's first chunk, 16 bytes apart per row
         ins(f"mul.wide.u32 {rowb}, {row}, 16")
         ins(f"add.u64 {rowb}, {rowb}, {ws}")

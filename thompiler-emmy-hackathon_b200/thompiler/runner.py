@@ -92,6 +92,9 @@ def library() -> ctypes.CDLL:
             "thr_release_buffers": ([], i32),
             "thr_last_error": ([ctypes.c_char_p, ctypes.c_size_t], i32),
             "thr_run_batch": ([ctypes.POINTER(ThrRunDesc), i32, ctypes.c_double], i32),
+            "thr_tmap_bind": ([u64, ctypes.POINTER(ThrTmapSpec), i32, ctypes.c_char_p, ctypes.POINTER(u64), i32,
+                               u64, ctypes.POINTER(i32)], i32),
+            "thr_tmap_launched": ([u64, i32, u64], i32),
             "thr_peer_alloc": ([u64, ctypes.POINTER(u64), ctypes.c_char_p], i32),
             "thr_peer_open": ([ctypes.c_char_p, ctypes.POINTER(u64)], i32),
             "thr_peer_close": ([u64], i32),
@@ -253,23 +256,30 @@ def encode_tensor_map(spec: dict, base: int) -> bytes:
     return out.raw
 
 
-def prepare(module: Module, plan: LaunchPlan, arg_order: list[str], ptrs: dict[str, int], stream: int = 0) -> None:
-    """Write the tensor maps a tuned launch reads, and the pointers they were
-    encoded for, into the module's globals (device-pointer launches)."""
-    lib = library()
-    for t in plan.tmaps:
-        raw = encode_tensor_map(t, ptrs[t["param"]])
-        dst, n = module.global_ptr(t["global"])
-        if n < 128:
-            raise RunnerError("lookup", f"tensor-map global {t['global']} is {n} bytes")
-        buf = ctypes.create_string_buffer(raw, 128)
-        check(lib.thr_memcpy_htod(dst, buf, 128, int(stream)), "tensor map upload")
-        check(lib.thr_synchronize(), "tensor map upload")      # the host buffer must outlive the copy
-    if plan.tmap_ptrs:
-        vals = (ctypes.c_uint64 * len(plan.tmap_ptrs["params"]))(*[ptrs[n] for n in plan.tmap_ptrs["params"]])
-        dst, n = module.global_ptr(plan.tmap_ptrs["global"])
-        check(lib.thr_memcpy_htod(dst, vals, ctypes.sizeof(vals), int(stream)), "tensor-map pointer upload")
-        check(lib.thr_synchronize(), "tensor-map pointer upload")
+class TensorMaps:
+    """The tensor maps of one tuned launch plan, for launches on device pointers: ``bind`` makes
+    the module's tensor-map set for the given buffers current on a stream (encoding and uploading
+    it, stream-ordered, when no set holds those buffers yet) and returns its index; ``launched``
+    records that a launch reading the set was just issued on the stream, so that re-encoding the
+    set later waits for it (thr_tmap_bind / thr_tmap_launched)."""
+
+    def __init__(self, module: Module, plan: LaunchPlan, arg_order: list[str]):
+        self.module, self.arg_order = module, list(arg_order)
+        self.specs, self._names = _tmap_specs(plan, self.arg_order)
+        self.n = len(plan.tmaps)
+        self.table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
+        self._args = (ctypes.c_uint64 * len(self.arg_order))()
+        self._set = ctypes.c_int()
+
+    def bind(self, ptrs: dict[str, int], stream: int = 0) -> int:
+        for i, name in enumerate(self.arg_order):
+            self._args[i] = ptrs[name]
+        check(library().thr_tmap_bind(self.module.handle, self.specs, self.n, self.table, self._args,
+                                      len(self.arg_order), int(stream), ctypes.byref(self._set)), "tensor maps")
+        return self._set.value
+
+    def launched(self, set_: int, stream: int = 0) -> None:
+        check(library().thr_tmap_launched(self.module.handle, int(set_), int(stream)), "tensor maps")
 
 
 def read_error_word(module: Module, plan: LaunchPlan) -> int:
