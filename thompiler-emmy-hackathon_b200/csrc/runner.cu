@@ -322,11 +322,44 @@ int tmap_bind(uint64_t module, const thr_tmap_spec *tmaps, int ntmaps, const cha
     if (capturing)
         return fail(THR_ERR_REQUEST, "tensor maps: no set of the module is encoded for these buffers, and a "
                                      "captured stream cannot upload one (launch on them once before capturing)");
+    // A kernel picks the lowest set whose addresses equal its parameters, reading the table while
+    // another stream may rewrite a set.  A launch in flight on buffers T could then match a set
+    // caught half-way from its old addresses O to the new ones N if every T[i] is O[i] or N[i]:
+    // such a set is not re-encoded while that launch may run.
+    auto in_flight = [&](TmapSet &o) -> bool {
+        if (!o.read_pending) return false;
+        cudaError_t q = cudaEventQuery(o.read);
+        if (q == cudaSuccess) o.read_pending = false;
+        return o.read_pending || o.pinned;
+    };
+    auto confusable = [&](int v) -> int {         // a set in flight that v's rewrite could alias, or -1
+        const std::vector<uint64_t> &old_ = r->s[v].ptrs;
+        if (old_.empty()) return -1;
+        for (int k = 0; k < r->sets; ++k) {
+            TmapSet &o = r->s[k];
+            if (k == v || o.ptrs.empty() || !in_flight(o)) continue;
+            bool mix = true;
+            for (int i = 0; i < ntmaps && mix; ++i) mix = o.ptrs[i] == old_[i] || o.ptrs[i] == want[i];
+            if (mix) return k;
+        }
+        return -1;
+    };
     int victim = -1;
     for (int k = 0; k < r->sets; ++k)
-        if (!r->s[k].pinned && (victim < 0 || r->s[k].stamp < r->s[victim].stamp)) victim = k;
-    if (victim < 0)
-        return fail(THR_ERR_REQUEST, "tensor maps: all %d sets of the module are read by captured graphs", r->sets);
+        if (!r->s[k].pinned && confusable(k) < 0 && (victim < 0 || r->s[k].stamp < r->s[victim].stamp)) victim = k;
+    if (victim < 0) {                             // every free set could be aliased: wait for the reader
+        for (int k = 0; k < r->sets; ++k)
+            if (!r->s[k].pinned && (victim < 0 || r->s[k].stamp < r->s[victim].stamp)) victim = k;
+        if (victim < 0)
+            return fail(THR_ERR_REQUEST, "tensor maps: all %d sets of the module are read by captured graphs", r->sets);
+        for (int c; (c = confusable(victim)) >= 0;) {
+            if (r->s[c].pinned)
+                return fail(THR_ERR_REQUEST, "tensor maps: re-encoding a set could alias one a captured graph reads");
+            cudaError_t e = cudaEventSynchronize(r->s[c].read);
+            if (e != cudaSuccess) return cuda_fail(e, "waiting for a tensor-map reader");
+            r->s[c].read_pending = false;
+        }
+    }
     TmapSet &t = r->s[victim];
     if ((s = settle(t.read, t.read_pending, "the set's last reader"))) return s;
     cudaError_t e;

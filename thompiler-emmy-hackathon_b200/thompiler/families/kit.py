@@ -17,7 +17,7 @@ from __future__ import annotations
 
 WAIT_LIMIT = 1 << 18          # try_wait rounds (~4 us each while the phase is open): ~1 s
 SWIZZLE_128B = 2
-TMAP_SETS = 4                 # tensor-map sets a tuned module keeps (launches in flight on other buffers)
+TMAP_SETS = 8                 # tensor-map sets a tuned module keeps (launches in flight on other buffers)
 TMAP_RING, TMAP_TABLE = "thc_tmap_ring", "thc_tmap_ptr"
 
 
@@ -31,7 +31,8 @@ def declare_tmap_ring(em, nmaps: int) -> None:
 def select_tmap_set(em, params: list[str], generic: str) -> str:
     """Guard code: a register with the index of the set whose recorded addresses equal the kernel
     parameters ``params`` (in map order); no such set (or a null first parameter) branches to the
-    generic lowering."""
+    generic lowering.  The whole table is loaded first (independent loads, one memory latency),
+    then compared."""
     p = em.tmp("pred")
     raws = []
     for name in params:
@@ -40,20 +41,23 @@ def select_tmap_set(em, params: list[str], generic: str) -> str:
         raws.append(r)
     em.ins(f"setp.eq.u64 {p}, {raws[0]}, 0")
     em.ins(f"@{p} bra {generic}")
-    found, sel = em.label("tmap_set"), em.tmp("b32")
     n = len(params)
-    for k in range(TMAP_SETS):
-        nxt = em.label("tmap_next")
+    table = [em.tmp("b64") for _ in range(TMAP_SETS * n)]
+    for j in range(0, len(table) - 1, 2):
+        em.ins(f"ld.global.nc.v2.u64 {{{table[j]}, {table[j + 1]}}}, [{TMAP_TABLE}+{8 * j}]")
+    if len(table) % 2:
+        em.ins(f"ld.global.nc.u64 {table[-1]}, [{TMAP_TABLE}+{8 * (len(table) - 1)}]")
+    sel, hit, eq = em.tmp("b32"), em.tmp("pred"), em.tmp("pred")
+    em.ins(f"mov.u32 {sel}, {TMAP_SETS}")
+    for k in reversed(range(TMAP_SETS)):            # the lowest matching set wins
         for i, raw in enumerate(raws):
-            want = em.tmp("b64")
-            em.ins(f"ld.global.u64 {want}, [{TMAP_TABLE}+{8 * (k * n + i)}]")
-            em.ins(f"setp.ne.u64 {p}, {raw}, {want}")
-            em.ins(f"@{p} bra {nxt}")
-        em.ins(f"mov.u32 {sel}, {k}")
-        em.ins(f"bra {found}")
-        em.place(nxt)
-    em.ins(f"bra {generic}")
-    em.place(found)
+            if i == 0:
+                em.ins(f"setp.eq.u64 {hit}, {raw}, {table[k * n]}")
+            else:
+                em.ins(f"setp.eq.and.u64 {hit}, {raw}, {table[k * n + i]}, {hit}")
+        em.ins(f"selp.u32 {sel}, {k}, {sel}, {hit}")
+    em.ins(f"setp.eq.u32 {eq}, {sel}, {TMAP_SETS}")
+    em.ins(f"@{eq} bra {generic}")
     return sel
 
 
