@@ -250,16 +250,21 @@ int ring_of(uint64_t module, const thr_tmap_spec *tmaps, int ntmaps, const char 
     for (int i = 1; i < ntmaps; ++i) one = one && !strcmp(tmaps[i].global, tmaps[0].global);
     uint64_t g = 0, n = 0;
     int s;
-    if (one && ntmaps > 0) {
-        if ((s = thr_module_global(module, tmaps[0].global, &g, &n))) return s;
-        r.ring = n >= 2 * 128 * (uint64_t)ntmaps;
-    }
+    // every spec naming one global: a ring of sets x ntmaps maps (one set fits exactly)
+    r.ring = one && ntmaps > 0;
     if (r.ring) {
+        if ((s = thr_module_global(module, tmaps[0].global, &g, &n))) return s;
         r.sets = (int)(n / (128 * (uint64_t)ntmaps));
+        if (r.sets < 1)
+            return fail(THR_ERR_LOOKUP, "tensor-map global %s holds %llu bytes, %d maps need %d", tmaps[0].global,
+                        (unsigned long long)n, ntmaps, 128 * ntmaps);
         r.globals.assign(ntmaps, g);
     } else {
         r.sets = 1;
         for (int i = 0; i < ntmaps; ++i) {
+            for (int j = 0; j < i; ++j)
+                if (!strcmp(tmaps[i].global, tmaps[j].global))
+                    return fail(THR_ERR_REQUEST, "tensor maps %d and %d share the global %s", j, i, tmaps[i].global);
             if ((s = thr_module_global(module, tmaps[i].global, &g, &n))) return s;
             if (n < 128) return fail(THR_ERR_LOOKUP, "tensor-map global %s is %llu bytes", tmaps[i].global,
                                      (unsigned long long)n);

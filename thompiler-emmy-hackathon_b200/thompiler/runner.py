@@ -267,6 +267,12 @@ class TensorMaps:
         self.module, self.arg_order = module, list(arg_order)
         self.specs, self._names = _tmap_specs(plan, self.arg_order)
         self.n = len(plan.tmaps)
+        sets = (module.sidecar or {}).get("tmap_sets")
+        if sets is not None:                   # the ring the runner finds must be the one the kernel reads
+            _, size = module.global_ptr(plan.tmaps[0]["global"])
+            if size != sets * self.n * 128 or len({t["global"] for t in plan.tmaps}) != 1:
+                raise RunnerError("lookup", f"tensor-map ring {plan.tmaps[0]['global']}: {size} bytes for "
+                                            f"{sets} sets of {self.n} maps")
         self.table = plan.tmap_ptrs["global"].encode() if plan.tmap_ptrs else None
         self._args = (ctypes.c_uint64 * len(self.arg_order))()
         self._set = ctypes.c_int()
