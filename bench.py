@@ -559,9 +559,16 @@ class FullSum:
         hx.copy_(self.x)
         ho = torch.zeros(1)
         args = [{"array": hx.numpy()}, {"array": ho.numpy(), "output": True}]
+        def ranks_together():
+            # the in-kernel combine waits (bounded) for every rank's kernel: enter each launch together
+            if self.collective == "peer":
+                import torch.distributed as dist
+                dist.barrier()
+        ranks_together()
         runner.run(self.k.fn, self.k.plan, args)
         t = time.perf_counter()
         for _ in range(steps):
+            ranks_together()
             r = runner.run(self.k.fn, self.k.plan, args)
             if not r["ok"]:
                 raise RuntimeError(r["stderr"])
