@@ -81,14 +81,17 @@ def test_strided_sum_plans():
     assert "peer" not in (r03.sidecar() or {})                 # a mean is not combined across GPUs
 
 
-@pytest.mark.parametrize("M,N,K,lay,bn,tiles,stages,rem,parts", [
-    (4096, 4096, 4096, "col", 0, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 384, 6, 0, 1),
-    (2048, 2560, 2048, "col", 0, 80, 6, 6, 2), (256, 128, 256, "row", 0, 1, 8, 0, 1),
-    (512, 256, 256, "col", 128, 4, 8, 0, 1)])
-def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages, rem, parts):
+@pytest.mark.parametrize("M,N,K,lay,bn,want_bn,tiles,stages,rem,parts", [
+    (4096, 4096, 4096, "col", 0, 256, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 192, 512, 6, 0, 1),
+    (8192, 3072, 1024, "col", 256, 256, 384, 6, 0, 1), (8192, 3072, 1024, "row", 0, 256, 384, 6, 0, 1),
+    (2048, 2560, 2048, "col", 0, 256, 80, 6, 6, 2), (256, 128, 256, "row", 0, 128, 1, 8, 0, 1),
+    (512, 256, 256, "col", 128, 128, 4, 8, 0, 1)])
+def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tiles, stages, rem, parts):
     """The CTA-pair matmul (the default where it applies): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
     of B; one pair per two SMs; a cluster launch of an even grid; shared memory (with the
-    generic path's static arrays) inside one SM's 227 KB."""
+    generic path's static arrays) inside one SM's 227 KB.  The width balances the waves: the
+    8192 x 3072 x 1024 rectangle takes 192 (512 tiles, 6.92 waves of 74 pairs, against 5.19 at
+    256) when B is K-major, 256 when B is MN-major (64-column loads)."""
     from thompiler.families.matmul_pair import TcMatmulPair
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay)
     monkeypatch.setattr(TUNING, "matmul_pair", False)
@@ -98,7 +101,7 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, tiles, stages
         monkeypatch.setattr(TUNING, "matmul_bn", bn)
     fam = recognise(_kernel(_ir(d)))
     assert isinstance(fam, TcMatmulPair)
-    assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, bn or (256 if N % 256 == 0 else 128))
+    assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, want_bn)
     assert fam.b_bytes == fam.BN // 2 * 64 * 2 and fam.a_bytes == 128 * 64 * 2
     assert (fam.rem, fam.parts) == (rem, parts)                  # the last wave cut along K
     assert fam.units == tiles - rem + rem * parts

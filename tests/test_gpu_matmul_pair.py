@@ -32,7 +32,8 @@ def _pair(monkeypatch):
 
 @pytest.mark.parametrize("M,N,K,lay,out,bn", [(256, 256, 512, "col", "f32", 0), (256, 128, 256, "row", "f32", 0),
                                               (512, 512, 256, "col", "f16", 0), (256, 256, 320, "row", "f16", 0),
-                                              (512, 256, 256, "col", "f32", 128)])
+                                              (512, 256, 256, "col", "f32", 128), (512, 384, 256, "col", "f32", 192),
+                                              (768, 576, 320, "col", "f16", 192)])
 def test_pair_small_vs_oracle(tmp_path, monkeypatch, M, N, K, lay, out, bn):
     if bn:
         monkeypatch.setattr(TUNING, "matmul_bn", bn)

@@ -37,6 +37,11 @@ from thompiler.lowering.types import F32
 
 PM = 2 * BM                  # rows of a pair tile
 PAIR_SLOTS = SM_COUNT // 2   # pairs resident at once
+# pair tile widths and their efficiency relative to 256 at full waves, measured on B200: 128 is 0.71
+# of 256 at 4096^3 and 192 about 0.8 at 8192 x 3072 x 1024 (0.0530 against 0.0494 ms although it
+# fills 6.92 waves of pairs instead of 5.19): per flop each CTA feeds more operand bytes from
+# shared memory at narrower tiles
+PAIR_WIDTHS = ((256, 1.0), (192, 0.80), (128, 0.71))
 SMEM_LIMIT = 227 * 1024
 
 
@@ -51,20 +56,29 @@ class TcMatmulPair(TcMatmul):
         one = TcMatmul.match.__func__(TcMatmul, kernel)
         if one is None or one.M % PM or kernel.grid[0] % 2:
             return None                    # the cluster launch needs an even generic grid too
-        bn = cls.pair_bn(one.M, one.N, one.S)
+        bn = cls.pair_bn(one.M, one.N, one.S, one.b_kmajor)
         if bn is None:
             return None
         return cls(kernel, one.a, one.b, one.c, one.M, one.N, one.K, one.S, one.b_kmajor, bn, one.static_smem)
 
     @staticmethod
-    def pair_bn(M: int, N: int, S: int) -> int | None:
+    def pair_bn(M: int, N: int, S: int, b_kmajor: bool = True) -> int | None:
+        """The pair tile's width: the best of wave efficiency (pair tiles over the 74 pairs
+        resident at once) times the width's own efficiency.  192 needs K-major B (an MN-major B
+        is loaded in 64-column boxes, and a CTA holds 96 columns)."""
         forced = TUNING.matmul_bn
-        if forced in (128, 256) and N % forced == 0:
+        if forced in (128, 192, 256) and N % forced == 0 and (forced != 192 or b_kmajor):
             return forced
-        for bn in (256, 128):
-            if N % bn == 0:
-                return bn
-        return None
+        best, best_score = None, -1.0
+        for bn, pref in PAIR_WIDTHS:
+            if N % bn or (bn == 192 and not b_kmajor):
+                continue
+            tiles = (M // PM) * (N // bn) * S
+            waves = -(-tiles // PAIR_SLOTS)
+            score = pref * (tiles / (waves * PAIR_SLOTS) if tiles >= PAIR_SLOTS else tiles / PAIR_SLOTS)
+            if score > best_score + 1e-9:
+                best, best_score = bn, score
+        return best
 
     def __init__(self, kernel, a, b, c, M, N, K, S, b_kmajor, bn, static_smem):  # noqa: D107
         TunedKernel.__init__(self, kernel)
@@ -90,7 +104,7 @@ class TcMatmulPair(TcMatmul):
         # as in the single-CTA kernel (each CTA of a pair keeps its own partial and counter)
         kblocks = self.Ks // BK
         rem = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
-        parts = min(kblocks // 16, PAIR_SLOTS // rem) if rem else 1
+        parts = min(kblocks // TUNING.matmul_tail_kblocks, PAIR_SLOTS // rem) if rem else 1
         if S != 1 or c.ty is not F32 or parts < 2 or not TUNING.matmul_split_tail:
             rem, parts = 0, 1
         self.rem, self.parts = rem, parts

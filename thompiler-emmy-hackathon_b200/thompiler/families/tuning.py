@@ -22,6 +22,8 @@ class Tuning:
     matmul_stages: int = 0
     # cut a partial last wave of matmul tiles along K
     matmul_split_tail: bool = True
+    # the fewest 64-deep K blocks a part of a split tile keeps (CTA-pair kernel)
+    matmul_tail_kblocks: int = 16
 
 
 TUNING = Tuning()
