@@ -82,16 +82,18 @@ def test_strided_sum_plans():
 
 
 @pytest.mark.parametrize("M,N,K,lay,bn,want_bn,tiles,stages,rem,parts", [
-    (4096, 4096, 4096, "col", 0, 256, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 192, 512, 6, 0, 1),
-    (8192, 3072, 1024, "col", 256, 256, 384, 6, 0, 1), (8192, 3072, 1024, "row", 0, 256, 384, 6, 0, 1),
+    (4096, 4096, 4096, "col", 0, 256, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 256, 384, 6, 0, 1),
+    (8192, 3072, 1024, "col", 192, 192, 512, 6, 0, 1), (8192, 3072, 1024, "row", 0, 256, 384, 6, 0, 1),
+    (6400, 768, 1024, "col", 0, 192, 100, 6, 0, 1),
     (2048, 2560, 2048, "col", 0, 256, 80, 6, 6, 2), (256, 128, 256, "row", 0, 128, 1, 8, 0, 1),
     (512, 256, 256, "col", 128, 128, 4, 8, 0, 1)])
 def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tiles, stages, rem, parts):
     """The CTA-pair matmul (the default where it applies): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
     of B; one pair per two SMs; a cluster launch of an even grid; shared memory (with the
-    generic path's static arrays) inside one SM's 227 KB.  The width balances the waves: the
-    8192 x 3072 x 1024 rectangle takes 192 (512 tiles, 6.92 waves of 74 pairs, against 5.19 at
-    256) when B is K-major, 256 when B is MN-major (64-column loads)."""
+    generic path's static arrays) inside one SM's 227 KB.  The width scores wave efficiency times
+    the width's own (192: 0.8 of 256, measured): 8192 x 3072 x 1024 keeps 256 (5.19 waves of 74
+    pairs; 192's 6.92 waves do not make up for it), 6400 x 768 x 1024 takes 192 (75 tiles at 256
+    fill 1.01 waves of pairs, 100 at 192 fill 1.35); 192 needs K-major B."""
     from thompiler.families.matmul_pair import TcMatmulPair
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout=lay)
     monkeypatch.setattr(TUNING, "matmul_pair", False)
