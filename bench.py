@@ -283,7 +283,8 @@ class RowOps:
         d2h = sum(h[1].nbytes for h in host.values())
         # the device-API pipeline for comparison (one GPU only: it pins another 768 MB of host memory)
         streamed = self.e2e_streamed(steps) if self.world == 1 else None
-        out = {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+        out = {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "work": self.bytes_per_step,
+               "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3,
                "how": f"one thr_run_batch per step on pinned host buffers (the C-ABI host-buffer call, its "
                       f"descriptors prepared once), the three row ops as {3 * self.rows // chunk} requests of "
@@ -457,7 +458,7 @@ class Pointwise:
         sec = (time.perf_counter() - t) / steps
         runner.release()
         k.close()
-        return {"value": 12 * m / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 8 * m,
+        return {"value": 12 * m / sec / 1e9, "unit": "GB/s", "work": 12 * m, "h2d_bytes_per_step": 8 * m,
                 "d2h_bytes_per_step": 4 * m, "ms_per_step": sec * 1e3, "elements": m}
 
     def cpu_baseline(self) -> dict:
@@ -579,7 +580,8 @@ class FullSum:
                 float(v.item())
         sec = (time.perf_counter() - t) / steps
         runner.release()
-        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "h2d_bytes_per_step": hx.numel() * 4,
+        return {"value": self.bytes_per_step / sec / 1e9, "unit": "GB/s", "work": self.n * 4 + 4,
+                "h2d_bytes_per_step": hx.numel() * 4,
                 "d2h_bytes_per_step": 4, "ms_per_step": sec * 1e3}
 
     def cpu_baseline(self) -> dict:
@@ -713,7 +715,8 @@ class Matmul:
                     raise RuntimeError(r["stderr"])
         sec = (time.perf_counter() - t) / steps
         runner.release()
-        return {"value": self.flops_per_step / sec / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        return {"value": self.flops_per_step / sec / 1e12, "unit": "TFLOP/s", "work": self.flops_per_step,
+                "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": sec * 1e3}
 
     def cpu_baseline(self) -> dict:
@@ -842,7 +845,7 @@ class Attention:
         sec = (time.perf_counter() - t) / steps
         runner.release()
         kc.close()
-        return {"value": self.flops["attention"] / sec / 1e12, "unit": "TFLOP/s",
+        return {"value": self.flops["attention"] / sec / 1e12, "unit": "TFLOP/s", "work": self.flops["attention"],
                 "h2d_bytes_per_step": 3 * self.q.numel() * 2 + 4, "d2h_bytes_per_step": self.o.numel() * 2,
                 "ms_per_step": sec * 1e3,
                 "how": f"one thr_run_batch per step on pinned host buffers: {units // chunk} requests of {chunk} "
@@ -1084,11 +1087,15 @@ def measure(name: str, w, args, steps: int, world: int, rank: int, local: int) -
     if not args.no_e2e:
         e2e = w.e2e(max(1, min(steps, 5)))
         if world > 1:
-            v = torch.tensor([e2e["ms_per_step"]], device=f"cuda:{local}")
+            # the job's e2e rate: the work every rank did in one step over the slowest rank's step
+            v = torch.tensor([e2e["ms_per_step"]], device=f"cuda:{local}", dtype=torch.float64)
             dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            wk = torch.tensor([float(e2e["work"])], device=f"cuda:{local}", dtype=torch.float64)
+            dist.all_reduce(wk, op=dist.ReduceOp.SUM)
             unit_scale = 1e12 if getattr(w, "bound", "hbm") == "tensor" else 1e9
-            work = w.bytes_per_step if getattr(w, "sharded", False) else w.bytes_per_step * world
-            e2e["value"] = work / (float(v.item()) / 1e3) / unit_scale
+            e2e["value"] = float(wk.item()) / (float(v.item()) / 1e3) / unit_scale
+            e2e["ms_per_step"] = float(v.item())
+            e2e["work"] = float(wk.item())
     if rank != 0:
         return None
     pk = peaks()
