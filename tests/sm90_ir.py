@@ -568,3 +568,34 @@ def dequant_fp4(codes: "np.ndarray", scales: "np.ndarray") -> "np.ndarray":
     vals = table[nib]
     sc = np.exp2(scales.astype(np.float64) - 127.0)
     return vals * np.repeat(sc, 32, axis=1)
+
+
+def window_package(outdir: Path, W: int = 4) -> Path:
+    """Carried state indexed at run time, one thread per row of x[ROWS, COLS]: a ring of W cells
+    holds the row's last W values, cell j % W written at step j, so the step reads the value of
+    step j - W from the same cell before setting it: y[r, j] = x[r, j] - x[r, j - W] (0 for
+    j < W), and t[r] = the cell of the last step (x[r, COLS - 1]), read after the loop."""
+    f32 = F32T
+    cell = (B("%", V("j"), L(W)),)
+    step = (
+        ir.Pre("old", "win", cell),
+        ir.Load(("v",), "x", (V("r"), V("j")), f32),
+        assign("d", "subtract", "v", "old"),
+        ir.Carry("win", "v", cell, L(0.0, "float"), f32),
+        ir.Write("y", (V("r"), V("j")), ("d",), f32, False, "NONE"),
+    )
+    body = (
+        ir.Loop(axis("j", COLS), step, False, False),
+        ir.Pre("last", "win", (L((COLS - 1) % W),)),
+        ir.Write("t", (V("r"),), ("last",), f32, False, "NONE"),
+    )
+    tile = ir.Tile((axis("r", ROWS),), body, 128, 0, None, None, "m")
+    g = _graph({"x": ((ROWS, COLS), "f32")}, {}, "y", (ROWS, COLS), "k_window", tile)
+    g["nodes"]["y"]["outputs"] += [{"name": "t", "shape": [ROWS], "dtype": "f32"}]
+    g["outputs"] = ["y", "t"]
+    args = [{"name": "x", "dtype": "f32", "shape": [ROWS, COLS], "seed": 0},
+            {"name": "y", "dtype": "f32", "shape": [ROWS, COLS], "output": True},
+            {"name": "t", "dtype": "f32", "shape": [ROWS], "output": True}]
+    kmeta = {"node": "y", "arg_order": ["x", "y", "t"], "grid": [ROWS // 128, 1, 1], "block": [128, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_window", f"x - shifted(x, {W})", "k_window", g, kmeta, 0, 0)

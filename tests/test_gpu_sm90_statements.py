@@ -9,7 +9,8 @@ import pytest
 
 from sm90_ir import (COLS, EPILOGUE_FORMS, FRAGMENT_ATTENTION_EXTRAS, M, N, ROWS, blockscaled_matmul_package,
                      dequant_fp4, epilogue_matmul_package, fragment_attention_package, promote_matmul_package,
-                     scan_package, select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package)
+                     scan_package, select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package,
+                     window_package)
 from thompiler import problems, runner
 from thompiler.device import DeviceKernel
 
@@ -171,6 +172,19 @@ def test_blockscaled_fp4_matmul(tmp_path, M, N, K):
     want = dequant_fp4(x["xa"], x["sa"]) @ dequant_fp4(x["xb"], x["sb"]).T
     got = res["outputs"]["y"].astype(np.float64)
     assert np.max(np.abs(got - want)) <= 1e-5 * np.max(np.abs(want)), np.max(np.abs(got - want))
+
+
+def test_carried_state_run_time_cells(tmp_path):
+    """A carrier indexed at run time (cell j % 4 of a 4-cell ring, .local arrays): y[r, j] =
+    x[r, j] - x[r, j - 4] (x[r, j] for j < 4, the seed 0) and the last step's cell read after
+    the loop -- bit-exact against numpy float32."""
+    pkg = problems.load_package(window_package(tmp_path / "w", 4))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)["x"]
+    want = x.copy()
+    want[:, 4:] = x[:, 4:] - x[:, :-4]
+    np.testing.assert_array_equal(res["outputs"]["y"], want)
+    np.testing.assert_array_equal(res["outputs"]["t"].reshape(-1), x[:, -1])
 
 
 def test_promote_matmul_exact(tmp_path):

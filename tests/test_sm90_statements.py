@@ -8,7 +8,7 @@ import subprocess
 
 import pytest
 
-from sm90_ir import N, TILE, scan_package, select_package, tma_transpose_package
+from sm90_ir import N, TILE, scan_package, select_package, tma_transpose_package, window_package
 from thompiler import ir, load, synth
 from thompiler.compiler import compile_kernel
 from thompiler.emitter import read_sidecar
@@ -126,12 +126,23 @@ def test_carried_state_lowers(tmp_path):
     _ptxas(ptx, tmp_path)
 
 
-def test_carried_state_needs_constant_cells(tmp_path):
+def test_carried_state_run_time_cells(tmp_path):
+    """A carrier indexed at run time keeps its cells in per-thread .local arrays over the range
+    its indices reach: here j % 4 for the loop variable j, so 4 cells (16 bytes) per array."""
+    ptx = _ptx(window_package(tmp_path / "w", 4))
+    assert ".local .align 8 .b8 thl_win_cur[16];" in ptx and ".local .align 8 .b8 thl_win_next[16];" in ptx
+    assert "st.local.f32" in ptx and "ld.local.f32" in ptx
+    _ptxas(ptx, tmp_path)
+
+
+def test_carried_state_index_must_be_bounded(tmp_path):
+    """A run-time cell index with no bound from the axes (a value loaded from data) is refused."""
     d = scan_package(tmp_path / "c")
     f = next(d.glob("*.ir.json"))
-    f.write_text(f.read_text().replace("Carry(name='fib', value='fs', index=(Literal(value=1, dtype='int'),)",
-                                       "Carry(name='fib', value='fs', index=(Var(name='r'),)"))
-    with pytest.raises(NotImplementedError, match="fold to a constant"):
+    text = f.read_text().replace("Carry(name='fib', value='fs', index=(Literal(value=1, dtype='int'),)",
+                                 "Carry(name='fib', value='fs', index=(CastExpr(dtype='int', expr=Var(name='fs')),)")
+    f.write_text(text)
+    with pytest.raises(NotImplementedError, match="must be bounded by axis extents"):
         _ptx(d)
 
 

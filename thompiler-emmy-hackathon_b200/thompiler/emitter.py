@@ -36,6 +36,7 @@ class Emitter:
         self.builtins: set[str] = set()        # "lane", "warp" when read
         self.sidecar: dict | None = None       # tuned launch, rendered as a comment
         self.entry_attrs: list[str] = []       # .maxntid / .minnctapersm ...
+        self.local_decls: list[str] = []       # per-thread .local arrays, declared in the entry
 
     # ---- registers --------------------------------------------------------
 
@@ -98,6 +99,12 @@ class Emitter:
     def place(self, label: str) -> None:
         self.lines.append(f"{label}:")
 
+    def local(self, decl: str) -> None:
+        """A declaration at the top of the entry's body (a per-thread .local array)."""
+        line = decl if decl.rstrip().endswith(";") else f"{decl};"
+        if line not in self.local_decls:
+            self.local_decls.append(line)
+
     def module(self, decl: str) -> None:
         line = decl if decl.rstrip().endswith(";") else f"{decl};"
         if line not in self.module_decls:
@@ -122,7 +129,7 @@ class Emitter:
             side = [SIDECAR_TAG + json.dumps(self.sidecar, sort_keys=True, separators=(",", ":"))]
         sig = [f".visible .entry {entry}(", ",\n".join(f"\t{p}" for p in params), ")"]
         text = "\n".join([*header, *side, "", *self.module_decls, "", *sig, *self.entry_attrs,
-                          "{", *decls, "", *prologue, *self.lines, "}", ""])
+                          "{", *decls, *(f"\t{d}" for d in self.local_decls), "", *prologue, *self.lines, "}", ""])
         if not text.isascii():
             raise ValueError("PTX must be ASCII")
         return text
