@@ -599,3 +599,42 @@ def window_package(outdir: Path, W: int = 4) -> Path:
     kmeta = {"node": "y", "arg_order": ["x", "y", "t"], "grid": [ROWS // 128, 1, 1], "block": [128, 1, 1],
              "smem_bytes": 0, "zero_outputs": [], "args": args}
     return _write(outdir, "sm90_window", f"x - shifted(x, {W})", "k_window", g, kmeta, 0, 0)
+
+
+def chained_matmul_package(outdir: Path) -> Path:
+    """y = f16(x0 @ x1^T) @ x2^T on one 64 x 64 tile (x0, x1, x2 f16 [64, 64], K-major B operands):
+    the first product's C fragments go to a shared array with the 128-byte swizzle (RegStore
+    into shared memory, rounded to f16), which the second product reads back as A fragments
+    with ldmatrix under the same swizzle -- the staging a chained contraction needs."""
+    F16 = F16T
+    tid = B("+", B("*", V("_w"), L(32)), V("_lane"))
+    row0 = B("*", V("_w"), L(16))
+    frags = [ir.RegFragment("a", "a", (16, 8, 16), F16, 4, None), ir.RegFragment("b", "b", (16, 8, 16), F16, 8, None),
+             ir.RegFragment("c", "c", (16, 8, 16), F32T, 8, None), ir.RegFragment("pa", "a", (16, 8, 16), F16, 4, None),
+             ir.RegFragment("b2", "b", (16, 8, 16), F16, 8, None), ir.RegFragment("c2", "c", (16, 8, 16), F32T, 8, None)]
+    smem = [ir.Smem(n, (64, 64), "__half", 1024) for n in ("a_s", "b_s", "p_s", "b2_s")]
+    copies = [*_copy_tile("a_s", "x0", L(0), tid), *_copy_tile("b_s", "x1", L(0), tid),
+              *_copy_tile("b2_s", "x2", L(0), tid), ir.CpAsyncCommit(), ir.CpAsyncWait(0), ir.Sync(0, None, False)]
+
+    def gemm(afr, asmem, bfr, bsmem, cfr):
+        return _unrolled("_kk", 4, [
+            _ldm(f"{afr}[_kk]", asmem, (row0, B("*", V("_kk"), L(16))), "a"),
+            _unrolled("_j", 4, [_ldm(f"{bfr}[_j * 2]", bsmem, (B("*", V("_j"), L(16)), B("*", V("_kk"), L(16))), "b",
+                                     True, f"{bfr}[_j * 2 + 1]")]),
+            _unrolled("_n", 8, [ir.MmaSyncPtx(f"{cfr}[_n]", f"{afr}[_kk]", f"{bfr}[_n]", (16, 8, 16), "f16", "f32",
+                                              False, None, None)])])
+
+    def store(dst, cfr, swizzle):
+        return _unrolled("_s", 8, [ir.RegStore(dst, (row0, B("*", V("_s"), L(8))), f"{cfr}[_s]", (16, 8, 16), 0, None,
+                                               (), None, None, False, "m16n8k16", False, None, swizzle, None, None)])
+    body = (*frags, *smem, *copies, gemm("a", "a_s", "b", "b_s", "c"), store("p_s", "c", "B128"),
+            ir.Sync(0, None, False), gemm("pa", "p_s", "b2", "b2_s", "c2"), store("y", "c2", "NONE"))
+    tile = ir.Tile((axis("_w", 4), axis("_lane", 32)), body, 128, 0, None, None, "m")
+    entry = "k_chained_matmul"
+    g = _graph({"x0": ((64, 64), "f16"), "x1": ((64, 64), "f16"), "x2": ((64, 64), "f16")}, {}, "y", (64, 64), entry,
+               tile)
+    args = [{"name": n, "dtype": "f16", "shape": [64, 64], "seed": i} for i, n in enumerate(("x0", "x1", "x2"))]
+    args.append({"name": "y", "dtype": "f32", "shape": [64, 64], "output": True})
+    kmeta = {"node": "y", "arg_order": ["x0", "x1", "x2", "y"], "grid": [1, 1, 1], "block": [128, 1, 1],
+             "smem_bytes": 0, "zero_outputs": [], "args": args}
+    return _write(outdir, "sm90_chained_matmul", "(x0 @ x1.T).half() @ x2.T", entry, g, kmeta, 2e-2, 2e-3)

@@ -10,8 +10,8 @@ import subprocess
 
 import pytest
 
-from sm90_ir import (FRAGMENT_ATTENTION_EXTRAS, blockscaled_matmul_package, fragment_attention_package,
-                     promote_matmul_package)
+from sm90_ir import (FRAGMENT_ATTENTION_EXTRAS, blockscaled_matmul_package, chained_matmul_package,
+                     fragment_attention_package, promote_matmul_package)
 from thompiler import ir, load, synth
 from thompiler.compiler import compile_kernel
 
@@ -164,3 +164,24 @@ def test_fp4_decode_table():
     from thompiler.handlers.blockscale import e2m1_value
     assert [e2m1_value(n) for n in range(8)] == [0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0]
     assert [e2m1_value(n) for n in range(8, 16)] == [-0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+def test_regstore_into_swizzled_shared_memory(tmp_path):
+    """RegStore into a shared array with the 128-byte swizzle: each register pair of the first
+    product becomes one f16x2 store at the swizzled element (row 16 w + g (+ 8), column 8 s + 2 t),
+    which the second product's ldmatrix reads back under the same swizzle.  A swizzle on a
+    global output and the Volta layout stay refused."""
+    d = chained_matmul_package(tmp_path / "c")
+    ptx = _ptx(d)
+    body = ptx.splitlines()
+    assert sum("st.shared.b32" in ln for ln in body) == 8 * 2
+    assert sum(ln.strip().startswith("cvt.rn.f16x2.f32") for ln in body) == 8 * 2
+    _ptxas(ptx, tmp_path)
+    _edit(d, "swizzle='NONE', row_dim=None, col_dim=None)", "swizzle='B128', row_dim=None, col_dim=None)")
+    with pytest.raises(NotImplementedError, match="into global memory"):
+        _ptx(d)
+    d = chained_matmul_package(tmp_path / "v")
+    _edit(d, "volta_interleaved=False, fragment_index=None, swizzle='NONE'",
+          "volta_interleaved=True, fragment_index=None, swizzle='NONE'")
+    with pytest.raises(NotImplementedError, match="Volta"):
+        _ptx(d)

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from sm90_ir import (COLS, EPILOGUE_FORMS, FRAGMENT_ATTENTION_EXTRAS, M, N, ROWS, blockscaled_matmul_package,
-                     dequant_fp4, epilogue_matmul_package, fragment_attention_package, promote_matmul_package,
+                     chained_matmul_package, dequant_fp4, epilogue_matmul_package, fragment_attention_package, promote_matmul_package,
                      scan_package, select_package, stuck_wait_package, tma_transpose_package, wgmma_gemm_package,
                      window_package)
 from thompiler import problems, runner
@@ -172,6 +172,18 @@ def test_blockscaled_fp4_matmul(tmp_path, M, N, K):
     want = dequant_fp4(x["xa"], x["sa"]) @ dequant_fp4(x["xb"], x["sb"]).T
     got = res["outputs"]["y"].astype(np.float64)
     assert np.max(np.abs(got - want)) <= 1e-5 * np.max(np.abs(want)), np.max(np.abs(got - want))
+
+
+def test_regstore_into_swizzled_shared_memory(tmp_path):
+    """A product's C fragments staged in shared memory with the 128-byte swizzle (RegStore, f16)
+    and read back by ldmatrix under the same swizzle as the A operand of a second product:
+    y = f16(x0 @ x1^T) @ x2^T against float64 numpy with the intermediate rounded to f16."""
+    pkg = problems.load_package(chained_matmul_package(tmp_path / "c"))
+    res = problems.run_package(pkg, problems.compile_package(pkg))
+    x = problems.make_inputs(pkg)
+    p = (x["x0"].astype(np.float64) @ x["x1"].astype(np.float64).T).astype(np.float16).astype(np.float64)
+    want = p @ x["x2"].astype(np.float64).T
+    np.testing.assert_allclose(res["outputs"]["y"], want, rtol=2e-2, atol=2e-3)
 
 
 def test_carried_state_run_time_cells(tmp_path):

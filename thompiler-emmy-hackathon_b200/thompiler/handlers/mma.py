@@ -268,6 +268,44 @@ def _plus(addr: str, nbytes: int) -> str:
     return f"{base}+{int(off or 0) + nbytes}"
 
 
+def _reg_store_shared(w: "Walker", st: ir.RegStore) -> None:
+    """A C fragment into a shared array (row-major by its extents, after ``swizzle``: the layout
+    ldmatrix and cp.async read with the same mode), as f32 or rounded to f16 -- e.g. a product
+    staged for the next MMA's A operand.  Each register pair is one 8- (f32) or 4-byte (f16
+    pair) store: its two columns share a swizzle chunk."""
+    em = w.em
+    arr = w.smem[st.dst_buffer]
+    if st.epilogue is not None or st.extra_frags or st.m_guard is not None or st.n_guard is not None or st.atomic:
+        raise NotImplementedError("RegStore into shared memory: epilogues, guards and atomics are for global outputs")
+    shape = tuple(int(x) for x in st.shape)
+    if shape != (16, 8, 16):
+        raise NotImplementedError(f"RegStore of shape {st.shape} into shared memory")
+    if arr.ty not in (F32, F16):
+        raise NotImplementedError(f"RegStore into a {arr.ty.name} shared array")
+    frag, regs = fragment_regs(w, st.frag)
+    if frag.role != "c" or frag.ty is not F32 or len(regs) != 4:
+        raise ValueError(f"RegStore of {st.frag}: not an f32 m16n8 accumulator")
+    index = list(st.dst_index)
+    if len(index) != len(arr.extents):
+        raise ValueError(f"RegStore to {arr.name}: {len(index)}-d index for a {len(arr.extents)}-d array")
+    lane = ir.Var("lane")
+    g = _lane_expr("/", lane, 4)
+    col = _lane_expr("*", _lane_expr("%", lane, 4), 2)
+    for dr in (0, 8):
+        idx = list(index)
+        idx[-2] = ir.BinaryExpr("+", index[-2], g if dr == 0 else _lane_expr("+", g, dr))
+        idx[-1] = ir.BinaryExpr("+", index[-1], col)
+        flat = address.flat_index(w, arr.extents, tuple(idx), arr.name)
+        addr = address.shared_element_address(w, arr, flat, st.swizzle or "NONE")
+        lo, hi = regs[2 if dr else 0], regs[3 if dr else 1]
+        if arr.ty is F32:
+            em.ins(f"st.shared.v2.f32 [{addr}], {{{lo}, {hi}}}")
+        else:
+            packed = em.tmp("b32")
+            em.ins(f"cvt.rn.f16x2.f32 {packed}, {hi}, {lo}")
+            em.ins(f"st.shared.b32 [{addr}], {packed}")
+
+
 def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
     """A C fragment (an m16n8 ``mma.sync`` accumulator or an m64nN warpgroup one) to global
     memory, each lane storing its registers at the rows and columns of the accumulator layout.
@@ -289,9 +327,13 @@ def emit_reg_store(w: "Walker", st: ir.RegStore) -> None:
     alone keeps the pair stores."""
     em = w.em
     em.note(f"RegStore {st.dst_buffer} <- {st.frag}")
-    if (st.fragment_layout not in ("m16n8k16", "m64nNk16") or st.volta_interleaved
-            or st.swizzle not in ("NONE", None)):
-        raise NotImplementedError("RegStore form: swizzled or Volta layout")
+    if st.fragment_layout not in ("m16n8k16", "m64nNk16") or st.volta_interleaved:
+        raise NotImplementedError("RegStore form: Volta (interleaved) layout, which no MMA of this backend produces")
+    if st.dst_buffer in w.smem:
+        _reg_store_shared(w, st)
+        return
+    if st.swizzle not in ("NONE", None):
+        raise NotImplementedError(f"RegStore with swizzle {st.swizzle} into global memory (shared arrays only)")
     if st.epilogue is not None and not isinstance(st.epilogue, ir.Lambda):
         raise NotImplementedError(f"RegStore epilogue {type(st.epilogue).__name__} (a Lambda expected)")
     if st.extra_frags and st.epilogue is None:
