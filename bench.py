@@ -1043,8 +1043,8 @@ def measure(name: str, w, args, steps: int, world: int, rank: int, local: int) -
     torch.cuda.synchronize()
     per_kernel = {k: statistics.mean(a.elapsed_time(b) for a, b in events[k]) for k in w.kinds}
     # the timed region: the K steps replayed from CUDA graphs of G steps each (no host launch
-    # overhead between kernels), or launched one by one when a step holds an NCCL collective
-    use_graph = not args.no_graph and getattr(w, "collective", None) != "nccl"
+    # overhead between kernels; a step's NCCL all-reduce is captured with it)
+    use_graph = not args.no_graph
     graph, G = None, 1
     if use_graph:
         G = next(g for g in range(min(steps, 500), 0, -1) if steps % g == 0)
@@ -1056,10 +1056,18 @@ def measure(name: str, w, args, steps: int, world: int, rank: int, local: int) -
         graph.replay()
         torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # the clock sampler starts before the ranks meet, so they all start the timed region right
+    # after the barrier (a combine inside the kernels makes early ranks wait for late ones)
+    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
+    if world > 1:
+        # the host barrier releases the ranks some microseconds apart; a one-element all-reduce
+        # queued just before the start event lines the GPUs up, so a short region is not
+        # lengthened on the early ranks by the late ranks' start
+        tick = torch.zeros(1, device=f"cuda:{local}")
+        dist.all_reduce(tick)
     start.record()
     if graph is not None:
         for _ in range(steps // G):
