@@ -53,6 +53,7 @@ typedef CUresult (*PFN_FuncGetAttribute)(int *, CUfunction_attribute, CUfunction
 typedef CUresult (*PFN_FuncSetAttribute)(CUfunction, CUfunction_attribute, int);
 typedef CUresult (*PFN_LaunchKernel)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned,
                                      unsigned, unsigned, CUstream, void **, void **);
+typedef CUresult (*PFN_LaunchKernelEx)(const CUlaunchConfig *, CUfunction, void **, void **);
 typedef CUresult (*PFN_TensorMapEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                              const cuuint64_t *, const cuuint64_t *,
                                              const cuuint32_t *, const cuuint32_t *,
@@ -69,6 +70,7 @@ struct Driver {
     PFN_FuncGetAttribute func_get = nullptr;
     PFN_FuncSetAttribute func_set = nullptr;
     PFN_LaunchKernel launch = nullptr;
+    PFN_LaunchKernelEx launch_ex = nullptr;
     PFN_TensorMapEncodeTiled tmap = nullptr;
     PFN_GetErrorString err_string = nullptr;
 };
@@ -110,6 +112,7 @@ int ensure_driver() {
                entry("cuFuncGetAttribute", &d.func_get) && entry("cuFuncSetAttribute", &d.func_set) &&
                entry("cuLaunchKernel", &d.launch) && entry("cuGetErrorString", &d.err_string);
     entry("cuTensorMapEncodeTiled", &d.tmap);  // optional: only TMA kernels need it
+    entry("cuLaunchKernelEx", &d.launch_ex);   // optional: launches that overlap the previous kernel
     if (!all) return fail(THR_ERR_CUDA, "the CUDA driver does not export the required entry points");
     d.ok = true;
     g_drv = d;
@@ -554,9 +557,15 @@ int thr_module_global(uint64_t module, const char *name, uint64_t *dptr, uint64_
 
 int thr_launch(uint64_t function, const uint32_t grid[3], const uint32_t block[3], uint32_t smem_bytes,
                const uint64_t *args, int nargs, uint64_t stream) {
+    return thr_launch_ex(function, grid, block, smem_bytes, args, nargs, stream, 0);
+}
+
+int thr_launch_ex(uint64_t function, const uint32_t grid[3], const uint32_t block[3], uint32_t smem_bytes,
+                  const uint64_t *args, int nargs, uint64_t stream, uint32_t flags) {
     int s = ensure_driver();
     if (s) return s;
-    if (!grid || !block || nargs < 0 || (nargs > 0 && !args)) return fail(THR_ERR_REQUEST, "thr_launch: bad arguments");
+    if (!grid || !block || nargs < 0 || (nargs > 0 && !args) || (flags & ~THR_LAUNCH_OVERLAP_PREVIOUS))
+        return fail(THR_ERR_REQUEST, "thr_launch: bad arguments");
     CUfunction f = (CUfunction)(uintptr_t)function;
     if (smem_bytes > 48 * 1024) {
         CUresult r = g_drv.func_set(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)smem_bytes);
@@ -565,6 +574,29 @@ int thr_launch(uint64_t function, const uint32_t grid[3], const uint32_t block[3
     std::vector<uint64_t> vals(args, args + nargs);
     std::vector<void *> params(nargs);
     for (int i = 0; i < nargs; ++i) params[i] = &vals[i];
+    if ((flags & THR_LAUNCH_OVERLAP_PREVIOUS) && g_drv.launch_ex) {
+        // programmatic stream serialisation: the launch may begin while the stream's previous
+        // kernel is still running (once that kernel's CTAs signal griddepcontrol.launch_dependents);
+        // the kernel itself waits (griddepcontrol.wait) before it touches global data
+        CUlaunchAttribute attr;
+        memset(&attr, 0, sizeof attr);
+        attr.id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attr.value.programmaticStreamSerializationAllowed = 1;
+        CUlaunchConfig cfg;
+        memset(&cfg, 0, sizeof cfg);
+        cfg.gridDimX = grid[0];
+        cfg.gridDimY = grid[1];
+        cfg.gridDimZ = grid[2];
+        cfg.blockDimX = block[0];
+        cfg.blockDimY = block[1];
+        cfg.blockDimZ = block[2];
+        cfg.sharedMemBytes = smem_bytes;
+        cfg.hStream = (CUstream)(uintptr_t)stream;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        CUresult r = g_drv.launch_ex(&cfg, f, nargs ? params.data() : nullptr, nullptr);
+        return r == CUDA_SUCCESS ? THR_OK : fail(THR_ERR_RUN, "cuLaunchKernelEx: %s", cu_name(r));
+    }
     CUresult r = g_drv.launch(f, grid[0], grid[1], grid[2], block[0], block[1], block[2], smem_bytes,
                               (CUstream)(uintptr_t)stream, nargs ? params.data() : nullptr, nullptr);
     return r == CUDA_SUCCESS ? THR_OK : fail(THR_ERR_RUN, "cuLaunchKernel: %s", cu_name(r));

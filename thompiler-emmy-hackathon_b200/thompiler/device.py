@@ -45,12 +45,16 @@ class DeviceKernel:
         return m.group(1) if m else "generic"
 
     def __call__(self, ptrs: dict[str, int], stream: int = 0) -> None:
+        """Launch on device pointers.  A tuned launch whose kernel waits for the previous grid
+        before touching global data (``plan.pdl``) is issued as a programmatic dependent launch:
+        its CTAs may start, and set up, while the stream's previous kernel finishes."""
         args = [ptrs[n] for n in self.arg_order]
+        pdl = self.plan.pdl
         if self.tmaps is None:
-            self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream)
+            self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream, overlap=pdl)
             return
         k = self.tmaps.bind(ptrs, stream)
-        self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream)
+        self.fn.launch(self.plan.grid, self.plan.block, self.plan.smem, args, stream, overlap=pdl)
         self.tmaps.launched(k, stream)
 
     def error_word(self) -> int:

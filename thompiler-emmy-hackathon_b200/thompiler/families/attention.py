@@ -203,6 +203,7 @@ class TcAttention(TunedKernel):
         KS, VS = self.ks, self.vs
         commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64"
         tma = "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        self.pdl_trigger()
 
         tid, warp, lane = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {tid}, %tid.x")
@@ -258,6 +259,9 @@ class TcAttention(TunedKernel):
         ins("tcgen05.fence::before_thread_sync")
         ins("bar.sync 0")
         ins("tcgen05.fence::after_thread_sync")
+        # barriers and TMEM are set up while the stream's previous kernel may still run; from
+        # here on the CTA reads and writes global data
+        self.pdl_wait()
         tmem = t("b32")
         ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
         # TMEM columns: O_g at 128 g, S_g at 256 + 128 g; P_g (f16 pairs) in the first 64 columns of S_g

@@ -18,6 +18,7 @@ from __future__ import annotations
 
 from thompiler import prologue
 from thompiler.emitter import Emitter
+from thompiler.families.tuning import TUNING
 from thompiler.load import KernelInfo
 from thompiler.walk import Walker
 
@@ -29,6 +30,22 @@ class TunedKernel:
         self.k = kernel
         self.em = Emitter()
         self.w = Walker(self.em, kernel)
+        self.pdl = False            # set by pdl_wait: the tuned body waits for the previous grid
+
+    # programmatic dependent launch ----------------------------------------------
+    def pdl_trigger(self) -> None:
+        """Let the stream's next kernel launch (its CTAs start and set up while this grid runs;
+        it still waits for this grid's completion before touching global data)."""
+        if TUNING.pdl:
+            self.em.ins("griddepcontrol.launch_dependents")
+
+    def pdl_wait(self) -> None:
+        """Wait until the stream's previous grid has completed and its writes are visible: every
+        thread of a tuned body runs this before its first access to global data, so the launch
+        may be a programmatic dependent one (the launch record's ``pdl``)."""
+        if TUNING.pdl:
+            self.em.ins("griddepcontrol.wait")
+            self.pdl = True
 
     # subclasses implement these -------------------------------------------
     def guard(self, generic_label: str) -> None:
@@ -53,6 +70,8 @@ class TunedKernel:
         em.ins("ret")
         em.place(generic)
         em.note("generic lowering of the same IR (any launch geometry)")
+        if self.pdl:                 # the generic path too waits for the previous grid first
+            em.ins("griddepcontrol.wait")
         w.load_hook = w.write_hook = None
         w.consts.clear()
         w.body(self.k.body)
@@ -61,6 +80,10 @@ class TunedKernel:
         if side is not None:
             # keep what the generic path's statements recorded (IR-level tensor maps)
             side = dict(em.sidecar or {}, **side, family=self.family)
+        if self.pdl:
+            # both paths wait for the previous grid before touching global data, so any launch of
+            # the module (the tuned one or meta.json's) may overlap the stream's previous kernel
+            side = dict(side if side is not None else (em.sidecar or {}), pdl=True)
         em.sidecar = side if side is not None else em.sidecar
         return em.render(prologue.header(), self.k.name, prologue.params(self.k))
 

@@ -270,6 +270,7 @@ class TcMatmul(TunedKernel):
         kblocks = self.Ks // BK
         tmem_cols = 512 if 2 * BN > 256 else 256
         ins, place, lab = em.ins, em.place, em.label
+        self.pdl_trigger()
 
         tid, warp, lane = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {tid}, %tid.x")
@@ -317,6 +318,9 @@ class TcMatmul(TunedKernel):
         ins("tcgen05.fence::before_thread_sync")
         ins("bar.sync 0")
         ins("tcgen05.fence::after_thread_sync")
+        # barriers and TMEM are set up while the stream's previous kernel may still run; from
+        # here on the CTA reads and writes global data
+        self.pdl_wait()
         tmem = t("b32")
         ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
         cta, ncta = self.special("%ctaid.x"), self.special("%nctaid.x")

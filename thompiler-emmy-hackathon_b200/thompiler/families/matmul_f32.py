@@ -187,6 +187,8 @@ class MatmulF32(TunedKernel):
     def emit_tuned(self) -> None:
         em = self.em
         t, ins, place, lab = em.tmp, em.ins, em.place, em.label
+        self.pdl_trigger()
+        self.pdl_wait()
         M, N, K, BM, BN, RM, RN = self.M, self.N, self.K, self.BM, self.BN, self.RM, self.RN
         AS = BM + 4                          # k-major A rows, padded against bank conflicts
         a_buf, b_buf = BK * AS * 4, BK * BN * 4

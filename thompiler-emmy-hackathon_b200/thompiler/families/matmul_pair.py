@@ -140,6 +140,7 @@ class TcMatmulPair(TcMatmul):
         kblocks = self.Ks // BK
         mcommit = "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
         tma_ld = "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        self.pdl_trigger()
 
         tid, warp, lane = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {tid}, %tid.x")
@@ -188,6 +189,9 @@ class TcMatmulPair(TcMatmul):
         ins("barrier.cluster.arrive.release")
         ins("barrier.cluster.wait.acquire")
         ins("tcgen05.fence::after_thread_sync")
+        # barriers and TMEM are set up while the stream's previous kernel may still run; from
+        # here on the pair reads and writes global data
+        self.pdl_wait()
         tmem = t("b32")
         ins(f"ld.shared.u32 {tmem}, [{bars}+{slot_off}]")
         lbars = t("b32")                                   # the leader's barriers, cluster address

@@ -114,6 +114,8 @@ class Pointwise(TunedKernel):
     def emit_tuned(self) -> None:
         from thompiler.lowering import address
         em, w = self.em, self.w
+        self.pdl_trigger()
+        self.pdl_wait()
         pos = {id(s): i for i, s in enumerate(self.stmts)}
 
         def load_hook(w_, load) -> bool:

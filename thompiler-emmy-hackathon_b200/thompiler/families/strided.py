@@ -307,6 +307,8 @@ class StridedReduce(TunedKernel):
 
     def emit_tuned(self) -> None:
         w = self.w
+        self.pdl_trigger()
+        self.pdl_wait()              # the body reads its inputs from the first instruction on
         w.load_hook = self._load_hook
         self._hoist_consts(tuple(self.l1.body) + (tuple(self.tail.body) if self.row_mode else ()))
         if self.row_mode:

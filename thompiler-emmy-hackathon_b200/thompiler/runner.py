@@ -79,6 +79,8 @@ def library() -> ctypes.CDLL:
             "thr_function_attrs": ([u64] + [ctypes.POINTER(i32)] * 4, i32),
             "thr_module_global": ([u64, ctypes.c_char_p, ctypes.POINTER(u64), ctypes.POINTER(u64)], i32),
             "thr_launch": ([u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(u64), i32, u64], i32),
+            "thr_launch_ex": ([u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(u64), i32, u64, ctypes.c_uint32],
+                              i32),
             "thr_run": ([u64, u32x3, u32x3, ctypes.c_uint32, ctypes.POINTER(ThrArg), i32, i32, i32,
                          ctypes.c_double, ctypes.POINTER(ctypes.c_float), u64], i32),
             "thr_tensor_map": ([p, i32, i32, u64, ctypes.POINTER(u64), ctypes.POINTER(u64),
@@ -137,6 +139,7 @@ def _dims(v) -> ctypes.Array:
     return (ctypes.c_uint32 * 3)(*[int(x) for x in v[:3]])
 
 
+OVERLAP_PREVIOUS = 1                                # THR_LAUNCH_OVERLAP_PREVIOUS
 ENTRY = re.compile(r"^\s*\.(?:visible\s+)?\.entry\s+([A-Za-z_$][\w$]*)\s*\(", re.M)
 
 
@@ -150,9 +153,13 @@ class Function:
     static_smem: int = 0
     local_bytes: int = 0
 
-    def launch(self, grid, block, smem: int, ptrs: list[int], stream: int = 0) -> None:
+    def launch(self, grid, block, smem: int, ptrs: list[int], stream: int = 0, overlap: bool = False) -> None:
+        """Launch on device pointers; ``overlap``: programmatic dependent launch (the kernel may
+        begin during the stream's previous kernel -- only for kernels that wait for it before
+        touching global data, ``LaunchPlan.pdl``)."""
         a = (ctypes.c_uint64 * max(1, len(ptrs)))(*[int(p) for p in ptrs])
-        check(library().thr_launch(self.handle, _dims(grid), _dims(block), int(smem), a, len(ptrs), int(stream)),
+        check(library().thr_launch_ex(self.handle, _dims(grid), _dims(block), int(smem), a, len(ptrs), int(stream),
+                                      OVERLAP_PREVIOUS if overlap else 0),
               f"launch of {self.name}")
 
 
@@ -229,6 +236,8 @@ class LaunchPlan:
     tmap_ptrs: dict | None = None                   # {"global": name, "params": [...]}
     error_word: str | None = None                   # module global a kernel records wait time-outs in
     counters: list = field(default_factory=list)    # self-resetting arrival counters (module globals)
+    pdl: bool = False                               # the tuned body waits (griddepcontrol.wait) before
+                                                    # global accesses: launches may overlap the previous kernel
 
 
 def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> LaunchPlan:
@@ -240,10 +249,10 @@ def plan_launch(module: Module, kmeta: dict, honour_meta: bool = False) -> Launc
     if "grid" not in side or honour_meta:
         err = side.get("error_word") if "grid" not in side else None
         return LaunchPlan(tuple(kmeta["grid"]), tuple(kmeta["block"]), int(kmeta.get("smem_bytes", 0)), False,
-                          ir_maps, None, err, counters)
+                          ir_maps, None, err, counters, bool(side.get("pdl", False)))
     return LaunchPlan(tuple(side["grid"]), tuple(side["block"]), int(side.get("smem_bytes", 0)), True,
                       list(side.get("tmaps", [])) + ir_maps, side.get("tmap_ptrs"), side.get("error_word"),
-                      counters)
+                      counters, bool(side.get("pdl", False)))
 
 
 def encode_tensor_map(spec: dict, base: int) -> bytes:
