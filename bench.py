@@ -1068,6 +1068,10 @@ def measure(name: str, w, args, steps: int, world: int, rank: int, local: int) -
         # lengthened on the early ranks by the late ranks' start
         tick = torch.zeros(1, device=f"cuda:{local}")
         dist.all_reduce(tick)
+    # a ~1 ms device-side delay (outside the timed region) before the start event: by the time
+    # it ends the host has queued every replay of the region, so a region of a few microseconds
+    # per step does not also time the host's submission of its first graph
+    torch.cuda._sleep(2_000_000)
     start.record()
     if graph is not None:
         for _ in range(steps // G):
