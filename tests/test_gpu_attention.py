@@ -131,3 +131,26 @@ def test_attention_rescale_in_part_of_a_warp(tmp_path, grid):
     ref = _sdpa64(q.cpu().numpy(), kk.cpu().numpy(), v.cpu().numpy())
     np.testing.assert_allclose(o.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL)
     k.close()
+
+
+@pytest.mark.parametrize("units", [16, 32, 64])
+def test_attention_shard_shapes(tmp_path, units):
+    """The kernels the ranks of a 8-, 4- and 2-GPU run compile for their share of the benchmark's
+    128 (batch, head) units: [units, 1, 2048, 128], i.e. 128, 256 and 512 tiles of 256 queries
+    over the 148 SMs (one partial wave; one full wave and a partial one; three and a partial
+    one).  Every unit against float32 PyTorch; the error word stays 0."""
+    import torch
+    shape = (units, 1, 2048, 128)
+    k = DeviceKernel(synth.attention_package(tmp_path / "att", *shape) / "k_attention.ir.json")
+    g = torch.Generator(device="cuda").manual_seed(53 + units)
+    q, kk, v = (torch.randn(*shape, device="cuda", generator=g).half() for _ in range(3))
+    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
+    o = torch.full(shape, float("nan"), device="cuda", dtype=torch.float16)
+    k({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": kk.data_ptr(), "v": v.data_ptr(), "attn": o.data_ptr()},
+      torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert k.error_word() == 0 and not torch.isnan(o).any()
+    s = (q[:, 0].float() @ kk[:, 0].float().transpose(-1, -2)) / shape[-1] ** 0.5
+    ref = torch.softmax(s, -1) @ v[:, 0].float()
+    assert torch.allclose(o[:, 0].float(), ref, rtol=RTOL, atol=ATOL), (o[:, 0].float() - ref).abs().max()
+    k.close()
