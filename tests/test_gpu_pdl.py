@@ -82,3 +82,58 @@ def test_overlapped_launches_in_a_cuda_graph(tmp_path):
     del graph
     for k in (pw, sm, rs):
         k.close()
+
+
+def test_tensor_core_kernels_read_what_the_previous_kernel_wrote(tmp_path):
+    """The tcgen05 families under programmatic dependent launch: an attention kernel writes O
+    (f16 [1, 2, 512, 128]) and a matmul launched right behind it reads O as its A operand through
+    TMA ([1024, 128] @ B^T, B [256, 128]); fresh Q, K, V every round, eagerly and in a CUDA graph.
+    C against the float64 product of the O the attention wrote, O against float32 attention."""
+    import torch
+    shape = (1, 2, 512, 128)
+    M, N, K = 1024, 256, 128
+    att = DeviceKernel(synth.attention_package(tmp_path / "att", *shape) / "k_attention.ir.json")
+    mm = DeviceKernel(synth.matmul_package(tmp_path / "mm", M, N, K) / "k_matmul_f16.ir.json")
+    assert att.plan.pdl and mm.plan.pdl and att.plan.tmaps and mm.plan.tmaps
+    g = torch.Generator(device="cuda").manual_seed(61)
+    q, k, v = (torch.empty(*shape, device="cuda", dtype=torch.float16) for _ in range(3))
+    c = torch.tensor([shape[-1] ** 0.5], device="cuda")
+    o = torch.empty(*shape, device="cuda", dtype=torch.float16)
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.05).half()
+    out = torch.empty(M, N, device="cuda")
+
+    def chain(stream):
+        att({"div_c1": c.data_ptr(), "q": q.data_ptr(), "k": k.data_ptr(), "v": v.data_ptr(),
+             "attn": o.data_ptr()}, stream)
+        mm({"x0": o.data_ptr(), "x1": b.data_ptr(), "matmul": out.data_ptr()}, stream)
+
+    def refill():
+        for x in (q, k, v):
+            x.copy_(torch.randn(*shape, device="cuda", generator=g))
+        o.fill_(float("nan"))
+        out.fill_(float("nan"))
+
+    def check():
+        s = (q[0].float() @ k[0].float().transpose(-1, -2)) / shape[-1] ** 0.5
+        ref_o = torch.softmax(s, -1) @ v[0].float()
+        assert torch.allclose(o[0].float(), ref_o, rtol=2e-2, atol=2e-3)
+        ref_c = o.view(M, K).double() @ b.double().t()
+        assert (out.double() - ref_c).abs().max().item() < 1e-4
+        assert att.error_word() == 0 and mm.error_word() == 0
+
+    for _ in range(4):
+        refill()
+        chain(torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        check()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain(torch.cuda.current_stream().cuda_stream)
+    for _ in range(4):
+        refill()
+        graph.replay()
+        torch.cuda.synchronize()
+        check()
+    del graph
+    att.close()
+    mm.close()
