@@ -50,9 +50,13 @@ def test_attention_plan_benchmark_shape(tmp_path, monkeypatch):
     # P handed over and O released by the 128 softmax threads of a group: four barriers of 128
     inits = re.findall(r"mbarrier\.init\.shared::cta\.b64 \[[^\]]+\], (\d+);", ptx)
     assert inits.count("128") == 2 + 2
+    # one-lane instructions under elect.sync (K / V producer, MMA issuer, Q loader, epilogue);
+    # each query tile's Q loaded on its own, the next tile's prefetched into L2
+    assert ptx.count("elect.sync") == 4
+    assert "cp.async.bulk.prefetch.tensor.2d.L2.global" in ptx
 
 
-@pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 192), ((2, 2, 384, 64), 1, 192),
+@pytest.mark.parametrize("shape,qt,threads", [((1, 1, 128, 64), 1, 224), ((2, 2, 384, 64), 1, 224),
                                               ((2, 2, 512, 64), 2, 384), ((1, 3, 512, 128), 2, 384)])
 def test_attention_plan_small(tmp_path, shape, qt, threads):
     fam = recognise(_kernel(_ir(synth.attention_package(tmp_path / "a", *shape))))
@@ -115,6 +119,7 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tile
         assert side["tmaps"][1]["box"] == [64, fam.BN // 2]
     ptx = fam.emit()
     assert ".reqnctapercluster 2, 1, 1" in ptx and "tcgen05.mma.cta_group::2.kind::f16" in ptx
+    assert ptx.count("elect.sync") == 3                          # producer, MMA issuer, epilogue
     assert "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global" in ptx   # each CTA's own loads
     assert not re.search(r"cp\.async\.bulk[^\n]*multicast", ptx)     # no load is multicast
     assert ("thc_tail_ws" in ptx) == bool(rem)

@@ -14,14 +14,17 @@ Tuned body: one CTA per (head, QT query tiles of 128), QT = 2 when S allows
 (384 threads), else 1 (192 threads):
   warps 0 .. 4QT-1  softmax, one warpgroup per query tile g; thread = query row,
             warp w reads TMEM lanes 32 (w % 4) ..;
-  warp 4QT  TMA: the Q tiles once, then K and V tiles of 128 keys through
-            their own rings (128B-swizzled rows of 64 d);
+  warp 4QT  TMA: K and V tiles of 128 keys through their own rings
+            (128B-swizzled rows of 64 d);
   warp 4QT+1  tcgen05 issuer: S_g = Q_g K_i^T (SS form, M = 128 queries,
             N = 128 keys, K = D) and O_g += P_g V_i (TS form: A = P_g from
             TMEM, B = V as an MN-major shared operand), ordered PV_0, S_0(next),
             PV_1, S_1(next) so each group's softmax overlaps the other's MMAs;
-  with QT = 2 warps 10-11 fill the third warpgroup, which hands registers to
+  warp 4QT+2  TMA: each query tile's Q_g once the previous tile's last S_g is
+            done, and an L2 prefetch of the next tile's Q;
+  with QT = 2 warp 11 completes the third warpgroup, which hands registers to
   the softmax warpgroups (setmaxnreg 168 -> 224 / 56).
+The single-thread instructions (MMA, commit, TMA) are guarded by elect.sync.
 TMEM (512 columns): O_g at 128 g, S_g at 256 + 128 g; P_g (f16 pairs) is
 written over the first 64 columns of S_g.  Softmax per row and key block: the
 128 scores in registers (four loads, one wait), a three-input max tree, O and
@@ -40,8 +43,8 @@ import math
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
-from thompiler.families.kit import (TMAP_RING, TMAP_SETS, TMAP_TABLE, Kit, declare_tmap_ring, desc_hi, idesc_f16,
-                                   select_tmap_set, tmap_address)
+from thompiler.families.kit import (TMAP_RING, TMAP_SETS, TMAP_TABLE, Kit, declare_tmap_ring, desc_hi, elect_one,
+                                   idesc_f16, select_tmap_set, tmap_address)
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
 
@@ -67,12 +70,12 @@ class TcAttention(TunedKernel):
         # two 128-query tiles per CTA (two softmax warp groups sharing each K / V tile) when they fit
         self.qt = 2 if Sq % (2 * BM) == 0 else 1
         # warps 0 .. 4 qt - 1 softmax, one thread per query row (warp w reads TMEM lanes 32 (w % 4) ..),
-        # then the TMA warp and the MMA warp; with two query tiles they fill one more warpgroup (two
-        # warps idle) whose registers go to the softmax warpgroups through setmaxnreg
+        # then the K / V TMA warp, the MMA warp and the Q TMA warp; with two query tiles they fill one
+        # more warpgroup (one warp idle) whose registers go to the softmax warpgroups through setmaxnreg
         sm_warps = 4 * self.qt
         self.sm_threads = 32 * sm_warps
-        self.w_tma, self.w_mma = sm_warps, sm_warps + 1
-        self.threads = 32 * sm_warps + 128 if self.qt == 2 else 192
+        self.w_tma, self.w_mma, self.w_q = sm_warps, sm_warps + 1, sm_warps + 2
+        self.threads = 32 * sm_warps + 128 if self.qt == 2 else 224
         # each of the SM's four sub-partitions holds 16384 registers and ceil(warps / 4) of the warps
         # (of the tuned CTA or of meta.json's, whichever is larger: the module serves both)
         warps = -(-max(self.threads, kernel.threads_per_cta) // 32)
@@ -227,7 +230,7 @@ class TcAttention(TunedKernel):
             nonlocal nb
             nb += 1
             return (nb - 1) * 8
-        q_full, q_free = bar(), bar()
+        q_full, q_free = [bar() for _ in range(QT)], [bar() for _ in range(QT)]
         k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
         v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
         s_full = [bar() for _ in range(QT)]
@@ -302,12 +305,15 @@ class TcAttention(TunedKernel):
             ins(f"setmaxnreg.dec.sync.aligned.u32 {self.reg_split[1]}")
         ins(f"setp.eq.u32 {p}, {warp}, {self.w_mma}")
         ins(f"@{p} bra {role_mma}")
+        role_q = lab("at_qload")
+        ins(f"setp.eq.u32 {p}, {warp}, {self.w_q}")
+        ins(f"@{p} bra {role_q}")
         ins(f"setp.ne.u32 {p}, {warp}, {self.w_tma}")
-        ins(f"@{p} bra {end}")                           # the warpgroup's idle warps
+        ins(f"@{p} bra {end}")                           # the warpgroup's idle warp
 
         # ---------------- producer (one warp) ----------------
         is0 = t("pred")
-        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        elect_one(em, is0)
 
         def ring(i: str, n_st: int, s0: str, full0: int, empty0: int, mapname: str, row: str) -> None:
             st, buf, fb, eb = t("b32"), t("b32"), t("b32"), t("b32")
@@ -327,21 +333,7 @@ class TcAttention(TunedKernel):
         ins(f"mov.u32 {j}, 0")
         ptile, pblk = lab("at_prod_tile"), lab("at_prod_blk")
         place(ptile)
-        qrow, kvrow = tile_rows(tile)
-        first_tile = lab("at_prod_q")
-        ins(f"setp.eq.u32 {p}, {ti}, 0")
-        ins(f"@{p} bra {first_tile}")
-        prev = t("b32")
-        ins(f"sub.u32 {prev}, {ti}, 1")
-        kit.wait(f"{bars}+{q_free}", kit.parity(prev, 1), 0)      # the last S of the previous tile is done
-        place(first_tile)
-        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full}], {QT * qb}")
-        for g in range(QT):
-            qr = t("b32")
-            ins(f"add.u32 {qr}, {qrow}, {g * BM}")
-            for db in range(dblk):
-                ins(f"@{is0} {tma} [{q_s}+{g * qb + db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qr}}}], "
-                    f"[{bars}+{q_full}]")
+        _, kvrow = tile_rows(tile)
         ins(f"mov.u32 {blk}, 0")
         place(pblk)
         row = t("b32")
@@ -358,10 +350,53 @@ class TcAttention(TunedKernel):
         ins(f"@{p} bra {ptile}")
         ins(f"bra {end}")
 
+        # ---------------- Q loads (one warp) ----------------
+        # Q_g of tile t + 1 goes into Q_g's buffer once the last S_g of tile t is done (q_free[g]),
+        # each query tile on its own, and was prefetched into L2 while tile t ran: the load at the
+        # tile change reads L2, under the softmax of the last key block
+        place(role_q)
+        isq = t("pred")
+        elect_one(em, isq)
+        qti, qtile = t("b32"), t("b32")
+        ins(f"mov.u32 {qti}, 0")
+        ins(f"mov.u32 {qtile}, {cta}")
+        qtop = lab("at_q_tile")
+        place(qtop)
+        qrow, _ = tile_rows(qtile)
+        for g in range(QT):
+            first = lab("at_q_first")
+            ins(f"setp.eq.u32 {p}, {qti}, 0")
+            ins(f"@{p} bra {first}")
+            qprev = t("b32")
+            ins(f"sub.u32 {qprev}, {qti}, 1")
+            kit.wait(f"{bars}+{q_free[g]}", kit.parity(qprev, 1), 0)     # tile t's last S_g is done
+            place(first)
+            ins(f"@{isq} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{q_full[g]}], {qb}")
+            qr = t("b32")
+            ins(f"add.u32 {qr}, {qrow}, {g * BM}")
+            for db in range(dblk):
+                ins(f"@{isq} {tma} [{q_s}+{g * qb + db * BM * 128}], [{tmaps['q']}, {{{db * 64}, {qr}}}], "
+                    f"[{bars}+{q_full[g]}]")
+        ins(f"add.u32 {qti}, {qti}, 1")
+        ins(f"add.u32 {qtile}, {qtile}, {ncta}")
+        nopf = lab("at_q_nopf")
+        ins(f"setp.ge.u32 {p}, {qti}, {nt}")
+        ins(f"@{p} bra {nopf}")
+        nrow, _ = tile_rows(qtile)
+        for g in range(QT):
+            qr = t("b32")
+            ins(f"add.u32 {qr}, {nrow}, {g * BM}")
+            for db in range(dblk):
+                ins(f"@{isq} cp.async.bulk.prefetch.tensor.2d.L2.global [{tmaps['q']}, {{{db * 64}, {qr}}}]")
+        place(nopf)
+        ins(f"setp.lt.u32 {p}, {qti}, {nt}")
+        ins(f"@{p} bra {qtop}")
+        ins(f"bra {end}")
+
         # ---------------- MMA issuer (one warp) ----------------
         place(role_mma)
         ism = t("pred")
-        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        elect_one(em, ism)
         zero = t("b32")
         ins(f"mov.u32 {zero}, 0")
         hi = t("b32")
@@ -421,26 +456,26 @@ class TcAttention(TunedKernel):
             if release_v:
                 ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
 
-        def q_released(jj: str) -> None:
-            """After the S of a tile's last key block: its Q tiles may be overwritten."""
+        def q_released(g: int, jj: str) -> None:
+            """After S_g of a tile's last key block: Q_g may be overwritten."""
             if n_blk == 1:
-                ins(f"@{ism} {commit} [{bars}+{q_free}]")
+                ins(f"@{ism} {commit} [{bars}+{q_free[g]}]")
                 return
             r_, skipq = t("b32"), lab("at_q_keep")
             ins(f"rem.u32 {r_}, {jj}, {n_blk}")
             ins(f"setp.ne.u32 {p}, {r_}, {n_blk - 1}")
             ins(f"@{p} bra {skipq}")
-            ins(f"@{ism} {commit} [{bars}+{q_free}]")
+            ins(f"@{ism} {commit} [{bars}+{q_free[g]}]")
             place(skipq)
 
         # S_g(0) of the first tile; then per key block j: PV_g(j) and S_g(j + 1) for each group in
         # turn -- S_g(j + 1) may already belong to the next tile (its Q is loaded once q_free fires)
-        kit.wait(f"{bars}+{q_full}", zero, 1)
-        ins("tcgen05.fence::after_thread_sync")
         ks_, kb_ = wait_k(zero)
         for g in range(QT):
+            kit.wait(f"{bars}+{q_full[g]}", zero, 1)
+            ins("tcgen05.fence::after_thread_sync")
             issue_s(g, ks_, kb_, g == QT - 1)
-        q_released(zero)
+            q_released(g, zero)
         mj, mblk, mti = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {mj}, 0")
         ins(f"mov.u32 {mblk}, 0")
@@ -467,24 +502,22 @@ class TcAttention(TunedKernel):
             if g == 0:
                 nk = lab("at_nok")
                 ins(f"@!{more} bra {nk}")
-                sameq = lab("at_same_q")
-                ins(f"@!{newtile} bra {sameq}")
-                nq = t("b32")
-                ins(f"add.u32 {nq}, {mti}, 1")
-                kit.wait(f"{bars}+{q_full}", kit.parity(nq, 1), 1)    # the next tile's Q landed
-                place(sameq)
                 ks2, kb2 = wait_k(nxt)
                 ins(f"mov.u32 {ks_}, {ks2}")
                 ins(f"mov.u32 {kb_}, {kb2}")
                 place(nk)
             skip_s = lab("at_nos")
             ins(f"@!{more} bra {skip_s}")
+            sameq = lab("at_same_q")
+            ins(f"@!{newtile} bra {sameq}")
+            nq = t("b32")
+            ins(f"add.u32 {nq}, {mti}, 1")
+            kit.wait(f"{bars}+{q_full[g]}", kit.parity(nq, 1), 1)     # the next tile's Q_g landed
+            ins("tcgen05.fence::after_thread_sync")
+            place(sameq)
             issue_s(g, ks_, kb_, g == QT - 1)
+            q_released(g, nxt)
             place(skip_s)
-        noq = lab("at_noq")
-        ins(f"@!{more} bra {noq}")
-        q_released(nxt)
-        place(noq)
         ins(f"mov.u32 {mj}, {nxt}")
         ins(f"add.u32 {mblk}, {mblk}, 1")
         ins(f"setp.eq.u32 {p}, {mblk}, {n_blk}")
@@ -517,7 +550,7 @@ class TcAttention(TunedKernel):
         ins(f"mad.lo.u32 {srowa}, {lane}, {self.box_bytes}, {wstage}")
         ins(f"and.b32 {r7}, {lane}, 7")
         lead = t("pred")
-        ins(f"setp.eq.u32 {lead}, {lane}, 0")
+        elect_one(em, lead)
         tmap_o = tmap_address(em, self.tmap_set, 4, 3)
         sc = t("f32")
         ins(f"ld.global.nc.f32 {sc}, [{em.buffer_reg(self.pscale.name)}]")

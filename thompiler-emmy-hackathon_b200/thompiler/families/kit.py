@@ -73,6 +73,18 @@ def tmap_address(em, sel: str, nmaps: int, i: int) -> str:
     return r
 
 
+def elect_one(em, pred: str) -> None:
+    """Set ``pred`` in one lane of the warp (the lowest; run where all 32 lanes are converged).
+
+    The single-thread instructions of the tuned bodies (``tcgen05.mma`` / ``commit``, TMA loads
+    and stores) are guarded by ``elect.sync`` rather than by a lane-id comparison: with it a
+    warp issues a ``tcgen05.mma`` 128x128x16 in 23-25 cycles, against 46-48 under
+    ``setp.eq lane, 0`` (clock stamps after each of 48 back-to-back MMAs), and a 128x128x16 MMA
+    executes in 64 -- under the comparison the issuing warp, not the tensor pipe, set the pace
+    of the attention's key loop."""
+    em.ins(f"elect.sync {em.tmp('b32')}|{pred}, 0xffffffff")
+
+
 def desc_hi(sbo: int, layout: int = SWIZZLE_128B) -> int:
     """High word: stride byte offset, version 1, layout type."""
     return ((sbo >> 4) & 0x3FFF) | (1 << 14) | (layout << 29)

@@ -45,7 +45,8 @@ from __future__ import annotations
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
-from thompiler.families.kit import TMAP_RING, TMAP_SETS, TMAP_TABLE, declare_tmap_ring, select_tmap_set, tmap_address
+from thompiler.families.kit import (TMAP_RING, TMAP_SETS, TMAP_TABLE, declare_tmap_ring, elect_one,
+                                    select_tmap_set, tmap_address)
 from thompiler.families.tuning import TUNING
 from thompiler.lowering.types import F16, F32
 from thompiler.load import KernelInfo
@@ -390,7 +391,7 @@ class TcMatmul(TunedKernel):
 
         # ---------------- producer (warp 0) ----------------
         is0 = t("pred")
-        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        elect_one(em, is0)
         it, pu = t("b32"), t("b32")
         ins(f"mov.u32 {it}, 0")
         ins(f"mov.u32 {pu}, {cta}")
@@ -455,7 +456,7 @@ class TcMatmul(TunedKernel):
         # ---------------- MMA issuer (warp 1) ----------------
         place(role_mma)
         ism = t("pred")
-        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        elect_one(em, ism)
         it2, mu, lt = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {it2}, 0")
         ins(f"mov.u32 {lt}, 0")
@@ -540,7 +541,7 @@ class TcMatmul(TunedKernel):
         lane_off = t("b32")
         ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
         lane0 = t("pred")
-        ins(f"setp.eq.u32 {lane0}, {lane}, 0")
+        elect_one(em, lane0)
         ebase = t("b32")
         ins(f"sub.u32 {ebase}, {warp}, 2")
         ins(f"mad.lo.u32 {ebase}, {ebase}, {2 * STAGE_TILE}, {b_st}")

@@ -28,7 +28,7 @@ No TMA load uses cluster multicast: each CTA loads its own halves.
 
 from __future__ import annotations
 
-from thompiler.families.kit import Kit, desc_hi, idesc_f16, tmap_address
+from thompiler.families.kit import Kit, desc_hi, elect_one, idesc_f16, tmap_address
 from thompiler.families.matmul import BK, BM, EPI_WARPS, SM_COUNT, STAGE_TILE, TcMatmul
 from thompiler.families.base import TunedKernel
 from thompiler.families.tuning import TUNING
@@ -246,7 +246,7 @@ class TcMatmulPair(TcMatmul):
 
         # ---------------- producer (warp 0 of each CTA: this CTA's A rows and B half) ----------------
         is0, post = t("pred"), t("pred")
-        ins(f"setp.eq.u32 {is0}, {lane}, 0")
+        elect_one(em, is0)
         ins(f"and.pred {post}, {is0}, {lead_cta}")       # the leader posts both CTAs' bytes
         it, pu = t("b32"), t("b32")
         ins(f"mov.u32 {it}, 0")
@@ -298,7 +298,7 @@ class TcMatmulPair(TcMatmul):
         place(role_mma)
         ins(f"@!{lead_cta} bra {end}")
         ism = t("pred")
-        ins(f"setp.eq.u32 {ism}, {lane}, 0")
+        elect_one(em, ism)
         hi = t("b32")
         ins(f"mov.u32 {hi}, {desc_hi(1024)}")
         idesc = idesc_f16(PM, BN, b_mn_major=not self.b_kmajor)
@@ -366,7 +366,7 @@ class TcMatmulPair(TcMatmul):
         lane_off = t("b32")
         ins(f"shl.b32 {lane_off}, {quarter}, 21")        # (32 * quarter) << 16
         lane0 = t("pred")
-        ins(f"setp.eq.u32 {lane0}, {lane}, 0")
+        elect_one(em, lane0)
         ebase = t("b32")
         ins(f"sub.u32 {ebase}, {warp}, 2")
         ins(f"mad.lo.u32 {ebase}, {ebase}, {2 * STAGE_TILE}, {b_st}")
