@@ -56,6 +56,22 @@ def test_attention_medium_vs_expression(tmp_path, shape):
                                rtol=RTOL, atol=ATOL)
 
 
+@pytest.mark.parametrize("poly", [0, 2, 8])
+def test_attention_exponential_paths(tmp_path, monkeypatch, poly):
+    """P from the exponential unit alone (0), or with 2 or all 8 of every 8 score pairs from the
+    polynomial 2^x on the FMA pipe (the default takes 1): all within the f16 tolerance."""
+    from thompiler.families.tuning import TUNING
+    monkeypatch.setattr(TUNING, "attention_poly_pairs", poly)
+    d = synth.attention_package(tmp_path / "att", 1, 3, 512, 128)
+    pkg = problems.load_package(d)
+    ptx = problems.compile_package(pkg)
+    assert ("0x4B4000004B400000" in ptx["k_attention"]) == (poly > 0)     # 1.5 * 2^23, the rounding constant
+    res = problems.run_package(pkg, ptx)
+    x = problems.make_inputs(pkg)
+    np.testing.assert_allclose(res["outputs"]["attn"].astype(np.float64), _sdpa64(x["q"], x["k"], x["v"]),
+                               rtol=RTOL, atol=ATOL)
+
+
 @pytest.mark.parametrize("shape,grid", [((2, 3, 512, 128), 1), ((2, 3, 512, 128), 5), ((1, 2, 384, 64), 4)])
 def test_attention_persistent_tiles(tmp_path, shape, grid):
     """Fewer CTAs than (head, query-tile) tiles: each CTA walks several tiles, carrying its

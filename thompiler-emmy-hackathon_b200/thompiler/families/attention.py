@@ -43,6 +43,7 @@ import math
 
 from thompiler import ir
 from thompiler.families.base import TunedKernel
+from thompiler.families.tuning import TUNING
 from thompiler.families.kit import (TMAP_RING, TMAP_SETS, TMAP_TABLE, Kit, declare_tmap_ring, desc_hi, elect_one,
                                    idesc_f16, select_tmap_set, tmap_address)
 from thompiler.lowering.types import F16, F32
@@ -87,7 +88,8 @@ class TcAttention(TunedKernel):
             self.reg_split = (inc, dec)
         else:
             self.reg_split = None
-        self.ks, self.vs = ((2, 2) if self.qt == 2 else (3, 2)) if D == 128 else (STAGES, STAGES)
+        # K and V rings of equal depth: producer step j loads V(j) and K(j + 1) under one barrier
+        self.ks = self.vs = 2 if D == 128 else STAGES
         # per softmax warp: a 32-row staging box for the output's TMA stores, 128 bytes wide
         # (128B swizzle), one thread per row
         self.box_bytes = 128
@@ -95,6 +97,8 @@ class TcAttention(TunedKernel):
         self.smem = (self.qt * self.q_bytes + (self.ks + self.vs) * self.kv_bytes + self.stage_bytes
                      + 1024 + 256)
         self.tiles = heads * (Sq // (BM * self.qt))
+        self.poly_pairs = TUNING.attention_poly_pairs
+        assert 0 <= self.poly_pairs <= 8
 
     # ---- recognition -------------------------------------------------------------
 
@@ -231,8 +235,8 @@ class TcAttention(TunedKernel):
             nb += 1
             return (nb - 1) * 8
         q_full, q_free = [bar() for _ in range(QT)], [bar() for _ in range(QT)]
-        k_full, k_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]
-        v_full, v_empty = [bar() for _ in range(VS)], [bar() for _ in range(VS)]
+        k0_full = bar()                                   # K(0) of the CTA's first tile
+        kv_full, kv_empty = [bar() for _ in range(KS)], [bar() for _ in range(KS)]   # V(j) + K(j + 1)
         s_full = [bar() for _ in range(QT)]
         p_full = [bar() for _ in range(QT)]              # P_g stored by group g's 128 softmax threads
         o_done = [bar() for _ in range(QT)]
@@ -315,18 +319,24 @@ class TcAttention(TunedKernel):
         is0 = t("pred")
         elect_one(em, is0)
 
-        def ring(i: str, n_st: int, s0: str, full0: int, empty0: int, mapname: str, row: str) -> None:
-            st, buf, fb, eb = t("b32"), t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st}, {i}, {n_st}")
-            ins(f"mad.lo.u32 {buf}, {st}, {kvb}, {s0}")
-            ins(f"mad.lo.u32 {fb}, {st}, 8, {bars}")
-            ins(f"add.u32 {eb}, {fb}, {empty0}")
-            ins(f"add.u32 {fb}, {fb}, {full0}")
-            kit.wait(eb, kit.parity(i, n_st, flip=True), 0)
-            ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {kvb}")
+        # step j (over all of the CTA's key blocks, tile after tile): V(j) and K(j + 1) -- the keys
+        # of the next S, which may open the next tile -- into ring slots j % KS and (j + 1) % KS
+        # under kv_full[j % KS].  Their previous occupants V(j - KS) and K(j + 1 - KS) are
+        # consumed by the MMA warp's block j - KS, whose release goes to kv_empty[(j + 1) % KS]
+        # (the S(0) that consumes K(0), loaded first, releases as block -1, into kv_empty[0])
+        def load(mapname: str, sbase: str, slot: str, row: str, fb: str, pred: str) -> None:
+            buf = t("b32")
+            ins(f"mad.lo.u32 {buf}, {slot}, {kvb}, {sbase}")
             for db in range(dblk):
-                ins(f"@{is0} {tma} [{buf}+{db * BN * 128}], [{tmaps[mapname]}, {{{db * 64}, {row}}}], [{fb}]")
+                ins(f"@{pred} {tma} [{buf}+{db * BN * 128}], [{tmaps[mapname]}, {{{db * 64}, {row}}}], [{fb}]")
 
+        _, kvrow = tile_rows(cta)
+        ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{k0_full}], {kvb}")
+        zs = t("b32")
+        ins(f"mov.u32 {zs}, 0")
+        k0b = t("b32")
+        ins(f"add.u32 {k0b}, {bars}, {k0_full}")
+        load("k", k0, zs, kvrow, k0b, is0)
         ti, tile, j, blk = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {ti}, 0")
         ins(f"mov.u32 {tile}, {cta}")
@@ -334,13 +344,38 @@ class TcAttention(TunedKernel):
         ptile, pblk = lab("at_prod_tile"), lab("at_prod_blk")
         place(ptile)
         _, kvrow = tile_rows(tile)
+        nt_ = t("b32")
+        ins(f"add.u32 {nt_}, {tile}, {ncta}")
+        _, nkvrow = tile_rows(nt_)                       # the next tile's first key row (if it has one)
         ins(f"mov.u32 {blk}, 0")
         place(pblk)
+        st, fb, eb, hask, lk, lv = t("b32"), t("b32"), t("b32"), t("pred"), t("pred"), t("pred")
+        j1 = t("b32")
+        ins(f"add.u32 {j1}, {j}, 1")
+        ins(f"rem.u32 {eb}, {j1}, {KS}")
+        ins(f"mad.lo.u32 {eb}, {eb}, 8, {bars}")
+        ins(f"add.u32 {eb}, {eb}, {kv_empty[0]}")
+        kit.wait(eb, kit.parity(j1, KS, flip=True), 0)
+        ins(f"rem.u32 {st}, {j}, {KS}")
+        ins(f"mad.lo.u32 {fb}, {st}, 8, {bars}")
+        ins(f"add.u32 {fb}, {fb}, {kv_full[0]}")
+        ins(f"setp.lt.u32 {hask}, {j1}, {total}")
+        ins(f"and.pred {lk}, {is0}, {hask}")
+        ins(f"not.pred {lv}, {hask}")
+        ins(f"and.pred {lv}, {is0}, {lv}")
+        ins(f"@{lk} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {2 * kvb}")
+        ins(f"@{lv} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fb}], {kvb}")
         row = t("b32")
         ins(f"mad.lo.u32 {row}, {blk}, {BN}, {kvrow}")
-        ring(j, KS, k0, k_full[0], k_empty[0], "k", row)
-        ring(j, VS, v0, v_full[0], v_empty[0], "v", row)
-        ins(f"add.u32 {j}, {j}, 1")
+        load("v", v0, st, row, fb, is0)
+        krow, kst, pin = t("b32"), t("b32"), t("pred")
+        ins(f"add.u32 {krow}, {row}, {BN}")
+        ins(f"add.u32 {kst}, {blk}, 1")
+        ins(f"setp.ge.u32 {pin}, {kst}, {n_blk}")
+        ins(f"selp.u32 {krow}, {nkvrow}, {krow}, {pin}")       # K(j + 1) opens the next tile
+        ins(f"rem.u32 {kst}, {j1}, {KS}")
+        load("k", k0, kst, krow, fb, lk)
+        ins(f"mov.u32 {j}, {j1}")
         ins(f"add.u32 {blk}, {blk}, 1")
         ins(f"setp.lt.u32 {p}, {blk}, {n_blk}")
         ins(f"@{p} bra {pblk}")
@@ -408,8 +443,8 @@ class TcAttention(TunedKernel):
         ins(f"setp.eq.u32 {always}, {zero}, 0")
         ins(f"setp.ne.u32 {never}, {zero}, 0")
 
-        def issue_s(g: int, ks_: str, kb_: str, release_k: bool) -> None:
-            """S_g = Q_g K^T for the K tile in slot ks_ (already waited for)."""
+        def issue_s(g: int, ks_: str) -> None:
+            """S_g = Q_g K^T for the K tile at ks_ (already waited for)."""
             kd = kit.desc(ks_, 16, hi)
             dcol = t("b32")
             ins(f"add.u32 {dcol}, {tmem}, {S_COL + 128 * g}")
@@ -419,30 +454,12 @@ class TcAttention(TunedKernel):
                 ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], {a}, {bb}, {id_s}, "
                     f"{never if kk == 0 else always}")
             ins(f"@{ism} {commit} [{bars}+{s_full[g]}]")
-            if release_k:
-                ins(f"@{ism} {commit} [{kb_}+{k_empty[0]}]")
 
-        def wait_k(jj: str):
-            st_, ks_, kb_, kf = t("b32"), t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {jj}, {KS}")
-            ins(f"mad.lo.u32 {ks_}, {st_}, {kvb}, {k0}")
-            ins(f"mad.lo.u32 {kb_}, {st_}, 8, {bars}")
-            ins(f"add.u32 {kf}, {kb_}, {k_full[0]}")
-            kit.wait(kf, kit.parity(jj, KS), 1)
-            ins("tcgen05.fence::after_thread_sync")
-            return ks_, kb_
-
-        def issue_pv(g: int, jj: str, acc0: str, release_v: bool) -> None:
-            """O_g (+)= P_g V_jj, P_g read from TMEM (the TS form); acc0 false starts a tile."""
-            st_, vs_, vb_ = t("b32"), t("b32"), t("b32")
-            ins(f"rem.u32 {st_}, {jj}, {VS}")
-            ins(f"mad.lo.u32 {vb_}, {st_}, 8, {bars}")
-            if g == 0:
-                vf = t("b32")
-                ins(f"add.u32 {vf}, {vb_}, {v_full[0]}")
-                kit.wait(vf, kit.parity(jj, VS), 1)
-            ins("tcgen05.fence::after_thread_sync")
-            ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
+        def issue_pv(g: int, vs_: str, acc0: str, last: str) -> None:
+            """O_g (+)= P_g V for the V tile at vs_, P_g read from TMEM (the TS form); acc0 false
+            starts a tile.  o_done[g] is committed at a tile's last block only (the epilogue's
+            wait): within a tile the softmax's view of S_g(j + 1) already covers PV_g(j), which
+            the same thread issued before it."""
             vd = kit.desc(vs_, BN * 128, hi)
             dcol = t("b32")
             ins(f"add.u32 {dcol}, {tmem}, {O_COL + 128 * g}")
@@ -452,9 +469,7 @@ class TcAttention(TunedKernel):
                 bb = kit.desc_add(vd, kk * 16 * 128)
                 ins(f"@{ism} tcgen05.mma.cta_group::1.kind::f16 [{dcol}], [{a}], {bb}, {id_o}, "
                     f"{acc0 if kk == 0 else always}")
-            ins(f"@{ism} {commit} [{bars}+{o_done[g]}]")
-            if release_v:
-                ins(f"@{ism} {commit} [{vb_}+{v_empty[0]}]")
+            ins(f"@{last} {commit} [{bars}+{o_done[g]}]")
 
         def q_released(g: int, jj: str) -> None:
             """After S_g of a tile's last key block: Q_g may be overwritten."""
@@ -468,14 +483,16 @@ class TcAttention(TunedKernel):
             ins(f"@{ism} {commit} [{bars}+{q_free[g]}]")
             place(skipq)
 
-        # S_g(0) of the first tile; then per key block j: PV_g(j) and S_g(j + 1) for each group in
-        # turn -- S_g(j + 1) may already belong to the next tile (its Q is loaded once q_free fires)
-        ks_, kb_ = wait_k(zero)
+        # S_g(0) of the first tile; then per key block j: one wait for V(j) and K(j + 1), PV_g(j)
+        # and S_g(j + 1) for each group in turn -- S_g(j + 1) may already belong to the next tile
+        # (its Q_g is loaded once q_free[g] fires) -- and one release of the ring step
+        kit.wait(f"{bars}+{k0_full}", zero, 1)
         for g in range(QT):
             kit.wait(f"{bars}+{q_full[g]}", zero, 1)
             ins("tcgen05.fence::after_thread_sync")
-            issue_s(g, ks_, kb_, g == QT - 1)
+            issue_s(g, k0)
             q_released(g, zero)
+        ins(f"@{ism} {commit} [{bars}+{kv_empty[0]}]")                # K(0) consumed (block -1)
         mj, mblk, mti = t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {mj}, 0")
         ins(f"mov.u32 {mblk}, 0")
@@ -484,10 +501,21 @@ class TcAttention(TunedKernel):
         place(mtop)
         nxt = t("b32")
         ins(f"add.u32 {nxt}, {mj}, 1")
-        more, acc0, newtile = t("pred"), t("pred"), t("pred")
+        more, acc0, newtile, last = t("pred"), t("pred"), t("pred"), t("pred")
         ins(f"setp.lt.u32 {more}, {nxt}, {total}")
         ins(f"setp.ne.u32 {acc0}, {mblk}, 0")
         ins(f"setp.eq.u32 {newtile}, {mblk}, {n_blk - 1}")           # S(j + 1) opens the next tile
+        ins(f"and.pred {last}, {ism}, {newtile}")
+        st_, fb_, vs_, ks_ = t("b32"), t("b32"), t("b32"), t("b32")
+        ins(f"rem.u32 {st_}, {mj}, {KS}")
+        ins(f"mad.lo.u32 {fb_}, {st_}, 8, {bars}")
+        ins(f"mad.lo.u32 {vs_}, {st_}, {kvb}, {v0}")
+        kst = t("b32")
+        ins(f"rem.u32 {kst}, {nxt}, {KS}")
+        ins(f"mad.lo.u32 {ks_}, {kst}, {kvb}, {k0}")
+        kf = t("b32")
+        ins(f"add.u32 {kf}, {fb_}, {kv_full[0]}")
+        kit.wait(kf, kit.parity(mj, KS), 1)                          # V(j) and K(j + 1) landed
         for g in range(QT):
             kit.wait(f"{bars}+{p_full[g]}", kit.parity(mj, 1), 1)
             nowait = lab("at_o_ready")
@@ -498,14 +526,8 @@ class TcAttention(TunedKernel):
             ins(f"sub.u32 {pt}, {mti}, 1")
             kit.wait(f"{bars}+{o_free[g]}", kit.parity(pt, 1), 1)     # the previous tile's O_g was read
             place(nowait)
-            issue_pv(g, mj, acc0, g == QT - 1)
-            if g == 0:
-                nk = lab("at_nok")
-                ins(f"@!{more} bra {nk}")
-                ks2, kb2 = wait_k(nxt)
-                ins(f"mov.u32 {ks_}, {ks2}")
-                ins(f"mov.u32 {kb_}, {kb2}")
-                place(nk)
+            ins("tcgen05.fence::after_thread_sync")
+            issue_pv(g, vs_, acc0, last)
             skip_s = lab("at_nos")
             ins(f"@!{more} bra {skip_s}")
             sameq = lab("at_same_q")
@@ -515,9 +537,13 @@ class TcAttention(TunedKernel):
             kit.wait(f"{bars}+{q_full[g]}", kit.parity(nq, 1), 1)     # the next tile's Q_g landed
             ins("tcgen05.fence::after_thread_sync")
             place(sameq)
-            issue_s(g, ks_, kb_, g == QT - 1)
+            issue_s(g, ks_)
             q_released(g, nxt)
             place(skip_s)
+        ke = t("b32")
+        ins(f"mad.lo.u32 {ke}, {kst}, 8, {bars}")
+        ins(f"add.u32 {ke}, {ke}, {kv_empty[0]}")
+        ins(f"@{ism} {commit} [{ke}]")                      # V(j) and K(j + 1) consumed: release j
         ins(f"mov.u32 {mj}, {nxt}")
         ins(f"add.u32 {mblk}, {mblk}, 1")
         ins(f"setp.eq.u32 {p}, {mblk}, {n_blk}")
@@ -595,10 +621,7 @@ class TcAttention(TunedKernel):
         ins(f"mul.rn.f32 {l}, {l}, {alpha}")
         ins(f"setp.eq.u32 {p}, {blk2}, 0")
         ins(f"@{p} bra {noowait}")
-        prevb = t("b32")
-        ins(f"sub.u32 {prevb}, {sj}, 1")
-        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(prevb, 1), 3)
-        ins("tcgen05.fence::after_thread_sync")
+        # PV_g(j - 1) is complete: the commit this thread waited for (S_g(j)) covers it
         rw = 16                             # columns at a time: the scores hold the registers
         for c in range(D // rw):
             ov = [t("f32") for _ in range(rw)]
@@ -624,6 +647,7 @@ class TcAttention(TunedKernel):
         pair = t("b64"), t("b64")
         ins(f"mov.b64 {pair[0]}, {{{sc}, {sc}}}")
         ins(f"mov.b64 {pair[1]}, {{{negm}, {negm}}}")
+        ex2 = _Exp2(em) if self.poly_pairs else None
         for c in range(BN // 16):
             sv = srow[16 * c:16 * c + 16]
             packs = []
@@ -632,6 +656,9 @@ class TcAttention(TunedKernel):
                 d = t("b64")
                 ins(f"mov.b64 {d}, {{{x0}, {x1}}}")
                 ins(f"fma.rn.ftz.f32x2 {d}, {d}, {pair[0]}, {pair[1]}")
+                if k < self.poly_pairs:
+                    packs.append(ex2.pair(d, x0, x1))
+                    continue
                 ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
                 ins(f"ex2.approx.ftz.f32 {x0}, {x0}")
                 ins(f"ex2.approx.ftz.f32 {x1}, {x1}")
@@ -663,9 +690,7 @@ class TcAttention(TunedKernel):
         orow = t("b32")
         ins(f"add.u32 {orow}, {qrow_s}, {rowoff}")
         ins(f"sub.u32 {orow}, {orow}, {lane}")                    # the warp's first row
-        lastb = t("b32")
-        ins(f"sub.u32 {lastb}, {sj}, 1")
-        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(lastb, 1), 3)
+        kit.wait(f"{gb8}+{o_done[0]}", kit.parity(sti, 1), 3)           # the tile's last PV_g
         ins("tcgen05.fence::after_thread_sync")
         ov = [t("f32") for _ in range(D)]
         for c in range(D // 32):
@@ -718,6 +743,54 @@ class TcAttention(TunedKernel):
 def _f32bits(x: float) -> str:
     import struct
     return "%08X" % struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+class _Exp2:
+    """2^x for a pair of f32 lanes on the FMA pipe (packed f32x2), in place of two ex2.approx.
+
+    Range reduction in the Cody-Waite manner: x (clamped to >= -125, where 2^x already rounds to
+    0 in the f16 P tile) is split as x = j + f, j = round(x) by adding and subtracting 1.5 * 2^23,
+    |f| <= 1/2.  2^f comes from a degree-3 polynomial fitted for this kernel (least squares on
+    Chebyshev nodes of [-1/2, 1/2], reweighted toward equal relative error: at most 7.5e-5
+    relative, evaluated in f32, under the 2^-11 rounding of the f16 P), and j is added into the
+    exponent field as an integer: the low bits of (x + 1.5 * 2^23) hold j, so (its bits << 23)
+    is j << 23 modulo 2^32.
+    """
+
+    COEF = (0.9999280727914258, 0.6932609870112008, 0.24261113509452387, 0.055171666814684134)
+
+    def __init__(self, em):
+        self.em = em
+        self.k = []
+        for v in (12582912.0,) + self.COEF:
+            r = em.tmp("b64")
+            h = _f32bits(v)
+            em.ins(f"mov.b64 {r}, 0x{h}{h}")
+            self.k.append(r)
+
+    def pair(self, d: str, x0: str, x1: str) -> str:
+        em, ins = self.em, self.em.ins
+        mag, c0, c1, c2, c3 = self.k
+        ins(f"mov.b64 {{{x0}, {x1}}}, {d}")
+        ins(f"max.f32 {x0}, {x0}, 0fC2FA0000")
+        ins(f"max.f32 {x1}, {x1}, 0fC2FA0000")
+        x, tj, f, p = em.tmp("b64"), em.tmp("b64"), em.tmp("b64"), em.tmp("b64")
+        ins(f"mov.b64 {x}, {{{x0}, {x1}}}")
+        ins(f"add.rn.f32x2 {tj}, {x}, {mag}")
+        ins(f"sub.rn.f32x2 {f}, {tj}, {mag}")
+        ins(f"sub.rn.f32x2 {f}, {x}, {f}")
+        ins(f"fma.rn.f32x2 {p}, {f}, {c3}, {c2}")
+        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c1}")
+        ins(f"fma.rn.f32x2 {p}, {p}, {f}, {c0}")
+        j0, j1, p0, p1 = (em.tmp("b32") for _ in range(4))
+        ins(f"mov.b64 {{{j0}, {j1}}}, {tj}")
+        ins(f"mov.b64 {{{p0}, {p1}}}, {p}")
+        for j, q, x_ in ((j0, p0, x0), (j1, p1, x1)):
+            ins(f"mad.lo.u32 {q}, {j}, {1 << 23}, {q}")
+            ins(f"mov.b32 {x_}, {q}")
+        r = em.tmp("b64")
+        ins(f"mov.b64 {r}, {{{x0}, {x1}}}")
+        return r
 
 
 def _tree(em, op: str, regs: list[str], arity: int = 2, kind: str = "f32") -> str:

@@ -27,6 +27,9 @@ class Tuning:
     # programmatic dependent launch: tuned bodies signal griddepcontrol.launch_dependents and wait
     # (griddepcontrol.wait) before global accesses, and their launches may overlap the previous kernel
     pdl: bool = True
+    # attention: of every 8 score pairs, this many take 2^x from a polynomial on the FMA pipe
+    # instead of the exponential unit (0 .. 8)
+    attention_poly_pairs: int = 1
 
 
 TUNING = Tuning()
