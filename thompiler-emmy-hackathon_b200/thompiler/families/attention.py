@@ -11,15 +11,17 @@ reference).  Q, K, V and the output are f16 [..., S, D] buffers (D = 64 or
 run time.
 
 Tuned body: one CTA per (head, QT query tiles of 128), QT = 2 when S allows
-(384 threads), else 1 (192 threads):
+(384 threads), else 1 (224 threads):
   warps 0 .. 4QT-1  softmax, one warpgroup per query tile g; thread = query row,
             warp w reads TMEM lanes 32 (w % 4) ..;
-  warp 4QT  TMA: K and V tiles of 128 keys through their own rings
-            (128B-swizzled rows of 64 d);
+  warp 4QT  TMA: K and V tiles of 128 keys through two-slot rings
+            (128B-swizzled rows of 64 d); step j loads V(j) and K(j + 1) under
+            one barrier, so the MMA warp waits once per key block;
   warp 4QT+1  tcgen05 issuer: S_g = Q_g K_i^T (SS form, M = 128 queries,
             N = 128 keys, K = D) and O_g += P_g V_i (TS form: A = P_g from
             TMEM, B = V as an MN-major shared operand), ordered PV_0, S_0(next),
-            PV_1, S_1(next) so each group's softmax overlaps the other's MMAs;
+            PV_1, S_1(next) so each group's softmax overlaps the other's MMAs,
+            and one commit per block releases the ring step;
   warp 4QT+2  TMA: each query tile's Q_g once the previous tile's last S_g is
             done, and an L2 prefetch of the next tile's Q;
   with QT = 2 warp 11 completes the third warpgroup, which hands registers to
@@ -30,8 +32,9 @@ written over the first 64 columns of S_g.  Softmax per row and key block: the
 128 scores in registers (four loads, one wait), a three-input max tree, O and
 the running sum rescaled only when the max grew by more than 2^8 (P <= 256
 stays exact in f16, the rescale is rare), P = 2^(s c' - m) with packed f32x2
-FMAs and ex2.approx, packed sums, f16 pairs stored back to TMEM.  Epilogue: O / l as f16 through each warp's
-own 32-row staging box (128B-swizzled), one TMA store per box.
+FMAs and ex2.approx (one pair in 8 from a polynomial on the FMA pipe), packed
+sums, f16 pairs stored back to TMEM.  Epilogue: O / l as f16 through each
+warp's own 32-row staging box (128B-swizzled), one TMA store per box.
 Scores run in the base-2 domain: c' = log2(e) / c, so exp(x) = 2^(x log2 e)
 exactly as the IR's exp lowering.  All mbarrier waits are bounded
 (thompiler.families.kit).
