@@ -110,7 +110,10 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tile
     assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, want_bn)
     assert fam.b_bytes == fam.BN // 2 * 64 * 2 and fam.a_bytes == 128 * 64 * 2
     assert (fam.rem, fam.parts) == (rem, parts)                  # the last wave cut along K
-    assert fam.units == tiles - rem + rem * parts
+    # or, where K is too short for parts, along N into 256 x 128 halves (K-major B, 256 wide)
+    hrem = 14 if (M, N, K, lay, want_bn) == (8192, 3072, 1024, "col", 256) else 0
+    assert fam.hrem == hrem
+    assert fam.units == tiles - rem - hrem + rem * parts + 2 * hrem
     assert fam.ctas == 2 * min(fam.units, 74)
     side = fam.sidecar()
     assert side["cluster"] == [2, 1, 1] and side["grid"] == [fam.ctas, 1, 1]

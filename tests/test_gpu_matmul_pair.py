@@ -121,3 +121,26 @@ def test_pair_split_tail(tmp_path, grid):
     ref = a.double() @ b.double().t()
     assert (c.double() - ref).abs().max().item() < 1e-4
     k.close()
+
+
+@pytest.mark.parametrize("grid", [0, 10])
+def test_pair_half_tail(tmp_path, grid):
+    """A partial last wave whose K is too short to cut (2048 x 2560 x 1024: 80 pair tiles on 74
+    pairs, 16 K blocks): its 6 tiles run as 12 units of 256 x 128 over the full K, N = 128 MMAs
+    on the same B boxes loaded at the half's column offset, no workspace.  grid 10 (5 pairs)
+    puts whole tiles and halves on each pair; the last tile column's second half reads rows
+    past N as the tensor map's zero fill."""
+    import torch
+    M, N, K = 2048, 2560, 1024
+    d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
+    k = DeviceKernel(d / "k_matmul_f16.ir.json")
+    assert k.family == "tcgen05-matmul-pair" and "thc_tail_ws" not in k.ptx
+    if grid:
+        k.plan.grid = (grid, 1, 1)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = (torch.randn(M, K, device="cuda", generator=g) * 0.02).half()
+    b = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    c = _run_twice(k, a, b, M, N, torch.cuda.current_stream().cuda_stream)
+    ref = a.double() @ b.double().t()
+    assert (c.double() - ref).abs().max().item() < 1e-4
+    k.close()

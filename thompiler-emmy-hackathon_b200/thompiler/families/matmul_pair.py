@@ -103,13 +103,22 @@ class TcMatmulPair(TcMatmul):
         # the last, partial wave of pair tiles: its `rem` tiles are cut along K into `parts` units,
         # as in the single-CTA kernel (each CTA of a pair keeps its own partial and counter)
         kblocks = self.Ks // BK
-        rem = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
+        rem0 = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
+        rem = rem0
         parts = min(kblocks // TUNING.matmul_tail_kblocks, PAIR_SLOTS // rem) if rem else 1
         if S != 1 or c.ty is not F32 or parts < 2 or not TUNING.matmul_split_tail:
             rem, parts = 0, 1
+        # a partial last wave the K split does not take (its parts would be too short): each of
+        # its 256-wide tiles becomes two 256 x 128 units over the full K (no partials), as long as
+        # they fit one wave of pairs.  B must be K-major: a half unit loads the same 128-row box of
+        # B at its own column offset and its N = 128 MMA reads the first 64 rows of each CTA's box.
+        self.hrem = 0
+        if (not rem and rem0 and 2 * rem0 <= PAIR_SLOTS and bn == 256 and S == 1 and b_kmajor
+                and TUNING.matmul_half_tail):
+            self.hrem = rem0
         self.rem, self.parts = rem, parts
-        self.full_tiles = self.tiles - rem
-        self.units = self.full_tiles + rem * parts
+        self.full_tiles = self.tiles - rem - self.hrem
+        self.units = self.full_tiles + rem * parts + 2 * self.hrem
         self.pairs = min(self.units, PAIR_SLOTS)
         self.ctas = 2 * self.pairs
 
@@ -220,7 +229,8 @@ class TcMatmulPair(TcMatmul):
 
         def unit(u: str):
             """Work unit u -> (pair tile, first and end K block, is-whole-tile predicate, part):
-            units below full_tiles are whole tiles, the rest cut the last tiles along K."""
+            units below full_tiles are whole tiles, the rest cut the last tiles along K into
+            parts, or along N into halves (part = the half, 0 or 1)."""
             tile_, lo, hi_, part, v, whole = t("b32"), t("b32"), t("b32"), t("b32"), t("b32"), t("pred")
             ins(f"setp.lt.u32 {whole}, {u}, {full_tiles}")
             ins(f"mov.u32 {tile_}, {u}")
@@ -236,6 +246,11 @@ class TcMatmulPair(TcMatmul):
                 ins(f"@!{whole} div.u32 {lo}, {lo}, {parts}")
                 ins(f"@!{whole} mad.lo.u32 {hi_}, {part}, {kblocks}, {kblocks}")
                 ins(f"@!{whole} div.u32 {hi_}, {hi_}, {parts}")
+            if self.hrem:
+                ins(f"sub.u32 {v}, {u}, {full_tiles}")
+                ins(f"@!{whole} shr.u32 {tile_}, {v}, 1")
+                ins(f"@!{whole} add.u32 {tile_}, {tile_}, {full_tiles}")
+                ins(f"@!{whole} and.b32 {part}, {v}, 1")
             return tile_, lo, hi_, whole, part
 
         role_mma, role_epi = lab("mp_mma"), lab("mp_epi")
@@ -255,13 +270,21 @@ class TcMatmulPair(TcMatmul):
         ins(f"setp.ge.u32 {p}, {pu}, {units}")
         ins(f"@{p} bra {end}")
         place(ptop)
-        ptile, kb, kend, _, _ = unit(pu)
+        ptile, kb, kend, pwhole, ppart = unit(pu)
         tm_, tn_, ts_ = decode(ptile)
         m0, n0, k0 = t("b32"), t("b32"), t("b32")
         ins(f"mul.lo.u32 {m0}, {tm_}, {PM}")
         ins(f"mad.lo.u32 {m0}, {rank}, {BM}, {m0}")
         ins(f"mul.lo.u32 {n0}, {tn_}, {BN}")
+        if self.hrem:
+            # half unit h: columns 128 h .. of the tile, 64 per CTA; the box still spans 128 rows
+            # (the second 64 are not read; past N they are the tensor map's zero fill)
+            nh = t("b32")
+            ins(f"mad.lo.u32 {nh}, {ppart}, {BN // 2}, {n0}")
+            ins(f"mad.lo.u32 {nh}, {rank}, {HN // 2}, {nh}")
         ins(f"mad.lo.u32 {n0}, {rank}, {HN}, {n0}")
+        if self.hrem:
+            ins(f"@!{pwhole} mov.u32 {n0}, {nh}")
         ins(f"mul.lo.u32 {k0}, {ts_}, {self.Ks}")
         ktop = lab("mp_prod_k")
         place(ktop)
@@ -315,7 +338,11 @@ class TcMatmulPair(TcMatmul):
         ins(f"setp.ge.u32 {p}, {mu}, {units}")
         ins(f"@{p} bra {end}")
         place(mtop)
-        _, kb2, kend2, _, _ = unit(mu)
+        _, kb2, kend2, mwhole, _ = unit(mu)
+        idr = t("b32")
+        ins(f"mov.u32 {idr}, {idesc}")
+        if self.hrem:
+            ins(f"@!{mwhole} mov.u32 {idr}, {idesc_f16(PM, BN // 2, b_mn_major=not self.b_kmajor)}")
         kfirst = t("b32")
         ins(f"mov.u32 {kfirst}, {kb2}")
         buf, ab = t("b32"), t("b32")
@@ -344,7 +371,7 @@ class TcMatmulPair(TcMatmul):
         for k in range(BK // 16):
             ad = kit.desc_add(ad0, k * 32)
             bd = kit.desc_add(bd0, k * 32 if self.b_kmajor else k * 16 * 128)
-            ins(f"@{ism} tcgen05.mma.cta_group::2.kind::f16 [{dt}], {ad}, {bd}, {idesc}, "
+            ins(f"@{ism} tcgen05.mma.cta_group::2.kind::f16 [{dt}], {ad}, {bd}, {idr}, "
                 f"{first if k == 0 else always}")
         ins(f"@{ism} {mcommit} [{fb2}+{empty_off}], {mask}")
         ins(f"add.u32 {it2}, {it2}, 1")
@@ -419,16 +446,16 @@ class TcMatmulPair(TcMatmul):
             ins("bar.warp.sync -1")
             ins(f"@{lane0} mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{lab3}+{acce_off}]")
 
-        def store_boxes(values, free_after_last: bool) -> None:
-            """Columns c0 .. c0 + cw of this warp's 32 rows, for each c0: ``values(c0)`` gives the
-            row's cw values as b32 registers (f32, or f16 pairs), staged (64-byte swizzle) and
-            stored with TMA."""
-            for j, c0 in enumerate(range(0, BN, cw)):
+        def store_boxes(values, free_after_last: bool, width: int = BN) -> None:
+            """Columns c0 .. c0 + cw of this warp's 32 rows, for each c0 < width: ``values(c0)``
+            gives the row's cw values as b32 registers (f32, or f16 pairs), staged (64-byte
+            swizzle) and stored with TMA."""
+            for j, c0 in enumerate(range(0, width, cw)):
                 sbuf = stage_buf[j % 2]
                 ins(f"@{lane0} cp.async.bulk.wait_group.read 1")
                 ins("bar.warp.sync -1")
                 v = values(c0)
-                if free_after_last and c0 + cw == BN:
+                if free_after_last and c0 + cw == width:
                     free_accumulator()
                 for i in range(4):
                     a_ = t("b32")
@@ -457,9 +484,15 @@ class TcMatmulPair(TcMatmul):
             return v
 
         tail = lab("mp_epi_tail")
-        if self.rem:
+        if self.rem or self.hrem:
             ins(f"@!{whole3} bra {tail}")
         store_boxes(from_tmem, True)
+        if self.hrem:
+            # a half unit: 128 columns of the tile, starting at 128 h
+            ins(f"bra {enext}")
+            place(tail)
+            ins(f"mad.lo.u32 {col0}, {part3}, {BN // 2}, {col0}")
+            store_boxes(from_tmem, True, BN // 2)
         if self.rem:
             ins(f"bra {enext}")
             self._pair_tail(tail, enext, tile3, part3, rank, taddr, row, bars, ls, store_boxes, free_accumulator,
