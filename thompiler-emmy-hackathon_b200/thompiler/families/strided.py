@@ -609,7 +609,8 @@ class StridedReduce(TunedKernel):
         em.ins(f"mad.wide.u32 {slot}, {cta}, {S * ty.nbytes}, {parts}")
         for i, s in enumerate(self.states):
             em.ins(f"st.global.cg.{ty.mov} [{slot}+{i * ty.nbytes}], {em.get(s)}")
-        em.ins("fence.acq_rel.gpu")
+        # the arrival is an acq_rel atomic: its release orders this thread's partial stores before
+        # it, and the last CTA's acquire (then its barrier and fence) makes them visible to the fold
         old, lim, flag = em.tmp("b32"), em.tmp("b32"), em.tmp("b32")
         em.ins(f"sub.u32 {lim}, {nct}, 1")
         em.ins(f"atom.acq_rel.gpu.global.inc.u32 {old}, [{cnt}], {lim}")
