@@ -86,10 +86,10 @@ def test_strided_sum_plans():
 
 
 @pytest.mark.parametrize("M,N,K,lay,bn,want_bn,tiles,stages,rem,parts", [
-    (4096, 4096, 4096, "col", 0, 256, 256, 6, 34, 2), (8192, 3072, 1024, "col", 0, 256, 384, 6, 0, 1),
+    (4096, 4096, 4096, "col", 0, 256, 256, 6, 0, 1), (8192, 3072, 1024, "col", 0, 256, 384, 6, 0, 1),
     (8192, 3072, 1024, "col", 192, 192, 512, 6, 0, 1), (8192, 3072, 1024, "row", 0, 256, 384, 6, 0, 1),
     (6400, 768, 1024, "col", 0, 192, 100, 6, 0, 1),
-    (2048, 2560, 2048, "col", 0, 256, 80, 6, 6, 2), (256, 128, 256, "row", 0, 128, 1, 8, 0, 1),
+    (2048, 2560, 2048, "col", 0, 256, 80, 6, 0, 1), (256, 128, 256, "row", 0, 128, 1, 8, 0, 1),
     (512, 256, 256, "col", 128, 128, 4, 8, 0, 1)])
 def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tiles, stages, rem, parts):
     """The CTA-pair matmul (the default where it applies): 256 x BN pair tiles, each CTA's stage A 128 x 64 plus half
@@ -110,8 +110,9 @@ def test_matmul_pair_plan(tmp_path, monkeypatch, M, N, K, lay, bn, want_bn, tile
     assert (fam.tiles, fam.stages, fam.BN) == (tiles, stages, want_bn)
     assert fam.b_bytes == fam.BN // 2 * 64 * 2 and fam.a_bytes == 128 * 64 * 2
     assert (fam.rem, fam.parts) == (rem, parts)                  # the last wave cut along K
-    # or, where K is too short for parts, along N into 256 x 128 halves (K-major B, 256 wide)
-    hrem = 14 if (M, N, K, lay, want_bn) == (8192, 3072, 1024, "col", 256) else 0
+    # or, where its tiles halved fit one wave (K-major B, 256 wide), along N into 256 x 128 units
+    hrem = {(8192, 3072, 1024): 14, (4096, 4096, 4096): 34, (2048, 2560, 2048): 6}.get((M, N, K), 0) \
+        if (lay, want_bn) == ("col", 256) else 0
     assert fam.hrem == hrem
     assert fam.units == tiles - rem - hrem + rem * parts + 2 * hrem
     assert fam.ctas == 2 * min(fam.units, 74)
@@ -170,3 +171,17 @@ def test_matmul_f32_declines_an_accumulating_output(tmp_path):
     meta["kernels"][0]["zero_outputs"] = []
     (d / "meta.json").write_text(json.dumps(meta))
     assert recognise(_kernel(_ir(d))) is None
+
+
+@pytest.mark.parametrize("M,N,K,rem,parts", [(4096, 4096, 4096, 34, 2), (2048, 2560, 2048, 6, 2),
+                                            (8192, 3072, 1024, 0, 1)])
+def test_matmul_pair_k_split_plan(tmp_path, monkeypatch, M, N, K, rem, parts):
+    """With the half tail off the pair kernel cuts a partial last wave along K, where K holds at
+    least two parts of 16 blocks (the rectangle's 16 blocks do not: it keeps whole tiles)."""
+    from thompiler.families.matmul_pair import TcMatmulPair
+    monkeypatch.setattr(TUNING, "matmul_pair", True)
+    monkeypatch.setattr(TUNING, "matmul_half_tail", False)
+    fam = recognise(_kernel(_ir(synth.matmul_package(tmp_path / "mm", M, N, K))))
+    assert isinstance(fam, TcMatmulPair)
+    assert (fam.rem, fam.parts, fam.hrem) == (rem, parts, 0)
+    assert ("thc_tail_ws" in fam.emit()) == bool(rem)

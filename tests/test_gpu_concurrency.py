@@ -31,11 +31,14 @@ def _att_ref(q, k, v):
     return torch.softmax(s, -1) @ v.float()
 
 
-def test_two_modules_on_two_streams(tmp_path):
-    """One attention module and one matmul module (a split-tail shape), each launched on six
-    buffer sets -- more than the module's tensor-map sets -- alternating between two streams,
-    interleaved; every output against float64 / float32 references."""
+def test_two_modules_on_two_streams(tmp_path, monkeypatch):
+    """One attention module and one matmul module (a K-split tail shape, the half tail switched
+    off so the per-set partials and counters are exercised), each launched on six buffer sets --
+    more than the module's tensor-map sets -- alternating between two streams, interleaved;
+    every output against float64 / float32 references."""
     import torch
+    from thompiler.families.tuning import TUNING
+    monkeypatch.setattr(TUNING, "matmul_half_tail", False)
     M, N, K = 2048, 2560, 2048                      # 80 pair tiles on 74 pairs: a split tail
     mm = DeviceKernel(synth.matmul_package(tmp_path / "mm", M, N, K) / "k_matmul_f16.ir.json")
     assert mm.plan.counters == ["thc_tile_arrivals"] and mm.module.sidecar["tmap_sets"] == TMAP_SETS

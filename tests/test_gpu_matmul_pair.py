@@ -102,13 +102,15 @@ def test_pair_large(tmp_path, M, N, K, grid):
 
 
 @pytest.mark.parametrize("grid", [0, 10])
-def test_pair_split_tail(tmp_path, grid):
+def test_pair_split_tail(tmp_path, monkeypatch, grid):
     """More pair tiles than pairs with a partial last wave (2048 x 2560 x 2048: 80 tiles of
-    256 x 256 on 74 pairs, 6 left over): those are cut along K into two parts whose partials
+    256 x 256 on 74 pairs, 6 left over), with the half tail switched off: those are cut along K
+    into two parts whose partials
     meet in the module's workspace per tile and CTA rank, the last part to arrive adding them in
     part order.  grid 10 (5 pairs) puts several whole tiles and several parts on each pair."""
     import torch
     M, N, K = 2048, 2560, 2048
+    monkeypatch.setattr(TUNING, "matmul_half_tail", False)          # the K split (else the half tail)
     d = synth.matmul_package(tmp_path / "mm", M, N, K, b_layout="col", out_dtype="f32")
     k = DeviceKernel(d / "k_matmul_f16.ir.json")
     assert k.family == "tcgen05-matmul-pair" and "thc_tail_ws" in k.ptx

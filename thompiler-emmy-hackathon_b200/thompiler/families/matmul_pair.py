@@ -104,18 +104,18 @@ class TcMatmulPair(TcMatmul):
         # as in the single-CTA kernel (each CTA of a pair keeps its own partial and counter)
         kblocks = self.Ks // BK
         rem0 = self.tiles % PAIR_SLOTS if self.tiles > PAIR_SLOTS else 0
-        rem = rem0
+        # the partial last wave: where its tiles halved fit one wave of pairs, each 256-wide tile
+        # becomes two 256 x 128 units over the full K (no partials; measured faster than the K
+        # split on 4096^3, and the only cut for a K too short to split).  B must be K-major: a half
+        # unit loads the same 128-row box of B at its own column offset and its N = 128 MMA reads
+        # the first 64 rows of each CTA's box.  Otherwise the tiles are cut along K into parts.
+        self.hrem = 0
+        if rem0 and 2 * rem0 <= PAIR_SLOTS and bn == 256 and S == 1 and b_kmajor and TUNING.matmul_half_tail:
+            self.hrem = rem0
+        rem = 0 if self.hrem else rem0
         parts = min(kblocks // TUNING.matmul_tail_kblocks, PAIR_SLOTS // rem) if rem else 1
         if S != 1 or c.ty is not F32 or parts < 2 or not TUNING.matmul_split_tail:
             rem, parts = 0, 1
-        # a partial last wave the K split does not take (its parts would be too short): each of
-        # its 256-wide tiles becomes two 256 x 128 units over the full K (no partials), as long as
-        # they fit one wave of pairs.  B must be K-major: a half unit loads the same 128-row box of
-        # B at its own column offset and its N = 128 MMA reads the first 64 rows of each CTA's box.
-        self.hrem = 0
-        if (not rem and rem0 and 2 * rem0 <= PAIR_SLOTS and bn == 256 and S == 1 and b_kmajor
-                and TUNING.matmul_half_tail):
-            self.hrem = rem0
         self.rem, self.parts = rem, parts
         self.full_tiles = self.tiles - rem - self.hrem
         self.units = self.full_tiles + rem * parts + 2 * self.hrem

@@ -24,8 +24,8 @@ class Tuning:
     matmul_split_tail: bool = True
     # the fewest 64-deep K blocks a part of a split tile keeps (CTA-pair kernel)
     matmul_tail_kblocks: int = 16
-    # CTA-pair kernel: a partial last wave that the K split does not take (K too short) has its
-    # 256-wide tiles cut along N into two 256 x 128 units
+    # CTA-pair kernel: a partial last wave whose tiles, halved, fit one wave of pairs has its
+    # 256-wide tiles cut along N into two 256 x 128 units (else, or when False, the K split)
     matmul_half_tail: bool = True
     # programmatic dependent launch: tuned bodies signal griddepcontrol.launch_dependents and wait
     # (griddepcontrol.wait) before global accesses, and their launches may overlap the previous kernel
