@@ -335,11 +335,11 @@ class TcAttention(TunedKernel):
 
         _, kvrow = tile_rows(cta)
         ins(f"@{is0} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{bars}+{k0_full}], {kvb}")
-        zs = t("b32")
-        ins(f"mov.u32 {zs}, 0")
-        k0b = t("b32")
-        ins(f"add.u32 {k0b}, {bars}, {k0_full}")
-        load("k", k0, zs, kvrow, k0b, is0)
+        slot0 = t("b32")
+        ins(f"mov.u32 {slot0}, 0")
+        k0_bar = t("b32")
+        ins(f"add.u32 {k0_bar}, {bars}, {k0_full}")
+        load("k", k0, slot0, kvrow, k0_bar, is0)                   # K(0) of the first tile, slot 0
         ti, tile, j, blk = t("b32"), t("b32"), t("b32"), t("b32")
         ins(f"mov.u32 {ti}, 0")
         ins(f"mov.u32 {tile}, {cta}")
@@ -371,11 +371,11 @@ class TcAttention(TunedKernel):
         row = t("b32")
         ins(f"mad.lo.u32 {row}, {blk}, {BN}, {kvrow}")
         load("v", v0, st, row, fb, is0)
-        krow, kst, pin = t("b32"), t("b32"), t("pred")
+        krow, kst, opens = t("b32"), t("b32"), t("pred")
         ins(f"add.u32 {krow}, {row}, {BN}")
-        ins(f"add.u32 {kst}, {blk}, 1")
-        ins(f"setp.ge.u32 {pin}, {kst}, {n_blk}")
-        ins(f"selp.u32 {krow}, {nkvrow}, {krow}, {pin}")       # K(j + 1) opens the next tile
+        ins(f"add.u32 {kst}, {blk}, 1")                             # K(j + 1)'s block in this tile ...
+        ins(f"setp.ge.u32 {opens}, {kst}, {n_blk}")
+        ins(f"selp.u32 {krow}, {nkvrow}, {krow}, {opens}")     # ... or the next tile's first
         ins(f"rem.u32 {kst}, {j1}, {KS}")
         load("k", k0, kst, krow, fb, lk)
         ins(f"mov.u32 {j}, {j1}")
